@@ -1,0 +1,474 @@
+// C ABI of flashcart_b200 (declared in include/flashcart_b200.h): argument checks,
+// zero-filling of accumulated outputs, and dispatch to the compiled kernels.
+#include <string>
+#include <cstdio>
+#include <cstdarg>
+
+#include "tp_common.cuh"
+#include "linear.cuh"
+#include "gen/tp_dispatch.inc"
+
+#ifndef FC_VERSION_STRING
+#define FC_VERSION_STRING "0.1.0"
+#endif
+
+namespace fc {
+
+template <typename T> int irreps_fwd_dispatch(const T*, T*, int64_t, int, cudaStream_t);
+template <typename T> int irreps_bwd_dispatch(const T*, const T*, T*, int64_t, int, cudaStream_t);
+template <typename T>
+int irreps_dbwd_dispatch(const T*, const T*, const T*, T*, T*, int64_t, int, cudaStream_t);
+int build_rowptr(const int64_t*, int64_t, int64_t, int64_t*, int*, cudaStream_t);
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+static int launch_status(int rc, const char* what) {
+  if (rc == 0) return FC_OK;
+#ifndef FC_HOST_EMU
+  if (rc == FC_ERR_LAUNCH) return fail(FC_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(cudaGetLastError()));
+#endif
+  return fail(rc, "%s failed with status %d", what, rc);
+}
+
+static int zero_fill(void* p, int64_t bytes, cudaStream_t s) {
+  if (p == nullptr || bytes <= 0) return 0;
+#ifdef FC_HOST_EMU
+  std::memset(p, 0, (size_t)bytes);
+  return 0;
+#else
+  return cudaMemsetAsync(p, 0, (size_t)bytes, s) == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+#endif
+}
+
+static bool path_ok(int l1, int l2, int lo) {
+  if (l1 < 0 || l2 < 0 || lo < 0) return false;
+  const int d = l1 > l2 ? l1 - l2 : l2 - l1;
+  return d <= lo && lo <= l1 + l2 && ((l1 + l2 + lo) & 1) == 0;
+}
+
+// Path counts per output rank, same enumeration as o3/utils.py:157-203.
+static void count_paths(const fc_tp_desc* d, int* npl) {
+  const int lmax = d->in1_l_max > d->in2_l_max ? d->in1_l_max : d->in2_l_max;
+  for (int lo = 0; lo <= d->out_l_max; ++lo) {
+    npl[lo] = 0;
+    for (int l1 = 0; l1 <= lmax; ++l1)
+      for (int l2 = 0; l2 <= l1; ++l2) {
+        if (path_ok(l1, l2, lo) && l1 <= d->in1_l_max && l2 <= d->in2_l_max) ++npl[lo];
+        if (!d->symmetric_product && l2 < l1 && path_ok(l1, l2, lo) && l1 <= d->in2_l_max && l2 <= d->in1_l_max)
+          ++npl[lo];
+      }
+  }
+}
+
+static int check_desc(const fc_tp_desc* d) {
+  if (d == nullptr) return fail(FC_ERR_INVALID, "tensor product: null descriptor");
+  if (d->in1_l_max < 0 || d->in2_l_max < 0 || d->out_l_max < 0)
+    return fail(FC_ERR_INVALID, "tensor product: negative rank");
+  if (d->in1_l_max > FC_MAX_L || d->in2_l_max > FC_MAX_L || d->out_l_max > FC_MAX_L)
+    return fail(FC_ERR_UNSUPPORTED,
+                "tensor product supports l_max <= %d; got in1_l_max=%d, in2_l_max=%d, out_l_max=%d.", FC_MAX_L,
+                d->in1_l_max, d->in2_l_max, d->out_l_max);
+  if (d->in1_features < 1 || d->in2_features < 1)
+    return fail(FC_ERR_INVALID, "tensor product: features must be positive");
+  if (!(d->in1_features == d->in2_features || d->in1_features == 1 || d->in2_features == 1))
+    return fail(FC_ERR_INVALID,
+                "Input dimensions must match unless one of them is 1. Got in1_features=%d and in2_features=%d.",
+                d->in1_features, d->in2_features);
+  if (d->dtype != FC_F32 && d->dtype != FC_F64) return fail(FC_ERR_INVALID, "tensor product: bad dtype %d", d->dtype);
+  return FC_OK;
+}
+
+static const TpSigEntry* find_sig(const fc_tp_desc* d) {
+  const int sym = d->symmetric_product ? 1 : 0;
+  for (int k = 0; k < kNumTpSignatures; ++k) {
+    const TpSigEntry& e = kTpSignatures[k];
+    if (e.l1 == d->in1_l_max && e.l2 == d->in2_l_max && e.lo == d->out_l_max && e.sym == sym) return &e;
+  }
+  return nullptr;
+}
+
+static int64_t out_dim(const fc_tp_desc* d) {
+  int npl[FC_MAX_L + 1];
+  count_paths(d, npl);
+  const int F = d->in1_features > d->in2_features ? d->in1_features : d->in2_features;
+  int64_t s = 0;
+  for (int l = 0; l <= d->out_l_max; ++l) {
+    if (d->reduce_paths) s += npl[l] ? (2 * l + 1) * (int64_t)F : 0;
+    else s += (int64_t)npl[l] * (2 * l + 1) * F;
+  }
+  return s;
+}
+
+template <typename P>
+static void fill_common(P& p, const fc_tp_desc* d, const int64_t* rowptr, const int64_t* idx_j, int64_t n_rows,
+                        int64_t n_in1, int32_t* status) {
+  p.rowptr = rowptr;
+  p.idx_j = idx_j;
+  p.n_rows = n_rows;
+  p.n_in1 = n_in1;
+  p.F1 = d->in1_features;
+  p.F2 = d->in2_features;
+  p.F = p.F1 > p.F2 ? p.F1 : p.F2;
+  p.shared_w = d->shared_weights ? 1 : 0;
+  p.reduce = d->reduce_paths ? 1 : 0;
+  p.status = reinterpret_cast<int*>(status);
+}
+
+// ------------------------------------------------------------------ linear helpers
+
+static int check_linear(const fc_linear_desc* d) {
+  if (d == nullptr) return fail(FC_ERR_INVALID, "linear: null descriptor");
+  if (d->n_active < 0 || d->n_active > FC_MAX_L + 1)
+    return fail(FC_ERR_UNSUPPORTED, "linear supports at most %d ranks, got %d", FC_MAX_L + 1, d->n_active);
+  if (d->in_dim < 0 || d->out_dim < 0) return fail(FC_ERR_INVALID, "linear: negative row width");
+  for (int l = 0; l < d->n_active; ++l) {
+    if (d->m_values[l] < 1 || d->f_in_values[l] < 1 || d->f_out_values[l] < 1)
+      return fail(FC_ERR_INVALID, "linear: bad metadata for rank %d", l);
+    if (d->in_offsets[l] < 0 || d->in_offsets[l] + (int64_t)d->m_values[l] * d->f_in_values[l] > d->in_dim)
+      return fail(FC_ERR_INVALID, "linear: rank %d exceeds the input row", l);
+    if (d->out_offsets[l] < 0 || d->out_offsets[l] + (int64_t)d->m_values[l] * d->f_out_values[l] > d->out_dim)
+      return fail(FC_ERR_INVALID, "linear: rank %d exceeds the output row", l);
+  }
+  if (d->dtype != FC_F32 && d->dtype != FC_F64) return fail(FC_ERR_INVALID, "linear: bad dtype");
+  if (d->precision != FC_PREC_IEEE && d->precision != FC_PREC_TF32)
+    return fail(FC_ERR_INVALID, "linear: bad precision");
+  return FC_OK;
+}
+
+// zero columns [from, width) of every row
+template <typename T>
+static int zero_tail(T* p, int64_t rows, int64_t width, int64_t from, cudaStream_t s) {
+  if (rows <= 0 || from >= width) return 0;
+#ifdef FC_HOST_EMU
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t k = from; k < width; ++k) p[r * width + k] = T(0);
+  return 0;
+#else
+  return cudaMemset2DAsync(p + from, width * sizeof(T), 0, (width - from) * sizeof(T), rows, s) == cudaSuccess
+             ? 0
+             : FC_ERR_LAUNCH;
+#endif
+}
+
+template <typename T>
+static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* weights, const T* scale, int64_t n,
+                        T* out, cudaStream_t s) {
+  int64_t end = 0;
+  if (d->n_active > 0) {
+    const int l = d->n_active - 1;
+    end = d->out_offsets[l] + (int64_t)d->m_values[l] * d->f_out_values[l];
+  }
+  if (int rc = zero_tail(out, n, d->out_dim, end, s)) return rc;
+  for (int l = 0; l < d->n_active; ++l) {
+    LinGemmArgs<T> a;
+    a.a = LinRows<T>{x, d->in_dim, d->in_offsets[l], d->f_in_values[l], d->m_values[l]};
+    a.w = (const T*)weights[l];
+    a.ldw = d->f_in_values[l];
+    a.trans_b = 1;
+    a.scale = scale + l;
+    a.c = LinRows<T>{out, d->out_dim, d->out_offsets[l], d->f_out_values[l], d->m_values[l]};
+    a.R = n * d->m_values[l];
+    a.K = d->f_in_values[l];
+    a.N = d->f_out_values[l];
+    if (int rc = lin_gemm<T>(a, s)) return rc;
+  }
+  return 0;
+}
+
+template <typename T>
+static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const void* const* weights, const T* scale,
+                        int64_t n, T* gx, void* const* gw, cudaStream_t s) {
+  if (gx) {
+    // columns of x outside the active ranks get zero gradient
+    int64_t prev = 0;
+    for (int l = 0; l < d->n_active; ++l) {
+      if (d->in_offsets[l] > prev)
+        if (int rc = zero_tail(gx, n, d->in_offsets[l], prev, s)) return rc;  // gap before rank l
+      prev = d->in_offsets[l] + (int64_t)d->m_values[l] * d->f_in_values[l];
+    }
+    if (int rc = zero_tail(gx, n, d->in_dim, prev, s)) return rc;
+    for (int l = 0; l < d->n_active; ++l) {
+      LinGemmArgs<T> a;
+      a.a = LinRows<T>{g, d->out_dim, d->out_offsets[l], d->f_out_values[l], d->m_values[l]};
+      a.w = (const T*)weights[l];
+      a.ldw = d->f_in_values[l];
+      a.trans_b = 0;
+      a.scale = scale + l;
+      a.c = LinRows<T>{gx, d->in_dim, d->in_offsets[l], d->f_in_values[l], d->m_values[l]};
+      a.R = n * d->m_values[l];
+      a.K = d->f_out_values[l];
+      a.N = d->f_in_values[l];
+      if (int rc = lin_gemm<T>(a, s)) return rc;
+    }
+  }
+  if (gw) {
+    for (int l = 0; l < d->n_active; ++l) {
+      if (gw[l] == nullptr) continue;
+      if (zero_fill(gw[l], (int64_t)d->f_out_values[l] * d->f_in_values[l] * sizeof(T), s)) return FC_ERR_LAUNCH;
+      LinWgradArgs<T> a;
+      a.g = LinRows<T>{g, d->out_dim, d->out_offsets[l], d->f_out_values[l], d->m_values[l]};
+      a.x = LinRows<T>{x, d->in_dim, d->in_offsets[l], d->f_in_values[l], d->m_values[l]};
+      a.scale = scale + l;
+      a.gw = (T*)gw[l];
+      a.R = n * d->m_values[l];
+      a.n_out = d->f_out_values[l];
+      a.k_in = d->f_in_values[l];
+      a.rows_per_split = 0;
+      if (int rc = lin_wgrad<T>(a, s)) return rc;
+    }
+  }
+  return 0;
+}
+
+}  // namespace fc
+
+using namespace fc;
+
+extern "C" {
+
+const char* fc_version(void) {
+#ifdef FC_HOST_EMU
+  return "flashcart_b200 " FC_VERSION_STRING " (host emulation build, test only)";
+#else
+  return "flashcart_b200 " FC_VERSION_STRING " (sm_100a)";
+#endif
+}
+
+const char* fc_last_error(void) { return g_last_error.c_str(); }
+
+int fc_build_rowptr(const int64_t* idx_i, int64_t n_edges, int64_t n_nodes, int64_t* rowptr, int32_t* status,
+                    fc_stream_t stream) {
+  if (n_edges < 0 || n_nodes < 0) return fail(FC_ERR_INVALID, "fc_build_rowptr: negative size");
+  if (rowptr == nullptr || (n_edges > 0 && idx_i == nullptr)) return fail(FC_ERR_INVALID, "fc_build_rowptr: null");
+  return launch_status(build_rowptr(idx_i, n_edges, n_nodes, rowptr, reinterpret_cast<int*>(status),
+                                    (cudaStream_t)stream),
+                       "fc_build_rowptr");
+}
+
+int fc_tp_num_paths(const fc_tp_desc* desc) {
+  if (int rc = check_desc(desc)) return rc;
+  int npl[FC_MAX_L + 1];
+  count_paths(desc, npl);
+  int s = 0;
+  for (int l = 0; l <= desc->out_l_max; ++l) s += npl[l];
+  return s;
+}
+
+int64_t fc_tp_out_dim(const fc_tp_desc* desc) {
+  if (int rc = check_desc(desc)) return rc;
+  return out_dim(desc);
+}
+
+int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const void* weights, const int64_t* rowptr,
+              const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows, void* out, int32_t* status,
+              fc_stream_t stream) {
+  if (int rc = check_desc(desc)) return rc;
+  if (n_out_rows < 0 || n_in1_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_fwd: negative size");
+  if (rowptr == nullptr && n_out_rows != n_in1_rows)
+    return fail(FC_ERR_INVALID, "fc_tp_fwd: dense product needs n_out_rows == n_in1_rows");
+  if (rowptr != nullptr && idx_j == nullptr) return fail(FC_ERR_INVALID, "fc_tp_fwd: convolution needs idx_j");
+  if (n_out_rows == 0) return FC_OK;
+  if (!in1 || !in2 || !weights || !out) return fail(FC_ERR_INVALID, "fc_tp_fwd: null tensor");
+  const TpSigEntry* sig = find_sig(desc);
+  if (sig == nullptr || sig->npaths == 0) {
+    // no path: output has zero width
+    return FC_OK;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  if (desc->dtype == FC_F32) {
+    TpParams<float> p;
+    fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
+    p.in1 = (const float*)in1; p.in2 = (const float*)in2; p.w = (const float*)weights; p.out = (float*)out;
+    return launch_status(sig->table->fwd_f32(p, s), "fc_tp_fwd");
+  }
+  TpParams<double> p;
+  fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
+  p.in1 = (const double*)in1; p.in2 = (const double*)in2; p.w = (const double*)weights; p.out = (double*)out;
+  return launch_status(sig->table->fwd_f64(p, s), "fc_tp_fwd");
+}
+
+int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2, const void* weights,
+              const int64_t* rowptr, const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows,
+              int64_t n_in2_rows, void* grad_in1, void* grad_in2, void* grad_weights, int32_t* status,
+              fc_stream_t stream) {
+  if (int rc = check_desc(desc)) return rc;
+  if (n_out_rows < 0 || n_in1_rows < 0 || n_in2_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_bwd: negative size");
+  if (rowptr != nullptr && idx_j == nullptr) return fail(FC_ERR_INVALID, "fc_tp_bwd: convolution needs idx_j");
+  if (rowptr == nullptr && (n_out_rows != n_in1_rows || n_in2_rows != n_in1_rows))
+    return fail(FC_ERR_INVALID, "fc_tp_bwd: dense product needs equal row counts");
+  const TpSigEntry* sig = find_sig(desc);
+  const bool conv = rowptr != nullptr;
+  const int esz = desc->dtype == FC_F32 ? 4 : 8;
+  const int F = desc->in1_features > desc->in2_features ? desc->in1_features : desc->in2_features;
+  const int64_t d1 = (int64_t)(desc->in1_l_max + 1) * (desc->in1_l_max + 1) * desc->in1_features;
+  const int64_t d2 = (int64_t)(desc->in2_l_max + 1) * (desc->in2_l_max + 1) * desc->in2_features;
+  const int np = sig ? sig->npaths : 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  // outputs accumulated by atomics start at zero; all others are fully overwritten
+  int rc = 0;
+  if (grad_in1 && (conv || desc->in1_features == 1 || np == 0)) rc |= zero_fill(grad_in1, n_in1_rows * d1 * esz, s);
+  if (grad_in2 && (desc->in2_features == 1 || np == 0)) rc |= zero_fill(grad_in2, n_in2_rows * d2 * esz, s);
+  if (grad_weights && (desc->shared_weights || np == 0 || (conv && n_out_rows == 0)))
+    rc |= zero_fill(grad_weights, (desc->shared_weights ? 1 : n_in2_rows) * (int64_t)np * F * esz, s);
+  if (rc) return launch_status(FC_ERR_LAUNCH, "fc_tp_bwd (zero fill)");
+  if (n_out_rows == 0 || np == 0) return FC_OK;
+  if (!grad_out || !in1 || !in2 || !weights) return fail(FC_ERR_INVALID, "fc_tp_bwd: null tensor");
+  if (desc->dtype == FC_F32) {
+    TpBwdParams<float> p;
+    fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
+    p.g_out = (const float*)grad_out; p.in1 = (const float*)in1; p.in2 = (const float*)in2;
+    p.w = (const float*)weights;
+    p.g_in1 = (float*)grad_in1; p.g_in2 = (float*)grad_in2; p.g_w = (float*)grad_weights;
+    return launch_status(sig->table->bwd_f32(p, s), "fc_tp_bwd");
+  }
+  TpBwdParams<double> p;
+  fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
+  p.g_out = (const double*)grad_out; p.in1 = (const double*)in1; p.in2 = (const double*)in2;
+  p.w = (const double*)weights;
+  p.g_in1 = (double*)grad_in1; p.g_in2 = (double*)grad_in2; p.g_w = (double*)grad_weights;
+  return launch_status(sig->table->bwd_f64(p, s), "fc_tp_bwd");
+}
+
+int fc_tp_dbwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2, const void* weights,
+               const void* v_in1, const void* v_in2, const void* v_weights, const int64_t* rowptr,
+               const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows, int64_t n_in2_rows, void* d_grad_out,
+               void* d_in1, void* d_in2, void* d_weights, int32_t* status, fc_stream_t stream) {
+  if (int rc = check_desc(desc)) return rc;
+  if (n_out_rows < 0 || n_in1_rows < 0 || n_in2_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_dbwd: negative size");
+  if (rowptr != nullptr && idx_j == nullptr) return fail(FC_ERR_INVALID, "fc_tp_dbwd: convolution needs idx_j");
+  if (rowptr == nullptr && (n_out_rows != n_in1_rows || n_in2_rows != n_in1_rows))
+    return fail(FC_ERR_INVALID, "fc_tp_dbwd: dense product needs equal row counts");
+  const TpSigEntry* sig = find_sig(desc);
+  const bool conv = rowptr != nullptr;
+  const int esz = desc->dtype == FC_F32 ? 4 : 8;
+  const int F = desc->in1_features > desc->in2_features ? desc->in1_features : desc->in2_features;
+  const int64_t d1 = (int64_t)(desc->in1_l_max + 1) * (desc->in1_l_max + 1) * desc->in1_features;
+  const int64_t d2 = (int64_t)(desc->in2_l_max + 1) * (desc->in2_l_max + 1) * desc->in2_features;
+  const int np = sig ? sig->npaths : 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = 0;
+  if (d_in1 && (conv || desc->in1_features == 1 || np == 0)) rc |= zero_fill(d_in1, n_in1_rows * d1 * esz, s);
+  if (d_in2 && (desc->in2_features == 1 || np == 0)) rc |= zero_fill(d_in2, n_in2_rows * d2 * esz, s);
+  if (d_weights && (desc->shared_weights || np == 0 || (conv && n_out_rows == 0)))
+    rc |= zero_fill(d_weights, (desc->shared_weights ? 1 : n_in2_rows) * (int64_t)np * F * esz, s);
+  if (d_grad_out && np == 0) rc |= zero_fill(d_grad_out, n_out_rows * out_dim(desc) * esz, s);
+  if (rc) return launch_status(FC_ERR_LAUNCH, "fc_tp_dbwd (zero fill)");
+  if (n_out_rows == 0 || np == 0) return FC_OK;
+  if (!grad_out || !in1 || !in2 || !weights) return fail(FC_ERR_INVALID, "fc_tp_dbwd: null tensor");
+  if (desc->dtype == FC_F32) {
+    TpDbwdParams<float> p;
+    fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
+    p.g_out = (const float*)grad_out; p.in1 = (const float*)in1; p.in2 = (const float*)in2;
+    p.w = (const float*)weights;
+    p.v1 = (const float*)v_in1; p.v2 = (const float*)v_in2; p.vw = (const float*)v_weights;
+    p.d_g = (float*)d_grad_out; p.d_in1 = (float*)d_in1; p.d_in2 = (float*)d_in2; p.d_w = (float*)d_weights;
+    return launch_status(sig->table->dbwd_f32(p, s), "fc_tp_dbwd");
+  }
+  TpDbwdParams<double> p;
+  fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
+  p.g_out = (const double*)grad_out; p.in1 = (const double*)in1; p.in2 = (const double*)in2;
+  p.w = (const double*)weights;
+  p.v1 = (const double*)v_in1; p.v2 = (const double*)v_in2; p.vw = (const double*)v_weights;
+  p.d_g = (double*)d_grad_out; p.d_in1 = (double*)d_in1; p.d_in2 = (double*)d_in2; p.d_w = (double*)d_weights;
+  return launch_status(sig->table->dbwd_f64(p, s), "fc_tp_dbwd");
+}
+
+// ------------------------------------------------------------------ irreps
+
+int fc_irreps_fwd(const void* x, int64_t n, int32_t l_max, int32_t dtype, void* out, fc_stream_t stream) {
+  if (l_max < 0 || l_max > FC_MAX_L)
+    return fail(FC_ERR_UNSUPPORTED, "Irreps supports l_max <= %d, got l_max=%d.", FC_MAX_L, l_max);
+  if (n < 0) return fail(FC_ERR_INVALID, "fc_irreps_fwd: negative size");
+  if (n == 0) return FC_OK;
+  if (!x || !out) return fail(FC_ERR_INVALID, "fc_irreps_fwd: null tensor");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == FC_F32)
+    return launch_status(irreps_fwd_dispatch<float>((const float*)x, (float*)out, n, l_max, s), "fc_irreps_fwd");
+  if (dtype == FC_F64)
+    return launch_status(irreps_fwd_dispatch<double>((const double*)x, (double*)out, n, l_max, s), "fc_irreps_fwd");
+  return fail(FC_ERR_INVALID, "fc_irreps_fwd: bad dtype");
+}
+
+int fc_irreps_bwd(const void* grad_out, const void* x, int64_t n, int32_t l_max, int32_t dtype, void* grad_x,
+                  fc_stream_t stream) {
+  if (l_max < 0 || l_max > FC_MAX_L)
+    return fail(FC_ERR_UNSUPPORTED, "Irreps supports l_max <= %d, got l_max=%d.", FC_MAX_L, l_max);
+  if (n < 0) return fail(FC_ERR_INVALID, "fc_irreps_bwd: negative size");
+  if (n == 0) return FC_OK;
+  if (!grad_out || !x || !grad_x) return fail(FC_ERR_INVALID, "fc_irreps_bwd: null tensor");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == FC_F32)
+    return launch_status(
+        irreps_bwd_dispatch<float>((const float*)grad_out, (const float*)x, (float*)grad_x, n, l_max, s),
+        "fc_irreps_bwd");
+  if (dtype == FC_F64)
+    return launch_status(
+        irreps_bwd_dispatch<double>((const double*)grad_out, (const double*)x, (double*)grad_x, n, l_max, s),
+        "fc_irreps_bwd");
+  return fail(FC_ERR_INVALID, "fc_irreps_bwd: bad dtype");
+}
+
+int fc_irreps_dbwd(const void* grad_out, const void* x, const void* v, int64_t n, int32_t l_max, int32_t dtype,
+                   void* d_grad_out, void* d_x, fc_stream_t stream) {
+  if (l_max < 0 || l_max > FC_MAX_L)
+    return fail(FC_ERR_UNSUPPORTED, "Irreps supports l_max <= %d, got l_max=%d.", FC_MAX_L, l_max);
+  if (n < 0) return fail(FC_ERR_INVALID, "fc_irreps_dbwd: negative size");
+  if (n == 0) return FC_OK;
+  if (!grad_out || !x || !v) return fail(FC_ERR_INVALID, "fc_irreps_dbwd: null tensor");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == FC_F32)
+    return launch_status(irreps_dbwd_dispatch<float>((const float*)grad_out, (const float*)x, (const float*)v,
+                                                     (float*)d_grad_out, (float*)d_x, n, l_max, s),
+                         "fc_irreps_dbwd");
+  if (dtype == FC_F64)
+    return launch_status(irreps_dbwd_dispatch<double>((const double*)grad_out, (const double*)x, (const double*)v,
+                                                      (double*)d_grad_out, (double*)d_x, n, l_max, s),
+                         "fc_irreps_dbwd");
+  return fail(FC_ERR_INVALID, "fc_irreps_dbwd: bad dtype");
+}
+
+int fc_linear_fwd(const fc_linear_desc* desc, const void* x, const void* const* weights, const void* scale,
+                  int64_t n, void* out, fc_stream_t stream) {
+  if (int rc = check_linear(desc)) return rc;
+  if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_fwd: negative size");
+  if (n == 0 || desc->out_dim == 0) return FC_OK;
+  if (!out || (desc->n_active > 0 && (!x || !scale || !weights)))
+    return fail(FC_ERR_INVALID, "fc_linear_fwd: null tensor");
+  for (int l = 0; l < desc->n_active; ++l)
+    if (!weights[l]) return fail(FC_ERR_INVALID, "fc_linear_fwd: null weight for rank %d", l);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (desc->dtype == FC_F32)
+    return launch_status(linear_fwd_t<float>(desc, (const float*)x, weights, (const float*)scale, n, (float*)out, s),
+                         "fc_linear_fwd");
+  return launch_status(
+      linear_fwd_t<double>(desc, (const double*)x, weights, (const double*)scale, n, (double*)out, s),
+      "fc_linear_fwd");
+}
+
+int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* x, const void* const* weights,
+                  const void* scale, int64_t n, void* grad_x, void* const* grad_weights, fc_stream_t stream) {
+  if (int rc = check_linear(desc)) return rc;
+  if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_bwd: negative size");
+  if (desc->n_active > 0 && (!grad_out || !x || !scale || !weights))
+    return fail(FC_ERR_INVALID, "fc_linear_bwd: null tensor");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (desc->dtype == FC_F32)
+    return launch_status(linear_bwd_t<float>(desc, (const float*)grad_out, (const float*)x, weights,
+                                             (const float*)scale, n, (float*)grad_x, grad_weights, s),
+                         "fc_linear_bwd");
+  return launch_status(linear_bwd_t<double>(desc, (const double*)grad_out, (const double*)x, weights,
+                                            (const double*)scale, n, (double*)grad_x, grad_weights, s),
+                       "fc_linear_bwd");
+}
+
+}  // extern "C"

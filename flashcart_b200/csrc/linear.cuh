@@ -1,0 +1,48 @@
+// Equivariant linear maps: row addressing and launcher declarations.
+#pragma once
+#include "fc_base.cuh"
+
+namespace fc {
+
+template <typename T>
+struct LinRows {
+  const T* p;
+  int64_t ld;   // elements between consecutive n
+  int64_t off;  // offset of the rank block
+  int64_t ms;   // elements between consecutive m
+  int M;        // 2l+1
+  FC_HD FC_INLINE const T* row(int64_t r) const {
+    const int64_t n = r / M, m = r - n * M;
+    return p + n * ld + off + m * ms;
+  }
+};
+
+template <typename T>
+struct LinGemmArgs {
+  LinRows<T> a;     // A(r, k), k contiguous
+  const T* w;       // weights of this rank
+  int ldw;          // row length of W
+  int trans_b;      // B(k, c) = trans_b ? W[c*ldw + k] : W[k*ldw + c]
+  const T* scale;   // device pointer to the scale of this rank
+  LinRows<T> c;     // C(r, col), col contiguous
+  int64_t R;
+  int K, N;
+};
+
+template <typename T>
+struct LinWgradArgs {
+  LinRows<T> g;     // grad_out rows (col = out channel)
+  LinRows<T> x;     // input rows (col = in channel)
+  const T* scale;
+  T* gw;            // (N_out, K_in) row-major
+  int64_t R;
+  int n_out, k_in;
+  int64_t rows_per_split;
+};
+
+template <typename T>
+int lin_gemm(const LinGemmArgs<T>& a, cudaStream_t s);
+template <typename T>
+int lin_wgrad(LinWgradArgs<T> a, cudaStream_t s);
+
+}  // namespace fc

@@ -1,0 +1,186 @@
+// Tensor-product kernel wrappers shared by every generated signature file.
+//
+// Thread mapping (forward, backward and double backward alike): one CTA per output
+// row (a receiver node of a convolution, or a row of a dense product), one thread
+// per feature channel (blockDim = F rounded up to a warp, at most FC_TP_BLOCK; wider
+// F loops over channel blocks). For a convolution the CTA walks the receiver's
+// CSR edge range; the edge index and the in2 / weight rows are uniform across the
+// CTA, the in1 gather of the sender row and the weight row are coalesced over
+// channels, the per-path outputs stay in registers and are stored once.
+#pragma once
+#include "fc_base.cuh"
+
+#ifndef FC_TP_BLOCK
+#define FC_TP_BLOCK 256
+#endif
+
+namespace fc {
+
+template <typename T>
+struct TpParams {
+  const T* in1; const T* in2; const T* w; T* out;
+  const int64_t* rowptr; const int64_t* idx_j;
+  int64_t n_rows, n_in1;
+  int F, F1, F2, shared_w, reduce;
+  int* status;
+};
+
+template <typename T>
+struct TpBwdParams {
+  const T* g_out; const T* in1; const T* in2; const T* w;
+  T* g_in1; T* g_in2; T* g_w;
+  const int64_t* rowptr; const int64_t* idx_j;
+  int64_t n_rows, n_in1;
+  int F, F1, F2, shared_w, reduce;
+  int* status;
+};
+
+template <typename T>
+struct TpDbwdParams {
+  const T* g_out; const T* in1; const T* in2; const T* w;
+  const T* v1; const T* v2; const T* vw;
+  T* d_g; T* d_in1; T* d_in2; T* d_w;
+  const int64_t* rowptr; const int64_t* idx_j;
+  int64_t n_rows, n_in1;
+  int F, F1, F2, shared_w, reduce;
+  int* status;
+};
+
+struct TpLaunch {
+  int grid;   // CTAs
+  int block;  // threads
+};
+
+// Function table of one compiled signature.
+struct TpTable {
+  int (*fwd_f32)(const TpParams<float>&, cudaStream_t);
+  int (*fwd_f64)(const TpParams<double>&, cudaStream_t);
+  int (*bwd_f32)(const TpBwdParams<float>&, cudaStream_t);
+  int (*bwd_f64)(const TpBwdParams<double>&, cudaStream_t);
+  int (*dbwd_f32)(const TpDbwdParams<float>&, cudaStream_t);
+  int (*dbwd_f64)(const TpDbwdParams<double>&, cudaStream_t);
+  int nacc;       // accumulators per channel (register budget indicator)
+};
+
+struct TpSigEntry {
+  int l1, l2, lo, sym, npaths;
+  const TpTable* table;
+};
+
+inline int tp_block_for(int F) {
+  int b = fc_round_up(F, 32);
+  return b > FC_TP_BLOCK ? FC_TP_BLOCK : b;
+}
+
+#ifndef FC_HOST_EMU
+// ------------------------------------------------------------------ device wrappers
+
+template <typename T, typename S>
+__global__ void __launch_bounds__(FC_TP_BLOCK) tp_fwd_kernel(TpParams<T> P) {
+  for (int cb = 0; cb < P.F; cb += blockDim.x) {
+    const int c = cb + threadIdx.x;
+    if (c >= P.F) break;
+    for (int64_t row = blockIdx.x; row < P.n_rows; row += gridDim.x) S::template fwd<T>(P, row, c);
+  }
+}
+
+template <typename T, typename S>
+__global__ void __launch_bounds__(FC_TP_BLOCK) tp_bwd_kernel(TpBwdParams<T> P) {
+  for (int cb = 0; cb < P.F; cb += blockDim.x) {
+    const int c = cb + threadIdx.x;
+    const bool active = c < P.F;
+    T keep[S::NP];
+    for (int q = 0; q < S::NP; ++q) keep[q] = T(0);
+    for (int64_t row = blockIdx.x; row < P.n_rows; row += gridDim.x)
+      S::template bwd<T>(P, row, active ? c : 0, active, keep);
+    if (P.shared_w && P.g_w != nullptr && active)
+      for (int q = 0; q < S::NP; ++q) atomicAdd(P.g_w + (int64_t)q * P.F + c, keep[q]);
+  }
+}
+
+template <typename T, typename S>
+__global__ void __launch_bounds__(FC_TP_BLOCK) tp_dbwd_kernel(TpDbwdParams<T> P) {
+  for (int cb = 0; cb < P.F; cb += blockDim.x) {
+    const int c = cb + threadIdx.x;
+    const bool active = c < P.F;
+    T keep[S::NP];
+    for (int q = 0; q < S::NP; ++q) keep[q] = T(0);
+    for (int64_t row = blockIdx.x; row < P.n_rows; row += gridDim.x)
+      S::template dbwd<T>(P, row, active ? c : 0, active, keep);
+    if (P.shared_w && P.d_w != nullptr && active)
+      for (int q = 0; q < S::NP; ++q) atomicAdd(P.d_w + (int64_t)q * P.F + c, keep[q]);
+  }
+}
+
+inline int tp_grid_for(int64_t n_rows, bool shared_accumulate) {
+  // One CTA per row; rows accumulating a shared weight gradient use a bounded grid so
+  // that each thread folds many rows before its single atomic per path.
+  int64_t g = n_rows;
+  const int64_t cap = shared_accumulate ? 148 * 16 : ((int64_t)1 << 31) - 1;
+  if (g > cap) g = cap;
+  return (int)(g < 1 ? 1 : g);
+}
+
+template <typename T, typename S>
+int tp_fwd_launch(const TpParams<T>& P, cudaStream_t s) {
+  if (P.n_rows == 0) return 0;
+  tp_fwd_kernel<T, S><<<tp_grid_for(P.n_rows, false), tp_block_for(P.F), 0, s>>>(P);
+  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+}
+template <typename T, typename S>
+int tp_bwd_launch(const TpBwdParams<T>& P, cudaStream_t s) {
+  if (P.n_rows == 0) return 0;
+  tp_bwd_kernel<T, S><<<tp_grid_for(P.n_rows, P.shared_w && P.g_w), tp_block_for(P.F), 0, s>>>(P);
+  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+}
+template <typename T, typename S>
+int tp_dbwd_launch(const TpDbwdParams<T>& P, cudaStream_t s) {
+  if (P.n_rows == 0) return 0;
+  tp_dbwd_kernel<T, S><<<tp_grid_for(P.n_rows, P.shared_w && P.d_w), tp_block_for(P.F), 0, s>>>(P);
+  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+}
+
+#else
+// ------------------------------------------------------------------ host emulation
+
+template <typename T, typename S>
+int tp_fwd_launch(const TpParams<T>& P, cudaStream_t) {
+  for (int64_t row = 0; row < P.n_rows; ++row)
+    for (int c = 0; c < P.F; ++c) S::template fwd<T>(P, row, c);
+  return 0;
+}
+template <typename T, typename S>
+int tp_bwd_launch(const TpBwdParams<T>& P, cudaStream_t) {
+  for (int c = 0; c < P.F; ++c) {
+    T keep[S::NP];
+    for (int q = 0; q < S::NP; ++q) keep[q] = T(0);
+    for (int64_t row = 0; row < P.n_rows; ++row) S::template bwd<T>(P, row, c, true, keep);
+    if (P.shared_w && P.g_w != nullptr)
+      for (int q = 0; q < S::NP; ++q) P.g_w[(int64_t)q * P.F + c] += keep[q];
+  }
+  return 0;
+}
+template <typename T, typename S>
+int tp_dbwd_launch(const TpDbwdParams<T>& P, cudaStream_t) {
+  for (int c = 0; c < P.F; ++c) {
+    T keep[S::NP];
+    for (int q = 0; q < S::NP; ++q) keep[q] = T(0);
+    for (int64_t row = 0; row < P.n_rows; ++row) S::template dbwd<T>(P, row, c, true, keep);
+    if (P.shared_w && P.d_w != nullptr)
+      for (int q = 0; q < S::NP; ++q) P.d_w[(int64_t)q * P.F + c] += keep[q];
+  }
+  return 0;
+}
+#endif
+
+}  // namespace fc
+
+// Instantiate the launch table of a generated signature; NS::Ops supplies the bodies.
+#define FC_DEFINE_TP_SIGNATURE(NAME, NS)                                                  \
+  extern const TpTable tp_table_##NAME;                                                   \
+  const TpTable tp_table_##NAME = {                                                       \
+      &tp_fwd_launch<float, NS::Ops>,  &tp_fwd_launch<double, NS::Ops>,                   \
+      &tp_bwd_launch<float, NS::Ops>,  &tp_bwd_launch<double, NS::Ops>,                   \
+      &tp_dbwd_launch<float, NS::Ops>, &tp_dbwd_launch<double, NS::Ops>, NS::Ops::NACC};
+
+#define FC_DECLARE_TP_SIGNATURE(NAME) extern const TpTable tp_table_##NAME

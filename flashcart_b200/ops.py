@@ -1,0 +1,626 @@
+"""``torch.ops.flashcart.*`` operators backed by the sm_100a kernels.
+
+Same operator names, schemas and autograd chains as the reference runtimes
+(``o3/_tensor_product.py:332-1096``, ``o3/_irreps.py:84-202``,
+``o3/_linear.py:328-778``), so compiled graphs and exported programs that call
+``flashcart::tp_fwd`` and friends resolve to these kernels. One addition,
+``flashcart::tp_dbwd``, is the second derivative that the reference launches
+inside the autograd of ``tp_bwd``; here it is an operator of its own so that it
+is visible to ``torch.compile``.
+
+Every operator requires CUDA tensors and calls the C ABI (``include/flashcart_b200.h``)
+on the current stream. There is no CPU path: a CPU tensor raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+from torch import Tensor
+
+from flashcart_b200 import _native as N
+
+__all__ = ["check_device_status", "status_word"]
+
+_DEBUG_CHECK = os.environ.get("FLASHCART_B200_CHECK", "0") not in ("", "0", "false", "False")
+
+
+# ----------------------------------------------------------------------------- plumbing
+
+
+def _require_cuda(*tensors: Optional[Tensor]) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "flashcart_b200 operators run only on CUDA tensors (sm_100a kernels); there is no CPU path.")
+
+
+def _code(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return N.FC_F32
+    if dtype == torch.float64:
+        return N.FC_F64
+    raise TypeError(f"flashcart_b200 kernels support float32 and float64, got {dtype}")
+
+
+def _p(t: Optional[Tensor]):
+    if t is None or t.numel() == 0:
+        return None
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+_STATUS: Dict[int, Tensor] = {}
+
+
+def status_word(device: torch.device) -> Tensor:
+    """Per-device int32 word into which kernels OR data-error bits (FC_DEV_*)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _STATUS.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS[idx] = w
+    return w
+
+
+def check_device_status(device: Optional[torch.device] = None, clear: bool = True) -> None:
+    """Synchronise and raise if a kernel flagged bad data since the last check.
+
+    Mirrors the reference's ``torch._assert_async`` guards: unsorted receivers
+    (``o3/_tensor_product.py:397-401``) and out-of-range edge indices.
+    """
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    w = status_word(device)
+    v = int(w.item())
+    if clear and v:
+        w.zero_()
+    msgs = []
+    if v & N.FC_DEV_UNSORTED:
+        msgs.append("Scatter tensor product requires a receiver-sorted idx_i "
+                    "(edges grouped by ascending destination index).")
+    if v & N.FC_DEV_BAD_INDEX:
+        msgs.append("An edge index points outside its node array.")
+    if msgs:
+        raise RuntimeError(" ".join(msgs))
+
+
+def _after(lib, rc: int, what: str, device: torch.device) -> None:
+    N.check(lib, rc, what)
+    if _DEBUG_CHECK:
+        check_device_status(device)
+
+
+def _idx(t: Optional[Tensor]) -> Optional[Tensor]:
+    if t is None:
+        return None
+    if t.dtype != torch.int64:
+        t = t.to(torch.int64)
+    return t.contiguous()
+
+
+# ----------------------------------------------------------------------------- tensor product
+
+
+def _paths_per_l(in1_l_max: int, in2_l_max: int, out_l_max: int, sym: bool) -> List[int]:
+    lmax = max(in1_l_max, in2_l_max)
+    out = []
+    for lo in range(out_l_max + 1):
+        c = 0
+        for l1 in range(lmax + 1):
+            for l2 in range(l1 + 1):
+                ok = abs(l1 - l2) <= lo <= l1 + l2 and (l1 + l2 + lo) % 2 == 0
+                if ok and l1 <= in1_l_max and l2 <= in2_l_max:
+                    c += 1
+                if ok and not sym and l2 < l1 and l1 <= in2_l_max and l2 <= in1_l_max:
+                    c += 1
+        out.append(c)
+    return out
+
+
+def tp_out_dim(in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmetric_product, reduce_paths) -> int:
+    F = max(in1_features, in2_features)
+    npl = _paths_per_l(in1_l_max, in2_l_max, out_l_max, symmetric_product)
+    if reduce_paths:
+        return sum((2 * l + 1) * F for l in range(out_l_max + 1) if npl[l])
+    return sum(npl[l] * (2 * l + 1) * F for l in range(out_l_max + 1))
+
+
+def _tp_desc(in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmetric_product, shared_weights,
+             reduce_paths, dtype) -> N.TpDesc:
+    return N.TpDesc(int(in1_l_max), int(in2_l_max), int(out_l_max), int(in1_features), int(in2_features),
+                    int(bool(symmetric_product)), int(bool(shared_weights)), int(bool(reduce_paths)), _code(dtype))
+
+
+def _rowptr(lib, idx_i: Tensor, n_nodes: int, device, stream, status) -> Tensor:
+    rowptr = torch.empty(n_nodes + 1, dtype=torch.int64, device=device)
+    rc = lib.fc_build_rowptr(_p(idx_i), idx_i.numel(), n_nodes, ctypes.c_void_p(rowptr.data_ptr()), status, stream)
+    N.check(lib, rc, "fc_build_rowptr")
+    return rowptr
+
+
+def _conv(idx_i, idx_j) -> bool:
+    return idx_i is not None and idx_j is not None
+
+
+@torch.library.custom_op("flashcart::tp_fwd", mutates_args=())
+def tp_fwd(in1: Tensor, in2: Tensor, weights: Tensor, idx_i: Optional[Tensor], idx_j: Optional[Tensor],
+           in1_l_max: int, in2_l_max: int, out_l_max: int, in1_features: int, in2_features: int,
+           symmetric_product: bool, shared_weights: bool, in1_offs: List[int], in2_offs: List[int],
+           out_sizes: List[int], n_paths_per_l: List[int], n_total_paths: int,
+           reduce_paths: bool = False) -> Tensor:
+    _require_cuda(in1, in2, weights, idx_i, idx_j)
+    lib = N.lib()
+    dev = in1.device
+    in1, in2, weights = in1.contiguous(), in2.contiguous(), weights.contiguous()
+    desc = _tp_desc(in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmetric_product,
+                    shared_weights, reduce_paths, in1.dtype)
+    out_dim = tp_out_dim(in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmetric_product,
+                         reduce_paths)
+    n_out = in1.shape[0]
+    out = torch.empty((n_out, out_dim), device=dev, dtype=in1.dtype)
+    stream = _stream(dev)
+    status = ctypes.c_void_p(status_word(dev).data_ptr())
+    if _conv(idx_i, idx_j):
+        idx_i, idx_j = _idx(idx_i), _idx(idx_j)
+        rowptr = _rowptr(lib, idx_i, n_out, dev, stream, status)
+        rc = lib.fc_tp_fwd(ctypes.byref(desc), _p(in1), _p(in2), _p(weights), ctypes.c_void_p(rowptr.data_ptr()),
+                           _p(idx_j), n_out, n_out, _p(out), status, stream)
+    else:
+        if in1.shape[0] != in2.shape[0]:
+            raise ValueError("idx_i and idx_j must be provided when in1 and in2 have different batch sizes. "
+                             f"Got in1_batch={in1.shape[0]}, in2_batch={in2.shape[0]}.")
+        rc = lib.fc_tp_fwd(ctypes.byref(desc), _p(in1), _p(in2), _p(weights), None, None, n_out, n_out, _p(out),
+                           status, stream)
+    _after(lib, rc, "fc_tp_fwd", dev)
+    return out
+
+
+@tp_fwd.register_fake
+def _(in1, in2, weights, idx_i, idx_j, in1_l_max, in2_l_max, out_l_max, in1_features, in2_features,
+      symmetric_product, shared_weights, in1_offs, in2_offs, out_sizes, n_paths_per_l, n_total_paths,
+      reduce_paths=False):
+    d = tp_out_dim(in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmetric_product, reduce_paths)
+    return in1.new_empty((in1.shape[0], d))
+
+
+@torch.library.custom_op("flashcart::tp_bwd", mutates_args=())
+def tp_bwd(grad_out: Tensor, in1: Tensor, in2: Tensor, weights: Tensor, idx_i: Optional[Tensor],
+           idx_j: Optional[Tensor], in1_l_max: int, in2_l_max: int, out_l_max: int, in1_features: int,
+           in2_features: int, symmetric_product: bool, shared_weights: bool, in1_offs: List[int],
+           in2_offs: List[int], out_sizes: List[int], n_paths_per_l: List[int], n_total_paths: int,
+           reduce_paths: bool, need_grad_in1: bool, need_grad_in2: bool,
+           need_grad_weights: bool) -> Tuple[Tensor, Tensor, Tensor]:
+    _require_cuda(grad_out, in1, in2, weights, idx_i, idx_j)
+    lib = N.lib()
+    dev = in1.device
+    grad_out = grad_out.contiguous()
+    in1, in2, weights = in1.contiguous(), in2.contiguous(), weights.contiguous()
+    desc = _tp_desc(in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmetric_product,
+                    shared_weights, reduce_paths, in1.dtype)
+    empty = in1.new_empty((0,))
+    g1 = torch.empty_like(in1) if need_grad_in1 else empty
+    g2 = torch.empty_like(in2) if need_grad_in2 else in2.new_empty((0,))
+    gw = torch.empty_like(weights) if need_grad_weights else weights.new_empty((0,))
+    if not (need_grad_in1 or need_grad_in2 or need_grad_weights):
+        return g1, g2, gw
+    stream = _stream(dev)
+    status = ctypes.c_void_p(status_word(dev).data_ptr())
+    if _conv(idx_i, idx_j):
+        idx_i, idx_j = _idx(idx_i), _idx(idx_j)
+        n_out = in1.shape[0]
+        rowptr = _rowptr(lib, idx_i, n_out, dev, stream, status)
+        rc = lib.fc_tp_bwd(ctypes.byref(desc), _p(grad_out), _p(in1), _p(in2), _p(weights),
+                           ctypes.c_void_p(rowptr.data_ptr()), _p(idx_j), n_out, n_out, in2.shape[0],
+                           _p(g1), _p(g2), _p(gw), status, stream)
+    else:
+        n = in1.shape[0]
+        rc = lib.fc_tp_bwd(ctypes.byref(desc), _p(grad_out), _p(in1), _p(in2), _p(weights), None, None, n, n, n,
+                           _p(g1), _p(g2), _p(gw), status, stream)
+    _after(lib, rc, "fc_tp_bwd", dev)
+    return g1, g2, gw
+
+
+@tp_bwd.register_fake
+def _(grad_out, in1, in2, weights, idx_i, idx_j, in1_l_max, in2_l_max, out_l_max, in1_features, in2_features,
+      symmetric_product, shared_weights, in1_offs, in2_offs, out_sizes, n_paths_per_l, n_total_paths, reduce_paths,
+      need_grad_in1, need_grad_in2, need_grad_weights):
+    return (torch.empty_like(in1) if need_grad_in1 else in1.new_empty((0,)),
+            torch.empty_like(in2) if need_grad_in2 else in2.new_empty((0,)),
+            torch.empty_like(weights) if need_grad_weights else weights.new_empty((0,)))
+
+
+@torch.library.custom_op("flashcart::tp_dbwd", mutates_args=())
+def tp_dbwd(grad_out: Tensor, in1: Tensor, in2: Tensor, weights: Tensor, v_in1: Optional[Tensor],
+            v_in2: Optional[Tensor], v_weights: Optional[Tensor], idx_i: Optional[Tensor], idx_j: Optional[Tensor],
+            in1_l_max: int, in2_l_max: int, out_l_max: int, in1_features: int, in2_features: int,
+            symmetric_product: bool, shared_weights: bool, reduce_paths: bool, need_d_grad_out: bool,
+            need_d_in1: bool, need_d_in2: bool, need_d_weights: bool) -> Tuple[Tensor, Tensor, Tensor, Tensor]:
+    _require_cuda(grad_out, in1, in2, weights, v_in1, v_in2, v_weights, idx_i, idx_j)
+    lib = N.lib()
+    dev = in1.device
+    grad_out = grad_out.contiguous()
+    in1, in2, weights = in1.contiguous(), in2.contiguous(), weights.contiguous()
+    v_in1 = v_in1.contiguous() if v_in1 is not None and v_in1.numel() else None
+    v_in2 = v_in2.contiguous() if v_in2 is not None and v_in2.numel() else None
+    v_weights = v_weights.contiguous() if v_weights is not None and v_weights.numel() else None
+    desc = _tp_desc(in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmetric_product,
+                    shared_weights, reduce_paths, in1.dtype)
+    dg = torch.empty_like(grad_out) if need_d_grad_out else grad_out.new_empty((0,))
+    d1 = torch.empty_like(in1) if need_d_in1 else in1.new_empty((0,))
+    d2 = torch.empty_like(in2) if need_d_in2 else in2.new_empty((0,))
+    dw = torch.empty_like(weights) if need_d_weights else weights.new_empty((0,))
+    if not (need_d_grad_out or need_d_in1 or need_d_in2 or need_d_weights):
+        return dg, d1, d2, dw
+    stream = _stream(dev)
+    status = ctypes.c_void_p(status_word(dev).data_ptr())
+    if _conv(idx_i, idx_j):
+        idx_i, idx_j = _idx(idx_i), _idx(idx_j)
+        n_out = in1.shape[0]
+        rowptr = _rowptr(lib, idx_i, n_out, dev, stream, status)
+        rc = lib.fc_tp_dbwd(ctypes.byref(desc), _p(grad_out), _p(in1), _p(in2), _p(weights), _p(v_in1), _p(v_in2),
+                            _p(v_weights), ctypes.c_void_p(rowptr.data_ptr()), _p(idx_j), n_out, n_out,
+                            in2.shape[0], _p(dg), _p(d1), _p(d2), _p(dw), status, stream)
+    else:
+        n = in1.shape[0]
+        rc = lib.fc_tp_dbwd(ctypes.byref(desc), _p(grad_out), _p(in1), _p(in2), _p(weights), _p(v_in1), _p(v_in2),
+                            _p(v_weights), None, None, n, n, n, _p(dg), _p(d1), _p(d2), _p(dw), status, stream)
+    _after(lib, rc, "fc_tp_dbwd", dev)
+    return dg, d1, d2, dw
+
+
+@tp_dbwd.register_fake
+def _(grad_out, in1, in2, weights, v_in1, v_in2, v_weights, idx_i, idx_j, in1_l_max, in2_l_max, out_l_max,
+      in1_features, in2_features, symmetric_product, shared_weights, reduce_paths, need_d_grad_out, need_d_in1,
+      need_d_in2, need_d_weights):
+    return (torch.empty_like(grad_out) if need_d_grad_out else grad_out.new_empty((0,)),
+            torch.empty_like(in1) if need_d_in1 else in1.new_empty((0,)),
+            torch.empty_like(in2) if need_d_in2 else in2.new_empty((0,)),
+            torch.empty_like(weights) if need_d_weights else weights.new_empty((0,)))
+
+
+_TP_SCALARS = 13  # in1_l_max ... reduce_paths
+
+
+def _tp_fwd_setup(ctx, inputs, output):
+    in1, in2, weights, idx_i, idx_j = inputs[:5]
+    ctx.save_for_backward(in1, in2, weights, idx_i, idx_j)
+    ctx.scalars = tuple(inputs[5:])
+
+
+def _tp_fwd_backward(ctx, grad_out):
+    n_extra = len(ctx.needs_input_grad) - 3
+    need1, need2, needw = (bool(ctx.needs_input_grad[i]) for i in range(3))
+    if grad_out is None or not (need1 or need2 or needw):
+        return (None, None, None) + (None,) * n_extra
+    in1, in2, weights, idx_i, idx_j = ctx.saved_tensors
+    s = ctx.scalars
+    reduce_paths = s[12] if len(s) > 12 else False
+    g1, g2, gw = torch.ops.flashcart.tp_bwd(grad_out, in1, in2, weights, idx_i, idx_j, *s[:12], reduce_paths,
+                                            need1, need2, needw)
+    return (g1 if need1 else None, g2 if need2 else None, gw if needw else None) + (None,) * n_extra
+
+
+tp_fwd.register_autograd(_tp_fwd_backward, setup_context=_tp_fwd_setup)
+
+
+def _tp_bwd_setup(ctx, inputs, output):
+    grad_out, in1, in2, weights, idx_i, idx_j = inputs[:6]
+    ctx.save_for_backward(grad_out, in1, in2, weights, idx_i, idx_j)
+    s = inputs[6:]
+    # (in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmetric, shared, ..., reduce, needs...)
+    ctx.desc_args = (s[0], s[1], s[2], s[3], s[4], s[5], s[6], s[12])
+    ctx.made = (bool(s[13]), bool(s[14]), bool(s[15]))
+    if hasattr(ctx, "set_materialize_grads"):
+        ctx.set_materialize_grads(False)
+
+
+def _tp_bwd_backward(ctx, v1, v2, vw):
+    n_extra = len(ctx.needs_input_grad) - 4
+    need = [bool(ctx.needs_input_grad[i]) for i in range(4)]
+    made1, made2, madew = ctx.made
+    v1 = v1 if (made1 and v1 is not None and v1.numel()) else None
+    v2 = v2 if (made2 and v2 is not None and v2.numel()) else None
+    vw = vw if (madew and vw is not None and vw.numel()) else None
+    if not any(need) or (v1 is None and v2 is None and vw is None):
+        return (None,) * (4 + n_extra)
+    grad_out, in1, in2, weights, idx_i, idx_j = ctx.saved_tensors
+    a = ctx.desc_args
+    dg, d1, d2, dw = torch.ops.flashcart.tp_dbwd(grad_out, in1, in2, weights, v1, v2, vw, idx_i, idx_j, a[0], a[1],
+                                                 a[2], a[3], a[4], a[5], a[6], a[7], need[0], need[1], need[2],
+                                                 need[3])
+    return (dg if need[0] else None, d1 if need[1] else None, d2 if need[2] else None,
+            dw if need[3] else None) + (None,) * n_extra
+
+
+tp_bwd.register_autograd(_tp_bwd_backward, setup_context=_tp_bwd_setup)
+
+
+# ----------------------------------------------------------------------------- direction tensors
+
+
+@torch.library.custom_op("flashcart::irreps_fwd", mutates_args=())
+def irreps_fwd(x: Tensor, l_max: int) -> Tensor:
+    _require_cuda(x)
+    lib = N.lib()
+    x = x.contiguous()
+    out = x.new_empty((x.shape[0], (l_max + 1) ** 2))
+    rc = lib.fc_irreps_fwd(_p(x), x.shape[0], int(l_max), _code(x.dtype), _p(out), _stream(x.device))
+    _after(lib, rc, "fc_irreps_fwd", x.device)
+    return out
+
+
+@irreps_fwd.register_fake
+def _(x, l_max):
+    return x.new_empty((x.shape[0], (l_max + 1) ** 2))
+
+
+@torch.library.custom_op("flashcart::irreps_bwd", mutates_args=())
+def irreps_bwd(grad_output: Tensor, x: Tensor, l_max: int) -> Tensor:
+    _require_cuda(grad_output, x)
+    lib = N.lib()
+    g, x = grad_output.contiguous(), x.contiguous()
+    gx = torch.empty_like(x)
+    rc = lib.fc_irreps_bwd(_p(g), _p(x), x.shape[0], int(l_max), _code(x.dtype), _p(gx), _stream(x.device))
+    _after(lib, rc, "fc_irreps_bwd", x.device)
+    return gx
+
+
+@irreps_bwd.register_fake
+def _(grad_output, x, l_max):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("flashcart::irreps_dbwd", mutates_args=())
+def irreps_dbwd(grad_output: Tensor, x: Tensor, v: Tensor, l_max: int) -> Tuple[Tensor, Tensor]:
+    _require_cuda(grad_output, x, v)
+    lib = N.lib()
+    g, x, v = grad_output.contiguous(), x.contiguous(), v.contiguous()
+    dg = x.new_empty((x.shape[0], (l_max + 1) ** 2))
+    dx = torch.empty_like(x)
+    rc = lib.fc_irreps_dbwd(_p(g), _p(x), _p(v), x.shape[0], int(l_max), _code(x.dtype), _p(dg), _p(dx),
+                            _stream(x.device))
+    _after(lib, rc, "fc_irreps_dbwd", x.device)
+    return dg, dx
+
+
+@irreps_dbwd.register_fake
+def _(grad_output, x, v, l_max):
+    return x.new_empty((x.shape[0], (l_max + 1) ** 2)), torch.empty_like(x)
+
+
+def _irreps_setup(ctx, inputs, output):
+    x, l_max = inputs
+    ctx.save_for_backward(x)
+    ctx.l_max = int(l_max)
+
+
+def _irreps_backward(ctx, grad_output):
+    if grad_output is None or not ctx.needs_input_grad[0]:
+        return None, None
+    (x,) = ctx.saved_tensors
+    return torch.ops.flashcart.irreps_bwd(grad_output, x, ctx.l_max), None
+
+
+def _irreps_bwd_setup(ctx, inputs, output):
+    g, x, l_max = inputs
+    if hasattr(ctx, "set_materialize_grads"):
+        ctx.set_materialize_grads(False)
+    ctx.save_for_backward(g, x)
+    ctx.l_max = int(l_max)
+
+
+def _irreps_bwd_backward(ctx, v):
+    need_g, need_x = bool(ctx.needs_input_grad[0]), bool(ctx.needs_input_grad[1])
+    if v is None or not (need_g or need_x):
+        return None, None, None
+    g, x = ctx.saved_tensors
+    dg, dx = torch.ops.flashcart.irreps_dbwd(g, x, v, ctx.l_max)
+    return dg if need_g else None, dx if need_x else None, None
+
+
+irreps_fwd.register_autograd(_irreps_backward, setup_context=_irreps_setup)
+irreps_bwd.register_autograd(_irreps_bwd_backward, setup_context=_irreps_bwd_setup)
+
+
+# ----------------------------------------------------------------------------- linear maps
+
+
+def _linear_desc(x: Tensor, out_dim: int, in_offsets, out_offsets, m_values, f_in_values, f_out_values,
+                 precision: str) -> N.LinearDesc:
+    d = N.LinearDesc()
+    n = len(in_offsets)
+    if n > N.FC_MAX_L + 1:
+        raise NotImplementedError(f"flashcart_b200 linear supports at most {N.FC_MAX_L + 1} ranks, got {n}")
+    d.n_active = n
+    d.dtype = _code(x.dtype)
+    d.precision = N.FC_PREC_TF32 if (precision == "tf32" and x.dtype == torch.float32) else N.FC_PREC_IEEE
+    d.in_dim = x.shape[1]
+    d.out_dim = int(out_dim)
+    for l in range(n):
+        d.in_offsets[l] = int(in_offsets[l])
+        d.out_offsets[l] = int(out_offsets[l])
+        d.m_values[l] = int(m_values[l])
+        d.f_in_values[l] = int(f_in_values[l])
+        d.f_out_values[l] = int(f_out_values[l])
+    return d
+
+
+def _ptr_array(tensors: Sequence[Optional[Tensor]]):
+    arr = (ctypes.c_void_p * max(1, len(tensors)))()
+    for i, t in enumerate(tensors):
+        arr[i] = None if t is None or t.numel() == 0 else t.data_ptr()
+    return arr
+
+
+def _linear_fwd_impl(x: Tensor, weights: Sequence[Tensor], out_dim: int, lists, precision: str,
+                     scale: Tensor) -> Tensor:
+    lib = N.lib()
+    x = x.contiguous()
+    n_active = len(lists[0])
+    ws = [w.to(x.dtype).contiguous() for w in weights[:n_active]]
+    sc = scale.to(device=x.device, dtype=x.dtype).contiguous()
+    out = x.new_empty((x.shape[0], int(out_dim)))
+    d = _linear_desc(x, out_dim, lists[0], lists[1], lists[3], lists[4], lists[5], precision)
+    rc = lib.fc_linear_fwd(ctypes.byref(d), _p(x), _ptr_array(ws), _p(sc), x.shape[0], _p(out), _stream(x.device))
+    _after(lib, rc, "fc_linear_fwd", x.device)
+    return out
+
+
+def _linear_bwd_impl(grad_out: Tensor, x: Tensor, weights: Sequence[Tensor], need_x: bool, need_w: bool,
+                     lists, precision: str, scale: Tensor) -> Tuple[Tensor, List[Tensor]]:
+    lib = N.lib()
+    g, x = grad_out.contiguous(), x.contiguous()
+    n_active = len(lists[0])
+    ws = [w.to(x.dtype).contiguous() for w in weights[:n_active]]
+    sc = scale.to(device=x.device, dtype=x.dtype).contiguous()
+    gx = torch.empty_like(x) if need_x else x.new_empty((0,))
+    gws = [torch.empty_like(w) for w in ws] if need_w else [w.new_empty((0,)) for w in ws]
+    if n_active == 0:
+        if need_x:
+            gx.zero_()
+        return gx, gws
+    d = _linear_desc(x, g.shape[1], lists[0], lists[1], lists[3], lists[4], lists[5], precision)
+    rc = lib.fc_linear_bwd(ctypes.byref(d), _p(g), _p(x), _ptr_array(ws), _p(sc), x.shape[0],
+                           _p(gx) if need_x else None, _ptr_array(gws) if need_w else None, _stream(x.device))
+    _after(lib, rc, "fc_linear_bwd", x.device)
+    return gx, gws
+
+
+@torch.library.custom_op("flashcart::linear_fwd", mutates_args=())
+def linear_fwd(x: Tensor, weights: List[Tensor], meta: Tensor, out_size: int, use_fp64: bool,
+               dot_input_precision: str, in_offsets: List[int], out_offsets: List[int], weight_offsets: List[int],
+               m_values: List[int], f_in_values: List[int], f_out_values: List[int], scale: Tensor) -> Tensor:
+    _require_cuda(x, *weights)
+    lists = (in_offsets, out_offsets, weight_offsets, m_values, f_in_values, f_out_values)
+    return _linear_fwd_impl(x, weights, out_size, lists, dot_input_precision, scale)
+
+
+@linear_fwd.register_fake
+def _(x, weights, meta, out_size, use_fp64, dot_input_precision, in_offsets, out_offsets, weight_offsets, m_values,
+      f_in_values, f_out_values, scale):
+    return x.new_empty((x.shape[0], int(out_size)))
+
+
+@torch.library.custom_op("flashcart::linear_bwd", mutates_args=())
+def linear_bwd(grad_out: Tensor, x: Tensor, weights: List[Tensor], need_x: bool, need_weight: bool, use_fp64: bool,
+               dot_input_precision: str, in_offsets: List[int], out_offsets: List[int], weight_offsets: List[int],
+               m_values: List[int], f_in_values: List[int], f_out_values: List[int],
+               scale: Tensor) -> Tuple[Tensor, List[Tensor]]:
+    _require_cuda(grad_out, x, *weights)
+    lists = (in_offsets, out_offsets, weight_offsets, m_values, f_in_values, f_out_values)
+    return _linear_bwd_impl(grad_out, x, weights, need_x, need_weight, lists, dot_input_precision, scale)
+
+
+@linear_bwd.register_fake
+def _(grad_out, x, weights, need_x, need_weight, use_fp64, dot_input_precision, in_offsets, out_offsets,
+      weight_offsets, m_values, f_in_values, f_out_values, scale):
+    n = len(in_offsets)
+    return (torch.empty_like(x) if need_x else x.new_empty((0,)),
+            [torch.empty_like(w) if need_weight else w.new_empty((0,)) for w in weights[:n]])
+
+
+@torch.library.custom_op("flashcart::linear_dbwd", mutates_args=())
+def linear_dbwd(grad_out: Tensor, x: Tensor, weights: List[Tensor], v_grad_x: Tensor, v_grad_weight: List[Tensor],
+                use_fp64: bool, dot_input_precision: str, need_d_grad_out: bool, need_d_x: bool,
+                need_d_weight: bool, has_v_grad_x: bool, has_v_grad_weight: bool, in_offsets: List[int],
+                out_offsets: List[int], weight_offsets: List[int], m_values: List[int], f_in_values: List[int],
+                f_out_values: List[int], scale: Tensor) -> Tuple[Tensor, Tensor, List[Tensor]]:
+    """VJP of linear_bwd, composed from the forward / backward kernels.
+
+    With gx = g (sW) and gW = s g^T x (per rank), tangents (vx, vW) give
+    d_g = vx (sW)^T + x (s vW)^T,  d_x = g (s vW),  d_W = s g^T vx.
+    """
+    _require_cuda(grad_out, x, *weights)
+    lists = (in_offsets, out_offsets, weight_offsets, m_values, f_in_values, f_out_values)
+    n = len(in_offsets)
+    out_dim = grad_out.shape[1]
+    d_g = grad_out.new_zeros(grad_out.shape) if need_d_grad_out else grad_out.new_empty((0,))
+    d_x = torch.zeros_like(x) if need_d_x else x.new_empty((0,))
+    d_w = [torch.zeros_like(w) if need_d_weight else w.new_empty((0,)) for w in weights[:n]]
+    if need_d_grad_out:
+        if has_v_grad_x:
+            d_g = d_g + _linear_fwd_impl(v_grad_x, weights, out_dim, lists, dot_input_precision, scale)
+        if has_v_grad_weight:
+            d_g = d_g + _linear_fwd_impl(x, v_grad_weight, out_dim, lists, dot_input_precision, scale)
+    if need_d_x and has_v_grad_weight:
+        d_x, _ = _linear_bwd_impl(grad_out, x, v_grad_weight, True, False, lists, dot_input_precision, scale)
+    if need_d_weight and has_v_grad_x:
+        _, d_w = _linear_bwd_impl(grad_out, v_grad_x, weights, False, True, lists, dot_input_precision, scale)
+    return d_g, d_x, d_w
+
+
+@linear_dbwd.register_fake
+def _(grad_out, x, weights, v_grad_x, v_grad_weight, use_fp64, dot_input_precision, need_d_grad_out, need_d_x,
+      need_d_weight, has_v_grad_x, has_v_grad_weight, in_offsets, out_offsets, weight_offsets, m_values, f_in_values,
+      f_out_values, scale):
+    n = len(in_offsets)
+    return (torch.empty_like(grad_out) if need_d_grad_out else grad_out.new_empty((0,)),
+            torch.empty_like(x) if need_d_x else x.new_empty((0,)),
+            [torch.empty_like(w) if need_d_weight else w.new_empty((0,)) for w in weights[:n]])
+
+
+def _linear_setup(ctx, inputs, output):
+    (x, weights, meta, out_size, use_fp64, prec, *lists, scale) = inputs
+    ctx.save_for_backward(x, *weights, scale)
+    ctx.n_w = len(weights)
+    ctx.use_fp64 = bool(use_fp64)
+    ctx.prec = prec
+    ctx.lists = tuple(list(v) for v in lists)
+
+
+def _linear_backward(ctx, grad_out):
+    saved = ctx.saved_tensors
+    x, weights, scale = saved[0], list(saved[1:1 + ctx.n_w]), saved[-1]
+    need_x, need_w = bool(ctx.needs_input_grad[0]), bool(ctx.needs_input_grad[1])
+    if grad_out is None or not (need_x or need_w):
+        return (None,) * 13
+    gx, gws = torch.ops.flashcart.linear_bwd(grad_out, x, weights, need_x, need_w, ctx.use_fp64, ctx.prec,
+                                             *ctx.lists, scale)
+    if need_w:
+        n = len(ctx.lists[0])
+        gws = list(gws) + [torch.zeros_like(w) for w in weights[n:]]
+    return (gx if need_x else None, gws if need_w else None) + (None,) * 11
+
+
+def _linear_bwd_setup(ctx, inputs, output):
+    (g, x, weights, need_x, need_w, use_fp64, prec, *lists, scale) = inputs
+    ctx.save_for_backward(g, x, *weights, scale)
+    ctx.n_w = len(weights)
+    ctx.made = (bool(need_x), bool(need_w))
+    ctx.use_fp64 = bool(use_fp64)
+    ctx.prec = prec
+    ctx.lists = tuple(list(v) for v in lists)
+    if hasattr(ctx, "set_materialize_grads"):
+        ctx.set_materialize_grads(False)
+
+
+def _linear_bwd_backward(ctx, v_gx, v_gw):
+    saved = ctx.saved_tensors
+    g, x, weights, scale = saved[0], saved[1], list(saved[2:2 + ctx.n_w]), saved[-1]
+    need_g, need_x, need_w = (bool(ctx.needs_input_grad[i]) for i in range(3))
+    if not (need_g or need_x or need_w):
+        return (None,) * 14
+    has_vx = v_gx is not None and v_gx.numel() != 0 and ctx.made[0]
+    has_vw = (v_gw is not None and len(v_gw) > 0 and any(v is not None and v.numel() for v in v_gw)
+              and ctx.made[1])
+    vx = v_gx if has_vx else x.new_empty((0,))
+    if has_vw:
+        vw = [v if (v is not None and v.numel()) else torch.zeros_like(w) for v, w in zip(v_gw, weights)]
+    else:
+        vw = [w.new_empty((0,)) for w in weights]
+    dg, dx, dw = torch.ops.flashcart.linear_dbwd(g, x, weights, vx, vw, ctx.use_fp64, ctx.prec, need_g, need_x,
+                                                 need_w, has_vx, has_vw, *ctx.lists, scale)
+    if need_w:
+        n = len(ctx.lists[0])
+        dw = list(dw) + [torch.zeros_like(w) for w in weights[n:]]
+    return (dg if need_g else None, dx if need_x else None, dw if need_w else None) + (None,) * 11
+
+
+linear_fwd.register_autograd(_linear_backward, setup_context=_linear_setup)
+linear_bwd.register_autograd(_linear_bwd_backward, setup_context=_linear_bwd_setup)

@@ -1,0 +1,170 @@
+/*
+ * flashcart_b200 -- C ABI of the B200 (sm_100a) kernels behind FlashCart's o3 operators.
+ *
+ * Every entry point takes plain pointers to DEVICE memory (row-major, contiguous),
+ * sizes, a POD descriptor and a cudaStream_t, and returns an int status
+ * (FC_OK = 0, negative values below). Nothing here allocates device memory, frees
+ * caller memory or synchronises the stream; outputs are owned by the caller.
+ * Accumulated outputs (scatter targets) are zero-filled inside the call with
+ * cudaMemsetAsync on the given stream. Errors in the DATA (an index out of range,
+ * an unsorted receiver list) are OR-ed into the optional device word `status`
+ * (FC_DEV_* bits) instead of faulting; pass NULL to skip the check.
+ *
+ * Layouts follow the reference exactly (reference = inm-leibniz/flashcart,
+ * paths relative to its src/flashcart/):
+ *  - feature rows are rank blocks l = 0..l_max, each (2l+1, features), component axis
+ *    outer and channels contiguous (o3/utils.py:206-262);
+ *  - stored STF component order per rank (o3/_codegen_common.py:37-73);
+ *  - tensor-product output rank block (2l+1, paths_l, F) or (2l+1, F) when paths are
+ *    reduced, F = max(in1_features, in2_features) (o3/_tensor_product.py:1146-1149);
+ *  - per-edge / per-row weights (rows, n_total_paths * F), path-major
+ *    (o3/utils.py:127-154), path order of o3/utils.py:157-203.
+ */
+#ifndef FLASHCART_B200_H
+#define FLASHCART_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef FC_HOST_EMU
+typedef struct CUstream_st* fc_stream_t;
+#else
+typedef void* fc_stream_t;
+#endif
+
+/* status codes returned by every entry point */
+#define FC_OK 0
+#define FC_ERR_INVALID -1     /* bad argument (shape, rank, null pointer, dtype) */
+#define FC_ERR_UNSUPPORTED -2 /* configuration outside the compiled kernels (rank > 3, ...) */
+#define FC_ERR_LAUNCH -3      /* CUDA launch or runtime error; see fc_last_error() */
+#define FC_ERR_CAPACITY -4    /* a size exceeds a fixed capacity of the entry point */
+
+/* bits of the optional device status word */
+#define FC_DEV_BAD_INDEX 1    /* an edge index pointed outside its node array */
+#define FC_DEV_UNSORTED 2     /* receiver indices were not ascending */
+
+/* dtypes */
+#define FC_F32 0
+#define FC_F64 1
+
+/* linear-map arithmetic */
+#define FC_PREC_IEEE 0 /* exact fp32 / fp64 FMA accumulation */
+#define FC_PREC_TF32 1 /* tensor cores with tf32 operands, fp32 accumulation */
+
+#define FC_MAX_L 3
+
+/* Version string "flashcart_b200 <semver> (<build info>)". */
+const char* fc_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* fc_last_error(void);
+
+/* ------------------------------------------------------------------------------
+ * Receiver CSR.
+ * Replaces torch.searchsorted(idx_i, arange(n_nodes + 1)) in the reference
+ * tp_fwd/tp_bwd ops (o3/_tensor_product.py:396-405): rowptr[k] = number of edges
+ * with idx_i < k, for k = 0..n_nodes. Also flags FC_DEV_UNSORTED when idx_i is not
+ * ascending (the reference's torch._assert_async, o3/_tensor_product.py:397-401)
+ * and FC_DEV_BAD_INDEX for idx_i outside [0, n_nodes).
+ * ------------------------------------------------------------------------------ */
+int fc_build_rowptr(const int64_t* idx_i, int64_t n_edges, int64_t n_nodes, int64_t* rowptr,
+                    int32_t* status, fc_stream_t stream);
+
+/* ------------------------------------------------------------------------------
+ * Cartesian tensor product.
+ * ------------------------------------------------------------------------------ */
+typedef struct fc_tp_desc {
+  int32_t in1_l_max, in2_l_max, out_l_max;
+  int32_t in1_features, in2_features; /* equal, or one of them 1 (broadcast) */
+  int32_t symmetric_product;          /* keep only l1 >= l2 paths (in1 == in2) */
+  int32_t shared_weights;             /* weights: (n_total_paths*F) instead of (rows, ...) */
+  int32_t reduce_paths;               /* sum the paths of each output rank */
+  int32_t dtype;                      /* FC_F32 / FC_F64 */
+} fc_tp_desc;
+
+/* Number of paths (sum over output ranks) of a descriptor, or a negative status. */
+int fc_tp_num_paths(const fc_tp_desc* desc);
+/* Width of one output row in elements, or a negative status. */
+int64_t fc_tp_out_dim(const fc_tp_desc* desc);
+
+/* Forward. Replaces flashcart::tp_fwd (o3/_tensor_product.py:332-479).
+ * Convolution when rowptr != NULL: out[i] = sum over edges e of receiver i of
+ *   W[e] (.) TP(in1[idx_j[e]], in2[e]);  in2/weights have one row per edge,
+ *   rowptr from fc_build_rowptr, n_out_rows = number of receivers, n_in1_rows =
+ *   rows of in1 (idx_j range).
+ * Dense when rowptr == NULL: row r of out from row r of in1, in2 and weights;
+ *   n_out_rows = n_in1_rows = rows. */
+int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const void* weights,
+              const int64_t* rowptr, const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows,
+              void* out, int32_t* status, fc_stream_t stream);
+
+/* Backward. Replaces flashcart::tp_bwd (o3/_tensor_product.py:588-787).
+ * grad_in1 / grad_in2 / grad_weights may be NULL (not requested). n_in2_rows = rows
+ * of in2 (edges for a convolution). Scatter targets are zero-filled here. */
+int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2,
+              const void* weights, const int64_t* rowptr, const int64_t* idx_j, int64_t n_out_rows,
+              int64_t n_in1_rows, int64_t n_in2_rows, void* grad_in1, void* grad_in2,
+              void* grad_weights, int32_t* status, fc_stream_t stream);
+
+/* Double backward: VJP of fc_tp_bwd with tangents (v_in1, v_in2, v_weights) on its
+ * three outputs (NULL = zero tangent). Replaces the autograd of flashcart::tp_bwd
+ * (tp_dbwd, o3/_tensor_product.py:837-1093). Outputs may be NULL. */
+int fc_tp_dbwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2,
+               const void* weights, const void* v_in1, const void* v_in2, const void* v_weights,
+               const int64_t* rowptr, const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows,
+               int64_t n_in2_rows, void* d_grad_out, void* d_in1, void* d_in2, void* d_weights,
+               int32_t* status, fc_stream_t stream);
+
+/* ------------------------------------------------------------------------------
+ * Direction tensors (edge attributes): stored STF components of T^l(x), l <= l_max,
+ * for unit vectors x (n, 3) -> (n, (l_max+1)^2).
+ * Replace flashcart::irreps_fwd / irreps_bwd / irreps_dbwd (o3/_irreps.py:84-186).
+ * ------------------------------------------------------------------------------ */
+int fc_irreps_fwd(const void* x, int64_t n, int32_t l_max, int32_t dtype, void* out, fc_stream_t stream);
+int fc_irreps_bwd(const void* grad_out, const void* x, int64_t n, int32_t l_max, int32_t dtype,
+                  void* grad_x, fc_stream_t stream);
+int fc_irreps_dbwd(const void* grad_out, const void* x, const void* v, int64_t n, int32_t l_max,
+                   int32_t dtype, void* d_grad_out, void* d_x, fc_stream_t stream);
+
+/* ------------------------------------------------------------------------------
+ * Equivariant linear map: for each active rank l (l <= min(in_l_max, out_l_max))
+ *   y[n, m, :] = x[n, m, :] @ (scale[l] * W_l)^T,   m = 0..m_values[l]-1,
+ *   W_l: (f_out_values[l], f_in_values[l]) row-major,
+ * where rank l of a row starts at in_offsets[l] (x) / out_offsets[l] (y) and its
+ * component m at + m * f_in (x) / + m * f_out (y). Output columns after the last
+ * active rank are zero. The descriptor carries the same metadata as the reference
+ * op flashcart::linear_fwd (in_offsets, out_offsets, m_values, f_in_values,
+ * f_out_values; o3/_linear.py:113-166, 328-385) plus the row widths.
+ * `weights` is a HOST array of per-rank DEVICE pointers, `scale` a DEVICE array with
+ * one entry per active rank (dtype of x).
+ * ------------------------------------------------------------------------------ */
+typedef struct fc_linear_desc {
+  int32_t n_active;                     /* active ranks, 0..FC_MAX_L+1 */
+  int32_t dtype;                        /* FC_F32 / FC_F64 */
+  int32_t precision;                    /* FC_PREC_IEEE or FC_PREC_TF32 (fp32 only) */
+  int32_t reserved;
+  int64_t in_dim, out_dim;              /* row widths of x and y */
+  int64_t in_offsets[FC_MAX_L + 1];
+  int64_t out_offsets[FC_MAX_L + 1];
+  int32_t m_values[FC_MAX_L + 1];
+  int32_t f_in_values[FC_MAX_L + 1];
+  int32_t f_out_values[FC_MAX_L + 1];
+} fc_linear_desc;
+
+/* Forward. Replaces flashcart::linear_fwd (o3/_linear.py:328-385). */
+int fc_linear_fwd(const fc_linear_desc* desc, const void* x, const void* const* weights,
+                  const void* scale, int64_t n, void* out, fc_stream_t stream);
+/* Backward. Replaces flashcart::linear_bwd (o3/_linear.py:457-538). grad_x may be
+ * NULL; grad_weights may be NULL or a host array of per-rank device pointers (each
+ * fully overwritten). Columns of grad_x outside the active ranks are zero. */
+int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* x,
+                  const void* const* weights, const void* scale, int64_t n, void* grad_x,
+                  void* const* grad_weights, fc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHCART_B200_H */

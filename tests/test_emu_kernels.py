@@ -1,0 +1,139 @@
+"""The generated kernel bodies and the C ABI, executed on the CPU (host-emulation build).
+
+The host-emulation library compiles the exact per-thread code of the sm_100a
+kernels (generated tensor-product bodies, direction-tensor polynomials, linear-map
+GEMMs, receiver CSR) with the host compiler; this suite drives it through the same
+C entry points and checks every output against the reference's golden vectors.
+"""
+
+import pytest
+import torch
+
+import abi_calls as A
+from flashcart_b200 import _native as N
+
+TOL = 1e-11
+
+
+def _tp_keys(golden):
+    return sorted({k.rsplit("/", 1)[0] for k in golden if k.startswith("tp/")})
+
+
+def _case(golden, key):
+    m = [int(v) for v in golden[key + "/meta"]]
+    idx_i = golden.get(key + "/idx_i")
+    idx_j = golden.get(key + "/idx_j")
+    return m, idx_i, idx_j
+
+
+def test_emu_tp_forward(golden, emu_lib):
+    for key in _tp_keys(golden):
+        m, idx_i, idx_j = _case(golden, key)
+        in1 = golden[key + "/in1"]
+        in2 = in1 if m[5] else golden[key + "/in2"]
+        out = A.tp_fwd(emu_lib, m, in1, in2, golden[key + "/w"], idx_i, idx_j)
+        assert (out - golden[key + "/out"]).abs().max() < TOL, key
+
+
+def test_emu_tp_backward(golden, emu_lib):
+    for key in _tp_keys(golden):
+        m, idx_i, idx_j = _case(golden, key)
+        in1 = golden[key + "/in1"]
+        sym = bool(m[5])
+        in2 = in1 if sym else golden[key + "/in2"]
+        g1, g2, gw = A.tp_bwd(emu_lib, m, golden[key + "/g"], in1, in2, golden[key + "/w"], idx_i, idx_j)
+        if sym:
+            assert (g1 + g2 - golden[key + "/grad_in1"]).abs().max() < TOL, key
+        else:
+            assert (g1 - golden[key + "/grad_in1"]).abs().max() < TOL, key
+            assert (g2 - golden[key + "/grad_in2"]).abs().max() < TOL, key
+        assert (gw - golden[key + "/grad_w"]).abs().max() < TOL, key
+
+
+def test_emu_tp_backward_partial_requests(golden, emu_lib):
+    key = "tp/l3x3to3_f21/conv"
+    m, idx_i, idx_j = _case(golden, key)
+    args = (golden[key + "/g"], golden[key + "/in1"], golden[key + "/in2"], golden[key + "/w"], idx_i, idx_j)
+    for need in [(True, False, False), (False, True, False), (False, False, True)]:
+        g = A.tp_bwd(emu_lib, m, *args, need=need)
+        for got, want, n in zip(g, ("grad_in1", "grad_in2", "grad_w"), need):
+            if n:
+                assert (got - golden[f"{key}/{want}"]).abs().max() < TOL
+            else:
+                assert got is None
+
+
+def test_emu_tp_double_backward(golden, emu_lib):
+    for key in _tp_keys(golden):
+        m, idx_i, idx_j = _case(golden, key)
+        in1 = golden[key + "/in1"]
+        sym = bool(m[5])
+        in2 = in1 if sym else golden[key + "/in2"]
+        v1 = golden[key + "/tan_in1"]
+        v2 = v1 if sym else golden[key + "/tan_in2"]
+        vw = golden[key + "/tan_w"]
+        dg, d1, d2, dw = A.tp_dbwd(emu_lib, m, golden[key + "/g"], in1, in2, golden[key + "/w"], v1, v2, vw,
+                                   idx_i, idx_j)
+        assert (dg - golden[key + "/dd_g"]).abs().max() < TOL, (key, "g")
+        if sym:
+            assert (d1 + d2 - golden[key + "/dd_in1"]).abs().max() < TOL, (key, "in1")
+        else:
+            assert (d1 - golden[key + "/dd_in1"]).abs().max() < TOL, (key, "in1")
+            assert (d2 - golden[key + "/dd_in2"]).abs().max() < TOL, (key, "in2")
+        assert (dw - golden[key + "/dd_w"]).abs().max() < TOL, (key, "w")
+
+
+@pytest.mark.parametrize("l", range(4))
+def test_emu_irreps(golden, emu_lib, l):
+    k = f"irreps/l{l}"
+    x, g, v = golden[k + "/x"], golden[k + "/g"], golden[k + "/tan_x"]
+    assert (A.irreps_fwd(emu_lib, x, l) - golden[k + "/out"]).abs().max() < TOL
+    assert (A.irreps_bwd(emu_lib, g, x, l) - golden[k + "/grad_x"]).abs().max() < TOL
+    dg, dx = A.irreps_dbwd(emu_lib, g, x, v, l)
+    assert (dg - golden[k + "/dd_g"]).abs().max() < TOL
+    assert (dx - golden[k + "/dd_x"]).abs().max() < TOL
+
+
+def test_emu_linear(golden, emu_lib):
+    names = sorted({k.split("/")[1] for k in golden if k.startswith("linear/")})
+    for name in names:
+        k = f"linear/{name}"
+        meta = [int(v) for v in golden[k + "/meta"]]
+        li, lo, fi, fo, has_ws = meta[:5]
+        paths = meta[5:]
+        common = min(li, lo)
+        ws = [golden[f"{k}/w{l}"] for l in range(common + 1)]
+        scale = torch.tensor([1.0 if has_ws == 1 else (fi * paths[l]) ** -0.5 for l in range(common + 1)],
+                             dtype=torch.float64)
+        d = A.linear_desc(li, lo, fi, fo, paths, torch.float64)
+        out = A.linear_fwd(emu_lib, d, golden[k + "/x"], ws, scale)
+        assert (out - golden[k + "/out"]).abs().max() < TOL, name
+        gx, gws = A.linear_bwd(emu_lib, d, golden[k + "/g"], golden[k + "/x"], ws, scale)
+        assert (gx - golden[k + "/grad_x"]).abs().max() < TOL, name
+        for l in range(common + 1):
+            assert (gws[l] - golden[f"{k}/grad_w{l}"]).abs().max() < TOL, (name, l)
+
+
+def test_emu_rowptr_and_status_flags(emu_lib):
+    idx = torch.tensor([0, 0, 1, 3, 3, 3], dtype=torch.int64)
+    status = torch.zeros(1, dtype=torch.int32)
+    rp = A.rowptr(emu_lib, idx, 5, status)
+    assert rp.tolist() == [0, 2, 3, 3, 6, 6]
+    assert int(status) == 0
+    bad = torch.tensor([0, 2, 1, 7], dtype=torch.int64)
+    A.rowptr(emu_lib, bad, 5, status)
+    assert int(status) & N.FC_DEV_UNSORTED
+    assert int(status) & N.FC_DEV_BAD_INDEX
+
+
+def test_emu_tp_out_of_range_sender_is_flagged_not_read(emu_lib):
+    m = [1, 1, 1, 2, 1, 0, 0, 0]
+    in1 = torch.randn(3, 4 * 2, dtype=torch.float64)
+    in2 = torch.randn(2, 4, dtype=torch.float64)
+    w = torch.randn(2, 3 * 2, dtype=torch.float64)
+    idx_i = torch.tensor([0, 1])
+    idx_j = torch.tensor([1, 99])
+    status = torch.zeros(1, dtype=torch.int32)
+    out = A.tp_fwd(emu_lib, m, in1, in2, w, idx_i, idx_j, status)
+    assert int(status) & N.FC_DEV_BAD_INDEX
+    assert torch.isfinite(out).all()

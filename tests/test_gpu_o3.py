@@ -1,0 +1,201 @@
+"""GPU parity of the sm_100a kernels (torch ops and the raw C ABI) against the reference.
+
+float64: against the reference's golden vectors at the reference's own tolerances
+(1e-12 forward / backward, 1e-10 second derivatives). float32: against the oracle in
+float64 with fp32 tolerances. Larger convolutions check size-independent
+properties (linearity in the weights, invariance to the edge order of a receiver).
+"""
+
+import pytest
+import torch
+
+import abi_calls as A
+from flashcart_b200 import _native as N
+from flashcart_b200 import o3
+from flashcart_b200.ops import check_device_status
+from oracle import stf_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _tp_keys(golden):
+    return sorted({k.rsplit("/", 1)[0] for k in golden if k.startswith("tp/")})
+
+
+def _dev(golden, key, dev):
+    t = golden.get(key)
+    return None if t is None else t.to(dev)
+
+
+def _second_order(fn, leaves, g, tangents):
+    leaves = [t.detach().clone().requires_grad_(True) for t in leaves]
+    g_leaf = g.detach().clone().requires_grad_(True)
+    out = fn(*leaves)
+    grads = torch.autograd.grad(out, leaves, g_leaf, create_graph=True, allow_unused=True)
+    s = sum((gr * v).sum() for gr, v in zip(grads, tangents) if gr is not None)
+    second = torch.autograd.grad(s, leaves + [g_leaf], allow_unused=True)
+    second = [torch.zeros_like(t) if d is None else d for t, d in zip(leaves + [g_leaf], second)]
+    grads = [torch.zeros_like(l) if gr is None else gr for l, gr in zip(leaves, grads)]
+    return out.detach(), [x.detach() for x in grads], second
+
+
+def test_gpu_tensor_products_match_reference_golden(golden, cuda_device):
+    dev = cuda_device
+    for key in _tp_keys(golden):
+        l1, l2, lo, f1, f2, sym, shared, red, conv = [int(v) for v in golden[key + "/meta"]]
+        tp = o3.TensorProduct(l1, l2, lo, f1, f2, symmetric_product=bool(sym), shared_weights=bool(shared),
+                              reduce_paths=bool(red))
+        idx_i, idx_j = _dev(golden, key + "/idx_i", dev), _dev(golden, key + "/idx_j", dev)
+        names = ("in1", "w") if sym else ("in1", "in2", "w")
+        leaves = [golden[f"{key}/{n}"].to(dev) for n in names]
+        tangents = [golden[f"{key}/tan_{n}"].to(dev) for n in names]
+        if sym:
+            fn = lambda a, w: tp(a, a, w, idx_i, idx_j)  # noqa: E731
+        else:
+            fn = lambda a, b, w: tp(a, b, w, idx_i, idx_j)  # noqa: E731
+        out, grads, second = _second_order(fn, leaves, golden[key + "/g"].to(dev), tangents)
+        assert (out.cpu() - golden[key + "/out"]).abs().max() < 1e-12, key
+        for n, gr in zip(names, grads):
+            assert (gr.cpu() - golden[f"{key}/grad_{n}"]).abs().max() < 1e-12, (key, n)
+        for n, d in zip(names + ("g",), second):
+            assert (d.cpu() - golden[f"{key}/dd_{n}"]).abs().max() < 1e-10, (key, "dd", n)
+    check_device_status(dev)
+
+
+@pytest.mark.parametrize("l", range(4))
+def test_gpu_irreps_match_reference_golden(golden, cuda_device, l):
+    k = f"irreps/l{l}"
+    ir = o3.Irreps(l)
+    fn = lambda a: ir.forward_normalized(a) + 0.0 * a.sum()  # noqa: E731
+    out, grads, second = _second_order(fn, [golden[k + "/x"].to(cuda_device)], golden[k + "/g"].to(cuda_device),
+                                       [golden[k + "/tan_x"].to(cuda_device)])
+    assert (out.cpu() - golden[k + "/out"]).abs().max() < 1e-12
+    assert (grads[0].cpu() - golden[k + "/grad_x"]).abs().max() < 1e-12
+    assert (second[0].cpu() - golden[k + "/dd_x"]).abs().max() < 1e-10
+    assert (second[1].cpu() - golden[k + "/dd_g"]).abs().max() < 1e-10
+
+
+def test_gpu_linear_matches_reference_golden(golden, cuda_device):
+    names = sorted({k.split("/")[1] for k in golden if k.startswith("linear/")})
+    for name in names:
+        k = f"linear/{name}"
+        meta = [int(v) for v in golden[k + "/meta"]]
+        li, lo, fi, fo, has_ws = meta[:5]
+        paths = meta[5:]
+        lin = o3.LinearLayer(li, lo, fi, fo, in_paths=paths, weight_scale=1.0 if has_ws == 1 else None)
+        lin = lin.to(cuda_device, torch.float64)
+        common = min(li, lo)
+        ws = [golden[f"{k}/w{l}"].to(cuda_device) for l in range(common + 1)]
+        with torch.no_grad():
+            for l in range(common + 1):
+                lin.weight[l].copy_(ws[l])
+        x = golden[k + "/x"].to(cuda_device).requires_grad_(True)
+        g = golden[k + "/g"].to(cuda_device).requires_grad_(True)
+        out = lin(x)
+        assert (out.detach().cpu() - golden[k + "/out"]).abs().max() < 1e-12, name
+        params = list(lin.weight)
+        grads = torch.autograd.grad(out, [x] + params, g, create_graph=True)
+        assert (grads[0].detach().cpu() - golden[k + "/grad_x"]).abs().max() < 1e-12, name
+        for l in range(common + 1):
+            assert (grads[1 + l].detach().cpu() - golden[f"{k}/grad_w{l}"]).abs().max() < 1e-12, (name, l)
+        tangents = [golden[k + "/tan_x"].to(cuda_device)] + [golden[f"{k}/tan_w{l}"].to(cuda_device)
+                                                            for l in range(common + 1)]
+        s = sum((gr * v).sum() for gr, v in zip(grads, tangents))
+        second = torch.autograd.grad(s, [x] + params + [g])
+        assert (second[0].cpu() - golden[k + "/dd_x"]).abs().max() < 1e-10, name
+        for l in range(common + 1):
+            assert (second[1 + l].cpu() - golden[f"{k}/dd_w{l}"]).abs().max() < 1e-10, (name, l)
+        assert (second[-1].cpu() - golden[k + "/dd_g"]).abs().max() < 1e-10, name
+
+
+def test_gpu_raw_c_abi_matches_golden(golden, cuda_device):
+    """The C entry points called directly with device pointers (no torch operator layer)."""
+    lib = N.lib()
+    for key in ("tp/l3x3to3_f21/conv", "tp/l3x3to3_f22_shared_reduce/dense", "tp/l2x2to2_f41/conv"):
+        m = [int(v) for v in golden[key + "/meta"]]
+        t = {n: golden[f"{key}/{n}"].to(cuda_device) for n in ("in1", "in2", "w", "g")}
+        idx_i, idx_j = _dev(golden, key + "/idx_i", cuda_device), _dev(golden, key + "/idx_j", cuda_device)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        out = A.tp_fwd(lib, m, t["in1"], t["in2"], t["w"], idx_i, idx_j, status)
+        g1, g2, gw = A.tp_bwd(lib, m, t["g"], t["in1"], t["in2"], t["w"], idx_i, idx_j, status=status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert (out.cpu() - golden[key + "/out"]).abs().max() < 1e-12, key
+        assert (g1.cpu() - golden[key + "/grad_in1"]).abs().max() < 1e-12, key
+        assert (g2.cpu() - golden[key + "/grad_in2"]).abs().max() < 1e-12, key
+        assert (gw.cpu() - golden[key + "/grad_w"]).abs().max() < 1e-12, key
+
+
+def _conv_inputs(n_nodes, n_edges, C, l1, l2, seed, dtype, dev):
+    g = torch.Generator().manual_seed(seed)
+    idx_i = torch.sort(torch.randint(0, n_nodes, (n_edges,), generator=g)).values
+    idx_j = torch.randint(0, n_nodes, (n_edges,), generator=g)
+    in1 = torch.randn(n_nodes, (l1 + 1) ** 2 * C, generator=g, dtype=torch.float64)
+    r = torch.nn.functional.normalize(torch.randn(n_edges, 3, generator=g, dtype=torch.float64), dim=-1)
+    in2 = O.irreps(r, l2)
+    return [t.to(dev) for t in (idx_i, idx_j)] + [t.to(dev, dtype) for t in (in1, in2)]
+
+
+@pytest.mark.parametrize("sig", [(2, 2, 2, 64), (3, 3, 3, 128), (0, 3, 3, 128), (2, 3, 3, 32)])
+def test_gpu_fp32_convolution_vs_oracle(cuda_device, sig):
+    l1, l2, lo, C = sig
+    dev = cuda_device
+    n_nodes, n_edges = 96, 1536
+    idx_i, idx_j, in1, in2 = _conv_inputs(n_nodes, n_edges, C, l1, l2, 3, torch.float32, dev)
+    tp = o3.TensorProduct(l1, l2, lo, C, 1)
+    w = torch.randn(n_edges, tp.n_total_paths * C, device=dev)
+    leaves = [in1.requires_grad_(True), in2.requires_grad_(True), w.requires_grad_(True)]
+    out = tp(*leaves, idx_i, idx_j)
+    g = torch.randn_like(out)
+    grads = torch.autograd.grad(out, leaves, g)
+    ref_leaves = [t.detach().double().cpu().requires_grad_(True) for t in leaves]
+    ref = O.tensor_product(*ref_leaves, idx_i.cpu(), idx_j.cpu(), l1, l2, lo, C, 1)
+    ref_grads = torch.autograd.grad(ref, ref_leaves, g.double().cpu())
+    scale = ref.abs().max().item()
+    # fp32 accumulation over ~16 edges x tens of paths: relative 1e-5 of the output range
+    assert (out.detach().double().cpu() - ref).abs().max().item() < 2e-5 * scale
+    for a, b in zip(grads, ref_grads):
+        assert (a.double().cpu() - b).abs().max().item() < 2e-5 * b.abs().max().item()
+    check_device_status(dev)
+
+
+def test_gpu_convolution_linearity_and_edge_order_at_size(cuda_device):
+    """Config-1 shapes (E = 2^20 edges, N = 2^16 nodes, C = 64, (2,2)->2): properties that need no oracle."""
+    dev = cuda_device
+    n_nodes, n_edges, C = 65536, 1048576, 64
+    idx_i, idx_j, in1, in2 = _conv_inputs(n_nodes, n_edges, C, 2, 2, 11, torch.float32, dev)
+    tp = o3.TensorProduct(2, 2, 2, C, 1)
+    w1 = torch.randn(n_edges, tp.n_total_paths * C, device=dev)
+    w2 = torch.randn_like(w1)
+    with torch.no_grad():
+        a = tp(in1, in2, w1, idx_i, idx_j)
+        b = tp(in1, in2, w2, idx_i, idx_j)
+        ab = tp(in1, in2, 0.5 * w1 - 2.0 * w2, idx_i, idx_j)
+        assert (ab - (0.5 * a - 2.0 * b)).abs().max().item() < 1e-4 * ab.abs().max().item()
+        # reverse the edge order inside every receiver segment: same sums up to rounding
+        perm = torch.arange(n_edges, device=dev)
+        key = idx_i * n_edges + (n_edges - 1 - perm)
+        order = torch.argsort(key)
+        c = tp(in1, in2[order], w1[order], idx_i[order], idx_j[order])
+        assert (c - a).abs().max().item() < 1e-4 * a.abs().max().item()
+    check_device_status(dev)
+
+
+def test_gpu_unsorted_receivers_are_reported(cuda_device):
+    dev = cuda_device
+    tp = o3.TensorProduct(1, 1, 1, 4, 1)
+    in1 = torch.randn(5, tp.in1_dim, device=dev)
+    in2 = torch.randn(4, tp.in2_dim, device=dev)
+    w = torch.randn(4, tp.n_total_paths * 4, device=dev)
+    idx_i = torch.tensor([0, 3, 1, 2], device=dev)
+    idx_j = torch.tensor([1, 2, 3, 4], device=dev)
+    check_device_status(dev)
+    tp(in1, in2, w, idx_i, idx_j)
+    with pytest.raises(RuntimeError, match="receiver-sorted"):
+        check_device_status(dev)
+
+
+def test_gpu_cpu_tensors_raise(cuda_device):
+    tp = o3.TensorProduct(1, 1, 1, 4, 1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        tp(torch.randn(3, tp.in1_dim), torch.randn(3, tp.in2_dim), torch.randn(3, tp.n_total_paths * 4))
