@@ -1,0 +1,334 @@
+#!/usr/bin/env python
+"""Headline benchmark: FlashCart potential energy + forces + stress at 27,648 atoms.
+
+Workload: a seeded 27,648-atom water-like periodic box (9,216 H2O,
+24 x 24 x 16 jittered lattice, 74.52 x 74.52 x 49.68 A), r_max 5 A (~1.49 M edges), the
+reference architecture with 128 channels, hidden and edge ranks <= 3, 2 interaction
+layers, correlation 3, random-init weights (torch.manual_seed(0)), float32. One step =
+``FlashCartPotential.predict(graph, compute_forces=True, compute_stress=True)``.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+With N > 1 (torchrun, one rank per GPU) every rank evaluates its own box (seed =
+rank): batched evaluation sharded over structures, no collective in the data path
+("scaling": "weak"); the timed region is bracketed by a barrier and a device
+synchronise on each rank and the max over ranks is reported. ``--impl reference``
+times the CPU reference port (the oracle) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "atom-steps/s (E+F+stress) at 27,648 atoms"
+UNIT = "atom-steps/s"
+WORKLOAD = ("config3: 27,648-atom water box (24x24x16 H2O lattice, r_max 5 A), FlashCart C=128, l<=3, "
+            "2 interactions, correlation 3, E+F+stress per step")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    return ap.parse_args()
+
+
+def _dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# --------------------------------------------------------------------------------- inputs
+
+
+def build_graph(seed: int, device):
+    from flashcart_b200.data import neighbors, synthetic
+
+    s = synthetic.water_box(24, 24, 16, seed=seed)
+    ei, sh = neighbors.neighbor_list(s["positions"], s["cell"], s["pbc"], 5.0,
+                                     device=str(device) if torch.cuda.is_available() else "cpu")
+    g = synthetic.graph_from_structure(s, ei, sh, device=device, dtype=torch.float32)
+    return g, ei.shape[1] / len(s["positions"])
+
+
+def build_model(avg_neighbors: float, device):
+    from flashcart_b200.model.flashcart import FlashCartPotential
+    from flashcart_b200.model.presets import water_model_kwargs
+
+    torch.manual_seed(0)
+    return FlashCartPotential(**water_model_kwargs("cfg3arch", avg_neighbors)).to(device)
+
+
+# --------------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idx = local_rank
+        if vis:
+            parts = [p.strip() for p in vis.split(",")]
+            if local_rank < len(parts) and parts[local_rank].isdigit():
+                idx = int(parts[local_rank])
+        self.idx = idx
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------- helpers
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def _profile_traffic(kernel: str):
+    """DRAM bytes per launch of a kernel from the committed ncu summaries (profiles/*.md)."""
+    pat = re.compile(r"traffic_bytes_per_launch\[" + re.escape(kernel) + r"\]\s*[:=]\s*([0-9.eE+]+)")
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for fn in sorted(os.listdir(d)):
+        if fn.endswith((".md", ".txt")):
+            m = pat.search(open(os.path.join(d, fn)).read())
+            if m:
+                return float(m.group(1))
+    return None
+
+
+def cpu_reference_sample(steps: int, warmup: int, min_seconds: float = 0.0):
+    """The oracle port of the potential on the host cores: 192-atom box, config-3 architecture."""
+    from flashcart_b200.data import neighbors, synthetic
+    from flashcart_b200.model.flashcart import FlashCartPotential
+    from flashcart_b200.model.presets import water_model_kwargs
+    from oracle import model_oracle
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    s = synthetic.config0_water()
+    ei, sh = neighbors.neighbor_list(s["positions"], s["cell"], s["pbc"], 5.0)
+    avg = ei.shape[1] / len(s["positions"])
+    cfg = water_model_kwargs("cfg3arch", avg)
+    torch.manual_seed(0)
+    sd = FlashCartPotential(**cfg).state_dict()
+    g = synthetic.graph_from_structure(s, ei, sh, device="cpu", dtype=torch.float32)
+    for _ in range(warmup):
+        model_oracle.predict(sd, cfg, g)
+    n_done, t0 = 0, time.perf_counter()
+    while n_done < steps or (time.perf_counter() - t0) < min_seconds:
+        model_oracle.predict(sd, cfg, g)
+        n_done += 1
+    dt = time.perf_counter() - t0
+    n_atoms = len(s["positions"])
+    return {"value": n_atoms * n_done / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n_done} E+F+S steps of a {n_atoms}-atom water box ({ei.shape[1]} edges) with the config-3 "
+                      f"architecture, float32, oracle port (torch CPU) on {cores} threads; per-atom rate"}, dt / n_done
+
+
+# --------------------------------------------------------------------------------- arms
+
+
+def run_reference(args):
+    rank, world, _ = _dist_env()
+    if rank != 0:
+        return
+    base, ms = cpu_reference_sample(args.steps, args.warmup)
+    line = {
+        "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": base["sample"], "parallelism": "host cores"},
+        "impl": "reference", "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    import torch.distributed as dist
+
+    from flashcart_b200 import ops
+
+    rank, world, local = _dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    graph, avg = build_graph(seed=rank, device=dev)
+    n_atoms = graph["positions"].shape[0]
+    n_edges = graph["edge_index"].shape[1]
+    model = build_model(avg, dev)
+
+    def step(g):
+        return model.predict(g, compute_forces=True, compute_stress=True)
+
+    for _ in range(max(args.warmup, 0)):
+        step(graph)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    timer = ops.KernelTimer()
+    ops.set_kernel_timer(timer)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out = step(graph)
+    e1.record()
+    torch.cuda.synchronize()
+    ops.set_kernel_timer(None)
+    ms = e0.elapsed_time(e1) / args.steps
+    clock_info = clocks.stop()
+    ops.check_device_status(dev)
+    if world > 1:
+        dist.barrier()
+
+    # end to end: host graph in pinned memory -> device, predict, results -> pinned host
+    keys = ["positions", "cell", "atom_types", "edge_index", "shifts", "batch", "n_atoms", "pbc"]
+    host = {k: graph[k].cpu().pin_memory() for k in keys}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    out_host = {k: torch.empty(out[k].shape, dtype=out[k].dtype, pin_memory=True) for k in ("energy", "forces",
+                                                                                             "stress")}
+    d2h = sum(t.numel() * t.element_size() for t in out_host.values())
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(args.steps):
+        g = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+        o = step(g)
+        for k in out_host:
+            out_host[k].copy_(o[k], non_blocking=True)
+    a1.record()
+    torch.cuda.synchronize()
+    e2e_ms = a0.elapsed_time(a1) / args.steps
+
+    # roofline of the dominant kernel (largest total device time in the timed region)
+    durs = timer.durations_ms()
+    nbytes = timer.bytes_per_call()
+    top = max(durs, key=lambda k: sum(durs[k]))
+    avg_ms = sum(durs[top]) / len(durs[top])
+    bytes_per_launch = sum(nbytes[top]) / len(nbytes[top])
+    peak, peak_src = _peaks()
+    achieved = bytes_per_launch / (avg_ms * 1e-3) / 1e9
+    traffic = _profile_traffic(top)
+    share = sum(durs[top]) / (ms * args.steps)
+
+    t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max, e2e_max = float(t[0]), float(t[1])
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_base, _ = cpu_reference_sample(steps=1, warmup=1, min_seconds=10.0)
+    if rank == 0:
+        value = world * n_atoms / (ms_max * 1e-3)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "atoms": n_atoms, "edges": n_edges,
+                       "l2": "inputs larger than L2 (per-edge path weights of layer 2: "
+                             f"{n_edges * 23 * 128 * 4 / 1e9:.1f} GB)",
+                       "parallelism": f"one box per GPU x{world} (structure-sharded batched evaluation)"},
+            "roofline": {"bound": "hbm", "kernel": top, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": f"{peak_src} (hbm_gbs)",
+                         "bytes_per_launch": bytes_per_launch, "ms_per_launch": avg_ms,
+                         "share_of_step": share},
+            "cpu_baseline": cpu_base,
+            "e2e": {"value": world * n_atoms / (e2e_max * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": timer.launches,
+            "clocks": clock_info,
+            "kernels_ms_per_step": {k: sum(v) / args.steps for k, v in sorted(durs.items(),
+                                                                               key=lambda kv: -sum(kv[1]))},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,246 @@
+"""FlashCart potential and energy/force/stress prediction on the B200 operators.
+
+``FlashCartPotential`` has the reference's constructor, submodules, state_dict keys
+and ``to_model_config``/``from_config`` (reference ``model/flashcart.py:25-483``), so a
+reference checkpoint (``model.pt`` + ``model_config.yaml``) loads unchanged.
+``predict`` follows ``model/atomistic.py:75-340``: a symmetric virtual strain for the
+stress, forces and stress from one ``torch.autograd.grad`` call, Voigt order
+xx, yy, zz, yz, xz, xy and ``virials = -stress * volume``.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Mapping
+from typing import Any, Dict, List, Optional
+
+import torch
+import torch.nn as nn
+
+from flashcart_b200 import o3
+from flashcart_b200.nn.layers import (EnergyReadoutLayer, EquivariantGatedLayer, InteractionLayer, ProductLayer,
+                                      ScaleShiftEnergyLayer)
+from flashcart_b200.nn.radial import ChebyshevBasis, PolynomialCutoff
+
+MIN_EDGE_LENGTH = 1.0e-4
+
+
+def get_edge_vectors(positions, cell, shifts, edge_index, batch, use_shifts: bool = True):
+    """v_e = r_j - r_i + S_e . cell (row 0 receivers i, row 1 senders j; reference ``utils/geometry.py:25-53``)."""
+    idx_i, idx_j = edge_index[0], edge_index[1]
+    if not use_shifts:
+        return positions[idx_j] - positions[idx_i]
+    shift_vec = (shifts.to(cell.dtype).unsqueeze(-2) @ cell[batch[idx_i]]).squeeze(-2)
+    return positions[idx_j] - positions[idx_i] + shift_vec
+
+
+def to_voigt6(t: torch.Tensor) -> torch.Tensor:
+    """(..., 3, 3) -> (..., 6) in xx, yy, zz, yz, xz, xy with averaged off-diagonals."""
+    return torch.stack([t[..., 0, 0], t[..., 1, 1], t[..., 2, 2], (t[..., 1, 2] + t[..., 2, 1]) / 2,
+                        (t[..., 0, 2] + t[..., 2, 0]) / 2, (t[..., 0, 1] + t[..., 1, 0]) / 2], dim=-1)
+
+
+def _uses_shifts(pbc) -> bool:
+    if pbc is None:
+        return True
+    if torch.is_tensor(pbc):
+        return bool(torch.any(pbc).item())
+    if isinstance(pbc, bool):
+        return pbc
+    return any(bool(v) for v in pbc)
+
+
+class FlashCartPotential(nn.Module):
+    """Equivariant interatomic potential (reference ``model/flashcart.py:25-317``)."""
+
+    def __init__(self, elements: List[str], r_max: float, r_min: float = 0.0, n_hidden_feats: int = 32,
+                 l_max_hidden_feats: int = 1, l_max_edge_attrs: int = 3, n_radial: int = 8,
+                 n_interactions: int = 2, correlation: int = 3, path_reduced_product: bool = True,
+                 element_agnostic_interaction: bool = True, element_agnostic_product: bool = True,
+                 n_element_interaction_features: int = 16, nonlinearity: bool = False,
+                 gate_activation: str = "silu", gate_bias: bool = True, layer_norm: bool = False,
+                 hidden_radial: Optional[List[int]] = None, hidden_readout: Optional[List[int]] = None,
+                 radial_mapping: str = "affine", cutoff_poly_order: int = 6, avg_neighbors: Optional[float] = None,
+                 atomic_shifts: Optional[List[float]] = None, fit_atomic_shifts: bool = True,
+                 recompute_radial: bool = False, use_triton: bool = False):
+        super().__init__()
+        self.elements = list(elements)
+        self.r_min = r_min
+        self.r_max = float(r_max)
+        self.n_hidden_feats = n_hidden_feats
+        self.l_max_hidden_feats = l_max_hidden_feats
+        self.l_max_edge_attrs = l_max_edge_attrs
+        self.n_radial = n_radial
+        self.n_interactions = n_interactions
+        self.correlation = correlation
+        self.path_reduced_product = path_reduced_product
+        self.hidden_radial = [64, 64] if hidden_radial is None else list(hidden_radial)
+        self.hidden_readout = [64, 64] if hidden_readout is None else list(hidden_readout)
+        self.radial_mapping = radial_mapping
+        self.cutoff_poly_order = cutoff_poly_order
+        self.atomic_shifts = None if atomic_shifts is None else list(atomic_shifts)
+        self.fit_atomic_shifts = bool(fit_atomic_shifts)
+        self.avg_neighbors = 1.0 if avg_neighbors is None else float(avg_neighbors)
+        self.auto_avg_neighbors = avg_neighbors is None
+        self.nonlinearity = nonlinearity
+        self.gate_activation = gate_activation
+        self.gate_bias = gate_bias
+        self.layer_norm = layer_norm
+        self.element_agnostic_interaction = element_agnostic_interaction
+        self.element_agnostic_product = element_agnostic_product
+        self.n_element_interaction_features = n_element_interaction_features
+        self.recompute_radial = recompute_radial
+        self.use_triton = use_triton
+        self.node_dim = sum((2 * l + 1) * n_hidden_feats for l in range(l_max_hidden_feats + 1))
+
+        self.embedding = nn.Embedding(len(elements), n_hidden_feats)
+        self.radial_basis = ChebyshevBasis(n_radial, r_max=r_max, r_min=r_min, mapping=radial_mapping)
+        self.cutoff_fn = PolynomialCutoff(r_max, poly_order=cutoff_poly_order)
+        self.irreps = o3.Irreps(l_max_edge_attrs, use_triton=use_triton)
+        product_out = [l_max_hidden_feats if i < n_interactions - 1 else 0 for i in range(n_interactions)]
+        inter_in = [0 if i == 0 else l_max_hidden_feats for i in range(n_interactions)]
+        self.use_products = correlation > 1
+        inter_out = [l_max_edge_attrs] * n_interactions if self.use_products else product_out
+        self.interactions = nn.ModuleList([
+            InteractionLayer(in1_l_max=li, in2_l_max=l_max_edge_attrs, out_l_max=lo, in1_features=n_hidden_feats,
+                             out_features=n_hidden_feats, n_radial=n_radial, hidden_radial=self.hidden_radial,
+                             n_elements=None if element_agnostic_interaction else len(elements),
+                             element_features=n_element_interaction_features, avg_neighbors=self.avg_neighbors,
+                             use_sc=True, use_layer_norm=layer_norm, use_triton=use_triton,
+                             recompute_radial=recompute_radial)
+            for li, lo in zip(inter_in, inter_out)])
+        self.products = nn.ModuleList([
+            ProductLayer(in_l_max=l_max_edge_attrs, out_l_max=po, in_features=n_hidden_feats,
+                         n_elements=None if element_agnostic_product else len(elements), correlation=correlation,
+                         path_reduced=path_reduced_product, use_sc=True, use_layer_norm=layer_norm,
+                         use_triton=use_triton)
+            for po in product_out] if self.use_products else [])
+        if nonlinearity:
+            self.nonlinearities = nn.ModuleList([
+                EquivariantGatedLayer(l_max=lo, in_features=n_hidden_feats, hidden_features=n_hidden_feats,
+                                      gate_activation=gate_activation, gate_bias=gate_bias, use_triton=use_triton)
+                for lo in inter_out])
+        self.readout = EnergyReadoutLayer(n_hidden_feats, n_interactions, hidden_readout=self.hidden_readout)
+        self.scale_shift = ScaleShiftEnergyLayer(len(elements))
+
+    # ------------------------------------------------------------------ forward
+
+    def forward(self, graph: Dict[str, Any]) -> torch.Tensor:
+        """Site energies of a graph dict (reference ``model/flashcart.py:223-317``).
+
+        ``graph`` holds ``edge_index`` (2, E) with receivers in row 0 (ascending),
+        ``batch``, ``atom_types`` and either ``vectors`` or ``positions``/``cell``/
+        ``shifts`` (+ optional ``use_shifts``).
+        """
+        if not isinstance(graph, Mapping):
+            raise TypeError(f"{self.__class__.__name__}.forward expects a tensor dictionary. Use predict() for Data.")
+        edge_index = graph["edge_index"]
+        batch = graph["batch"]
+        atom_types = graph["atom_types"]
+        vectors = graph.get("vectors")
+        if vectors is None:
+            use_shifts = graph.get("use_shifts", True)
+            if not isinstance(use_shifts, bool):
+                use_shifts = _uses_shifts(use_shifts)
+            vectors = get_edge_vectors(graph["positions"], graph["cell"], graph["shifts"], edge_index, batch,
+                                       use_shifts=use_shifts)
+        distances = vectors.norm(dim=-1)
+        directions = vectors / distances.clamp_min(MIN_EDGE_LENGTH).unsqueeze(-1)
+        edge_attrs = self.irreps.forward_normalized(directions)
+        edge_feats = self.radial_basis(distances)
+        envelope = self.cutoff_fn(distances)
+        node_feats = self.embedding(atom_types)
+        outputs = []
+        for i, interaction in enumerate(self.interactions):
+            feats = interaction(node_feats, edge_attrs, edge_feats, edge_index, envelope,
+                                atom_types=atom_types if not self.element_agnostic_interaction else None)
+            if self.nonlinearity:
+                feats = self.nonlinearities[i](feats)
+            if self.use_products:
+                node_feats = self.products[i](feats, None if self.element_agnostic_product else atom_types)
+            else:
+                node_feats = feats
+            outputs.append(node_feats[:, :self.n_hidden_feats])
+        energies = self.readout(outputs)
+        return self.scale_shift(energies, atom_types)
+
+    # ------------------------------------------------------------------ predict
+
+    def predict(self, graph, compute_forces: bool = False, compute_stress: bool = False,
+                create_graph: bool = False) -> Dict[str, torch.Tensor]:
+        """Energies and requested derivatives (reference ``model/atomistic.py:75-340``).
+
+        Returns ``node_energies`` (N,), ``energy`` (G,), and when requested ``forces``
+        (N, 3) = -dE/dR, ``stress`` (G, 6) = (dE/dD)/det(cell) in Voigt order and
+        ``virials`` = -stress * volume, D being a symmetric virtual strain applied to
+        positions and cell.
+        """
+        g = dict(graph.to_dict() if hasattr(graph, "to_dict") else graph)
+        g["use_shifts"] = _uses_shifts(g.get("use_shifts", g.get("pbc")))
+        positions = g["positions"].detach()
+        cell = g["cell"].detach() if torch.is_tensor(g.get("cell")) else None
+        displacement = None
+        if compute_stress:
+            if cell is None:
+                raise ValueError("Cannot compute stress without cell information.")
+            displacement = torch.zeros_like(cell).requires_grad_(True)
+            sym = 0.5 * (displacement + displacement.transpose(-1, -2))
+            scaling = torch.eye(3, device=cell.device, dtype=cell.dtype).unsqueeze(0) + sym
+            positions = (positions.unsqueeze(-2) @ scaling[g["batch"]]).squeeze(-2)
+            cell = cell @ scaling
+        if compute_forces:
+            positions.requires_grad_(True)
+        g["positions"] = positions
+        g["cell"] = cell
+        node_energies = self(g)
+        n_graphs = int(g["n_atoms"].shape[0]) if "n_atoms" in g else int(g["batch"].max().item()) + 1
+        energy = torch.zeros(n_graphs, dtype=node_energies.dtype, device=node_energies.device)
+        energy = energy.index_add(0, g["batch"], node_energies)
+        out = {"node_energies": node_energies, "energy": energy}
+        inputs = ([positions] if compute_forces else []) + ([displacement] if compute_stress else [])
+        if inputs:
+            grads = torch.autograd.grad(energy.sum(), inputs, create_graph=create_graph)
+            k = 0
+            if compute_forces:
+                out["forces"] = -grads[0]
+                k = 1
+            if compute_stress:
+                volume = torch.det(cell)
+                stress = to_voigt6(grads[k] / volume.view(-1, 1, 1))
+                out["stress"] = stress
+                out["virials"] = -stress * volume.unsqueeze(-1)
+            if not create_graph:
+                out["node_energies"] = out["node_energies"].detach()
+                out["energy"] = out["energy"].detach()
+        return out
+
+    # ------------------------------------------------------------------ config
+
+    def to_model_config(self) -> Dict[str, Any]:
+        return {
+            "elements": list(self.elements), "r_max": self.r_max, "r_min": self.r_min,
+            "n_hidden_feats": self.n_hidden_feats, "l_max_hidden_feats": self.l_max_hidden_feats,
+            "l_max_edge_attrs": self.l_max_edge_attrs, "n_radial": self.n_radial,
+            "n_interactions": self.n_interactions, "correlation": self.correlation,
+            "path_reduced_product": self.path_reduced_product,
+            "element_agnostic_interaction": self.element_agnostic_interaction,
+            "element_agnostic_product": self.element_agnostic_product,
+            "n_element_interaction_features": self.n_element_interaction_features,
+            "nonlinearity": self.nonlinearity, "gate_activation": self.gate_activation,
+            "gate_bias": self.gate_bias, "layer_norm": self.layer_norm,
+            "hidden_radial": list(self.hidden_radial), "hidden_readout": list(self.hidden_readout),
+            "radial_mapping": self.radial_mapping, "cutoff_poly_order": self.cutoff_poly_order,
+            "atomic_shifts": self.atomic_shifts, "fit_atomic_shifts": self.fit_atomic_shifts,
+            "avg_neighbors": float(self.avg_neighbors), "use_triton": self.use_triton,
+        }
+
+    @classmethod
+    def from_config(cls, cfg: Dict[str, Any]) -> "FlashCartPotential":
+        defaults = dict(r_min=0.0, n_hidden_feats=32, l_max_hidden_feats=1, l_max_edge_attrs=3, n_radial=8,
+                        n_interactions=2, correlation=3, path_reduced_product=True,
+                        element_agnostic_interaction=True, element_agnostic_product=True,
+                        n_element_interaction_features=16, nonlinearity=False, gate_activation="silu",
+                        gate_bias=True, layer_norm=False, hidden_radial=[64, 64], hidden_readout=[64, 64],
+                        radial_mapping="affine", cutoff_poly_order=6, atomic_shifts=None, fit_atomic_shifts=True,
+                        avg_neighbors=None, use_triton=False, recompute_radial=False)
+        kw = {k: cfg.get(k, v) for k, v in defaults.items()}
+        return cls(elements=cfg["elements"], r_max=cfg["r_max"], **kw)

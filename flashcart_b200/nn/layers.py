@@ -1,0 +1,422 @@
+"""Layers of the FlashCart potential on the B200 operators.
+
+Same classes, constructor arguments, parameter/buffer names, persistence and
+parameter-creation order as the reference ``nn/layers.py`` (so reference
+checkpoints load unchanged and a seeded construction draws the same random
+weights); every equivariant operation (tensor products, linear maps) goes through
+:mod:`flashcart_b200.o3`, i.e. the sm_100a kernels. Plain dense layers (radial and
+readout MLPs, gates) stay ``torch.nn.functional.linear``.
+"""
+
+from typing import List, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from flashcart_b200 import o3
+
+
+class RescaledSiLULayer(nn.Module):
+    """scale * silu(x); default scale 1/sqrt(E[silu(z)^2]), z ~ N(0,1) (reference ``nn/layers.py:12-44``)."""
+
+    def __init__(self, scale: Optional[float] = None):
+        super().__init__()
+        self.register_buffer("scale", torch.tensor(1.6765324703310907 if scale is None else scale,
+                                                   dtype=torch.get_default_dtype()), persistent=False)
+
+    def forward(self, x):
+        return self.scale * F.silu(x)
+
+
+class RescaledSigmoidLayer(nn.Module):
+    """scale * sigmoid(x); default scale 1/sqrt(E[sigmoid(z)^2]) (reference ``nn/layers.py:47-79``)."""
+
+    def __init__(self, scale: Optional[float] = None):
+        super().__init__()
+        self.register_buffer("scale", torch.tensor(1.8462285453386054 if scale is None else scale,
+                                                   dtype=torch.get_default_dtype()), persistent=False)
+
+    def forward(self, x):
+        return self.scale * torch.sigmoid(x)
+
+
+class LinearLayer(nn.Module):
+    """y = x (scale W)^T + b with N(0,1) W and scale 1/sqrt(in) (reference ``nn/layers.py:82-140``)."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False,
+                 weight_scale: Optional[float] = None):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        s = float(in_features) ** -0.5 if weight_scale is None else float(weight_scale)
+        self.register_buffer("scale", torch.tensor(s, dtype=torch.get_default_dtype()), persistent=False)
+        self.weight = nn.Parameter(torch.randn(out_features, in_features))
+        if bias:
+            self.bias = nn.Parameter(torch.zeros(out_features))
+        else:
+            self.register_parameter("bias", None)
+
+    def forward(self, x):
+        return F.linear(x, self.weight * self.scale, self.bias)
+
+
+def _mlp(widths: List[int]) -> nn.Sequential:
+    layers = []
+    for a, b in zip(widths[:-1], widths[1:]):
+        layers.append(LinearLayer(a, b))
+        layers.append(RescaledSiLULayer())
+    return nn.Sequential(*layers[:-1])
+
+
+class RMSLayerNorm(nn.Module):
+    """Normalise Cartesian features by an invariant mean square (reference ``nn/layers.py:413-540``).
+
+    The invariant squared norm of every rank comes from a symmetric scalar tensor
+    product (shared unit weights), weighted 1/((2l+1)(l_max+1)) and averaged over
+    channels; per-rank gains (and an l=0 bias with centering) follow.
+    """
+
+    def __init__(self, l_max: int, n_features: int, eps: float = 1.0e-12, affine: bool = True,
+                 centering: bool = False, use_triton: bool = False):
+        super().__init__()
+        self.l_max = l_max
+        self.n_features = n_features
+        self.eps = eps
+        self.affine = affine
+        self.centering = centering
+        self.slices = o3.utils.get_irreps_slices(l_max, n_features)
+        self.shapes = o3.utils.get_irreps_shapes(l_max, n_features)
+        self.block_dims = [a * b for a, b in self.shapes]
+        self.dim = sum(self.block_dims)
+        self.tp = o3.TensorProduct(l_max, l_max, 0, n_features, n_features, use_triton=use_triton,
+                                   symmetric_product=True, shared_weights=True, reduce_paths=False)
+        _, n_paths = o3.utils.count_output_paths(l_max, l_max, 0, symmetric_product=True)
+        self.register_buffer("dummy_tp_weights", torch.ones(n_paths * n_features), persistent=False)
+        self.register_buffer("l_weights", torch.tensor([1.0 / ((2 * l + 1) * (l_max + 1)) for l in range(l_max + 1)],
+                                                       dtype=torch.float64), persistent=False)
+        if affine:
+            self.weights = nn.ParameterList([nn.Parameter(torch.ones(n_features)) for _ in range(l_max + 1)])
+            reps = torch.tensor([2 * l + 1 for l in range(l_max + 1)])
+            self.register_buffer("l_expand_index", torch.arange(l_max + 1).repeat_interleave(reps),
+                                 persistent=False)
+            if centering:
+                self.bias = nn.Parameter(torch.zeros(n_features))
+            else:
+                self.register_parameter("bias", None)
+        else:
+            self.weights = nn.ParameterList()
+            self.register_parameter("bias", None)
+
+    def forward(self, node_feats: torch.Tensor) -> torch.Tensor:
+        if node_feats.shape[-1] != self.dim:
+            raise RuntimeError(f"Incorrect last dimension for node_feats. Expected {self.dim}, "
+                               f"got {node_feats.shape[-1]}.")
+        n = node_feats.shape[0]
+        feats = node_feats
+        if self.centering:
+            l0 = node_feats[:, :self.n_features]
+            feats = torch.cat([l0 - l0.mean(dim=-1, keepdim=True), node_feats[:, self.n_features:]], dim=-1)
+        inv = self.tp(feats, feats, self.dummy_tp_weights.to(feats.dtype)).view(n, self.l_max + 1, self.n_features)
+        mean_sq = (inv * self.l_weights.to(inv.dtype).view(1, -1, 1)).sum(dim=1).mean(dim=-1, keepdim=True)
+        scaled = feats * torch.pow(mean_sq + self.eps, -0.5)
+        if not self.affine:
+            return scaled
+        gains = torch.stack(tuple(self.weights)).index_select(0, self.l_expand_index).view(1, -1)
+        out = scaled * gains
+        if self.bias is not None:
+            out = torch.cat([out[:, :self.n_features] + self.bias, out[:, self.n_features:]], dim=-1)
+        return out
+
+
+class InteractionLayer(nn.Module):
+    """Tensor-product convolution with radial-MLP path weights (reference ``nn/layers.py:184-410``).
+
+    node feats -> linear_first -> conv TP with edge attributes, weights =
+    radial_mlp(basis * envelope) -> / sqrt(avg_neighbors) -> linear_second
+    (+ skip projection) (-> RMS layer norm).
+    """
+
+    def __init__(self, in1_l_max: int, in2_l_max: int, out_l_max: int, in1_features: int, out_features: int,
+                 n_radial: int, hidden_radial: Optional[List[int]] = None, n_elements: Optional[int] = None,
+                 element_features: Optional[int] = None, avg_neighbors: float = 1.0, use_sc: bool = False,
+                 use_layer_norm: bool = False, use_triton: bool = False, recompute_radial: bool = False):
+        super().__init__()
+        self.in1_l_max, self.in2_l_max, self.out_l_max = in1_l_max, in2_l_max, out_l_max
+        self.in1_features, self.out_features = in1_features, out_features
+        self.n_radial = n_radial
+        self.hidden_radial = [64, 64] if hidden_radial is None else list(hidden_radial)
+        self.use_sc = use_sc
+        self.use_layer_norm = use_layer_norm
+        self.recompute_radial = recompute_radial
+        if avg_neighbors <= 0.0:
+            raise ValueError(f"avg_neighbors must be positive. Provided: {avg_neighbors}.")
+        self.register_buffer("sqrt_avg_neighbors",
+                             torch.tensor(float(avg_neighbors) ** 0.5, dtype=torch.get_default_dtype()))
+        self.out_dim = sum((2 * l + 1) * out_features for l in range(out_l_max + 1))
+        out_paths, n_total_paths = o3.utils.count_output_paths(in1_l_max, in2_l_max, out_l_max)
+        if n_elements is not None and element_features is None:
+            raise ValueError("element_features must be provided when n_elements is set.")
+        self.element_features = element_features
+        radial_in = n_radial + 2 * element_features if n_elements is not None else n_radial
+        self.radial_mlp = _mlp([radial_in] + self.hidden_radial + [n_total_paths * in1_features])
+        self.tp = o3.TensorProduct(in1_l_max, in2_l_max, out_l_max, in1_features, 1, use_triton=use_triton,
+                                   reduce_paths=False)
+        self.linear_first = o3.LinearLayer(in1_l_max, in1_l_max, in1_features, in1_features, use_triton=use_triton)
+        self.linear_second = o3.LinearLayer(out_l_max, out_l_max, in1_features, out_features, in_paths=out_paths,
+                                            use_triton=use_triton)
+        if use_sc:
+            self.skip_projection = (LinearLayer(in1_features, out_features) if in1_l_max == 0 else
+                                    o3.LinearLayer(in1_l_max, out_l_max, in1_features, out_features,
+                                                   use_triton=use_triton))
+        else:
+            self.skip_projection = None
+        self.layer_norm = (RMSLayerNorm(out_l_max, out_features, eps=1.0e-6, use_triton=use_triton)
+                           if use_layer_norm else None)
+        if n_elements is not None:
+            self.emb_i = nn.Embedding(n_elements, element_features)
+            self.emb_j = nn.Embedding(n_elements, element_features)
+            nn.init.uniform_(self.emb_i.weight, a=-0.001, b=0.001)
+            nn.init.uniform_(self.emb_j.weight, a=-0.001, b=0.001)
+        else:
+            self.emb_i = None
+            self.emb_j = None
+
+    def forward(self, node_feats, edge_attrs, edge_feats, edge_index, envelope, atom_types=None, out_nodes=None):
+        idx_i, idx_j = edge_index[0], edge_index[1]
+        residual = node_feats if out_nodes is None else node_feats[:out_nodes]
+        if self.emb_i is not None:
+            if atom_types is None:
+                raise ValueError(f"atom_types required when n_elements is set. Provided: {atom_types}.")
+            mlp_in = torch.cat([edge_feats, self.emb_i(atom_types)[idx_i], self.emb_j(atom_types)[idx_j]], dim=-1)
+            mlp_in = mlp_in * envelope.unsqueeze(-1)
+        else:
+            mlp_in = edge_feats * envelope.unsqueeze(-1)
+        node_feats = self.linear_first(node_feats)
+        weights = self.radial_mlp(mlp_in)
+        aggregated = self.tp(node_feats, edge_attrs, weights, idx_i, idx_j)
+        if out_nodes is not None:
+            aggregated = aggregated[:out_nodes]
+        aggregated = aggregated / self.sqrt_avg_neighbors
+        out = self.linear_second(aggregated)
+        if self.skip_projection is not None:
+            skip = self.skip_projection(residual)
+            if self.in1_l_max == 0:
+                out = torch.cat([out[:, :self.out_features] + skip, out[:, self.out_features:]], dim=-1)
+            else:
+                out = out + skip
+        if self.layer_norm is not None:
+            out = self.layer_norm(out)
+        return out
+
+    def set_avg_neighbors(self, avg_neighbors: float) -> None:
+        if avg_neighbors <= 0.0:
+            raise ValueError(f"avg_neighbors must be positive. Provided: {avg_neighbors}.")
+        self.sqrt_avg_neighbors.fill_(float(avg_neighbors) ** 0.5)
+
+
+class EquivariantGatedLayer(nn.Module):
+    """Gated residual update, identity at initialisation (reference ``nn/layers.py:543-648``)."""
+
+    def __init__(self, l_max: int, in_features: int, hidden_features: Optional[int] = None,
+                 gate_activation: str = "silu", gate_bias: bool = True, use_triton: bool = False):
+        super().__init__()
+        if gate_activation not in ("silu", "sigmoid"):
+            raise ValueError(f"gate_activation must be 'silu' or 'sigmoid'. Provided: {gate_activation!r}.")
+        self.l_max = l_max
+        self.in_features = in_features
+        self.gate_activation_name = gate_activation
+        self.gate_bias = gate_bias
+        self.hidden_features = in_features if hidden_features is None else hidden_features
+        if self.hidden_features <= 0:
+            raise ValueError(f"hidden_features must be positive. Provided: {self.hidden_features}.")
+        self.in_dim = sum((2 * l + 1) * in_features for l in range(l_max + 1))
+        self.hidden_dim = sum((2 * l + 1) * self.hidden_features for l in range(l_max + 1))
+        self.hidden_slices = o3.utils.get_irreps_slices(l_max, self.hidden_features)
+        self.value_linear = o3.LinearLayer(l_max, l_max, in_features, self.hidden_features, use_triton=use_triton)
+        self.gate_linear = LinearLayer(in_features, (l_max + 1) * self.hidden_features, bias=gate_bias)
+        self.gate_activation = RescaledSiLULayer() if gate_activation == "silu" else RescaledSigmoidLayer()
+        self.output_linear = o3.LinearLayer(l_max, l_max, self.hidden_features, in_features, use_triton=use_triton)
+        for w in self.output_linear.weight:
+            nn.init.zeros_(w)
+
+    def forward(self, node_feats):
+        if node_feats.shape[-1] != self.in_dim:
+            raise RuntimeError(f"Incorrect last dimension for node_feats. Expected {self.in_dim}, "
+                               f"got {node_feats.shape[-1]}.")
+        n = node_feats.shape[0]
+        values = self.value_linear(node_feats)
+        gates = self.gate_activation(self.gate_linear(node_feats[:, :self.in_features]))
+        gates = gates.view(n, self.l_max + 1, self.hidden_features)
+        parts = []
+        for l, (a, b) in enumerate(self.hidden_slices):
+            parts.append((values[:, a:b].view(n, 2 * l + 1, self.hidden_features) * gates[:, l].unsqueeze(1))
+                         .flatten(1))
+        return node_feats + self.output_linear(torch.cat(parts, dim=-1))
+
+
+class IrrepsSelector(nn.Module):
+    """Keep the leading rank blocks up to out_l_max (reference ``nn/layers.py:651-698``)."""
+
+    def __init__(self, in_l_max: int, out_l_max: int, in_features: int, in_paths: Optional[List[int]] = None):
+        super().__init__()
+        if out_l_max > in_l_max:
+            raise ValueError("out_l_max must be less than or equal to in_l_max. "
+                             f"Provided: out_l_max={out_l_max}, in_l_max={in_l_max}.")
+        in_paths = [1] * (in_l_max + 1) if in_paths is None else list(in_paths)
+        self.stop = o3.utils.get_irreps_slices(in_l_max, in_features, in_paths)[out_l_max][1]
+        self.in_dim = sum((2 * l + 1) * in_features * in_paths[l] for l in range(in_l_max + 1))
+
+    def forward(self, x):
+        if x.shape[-1] != self.in_dim:
+            raise RuntimeError(f"Incorrect last dimension for x. Expected {self.in_dim}, got {x.shape[-1]}.")
+        return x[:, :self.stop]
+
+
+class ProductPathWeights(nn.Module):
+    """Per-path multiplicative weights 1 + delta (reference ``nn/layers.py:701-765``)."""
+
+    def __init__(self, n_weights: int, n_elements: Optional[int] = None, learnable: bool = False):
+        super().__init__()
+        if n_elements is not None and not learnable:
+            raise ValueError("Element-dependent path weights must be learnable. "
+                             "Provided: learnable=False with n_elements set.")
+        self.learnable = learnable
+        self.element_dependent = False
+        if not learnable:
+            self.register_buffer("delta", torch.zeros(n_weights), persistent=False)
+        elif n_elements is None:
+            self.delta = nn.Parameter(torch.zeros(n_weights))
+        else:
+            self.element_dependent = True
+            self.delta = nn.Embedding(n_elements, n_weights)
+            nn.init.zeros_(self.delta.weight)
+
+    def forward(self, atom_types=None):
+        if self.element_dependent:
+            if atom_types is None:
+                raise ValueError("atom_types required when n_elements is set.")
+            return 1.0 + self.delta(atom_types)
+        return 1.0 + self.delta
+
+
+class ProductLayer(nn.Module):
+    """Repeated node-local products up to the correlation order (reference ``nn/layers.py:768-1018``)."""
+
+    def __init__(self, in_l_max: int, out_l_max: int, in_features: int, n_elements: Optional[int] = None,
+                 correlation: int = 2, path_reduced: bool = False, use_sc: bool = False,
+                 use_layer_norm: bool = False, use_triton: bool = False):
+        super().__init__()
+        if correlation < 2:
+            raise ValueError("ProductLayer requires correlation >= 2. "
+                             "Use FlashCartPotential(correlation=1) for an interaction-only model.")
+        self.in_l_max, self.out_l_max, self.in_features = in_l_max, out_l_max, in_features
+        self.correlation = correlation
+        self.path_reduced = path_reduced
+        self.learnable_path_weights = path_reduced or n_elements is not None
+        self.use_sc = use_sc
+        self.use_layer_norm = use_layer_norm
+        self.in_dim = sum((2 * l + 1) * in_features for l in range(in_l_max + 1))
+        self.out_dim = sum((2 * l + 1) * in_features for l in range(out_l_max + 1))
+        self.skip_projection = (o3.LinearLayer(in_l_max, out_l_max, in_features, in_features, use_triton=use_triton)
+                                if use_sc else None)
+        self.layer_norm = (RMSLayerNorm(out_l_max, in_features, eps=1.0e-6, use_triton=use_triton)
+                           if use_layer_norm else None)
+        if path_reduced:
+            self.final_linear = o3.LinearLayer(out_l_max, out_l_max, in_features, in_features, use_triton=use_triton)
+        self.tensor_products = nn.ModuleList()
+        self.path_weights = nn.ModuleList()
+        self.irreps_selectors = nn.ModuleList()
+        self.product_linears = nn.ModuleList()
+        self.path_norm_names: List[Optional[str]] = []
+        for step in range(correlation):
+            step_out = out_l_max if step == correlation - 1 else in_l_max
+            in2_l_max, in2_features = (0, 1) if step == 0 else (in_l_max, in_features)
+            out_paths, n_total = o3.utils.count_output_paths(in_l_max, in2_l_max, step_out, symmetric_product=False)
+            self.path_weights.append(ProductPathWeights(n_total * in_features, n_elements=n_elements,
+                                                        learnable=self.learnable_path_weights))
+            if path_reduced:
+                norm = torch.cat([torch.full(((2 * l + 1) * in_features,), out_paths[l] ** -0.5)
+                                  for l in range(step_out + 1)])
+                if torch.all(norm == 1.0):
+                    self.path_norm_names.append(None)
+                else:
+                    name = f"path_norm_{step}"
+                    self.register_buffer(name, norm)
+                    self.path_norm_names.append(name)
+            else:
+                self.product_linears.append(o3.LinearLayer(step_out, step_out if step < correlation - 1 else out_l_max,
+                                                           in_features, in_features, in_paths=out_paths,
+                                                           use_triton=use_triton))
+            self.irreps_selectors.append(nn.Identity() if step_out == out_l_max else
+                                         IrrepsSelector(step_out, out_l_max, in_features))
+            if step > 0:
+                self.tensor_products.append(o3.TensorProduct(in_l_max, in2_l_max, step_out, in_features, in2_features,
+                                                             use_triton=use_triton, reduce_paths=path_reduced,
+                                                             symmetric_product=False,
+                                                             shared_weights=n_elements is None))
+        if self.learnable_path_weights:
+            self.register_buffer("step0_weight_index", torch.cat(
+                [torch.arange(l * in_features, (l + 1) * in_features).repeat(2 * l + 1) for l in range(in_l_max + 1)]),
+                persistent=False)
+        else:
+            self.step0_weight_index = None
+
+    def forward(self, node_feats, atom_types=None):
+        out = node_feats.new_zeros(node_feats.shape[0], self.out_dim)
+        prod = node_feats
+        for step in range(self.correlation):
+            if step == 0:
+                if self.step0_weight_index is not None:
+                    w = self.path_weights[0](atom_types)
+                    prod = node_feats * w[..., self.step0_weight_index]
+                else:
+                    prod = node_feats
+            else:
+                w = self.path_weights[step](atom_types).to(node_feats.dtype)
+                prod = self.tensor_products[step - 1](prod, node_feats, w)
+            if self.path_reduced:
+                name = self.path_norm_names[step]
+                if name is not None:
+                    prod = prod * getattr(self, name)
+            else:
+                prod = self.product_linears[step](prod)
+            out = out + self.irreps_selectors[step](prod)
+        if self.path_reduced:
+            out = self.final_linear(out)
+        if self.skip_projection is not None:
+            out = out + self.skip_projection(node_feats)
+        if self.layer_norm is not None:
+            out = self.layer_norm(out)
+        return out
+
+
+class EnergyReadoutLayer(nn.Module):
+    """MLP on the scalar channels of every layer (reference ``nn/layers.py:1021-1077``)."""
+
+    def __init__(self, in_features: int, n_layers: int, hidden_readout: Optional[List[int]] = None):
+        super().__init__()
+        self.in_features = in_features
+        self.n_layers = n_layers
+        self.hidden_readout = [64, 64] if hidden_readout is None else list(hidden_readout)
+        self.readout_mlp = _mlp([in_features * n_layers] + self.hidden_readout + [1])
+
+    def forward(self, node_feats: List[torch.Tensor]) -> torch.Tensor:
+        scalars = torch.cat([nf[:, :self.in_features] for nf in node_feats], dim=1)
+        if scalars.shape[-1] != self.in_features * self.n_layers:
+            raise RuntimeError(f"Incorrect last dimension for scalars. Expected: {self.in_features * self.n_layers}. "
+                               f"Provided: {scalars.shape[-1]}.")
+        return self.readout_mlp(scalars).squeeze(-1)
+
+
+class ScaleShiftEnergyLayer(nn.Module):
+    """Per-element energy scale; shifts stored for calculators (reference ``nn/layers.py:1080-1138``)."""
+
+    def __init__(self, n_elements: int):
+        super().__init__()
+        self.n_elements = n_elements
+        self.register_buffer("shifts", torch.zeros(n_elements))
+        self.register_buffer("scales", torch.ones(n_elements))
+
+    def forward(self, node_output, atom_types):
+        return self.scales[atom_types] * node_output

@@ -23,7 +23,7 @@ from torch import Tensor
 
 from flashcart_b200 import _native as N
 
-__all__ = ["check_device_status", "status_word"]
+__all__ = ["check_device_status", "status_word", "KernelTimer", "set_kernel_timer"]
 
 _DEBUG_CHECK = os.environ.get("FLASHCART_B200_CHECK", "0") not in ("", "0", "false", "False")
 
@@ -96,6 +96,65 @@ def _after(lib, rc: int, what: str, device: torch.device) -> None:
         check_device_status(device)
 
 
+class KernelTimer:
+    """Optional instrumentation: CUDA events around every C-ABI call on its stream.
+
+    ``records`` collects (name, start_event, end_event); ``launches`` counts the
+    kernels of this library enqueued while the timer is installed. Nothing is
+    skipped or reordered; the events only bracket the calls.
+    """
+
+    def __init__(self):
+        self.records = []
+        self.launches = 0
+
+    def durations_ms(self) -> Dict[str, List[float]]:
+        out: Dict[str, List[float]] = {}
+        for name, a, b, _ in self.records:
+            out.setdefault(name, []).append(a.elapsed_time(b))
+        return out
+
+    def bytes_per_call(self) -> Dict[str, List[int]]:
+        """Algorithmic bytes of each call: every tensor it reads or writes, counted once."""
+        out: Dict[str, List[int]] = {}
+        for name, _, _, nb in self.records:
+            out.setdefault(name, []).append(nb)
+        return out
+
+
+_TIMER: Optional[KernelTimer] = None
+
+
+def set_kernel_timer(timer: Optional[KernelTimer]) -> None:
+    global _TIMER
+    _TIMER = timer
+
+
+class _timed:
+    def __init__(self, name: str, kernels: int, nbytes: int = 0):
+        self.name, self.kernels, self.nbytes = name, kernels, nbytes
+
+    def __enter__(self):
+        t = _TIMER
+        if t is not None:
+            t.launches += self.kernels
+            self.a = torch.cuda.Event(enable_timing=True)
+            self.a.record()
+        return self
+
+    def __exit__(self, *exc):
+        t = _TIMER
+        if t is not None and exc[0] is None:
+            b = torch.cuda.Event(enable_timing=True)
+            b.record()
+            t.records.append((self.name, self.a, b, self.nbytes))
+        return False
+
+
+def _nbytes(*ts: Optional[Tensor]) -> int:
+    return sum(t.numel() * t.element_size() for t in ts if t is not None)
+
+
 def _idx(t: Optional[Tensor]) -> Optional[Tensor]:
     if t is None:
         return None
@@ -139,6 +198,8 @@ def _tp_desc(in1_l_max, in2_l_max, out_l_max, in1_features, in2_features, symmet
 
 def _rowptr(lib, idx_i: Tensor, n_nodes: int, device, stream, status) -> Tensor:
     rowptr = torch.empty(n_nodes + 1, dtype=torch.int64, device=device)
+    if _TIMER is not None:
+        _TIMER.launches += 1
     rc = lib.fc_build_rowptr(_p(idx_i), idx_i.numel(), n_nodes, ctypes.c_void_p(rowptr.data_ptr()), status, stream)
     N.check(lib, rc, "fc_build_rowptr")
     return rowptr
@@ -169,14 +230,17 @@ def tp_fwd(in1: Tensor, in2: Tensor, weights: Tensor, idx_i: Optional[Tensor], i
     if _conv(idx_i, idx_j):
         idx_i, idx_j = _idx(idx_i), _idx(idx_j)
         rowptr = _rowptr(lib, idx_i, n_out, dev, stream, status)
-        rc = lib.fc_tp_fwd(ctypes.byref(desc), _p(in1), _p(in2), _p(weights), ctypes.c_void_p(rowptr.data_ptr()),
-                           _p(idx_j), n_out, n_out, _p(out), status, stream)
+        nb = _nbytes(in1, in2, weights, out, idx_j, rowptr)
+        with _timed(f"tp_fwd_conv_{in1_l_max}{in2_l_max}{out_l_max}", 1, nb):
+            rc = lib.fc_tp_fwd(ctypes.byref(desc), _p(in1), _p(in2), _p(weights),
+                               ctypes.c_void_p(rowptr.data_ptr()), _p(idx_j), n_out, n_out, _p(out), status, stream)
     else:
         if in1.shape[0] != in2.shape[0]:
             raise ValueError("idx_i and idx_j must be provided when in1 and in2 have different batch sizes. "
                              f"Got in1_batch={in1.shape[0]}, in2_batch={in2.shape[0]}.")
-        rc = lib.fc_tp_fwd(ctypes.byref(desc), _p(in1), _p(in2), _p(weights), None, None, n_out, n_out, _p(out),
-                           status, stream)
+        with _timed(f"tp_fwd_dense_{in1_l_max}{in2_l_max}{out_l_max}", 1, _nbytes(in1, in2, weights, out)):
+            rc = lib.fc_tp_fwd(ctypes.byref(desc), _p(in1), _p(in2), _p(weights), None, None, n_out, n_out,
+                               _p(out), status, stream)
     _after(lib, rc, "fc_tp_fwd", dev)
     return out
 
@@ -215,13 +279,17 @@ def tp_bwd(grad_out: Tensor, in1: Tensor, in2: Tensor, weights: Tensor, idx_i: O
         idx_i, idx_j = _idx(idx_i), _idx(idx_j)
         n_out = in1.shape[0]
         rowptr = _rowptr(lib, idx_i, n_out, dev, stream, status)
-        rc = lib.fc_tp_bwd(ctypes.byref(desc), _p(grad_out), _p(in1), _p(in2), _p(weights),
-                           ctypes.c_void_p(rowptr.data_ptr()), _p(idx_j), n_out, n_out, in2.shape[0],
-                           _p(g1), _p(g2), _p(gw), status, stream)
+        nb = _nbytes(grad_out, in1, in2, weights, g1, g2, gw, idx_j, rowptr)
+        with _timed(f"tp_bwd_conv_{in1_l_max}{in2_l_max}{out_l_max}", 1, nb):
+            rc = lib.fc_tp_bwd(ctypes.byref(desc), _p(grad_out), _p(in1), _p(in2), _p(weights),
+                               ctypes.c_void_p(rowptr.data_ptr()), _p(idx_j), n_out, n_out, in2.shape[0],
+                               _p(g1), _p(g2), _p(gw), status, stream)
     else:
         n = in1.shape[0]
-        rc = lib.fc_tp_bwd(ctypes.byref(desc), _p(grad_out), _p(in1), _p(in2), _p(weights), None, None, n, n, n,
-                           _p(g1), _p(g2), _p(gw), status, stream)
+        with _timed(f"tp_bwd_dense_{in1_l_max}{in2_l_max}{out_l_max}", 1,
+                    _nbytes(grad_out, in1, in2, weights, g1, g2, gw)):
+            rc = lib.fc_tp_bwd(ctypes.byref(desc), _p(grad_out), _p(in1), _p(in2), _p(weights), None, None, n, n,
+                               n, _p(g1), _p(g2), _p(gw), status, stream)
     _after(lib, rc, "fc_tp_bwd", dev)
     return g1, g2, gw
 
@@ -350,6 +418,8 @@ def irreps_fwd(x: Tensor, l_max: int) -> Tensor:
     lib = N.lib()
     x = x.contiguous()
     out = x.new_empty((x.shape[0], (l_max + 1) ** 2))
+    if _TIMER is not None:
+        _TIMER.launches += 1
     rc = lib.fc_irreps_fwd(_p(x), x.shape[0], int(l_max), _code(x.dtype), _p(out), _stream(x.device))
     _after(lib, rc, "fc_irreps_fwd", x.device)
     return out
@@ -366,6 +436,8 @@ def irreps_bwd(grad_output: Tensor, x: Tensor, l_max: int) -> Tensor:
     lib = N.lib()
     g, x = grad_output.contiguous(), x.contiguous()
     gx = torch.empty_like(x)
+    if _TIMER is not None:
+        _TIMER.launches += 1
     rc = lib.fc_irreps_bwd(_p(g), _p(x), x.shape[0], int(l_max), _code(x.dtype), _p(gx), _stream(x.device))
     _after(lib, rc, "fc_irreps_bwd", x.device)
     return gx
@@ -467,7 +539,9 @@ def _linear_fwd_impl(x: Tensor, weights: Sequence[Tensor], out_dim: int, lists, 
     sc = scale.to(device=x.device, dtype=x.dtype).contiguous()
     out = x.new_empty((x.shape[0], int(out_dim)))
     d = _linear_desc(x, out_dim, lists[0], lists[1], lists[3], lists[4], lists[5], precision)
-    rc = lib.fc_linear_fwd(ctypes.byref(d), _p(x), _ptr_array(ws), _p(sc), x.shape[0], _p(out), _stream(x.device))
+    with _timed("linear_fwd", n_active, _nbytes(x, out, *ws)):
+        rc = lib.fc_linear_fwd(ctypes.byref(d), _p(x), _ptr_array(ws), _p(sc), x.shape[0], _p(out),
+                               _stream(x.device))
     _after(lib, rc, "fc_linear_fwd", x.device)
     return out
 
@@ -486,8 +560,9 @@ def _linear_bwd_impl(grad_out: Tensor, x: Tensor, weights: Sequence[Tensor], nee
             gx.zero_()
         return gx, gws
     d = _linear_desc(x, g.shape[1], lists[0], lists[1], lists[3], lists[4], lists[5], precision)
-    rc = lib.fc_linear_bwd(ctypes.byref(d), _p(g), _p(x), _ptr_array(ws), _p(sc), x.shape[0],
-                           _p(gx) if need_x else None, _ptr_array(gws) if need_w else None, _stream(x.device))
+    with _timed("linear_bwd", n_active * (int(need_x) + int(need_w)), _nbytes(g, x, gx, *ws, *gws)):
+        rc = lib.fc_linear_bwd(ctypes.byref(d), _p(g), _p(x), _ptr_array(ws), _p(sc), x.shape[0],
+                               _p(gx) if need_x else None, _ptr_array(gws) if need_w else None, _stream(x.device))
     _after(lib, rc, "fc_linear_bwd", x.device)
     return gx, gws
 

@@ -200,6 +200,25 @@ def enumerate_paths(in1_l_max: int, in2_l_max: int, out_l_max: int, symmetric: b
     return out
 
 
+@lru_cache(maxsize=None)
+def path_coefficients(l1: int, l2: int, lo: int) -> torch.Tensor:
+    """Dense float64 K[k, a, b] of one path on stored components, evaluated once by
+    running ``contract_path`` (full Cartesian tensors, explicit detracer) on every pair of
+    stored basis vectors; the product is then sum_ab K[k,a,b] S1_a S2_b."""
+    n1, n2 = 2 * l1 + 1, 2 * l2 + 1
+    e1 = torch.eye(n1, dtype=torch.float64)
+    e2 = torch.eye(n2, dtype=torch.float64)
+    s1 = e1[:, None, :].expand(n1, n2, n1).reshape(-1, n1)
+    s2 = e2[None, :, :].expand(n1, n2, n2).reshape(-1, n2)
+    y = contract_path(s1, s2, l1, l2, lo)  # (n1*n2, 2lo+1)
+    return y.reshape(n1, n2, 2 * lo + 1).permute(2, 0, 1).contiguous()
+
+
+def _apply_path(K: torch.Tensor, a: torch.Tensor, b: torch.Tensor, n: int, F: int) -> torch.Tensor:
+    """y[n, k, f] = sum_ij K[k, i, j] a[n, i, f] b[n, j, f]."""
+    return torch.einsum("kab,naf,nbf->nkf", K.to(a.dtype), a.expand(n, K.shape[1], F), b.expand(n, K.shape[2], F))
+
+
 def _rank_block(x: torch.Tensor, l: int, features: int) -> torch.Tensor:
     start = l * l * features
     return x[:, start: start + (2 * l + 1) * features].reshape(x.shape[0], 2 * l + 1, features)
@@ -229,9 +248,7 @@ def tensor_product(in1, in2, weights, idx_i, idx_j, in1_l_max, in2_l_max, out_l_
         else:
             a = _rank_block(in1, l1, in1_features)
             b = _rank_block(in2, l2, in2_features)
-        a = a.expand(n, 2 * l1 + 1, F).permute(0, 2, 1)
-        b = b.expand(n, 2 * l2 + 1, F).permute(0, 2, 1)
-        y = contract_path(a, b, l1, l2, lo).permute(0, 2, 1)  # (n, 2lo+1, F)
+        y = _apply_path(path_coefficients(l1, l2, lo), a, b, n, F)
         w = weights[p * F:(p + 1) * F] if shared_weights else weights[:, p * F:(p + 1) * F].unsqueeze(1)
         per_l[lo].append(y * w)
     blocks = []
@@ -277,8 +294,11 @@ def irreps(x: torch.Tensor, l_max: int) -> torch.Tensor:
 
 def linear(x: torch.Tensor, weights: Sequence[torch.Tensor], in_l_max: int, out_l_max: int, in_features: int,
            out_features: int, in_paths: Optional[Sequence[int]] = None,
-           weight_scale: Optional[float] = None) -> torch.Tensor:
-    """Per-rank channel mixing (reference ``o3/_linear.py:64-110``); missing ranks are zero."""
+           weight_scale: Optional[float] = None, scales: Optional[Sequence[float]] = None) -> torch.Tensor:
+    """Per-rank channel mixing (reference ``o3/_linear.py:64-110``); missing ranks are zero.
+
+    ``scales`` (one per shared rank) overrides the default 1/sqrt(in_features * paths_l).
+    """
     in_paths = [1] * (in_l_max + 1) if in_paths is None else list(in_paths)
     common = min(in_l_max, out_l_max)
     n = x.shape[0]
@@ -289,7 +309,10 @@ def linear(x: torch.Tensor, weights: Sequence[torch.Tensor], in_l_max: int, out_
         blk = x[:, off: off + (2 * l + 1) * width].reshape(n, 2 * l + 1, width)
         off += (2 * l + 1) * width
         if l <= common:
-            scale = weight_scale if weight_scale is not None else (in_features * in_paths[l]) ** -0.5
+            if scales is not None:
+                scale = scales[l]
+            else:
+                scale = weight_scale if weight_scale is not None else (in_features * in_paths[l]) ** -0.5
             outs.append((blk @ (weights[l] * scale).T).reshape(n, -1))
     for l in range(common + 1, out_l_max + 1):
         outs.append(x.new_zeros(n, (2 * l + 1) * out_features))

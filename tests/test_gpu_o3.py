@@ -82,7 +82,12 @@ def test_gpu_linear_matches_reference_golden(golden, cuda_device):
         meta = [int(v) for v in golden[k + "/meta"]]
         li, lo, fi, fo, has_ws = meta[:5]
         paths = meta[5:]
-        lin = o3.LinearLayer(li, lo, fi, fo, in_paths=paths, weight_scale=1.0 if has_ws == 1 else None)
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(torch.float64)  # scales computed in float64, as in the reference's fp64 tests
+        try:
+            lin = o3.LinearLayer(li, lo, fi, fo, in_paths=paths, weight_scale=1.0 if has_ws == 1 else None)
+        finally:
+            torch.set_default_dtype(prev)
         lin = lin.to(cuda_device, torch.float64)
         common = min(li, lo)
         ws = [golden[f"{k}/w{l}"].to(cuda_device) for l in range(common + 1)]
