@@ -23,6 +23,7 @@ FC_ERR_LAUNCH = -3
 FC_ERR_CAPACITY = -4
 FC_DEV_BAD_INDEX = 1
 FC_DEV_UNSORTED = 2
+FC_DEV_TIMEOUT = 4
 FC_F32 = 0
 FC_F64 = 1
 FC_PREC_IEEE = 0
@@ -91,9 +92,9 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_irreps_dbwd.restype = ctypes.c_int
     lib.fc_irreps_dbwd.argtypes = [_P, _P, _P, _I64, _I32, _I32, _P, _P, _P]
     lib.fc_linear_fwd.restype = ctypes.c_int
-    lib.fc_linear_fwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _I64, _P, _P]
+    lib.fc_linear_fwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _I64, _P, _P, _P]
     lib.fc_linear_bwd.restype = ctypes.c_int
-    lib.fc_linear_bwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P]
+    lib.fc_linear_bwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P, _P]
     return lib
 
 

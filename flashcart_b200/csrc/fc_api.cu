@@ -145,6 +145,17 @@ static int check_linear(const fc_linear_desc* d) {
   return FC_OK;
 }
 
+template <typename T>
+static int gemm_dispatch(const LinGemmArgs<T>& a, int precision, int* status, cudaStream_t s);
+template <>
+int gemm_dispatch<double>(const LinGemmArgs<double>& a, int, int*, cudaStream_t s) {
+  return lin_gemm<double>(a, s);
+}
+template <>
+int gemm_dispatch<float>(const LinGemmArgs<float>& a, int precision, int* status, cudaStream_t s) {
+  return lin_gemm_tc(a, precision != FC_PREC_TF32, status, s);
+}
+
 // zero columns [from, width) of every row
 template <typename T>
 static int zero_tail(T* p, int64_t rows, int64_t width, int64_t from, cudaStream_t s) {
@@ -162,7 +173,7 @@ static int zero_tail(T* p, int64_t rows, int64_t width, int64_t from, cudaStream
 
 template <typename T>
 static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* weights, const T* scale, int64_t n,
-                        T* out, cudaStream_t s) {
+                        T* out, int* status, cudaStream_t s) {
   int64_t end = 0;
   if (d->n_active > 0) {
     const int l = d->n_active - 1;
@@ -180,14 +191,14 @@ static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* 
     a.R = n * d->m_values[l];
     a.K = d->f_in_values[l];
     a.N = d->f_out_values[l];
-    if (int rc = lin_gemm<T>(a, s)) return rc;
+    if (int rc = gemm_dispatch<T>(a, d->precision, status, s)) return rc;
   }
   return 0;
 }
 
 template <typename T>
 static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const void* const* weights, const T* scale,
-                        int64_t n, T* gx, void* const* gw, cudaStream_t s) {
+                        int64_t n, T* gx, void* const* gw, int* status, cudaStream_t s) {
   if (gx) {
     // columns of x outside the active ranks get zero gradient
     int64_t prev = 0;
@@ -208,7 +219,7 @@ static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const v
       a.R = n * d->m_values[l];
       a.K = d->f_out_values[l];
       a.N = d->f_in_values[l];
-      if (int rc = lin_gemm<T>(a, s)) return rc;
+      if (int rc = gemm_dispatch<T>(a, d->precision, status, s)) return rc;
     }
   }
   if (gw) {
@@ -438,7 +449,7 @@ int fc_irreps_dbwd(const void* grad_out, const void* x, const void* v, int64_t n
 }
 
 int fc_linear_fwd(const fc_linear_desc* desc, const void* x, const void* const* weights, const void* scale,
-                  int64_t n, void* out, fc_stream_t stream) {
+                  int64_t n, void* out, int32_t* status, fc_stream_t stream) {
   if (int rc = check_linear(desc)) return rc;
   if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_fwd: negative size");
   if (n == 0 || desc->out_dim == 0) return FC_OK;
@@ -448,15 +459,17 @@ int fc_linear_fwd(const fc_linear_desc* desc, const void* x, const void* const* 
     if (!weights[l]) return fail(FC_ERR_INVALID, "fc_linear_fwd: null weight for rank %d", l);
   cudaStream_t s = (cudaStream_t)stream;
   if (desc->dtype == FC_F32)
-    return launch_status(linear_fwd_t<float>(desc, (const float*)x, weights, (const float*)scale, n, (float*)out, s),
+    return launch_status(linear_fwd_t<float>(desc, (const float*)x, weights, (const float*)scale, n, (float*)out,
+                                             reinterpret_cast<int*>(status), s),
                          "fc_linear_fwd");
-  return launch_status(
-      linear_fwd_t<double>(desc, (const double*)x, weights, (const double*)scale, n, (double*)out, s),
-      "fc_linear_fwd");
+  return launch_status(linear_fwd_t<double>(desc, (const double*)x, weights, (const double*)scale, n, (double*)out,
+                                            reinterpret_cast<int*>(status), s),
+                       "fc_linear_fwd");
 }
 
 int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* x, const void* const* weights,
-                  const void* scale, int64_t n, void* grad_x, void* const* grad_weights, fc_stream_t stream) {
+                  const void* scale, int64_t n, void* grad_x, void* const* grad_weights, int32_t* status,
+                  fc_stream_t stream) {
   if (int rc = check_linear(desc)) return rc;
   if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_bwd: negative size");
   if (desc->n_active > 0 && (!grad_out || !x || !scale || !weights))
@@ -464,10 +477,12 @@ int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* 
   cudaStream_t s = (cudaStream_t)stream;
   if (desc->dtype == FC_F32)
     return launch_status(linear_bwd_t<float>(desc, (const float*)grad_out, (const float*)x, weights,
-                                             (const float*)scale, n, (float*)grad_x, grad_weights, s),
+                                             (const float*)scale, n, (float*)grad_x, grad_weights,
+                                             reinterpret_cast<int*>(status), s),
                          "fc_linear_bwd");
   return launch_status(linear_bwd_t<double>(desc, (const double*)grad_out, (const double*)x, weights,
-                                            (const double*)scale, n, (double*)grad_x, grad_weights, s),
+                                            (const double*)scale, n, (double*)grad_x, grad_weights,
+                                            reinterpret_cast<int*>(status), s),
                        "fc_linear_bwd");
 }
 

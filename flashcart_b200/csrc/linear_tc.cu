@@ -1,0 +1,301 @@
+// Equivariant linear maps on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// C[r, n] = scale * sum_k A[r, k] * B(k, n) for one rank l, rows r = (node, m).
+// One CTA (128 threads) owns a 128-row x 128-column output tile whose fp32
+// accumulator lives in tensor memory (128 lanes x 128 columns). The k dimension is
+// consumed in 32-element slabs (one 128-byte swizzle row): every thread loads one
+// 128-byte row of A (rows are addressed through the (node, m) strides of the layout,
+// so no tensor map is needed), splits it into tf32 hi + lo parts in registers and
+// writes both into 128B-swizzled K-major shared-memory tiles; the weight slab is
+// split the same way. One thread issues, per 8-wide k step,
+//     D += A_hi B_hi,  D += A_hi B_lo,  D += A_lo B_hi        ("3xTF32")
+// which keeps the result at fp32 accuracy (the dropped lo*lo term is ~2^-22 relative).
+// Two smem stages let the loads of slab k+1 overlap the MMAs of slab k; a stage is
+// reused only after tcgen05.commit has signalled (through an mbarrier) that the MMAs
+// reading it completed. Every wait is bounded: on expiry the kernel flags an error in
+// the status word, still drains, frees its tensor memory and returns.
+// The epilogue reads the accumulator with tcgen05.ld (warp w owns lanes 32w..32w+31,
+// i.e. tile rows 32w..32w+31), applies the scale and stores whole rows.
+#include "linear.cuh"
+
+namespace fc {
+
+#ifndef FC_HOST_EMU
+
+namespace tc {
+
+constexpr int BM = 128;   // rows per tile (TMEM lanes)
+constexpr int BN = 128;   // output columns per tile (TMEM columns)
+constexpr int BK = 32;    // k per stage: one 128-byte swizzle row of fp32/tf32
+constexpr int TILE_A = BM * BK * 4;  // bytes of one A tile (16 KB)
+constexpr int TILE_B = BN * BK * 4;  // bytes of one B tile (16 KB)
+constexpr int STAGE = 2 * TILE_A + 2 * TILE_B;  // hi + lo of A and B
+constexpr int NSTAGE = 2;
+constexpr int SMEM_BYTES = NSTAGE * STAGE + 1024 /* alignment slack */ + 64;
+constexpr long long WAIT_LIMIT = 1ll << 20;  // polls of try_wait (each may suspend briefly): ~0.1-1 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// K-major, 128-byte swizzle, Blackwell descriptor (version 1); SBO = 1024 B between
+// 8-row groups, LBO unused for swizzled K-major layouts (set to 1 as CUTLASS does).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// kind::tf32 instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = BN.
+__host__ __device__ constexpr uint32_t idesc_tf32() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
+      :
+      : "r"(tmem_d), "l"(da), "l"(db), "r"(idesc_tf32()), "r"(accumulate));
+}
+
+__device__ __forceinline__ void commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar) : "memory");
+}
+
+// Bounded wait on an mbarrier phase; returns false on timeout.
+__device__ __forceinline__ bool wait_parity(uint32_t mbar, uint32_t parity) {
+  for (long long it = 0; it < WAIT_LIMIT; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(mbar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+// Write 32 consecutive values of one tile row (128 bytes) into a 128B-swizzled tile:
+// 16-byte chunk c of row r lands at chunk c ^ (r & 7).
+__device__ __forceinline__ void put_row(uint8_t* tile, int r, const uint32_t* v) {
+  uint8_t* row = tile + r * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 q = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = q;
+  }
+}
+
+template <bool SPLIT>
+__device__ __forceinline__ void split_store(uint8_t* hi_tile, uint8_t* lo_tile, int r, const float* x) {
+  uint32_t hi[32], lo[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    hi[k] = to_tf32(x[k]);
+    if (SPLIT) lo[k] = to_tf32(x[k] - __uint_as_float(hi[k]));
+  }
+  put_row(hi_tile, r, hi);
+  if (SPLIT) put_row(lo_tile, r, lo);
+}
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + NSTAGE * STAGE + 32);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t row0 = (int64_t)blockIdx.x * BM;
+  const int col0 = blockIdx.y * BN;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < NSTAGE; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&mbar[s])));
+    asm volatile("fence.mbarrier_init.release.cluster;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+
+  // this thread's A row (tile row = tid) and its B rows (tile rows tid for BN = 128)
+  const int64_t ar = row0 + tid;
+  const bool a_ok = ar < a.R;
+  const float* arow = a_ok ? a.a.row(ar) : a.a.p;
+  const int bn = col0 + tid;
+  const bool b_ok = bn < a.N;
+
+  const int nk = (a.K + BK - 1) / BK;
+  bool healthy = true;
+  for (int kt = 0; kt < nk; ++kt) {
+    const int s = kt & 1;
+    uint8_t* st = smem + s * STAGE;
+    uint8_t *a_hi = st, *a_lo = st + TILE_A, *b_hi = st + 2 * TILE_A, *b_lo = st + 2 * TILE_A + TILE_B;
+    if (kt >= NSTAGE && healthy) {
+      // the MMAs issued NSTAGE slabs ago read this stage; wait until they completed
+      if (!wait_parity(smem_u32(&mbar[s]), ((kt - NSTAGE) / NSTAGE) & 1)) {
+        healthy = false;
+        fc_flag(status, FC_DEV_TIMEOUT);
+      }
+    }
+    const int k0 = kt * BK;
+    float x[32];
+    // A: one row of 32 k values
+    if (a_ok && k0 + BK <= a.K && ((reinterpret_cast<uintptr_t>(arow + k0) & 15) == 0)) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(arow + k0) + c);
+        x[4 * c] = q.x; x[4 * c + 1] = q.y; x[4 * c + 2] = q.z; x[4 * c + 3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) x[k] = (a_ok && k0 + k < a.K) ? __ldg(arow + k0 + k) : 0.f;
+    }
+    split_store<SPLIT>(a_hi, a_lo, tid, x);
+    // B: tile row n = output column col0 + tid, 32 k values
+    if (a.trans_b) {
+      const float* wrow = a.w + (int64_t)(b_ok ? bn : 0) * a.ldw;
+      if (b_ok && k0 + BK <= a.K && ((reinterpret_cast<uintptr_t>(wrow + k0) & 15) == 0)) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(wrow + k0) + c);
+          x[4 * c] = q.x; x[4 * c + 1] = q.y; x[4 * c + 2] = q.z; x[4 * c + 3] = q.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) x[k] = (b_ok && k0 + k < a.K) ? __ldg(wrow + k0 + k) : 0.f;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) x[k] = (b_ok && k0 + k < a.K) ? __ldg(a.w + (int64_t)(k0 + k) * a.ldw + bn) : 0.f;
+    }
+    split_store<SPLIT>(b_hi, b_lo, tid, x);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (tid == 0 && healthy) {
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      const uint64_t dah = make_desc(smem_u32(a_hi)), dal = make_desc(smem_u32(a_lo));
+      const uint64_t dbh = make_desc(smem_u32(b_hi)), dbl = make_desc(smem_u32(b_lo));
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint64_t off = (uint64_t)((kk * 32) >> 4);  // advance 32 bytes along K inside the swizzle row
+        mma_tf32(tmem, dah + off, dbh + off, (kt > 0 || kk > 0) ? 1u : 0u);
+        if (SPLIT) {
+          mma_tf32(tmem, dah + off, dbl + off, 1u);
+          mma_tf32(tmem, dal + off, dbh + off, 1u);
+        }
+      }
+      commit(smem_u32(&mbar[s]));
+    }
+  }
+  // wait for the last commit (covers every earlier MMA of this thread's chain)
+  if (healthy && nk > 0) {
+    const int s = (nk - 1) & 1;
+    if (!wait_parity(smem_u32(&mbar[s]), ((nk - 1) / NSTAGE) & 1)) {
+      healthy = false;
+      fc_flag(status, FC_DEV_TIMEOUT);
+    }
+  }
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  if (nk == 0) {
+    // empty contraction: the product is zero (the accumulator was never written)
+    const int64_t r = row0 + warp * 32 + lane;
+    if (r < a.R) {
+      float* crow = const_cast<float*>(a.c.row(r));
+      for (int j = col0; j < a.N && j < col0 + BN; ++j) crow[j] = 0.f;
+    }
+  } else if (healthy) {
+    const float sc = *a.scale;
+    const int64_t r = row0 + warp * 32 + lane;
+    float* crow = (r < a.R) ? const_cast<float*>(a.c.row(r)) : nullptr;
+#pragma unroll 1
+    for (int cb = 0; cb < BN; cb += 32) {
+      uint32_t v[32];
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cb;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+            "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]),
+            "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+            "=r"(v[30]), "=r"(v[31])
+          : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (crow) {
+        const int cg = col0 + cb;
+        if (cg + 32 <= a.N && ((reinterpret_cast<uintptr_t>(crow + cg) & 15) == 0)) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            reinterpret_cast<float4*>(crow + cg)[c] =
+                make_float4(sc * __uint_as_float(v[4 * c]), sc * __uint_as_float(v[4 * c + 1]),
+                            sc * __uint_as_float(v[4 * c + 2]), sc * __uint_as_float(v[4 * c + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (cg + j < a.N) crow[cg + j] = sc * __uint_as_float(v[j]);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  }
+}
+
+}  // namespace tc
+
+int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s) {
+  if (a.R == 0 || a.N == 0) return 0;
+  const int64_t gx = (a.R + tc::BM - 1) / tc::BM;
+  if (gx > 0x7fffffff) return FC_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)gx, (unsigned)((a.N + tc::BN - 1) / tc::BN));
+  // the dynamic shared-memory opt-in is a per-device function attribute
+  static bool configured[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FC_ERR_LAUNCH;
+  if (!configured[dev][split ? 1 : 0]) {
+    cudaError_t e = split ? cudaFuncSetAttribute(tc::lin_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 tc::SMEM_BYTES)
+                          : cudaFuncSetAttribute(tc::lin_tc_kernel<false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
+    if (e != cudaSuccess) return FC_ERR_LAUNCH;
+    configured[dev][split ? 1 : 0] = true;
+  }
+  if (split)
+    tc::lin_tc_kernel<true><<<grid, 128, tc::SMEM_BYTES, s>>>(a, status);
+  else
+    tc::lin_tc_kernel<false><<<grid, 128, tc::SMEM_BYTES, s>>>(a, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+}
+
+#else
+
+int lin_gemm_tc(const LinGemmArgs<float>& a, bool, int*, cudaStream_t s) { return lin_gemm<float>(a, s); }
+
+#endif
+
+}  // namespace fc

@@ -25,12 +25,22 @@ MIN_EDGE_LENGTH = 1.0e-4
 
 
 def get_edge_vectors(positions, cell, shifts, edge_index, batch, use_shifts: bool = True):
-    """v_e = r_j - r_i + S_e . cell (row 0 receivers i, row 1 senders j; reference ``utils/geometry.py:25-53``)."""
+    """v_e = r_j - r_i + S_e . cell (row 0 receivers i, row 1 senders j; reference ``utils/geometry.py:25-53``).
+
+    Same value as the reference; the gathers use ``index_select`` (whose gradient is an
+    atomic scatter-add) and a single-cell batch multiplies the shifts by the cell as one
+    (E, 3) x (3, 3) product, so the position / cell gradients of forces and stress do
+    not go through the sort-based backward of advanced indexing.
+    """
     idx_i, idx_j = edge_index[0], edge_index[1]
+    vec = positions.index_select(0, idx_j) - positions.index_select(0, idx_i)
     if not use_shifts:
-        return positions[idx_j] - positions[idx_i]
-    shift_vec = (shifts.to(cell.dtype).unsqueeze(-2) @ cell[batch[idx_i]]).squeeze(-2)
-    return positions[idx_j] - positions[idx_i] + shift_vec
+        return vec
+    s = shifts.to(cell.dtype)
+    if cell.shape[0] == 1:
+        return vec + s @ cell[0]
+    per_edge_cell = cell.index_select(0, batch.index_select(0, idx_i))
+    return vec + torch.bmm(s.unsqueeze(1), per_edge_cell).squeeze(1)
 
 
 def to_voigt6(t: torch.Tensor) -> torch.Tensor:
@@ -166,7 +176,7 @@ class FlashCartPotential(nn.Module):
     # ------------------------------------------------------------------ predict
 
     def predict(self, graph, compute_forces: bool = False, compute_stress: bool = False,
-                create_graph: bool = False) -> Dict[str, torch.Tensor]:
+                create_graph: Optional[bool] = False) -> Dict[str, torch.Tensor]:
         """Energies and requested derivatives (reference ``model/atomistic.py:75-340``).
 
         Returns ``node_energies`` (N,), ``energy`` (G,), and when requested ``forces``
@@ -174,6 +184,18 @@ class FlashCartPotential(nn.Module):
         ``virials`` = -stress * volume, D being a symmetric virtual strain applied to
         positions and cell.
         """
+        if create_graph is False and (compute_forces or compute_stress):
+            # Forces and stress need derivatives with respect to the geometry only; with the
+            # parameters frozen the operators skip their weight gradients (identical results).
+            frozen = [p for p in self.parameters() if p.requires_grad]
+            for p in frozen:
+                p.requires_grad_(False)
+            try:
+                return self.predict(graph, compute_forces, compute_stress, create_graph=None)
+            finally:
+                for p in frozen:
+                    p.requires_grad_(True)
+        create_graph = bool(create_graph)
         g = dict(graph.to_dict() if hasattr(graph, "to_dict") else graph)
         g["use_shifts"] = _uses_shifts(g.get("use_shifts", g.get("pbc")))
         positions = g["positions"].detach()

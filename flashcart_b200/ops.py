@@ -86,6 +86,8 @@ def check_device_status(device: Optional[torch.device] = None, clear: bool = Tru
                     "(edges grouped by ascending destination index).")
     if v & N.FC_DEV_BAD_INDEX:
         msgs.append("An edge index points outside its node array.")
+    if v & N.FC_DEV_TIMEOUT:
+        msgs.append("A bounded device-side wait expired; the results of that call are invalid.")
     if msgs:
         raise RuntimeError(" ".join(msgs))
 
@@ -541,7 +543,7 @@ def _linear_fwd_impl(x: Tensor, weights: Sequence[Tensor], out_dim: int, lists, 
     d = _linear_desc(x, out_dim, lists[0], lists[1], lists[3], lists[4], lists[5], precision)
     with _timed("linear_fwd", n_active, _nbytes(x, out, *ws)):
         rc = lib.fc_linear_fwd(ctypes.byref(d), _p(x), _ptr_array(ws), _p(sc), x.shape[0], _p(out),
-                               _stream(x.device))
+                               ctypes.c_void_p(status_word(x.device).data_ptr()), _stream(x.device))
     _after(lib, rc, "fc_linear_fwd", x.device)
     return out
 
@@ -562,7 +564,8 @@ def _linear_bwd_impl(grad_out: Tensor, x: Tensor, weights: Sequence[Tensor], nee
     d = _linear_desc(x, g.shape[1], lists[0], lists[1], lists[3], lists[4], lists[5], precision)
     with _timed("linear_bwd", n_active * (int(need_x) + int(need_w)), _nbytes(g, x, gx, *ws, *gws)):
         rc = lib.fc_linear_bwd(ctypes.byref(d), _p(g), _p(x), _ptr_array(ws), _p(sc), x.shape[0],
-                               _p(gx) if need_x else None, _ptr_array(gws) if need_w else None, _stream(x.device))
+                               _p(gx) if need_x else None, _ptr_array(gws) if need_w else None,
+                               ctypes.c_void_p(status_word(x.device).data_ptr()), _stream(x.device))
     _after(lib, rc, "fc_linear_bwd", x.device)
     return gx, gws
 

@@ -45,14 +45,15 @@ typedef void* fc_stream_t;
 /* bits of the optional device status word */
 #define FC_DEV_BAD_INDEX 1    /* an edge index pointed outside its node array */
 #define FC_DEV_UNSORTED 2     /* receiver indices were not ascending */
+#define FC_DEV_TIMEOUT 4      /* a bounded device-side wait expired (results invalid) */
 
 /* dtypes */
 #define FC_F32 0
 #define FC_F64 1
 
 /* linear-map arithmetic */
-#define FC_PREC_IEEE 0 /* exact fp32 / fp64 FMA accumulation */
-#define FC_PREC_TF32 1 /* tensor cores with tf32 operands, fp32 accumulation */
+#define FC_PREC_IEEE 0 /* fp32-accurate: fp64 FMA, or fp32 on tensor cores as 3xTF32 (hi*hi+hi*lo+lo*hi) */
+#define FC_PREC_TF32 1 /* fp32 only: one tf32 tensor-core product, fp32 accumulation */
 
 #define FC_MAX_L 3
 
@@ -155,13 +156,13 @@ typedef struct fc_linear_desc {
 
 /* Forward. Replaces flashcart::linear_fwd (o3/_linear.py:328-385). */
 int fc_linear_fwd(const fc_linear_desc* desc, const void* x, const void* const* weights,
-                  const void* scale, int64_t n, void* out, fc_stream_t stream);
+                  const void* scale, int64_t n, void* out, int32_t* status, fc_stream_t stream);
 /* Backward. Replaces flashcart::linear_bwd (o3/_linear.py:457-538). grad_x may be
  * NULL; grad_weights may be NULL or a host array of per-rank device pointers (each
  * fully overwritten). Columns of grad_x outside the active ranks are zero. */
 int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* x,
                   const void* const* weights, const void* scale, int64_t n, void* grad_x,
-                  void* const* grad_weights, fc_stream_t stream);
+                  void* const* grad_weights, int32_t* status, fc_stream_t stream);
 
 #ifdef __cplusplus
 }

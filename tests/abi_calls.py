@@ -134,7 +134,7 @@ def ptr_array(ts):
 
 def linear_fwd(lib, d, x, ws, scale):
     out = torch.full((x.shape[0], d.out_dim), float("nan"), dtype=x.dtype, device=x.device)
-    N.check(lib, lib.fc_linear_fwd(ctypes.byref(d), p(x), ptr_array(ws), p(scale), x.shape[0], p(out),
+    N.check(lib, lib.fc_linear_fwd(ctypes.byref(d), p(x), ptr_array(ws), p(scale), x.shape[0], p(out), None,
                                    stream_of(x)), "fc_linear_fwd")
     return out
 
@@ -143,5 +143,5 @@ def linear_bwd(lib, d, g, x, ws, scale):
     gx = torch.full_like(x, float("nan"))
     gws = [torch.full_like(w, float("nan")) for w in ws]
     N.check(lib, lib.fc_linear_bwd(ctypes.byref(d), p(g), p(x), ptr_array(ws), p(scale), x.shape[0], p(gx),
-                                   ptr_array(gws), stream_of(x)), "fc_linear_bwd")
+                                   ptr_array(gws), None, stream_of(x)), "fc_linear_bwd")
     return gx, gws

@@ -204,3 +204,45 @@ def test_gpu_cpu_tensors_raise(cuda_device):
     tp = o3.TensorProduct(1, 1, 1, 4, 1)
     with pytest.raises(RuntimeError, match="CUDA"):
         tp(torch.randn(3, tp.in1_dim), torch.randn(3, tp.in2_dim), torch.randn(3, tp.n_total_paths * 4))
+
+
+@pytest.mark.parametrize("shape", [(3, 3, 128, 128, [4, 6, 7, 6], 300), (2, 2, 64, 64, [1, 1, 1], 1000),
+                                   (3, 1, 20, 5, [1, 2, 1, 3], 77), (1, 3, 200, 136, None, 129)])
+def test_gpu_fp32_linear_tensor_cores_vs_float64(cuda_device, shape):
+    """fp32 linear maps run on tcgen05 as 3xTF32: fp32-level agreement with float64."""
+    li, lo, fi, fo, paths, n = shape
+    torch.manual_seed(5)
+    lin = o3.LinearLayer(li, lo, fi, fo, in_paths=paths).to(cuda_device)
+    x = torch.randn(n, lin.in_dim, device=cuda_device, requires_grad=True)
+    out = lin(x)
+    g = torch.randn_like(out)
+    (gx,) = torch.autograd.grad(out, [x], g)
+    ws = [w.detach().double().cpu() for w in lin.weight]
+    xd = x.detach().double().cpu().requires_grad_(True)
+    scales = [float(s) for s in lin.scale.cpu()]
+    ref = O.linear(xd, ws, li, lo, fi, fo, paths, scales=scales)
+    (rgx,) = torch.autograd.grad(ref, [xd], g.double().cpu())
+    err = (out.detach().double().cpu() - ref).abs().max().item()
+    assert err < 2e-5 * max(1.0, ref.abs().max().item()), err
+    err_g = (gx.double().cpu() - rgx).abs().max().item()
+    assert err_g < 2e-5 * max(1.0, rgx.abs().max().item()), err_g
+    check_device_status(cuda_device)
+
+
+def test_gpu_tf32_mode_is_single_tf32_product(cuda_device):
+    """With TF32 matmuls allowed (the reference's "tf32" dot precision) one tf32 product is used."""
+    torch.manual_seed(6)
+    lin = o3.LinearLayer(2, 2, 128, 128).to(cuda_device)
+    x = torch.randn(512, lin.in_dim, device=cuda_device)
+    exact = lin(x)
+    prev = (torch.backends.cuda.matmul.allow_tf32, torch.get_float32_matmul_precision())
+    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.set_float32_matmul_precision("high")
+    try:
+        fast = lin(x)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev[0]
+        torch.set_float32_matmul_precision(prev[1])
+    rel = ((fast - exact).abs().max() / exact.abs().max()).item()
+    # reference tolerance for its tf32 path: atol 3e-3 / rtol 2e-3 (tests/o3/test_linear.py:37)
+    assert 0 < rel < 3e-3, rel
