@@ -27,7 +27,7 @@ import sys
 from fractions import Fraction
 from typing import Dict, List, Sequence, Tuple
 
-from flashcart_b200.codegen import stf
+from flashcart_b200.codegen import emit_conv, stf
 
 L_MAX = 3
 GEN_DIR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "csrc", "gen")
@@ -434,6 +434,9 @@ def emit_signature(sig: Sig) -> str:
     w("  }")
     w("}")
     w("")
+    w("#ifndef FC_HOST_EMU")
+    L.append(emit_conv.emit(sig, stores))
+    w("#endif")
     w("struct Ops {")
     w("  static constexpr int NP = sig_np, NACC = sig_nacc;".replace("sig_np", str(sig.npaths)).replace("sig_nacc", str(sig.nacc)))
     w("  template <typename T> FC_HD static FC_INLINE void fwd(const TpParams<T>& P, int64_t r, int c) "
@@ -442,6 +445,11 @@ def emit_signature(sig: Sig) -> str:
       "bool a, T* k) { bwd_body<T>(P, r, c, a, k); }")
     w("  template <typename T> FC_HD static FC_INLINE void dbwd(const TpDbwdParams<T>& P, int64_t r, int c, "
       "bool a, T* k) { dbwd_body<T>(P, r, c, a, k); }")
+    w("#ifndef FC_HOST_EMU")
+    w("  template <typename T> static int fwd2(const TpParams<T>& P, cudaStream_t s) { return launch_fwd2<T>(P, s); }")
+    w("  template <typename T> static int bwd2(const TpBwdParams<T>& P, cudaStream_t s) "
+      "{ return launch_bwd2<T>(P, s); }")
+    w("#endif")
     w("};")
     w(f"}}  // namespace sig_{n}")
     w("")

@@ -109,6 +109,14 @@ static int64_t out_dim(const fc_tp_desc* d) {
   return s;
 }
 
+// The second-generation convolution kernels: edge attributes shared by every channel,
+// one thread per channel (F a multiple of 32, at most 256), per-edge weights, paths kept.
+static bool conv2_eligible(const fc_tp_desc* d, bool conv) {
+  const int F = d->in1_features > d->in2_features ? d->in1_features : d->in2_features;
+  return conv && d->in2_features == 1 && d->in1_features == F && F % 32 == 0 && F <= 256 && !d->shared_weights &&
+         !d->reduce_paths;
+}
+
 template <typename P>
 static void fill_common(P& p, const fc_tp_desc* d, const int64_t* rowptr, const int64_t* idx_j, int64_t n_rows,
                         int64_t n_in1, int32_t* status) {
@@ -296,16 +304,17 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
     return FC_OK;
   }
   cudaStream_t s = (cudaStream_t)stream;
+  const bool v2 = conv2_eligible(desc, rowptr != nullptr) && sig->table->fwd2_f32 != nullptr;
   if (desc->dtype == FC_F32) {
     TpParams<float> p;
     fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
     p.in1 = (const float*)in1; p.in2 = (const float*)in2; p.w = (const float*)weights; p.out = (float*)out;
-    return launch_status(sig->table->fwd_f32(p, s), "fc_tp_fwd");
+    return launch_status(v2 ? sig->table->fwd2_f32(p, s) : sig->table->fwd_f32(p, s), "fc_tp_fwd");
   }
   TpParams<double> p;
   fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
   p.in1 = (const double*)in1; p.in2 = (const double*)in2; p.w = (const double*)weights; p.out = (double*)out;
-  return launch_status(sig->table->fwd_f64(p, s), "fc_tp_fwd");
+  return launch_status(v2 ? sig->table->fwd2_f64(p, s) : sig->table->fwd_f64(p, s), "fc_tp_fwd");
 }
 
 int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2, const void* weights,
@@ -334,20 +343,21 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
   if (rc) return launch_status(FC_ERR_LAUNCH, "fc_tp_bwd (zero fill)");
   if (n_out_rows == 0 || np == 0) return FC_OK;
   if (!grad_out || !in1 || !in2 || !weights) return fail(FC_ERR_INVALID, "fc_tp_bwd: null tensor");
+  const bool v2 = conv2_eligible(desc, conv) && sig->table->bwd2_f32 != nullptr;
   if (desc->dtype == FC_F32) {
     TpBwdParams<float> p;
     fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
     p.g_out = (const float*)grad_out; p.in1 = (const float*)in1; p.in2 = (const float*)in2;
     p.w = (const float*)weights;
     p.g_in1 = (float*)grad_in1; p.g_in2 = (float*)grad_in2; p.g_w = (float*)grad_weights;
-    return launch_status(sig->table->bwd_f32(p, s), "fc_tp_bwd");
+    return launch_status(v2 ? sig->table->bwd2_f32(p, s) : sig->table->bwd_f32(p, s), "fc_tp_bwd");
   }
   TpBwdParams<double> p;
   fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
   p.g_out = (const double*)grad_out; p.in1 = (const double*)in1; p.in2 = (const double*)in2;
   p.w = (const double*)weights;
   p.g_in1 = (double*)grad_in1; p.g_in2 = (double*)grad_in2; p.g_w = (double*)grad_weights;
-  return launch_status(sig->table->bwd_f64(p, s), "fc_tp_bwd");
+  return launch_status(v2 ? sig->table->bwd2_f64(p, s) : sig->table->bwd_f64(p, s), "fc_tp_bwd");
 }
 
 int fc_tp_dbwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2, const void* weights,

@@ -120,8 +120,11 @@ __global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, in
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + NSTAGE * STAGE + 32);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t row0 = (int64_t)blockIdx.x * BM;
-  const int col0 = blockIdx.y * BN;
+  // 1-D grid, column tiles fastest: the CTAs that share a row tile of A run together,
+  // so A is fetched from DRAM once and re-read from L2 for the other column tiles.
+  const int n_col_tiles = (a.N + BN - 1) / BN;
+  const int64_t row0 = (int64_t)(blockIdx.x / n_col_tiles) * BM;
+  const int col0 = (int)(blockIdx.x % n_col_tiles) * BN;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -270,9 +273,9 @@ __global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, in
 
 int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s) {
   if (a.R == 0 || a.N == 0) return 0;
-  const int64_t gx = (a.R + tc::BM - 1) / tc::BM;
-  if (gx > 0x7fffffff) return FC_ERR_UNSUPPORTED;
-  dim3 grid((unsigned)gx, (unsigned)((a.N + tc::BN - 1) / tc::BN));
+  const int64_t tiles = ((a.R + tc::BM - 1) / tc::BM) * ((a.N + tc::BN - 1) / tc::BN);
+  if (tiles > 0x7fffffff) return FC_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)tiles);
   // the dynamic shared-memory opt-in is a per-device function attribute
   static bool configured[64][2] = {};
   int dev = 0;

@@ -60,6 +60,11 @@ struct TpTable {
   int (*dbwd_f32)(const TpDbwdParams<float>&, cudaStream_t);
   int (*dbwd_f64)(const TpDbwdParams<double>&, cudaStream_t);
   int nacc;       // accumulators per channel (register budget indicator)
+  // convolution kernels for edge attributes shared by all channels (may be null)
+  int (*fwd2_f32)(const TpParams<float>&, cudaStream_t);
+  int (*fwd2_f64)(const TpParams<double>&, cudaStream_t);
+  int (*bwd2_f32)(const TpBwdParams<float>&, cudaStream_t);
+  int (*bwd2_f64)(const TpBwdParams<double>&, cudaStream_t);
 };
 
 struct TpSigEntry {
@@ -73,6 +78,49 @@ inline int tp_block_for(int F) {
 }
 
 #ifndef FC_HOST_EMU
+// ------------------------------------------------------------------ device helpers
+
+// Four consecutive shared-memory values (16-byte aligned) into registers.
+__device__ __forceinline__ void ld4(const float* p, float* v) {
+  const float4 q = *reinterpret_cast<const float4*>(p);
+  v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+__device__ __forceinline__ void ld4(const double* p, double* v) {
+  const double2 a = reinterpret_cast<const double2*>(p)[0], b = reinterpret_cast<const double2*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+// Sum N values (N a power of two <= 32) over the 32 lanes of a warp with log2(N) halving
+// exchanges: at offset o a lane keeps the upper half when its bit o is set and receives
+// the partner's copy of that half. Afterwards v[0] of a lane holds the warp total of one
+// component, returned as the index; 32/N consecutive lanes hold the same component.
+template <typename T, int N>
+__device__ __forceinline__ int fc_warp_transpose_reduce(T* v) {
+  const int lane = threadIdx.x & 31;
+  int comp = 0;
+  int n = N;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (n > 1) {
+      const int half = n >> 1;
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) {
+        if (i < half) {
+          const T keep = up ? v[i + half] : v[i];
+          const T send = up ? v[i] : v[i + half];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      if (up) comp += half;
+      n = half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+  return comp;
+}
+
 // ------------------------------------------------------------------ device wrappers
 
 template <typename T, typename S>
@@ -176,11 +224,18 @@ int tp_dbwd_launch(const TpDbwdParams<T>& P, cudaStream_t) {
 }  // namespace fc
 
 // Instantiate the launch table of a generated signature; NS::Ops supplies the bodies.
+#ifndef FC_HOST_EMU
+#define FC_CONV2_ENTRIES(NS)                                                              \
+  , &NS::Ops::fwd2<float>, &NS::Ops::fwd2<double>, &NS::Ops::bwd2<float>, &NS::Ops::bwd2<double>
+#else
+#define FC_CONV2_ENTRIES(NS) , nullptr, nullptr, nullptr, nullptr
+#endif
 #define FC_DEFINE_TP_SIGNATURE(NAME, NS)                                                  \
   extern const TpTable tp_table_##NAME;                                                   \
   const TpTable tp_table_##NAME = {                                                       \
       &tp_fwd_launch<float, NS::Ops>,  &tp_fwd_launch<double, NS::Ops>,                   \
       &tp_bwd_launch<float, NS::Ops>,  &tp_bwd_launch<double, NS::Ops>,                   \
-      &tp_dbwd_launch<float, NS::Ops>, &tp_dbwd_launch<double, NS::Ops>, NS::Ops::NACC};
+      &tp_dbwd_launch<float, NS::Ops>, &tp_dbwd_launch<double, NS::Ops>, NS::Ops::NACC    \
+      FC_CONV2_ENTRIES(NS)};
 
 #define FC_DECLARE_TP_SIGNATURE(NAME) extern const TpTable tp_table_##NAME

@@ -207,7 +207,11 @@ class FlashCartPotential(nn.Module):
             displacement = torch.zeros_like(cell).requires_grad_(True)
             sym = 0.5 * (displacement + displacement.transpose(-1, -2))
             scaling = torch.eye(3, device=cell.device, dtype=cell.dtype).unsqueeze(0) + sym
-            positions = (positions.unsqueeze(-2) @ scaling[g["batch"]]).squeeze(-2)
+            if scaling.shape[0] == 1:
+                positions = positions @ scaling[0]
+            else:
+                per_atom = scaling.index_select(0, g["batch"])
+                positions = torch.bmm(positions.unsqueeze(-2), per_atom).squeeze(-2)
             cell = cell @ scaling
         if compute_forces:
             positions.requires_grad_(True)

@@ -4,8 +4,8 @@ Same classes, constructor arguments, parameter/buffer names, persistence and
 parameter-creation order as the reference ``nn/layers.py`` (so reference
 checkpoints load unchanged and a seeded construction draws the same random
 weights); every equivariant operation (tensor products, linear maps) goes through
-:mod:`flashcart_b200.o3`, i.e. the sm_100a kernels. Plain dense layers (radial and
-readout MLPs, gates) stay ``torch.nn.functional.linear``.
+:mod:`flashcart_b200.o3`, i.e. the sm_100a kernels, and so do the dense layers of the
+radial / readout MLPs and gates (as one-rank linear maps on the tensor cores).
 """
 
 from typing import List, Optional
@@ -42,7 +42,12 @@ class RescaledSigmoidLayer(nn.Module):
 
 
 class LinearLayer(nn.Module):
-    """y = x (scale W)^T + b with N(0,1) W and scale 1/sqrt(in) (reference ``nn/layers.py:82-140``)."""
+    """y = x (scale W)^T + b with N(0,1) W and scale 1/sqrt(in) (reference ``nn/layers.py:82-140``).
+
+    Evaluated by the tensor-core kernel of ``flashcart::linear_fwd`` (one rank, one
+    component: a plain row-major GEMM), fp32 as 3xTF32, so the radial and readout MLPs
+    (1.5 M edge rows at the benchmark size) run on tcgen05 instead of fp32 SIMT.
+    """
 
     def __init__(self, in_features: int, out_features: int, bias: bool = False,
                  weight_scale: Optional[float] = None):
@@ -56,9 +61,19 @@ class LinearLayer(nn.Module):
             self.bias = nn.Parameter(torch.zeros(out_features))
         else:
             self.register_parameter("bias", None)
+        self._meta = torch.zeros(1, 6, dtype=torch.int64)
+        self._lists = ([0], [0], [0], [1], [in_features], [out_features])
 
     def forward(self, x):
-        return F.linear(x, self.weight * self.scale, self.bias)
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.in_features)
+        use_fp64, precision = o3.utils.get_linear_triton_kernel_options(x.dtype)
+        w = self.weight if self.weight.dtype == x.dtype else self.weight.to(x.dtype)
+        y = torch.ops.flashcart.linear_fwd(x2, [w], self._meta, self.out_features, use_fp64, precision,
+                                           *self._lists, self.scale.reshape(1))
+        if self.bias is not None:
+            y = y + self.bias
+        return y.reshape(*lead, self.out_features)
 
 
 def _mlp(widths: List[int]) -> nn.Sequential:

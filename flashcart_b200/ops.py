@@ -643,6 +643,13 @@ def _(grad_out, x, weights, v_grad_x, v_grad_weight, use_fp64, dot_input_precisi
             [torch.empty_like(w) if need_d_weight else w.new_empty((0,)) for w in weights[:n]])
 
 
+def _need(flag) -> bool:
+    """needs_input_grad entry as a bool: list arguments report one flag per element."""
+    if isinstance(flag, (list, tuple)):
+        return any(bool(f) for f in flag)
+    return bool(flag)
+
+
 def _linear_setup(ctx, inputs, output):
     (x, weights, meta, out_size, use_fp64, prec, *lists, scale) = inputs
     ctx.save_for_backward(x, *weights, scale)
@@ -655,15 +662,16 @@ def _linear_setup(ctx, inputs, output):
 def _linear_backward(ctx, grad_out):
     saved = ctx.saved_tensors
     x, weights, scale = saved[0], list(saved[1:1 + ctx.n_w]), saved[-1]
-    need_x, need_w = bool(ctx.needs_input_grad[0]), bool(ctx.needs_input_grad[1])
+    need_x, need_w = _need(ctx.needs_input_grad[0]), _need(ctx.needs_input_grad[1])
+    no_w = [None] * len(weights)
     if grad_out is None or not (need_x or need_w):
-        return (None,) * 13
+        return (None, no_w) + (None,) * 11
     gx, gws = torch.ops.flashcart.linear_bwd(grad_out, x, weights, need_x, need_w, ctx.use_fp64, ctx.prec,
                                              *ctx.lists, scale)
     if need_w:
         n = len(ctx.lists[0])
         gws = list(gws) + [torch.zeros_like(w) for w in weights[n:]]
-    return (gx if need_x else None, gws if need_w else None) + (None,) * 11
+    return (gx if need_x else None, gws if need_w else no_w) + (None,) * 11
 
 
 def _linear_bwd_setup(ctx, inputs, output):
@@ -681,9 +689,10 @@ def _linear_bwd_setup(ctx, inputs, output):
 def _linear_bwd_backward(ctx, v_gx, v_gw):
     saved = ctx.saved_tensors
     g, x, weights, scale = saved[0], saved[1], list(saved[2:2 + ctx.n_w]), saved[-1]
-    need_g, need_x, need_w = (bool(ctx.needs_input_grad[i]) for i in range(3))
+    need_g, need_x, need_w = (_need(ctx.needs_input_grad[i]) for i in range(3))
+    no_w = [None] * len(weights)
     if not (need_g or need_x or need_w):
-        return (None,) * 14
+        return (None, None, no_w) + (None,) * 11
     has_vx = v_gx is not None and v_gx.numel() != 0 and ctx.made[0]
     has_vw = (v_gw is not None and len(v_gw) > 0 and any(v is not None and v.numel() for v in v_gw)
               and ctx.made[1])
@@ -697,7 +706,7 @@ def _linear_bwd_backward(ctx, v_gx, v_gw):
     if need_w:
         n = len(ctx.lists[0])
         dw = list(dw) + [torch.zeros_like(w) for w in weights[n:]]
-    return (dg if need_g else None, dx if need_x else None, dw if need_w else None) + (None,) * 11
+    return (dg if need_g else None, dx if need_x else None, dw if need_w else no_w) + (None,) * 11
 
 
 linear_fwd.register_autograd(_linear_backward, setup_context=_linear_setup)

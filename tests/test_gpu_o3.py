@@ -246,3 +246,25 @@ def test_gpu_tf32_mode_is_single_tf32_product(cuda_device):
     rel = ((fast - exact).abs().max() / exact.abs().max()).item()
     # reference tolerance for its tf32 path: atol 3e-3 / rtol 2e-3 (tests/o3/test_linear.py:37)
     assert 0 < rel < 3e-3, rel
+
+
+@pytest.mark.parametrize("sig", [(3, 3, 3, 32), (2, 2, 2, 64), (0, 3, 3, 32), (1, 2, 2, 96), (3, 2, 1, 32)])
+def test_gpu_fp64_shared_attribute_convolution_vs_oracle(cuda_device, sig):
+    """The shared-edge-attribute convolution kernels (path groups, edge matrices in shared
+    memory) in float64 against the oracle, forward and all three gradients."""
+    l1, l2, lo, C = sig
+    dev = cuda_device
+    idx_i, idx_j, in1, in2 = _conv_inputs(40, 700, C, l1, l2, 9, torch.float64, dev)
+    tp = o3.TensorProduct(l1, l2, lo, C, 1)
+    w = torch.randn(700, tp.n_total_paths * C, device=dev, dtype=torch.float64)
+    leaves = [in1.requires_grad_(True), in2.requires_grad_(True), w.requires_grad_(True)]
+    out = tp(*leaves, idx_i, idx_j)
+    g = torch.randn_like(out)
+    grads = torch.autograd.grad(out, leaves, g)
+    ref_leaves = [t.detach().cpu().requires_grad_(True) for t in leaves]
+    ref = O.tensor_product(*ref_leaves, idx_i.cpu(), idx_j.cpu(), l1, l2, lo, C, 1)
+    ref_grads = torch.autograd.grad(ref, ref_leaves, g.cpu())
+    assert (out.detach().cpu() - ref).abs().max().item() < 1e-11 * max(1.0, ref.abs().max().item())
+    for a, b in zip(grads, ref_grads):
+        assert (a.cpu() - b).abs().max().item() < 1e-11 * max(1.0, b.abs().max().item())
+    check_device_status(dev)
