@@ -21,6 +21,7 @@ FC_ERR_INVALID = -1
 FC_ERR_UNSUPPORTED = -2
 FC_ERR_LAUNCH = -3
 FC_ERR_CAPACITY = -4
+FC_NOALLOC_MAX_NODES = 1 << 18
 FC_DEV_BAD_INDEX = 1
 FC_DEV_UNSORTED = 2
 FC_DEV_TIMEOUT = 4
@@ -33,7 +34,7 @@ FC_MAX_L = 3
 EXPORTED_SYMBOLS = (
     "fc_version", "fc_last_error", "fc_build_rowptr", "fc_tp_num_paths", "fc_tp_out_dim",
     "fc_tp_fwd", "fc_tp_bwd", "fc_tp_dbwd", "fc_irreps_fwd", "fc_irreps_bwd", "fc_irreps_dbwd",
-    "fc_linear_fwd", "fc_linear_bwd",
+    "fc_linear_fwd", "fc_linear_bwd", "fc_tp_conv_fwd_noalloc",
 )
 
 
@@ -93,6 +94,8 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_irreps_dbwd.argtypes = [_P, _P, _P, _I64, _I32, _I32, _P, _P, _P]
     lib.fc_linear_fwd.restype = ctypes.c_int
     lib.fc_linear_fwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _I64, _P, _P, _P]
+    lib.fc_tp_conv_fwd_noalloc.restype = ctypes.c_int
+    lib.fc_tp_conv_fwd_noalloc.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P]
     lib.fc_linear_bwd.restype = ctypes.c_int
     lib.fc_linear_bwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P, _P]
     return lib

@@ -3,6 +3,7 @@
 #include <string>
 #include <cstdio>
 #include <cstdarg>
+#include <mutex>
 
 #include "tp_common.cuh"
 #include "linear.cuh"
@@ -249,6 +250,41 @@ static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const v
   return 0;
 }
 
+// ------------------------------------------------------------------ allocation-free entry
+// Receiver-CSR workspace of fc_tp_conv_fwd_noalloc: a fixed array in the library's own
+// device memory (every device that loads the library holds it until process exit), so
+// that entry point never allocates. Host code must not take the array's address
+// directly (its name is a host-side stand-in): the device address comes from
+// cudaGetSymbolAddress, looked up once per device and cached.
+constexpr int64_t kNoAllocMaxNodes = int64_t(1) << 18;  // 262,144 receivers -> 2 MiB of int64
+#ifndef FC_HOST_EMU
+static __device__ __align__(256) int64_t g_noalloc_rowptr[kNoAllocMaxNodes + 1];
+static std::mutex g_noalloc_mutex;
+static int64_t* g_noalloc_ptr[64] = {};
+
+static int noalloc_rowptr(int64_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(FC_ERR_LAUNCH, "fc_tp_conv_fwd_noalloc: no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_rowptr);
+    if (e != cudaSuccess || ptr == nullptr)
+      return fail(FC_ERR_LAUNCH, "fc_tp_conv_fwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<int64_t*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return FC_OK;
+}
+#else
+static int64_t g_noalloc_rowptr_host[kNoAllocMaxNodes + 1];
+static int noalloc_rowptr(int64_t** out) {
+  *out = g_noalloc_rowptr_host;
+  return FC_OK;
+}
+#endif
+
 }  // namespace fc
 
 using namespace fc;
@@ -494,6 +530,27 @@ int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* 
                                             (const double*)scale, n, (double*)grad_x, grad_weights,
                                             reinterpret_cast<int*>(status), s),
                        "fc_linear_bwd");
+}
+
+// Convolution forward for callers that cannot allocate device memory (see the header).
+int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* in2, const void* weights,
+                           const int64_t* idx_i, const int64_t* idx_j, int64_t n_nodes, int64_t n_edges, void* out,
+                           int32_t* status, fc_stream_t stream) {
+  if (int rc = check_desc(desc)) return rc;
+  if (n_nodes < 0 || n_edges < 0) return fail(FC_ERR_INVALID, "fc_tp_conv_fwd_noalloc: negative size");
+  if (n_nodes > kNoAllocMaxNodes)
+    return fail(FC_ERR_CAPACITY,
+                "fc_tp_conv_fwd_noalloc: %lld receiver nodes exceed the fixed workspace of %lld nodes; use "
+                "fc_build_rowptr + fc_tp_fwd with a caller-provided workspace",
+                (long long)n_nodes, (long long)kNoAllocMaxNodes);
+  if (n_nodes == 0) return FC_OK;
+  if (n_edges > 0 && (idx_i == nullptr || idx_j == nullptr))
+    return fail(FC_ERR_INVALID, "fc_tp_conv_fwd_noalloc: null index array");
+  int64_t* rowptr = nullptr;
+  if (int rc = noalloc_rowptr(&rowptr)) return rc;
+  // the workspace is fully rewritten by this call, so nothing needs clearing
+  if (int rc = fc_build_rowptr(idx_i, n_edges, n_nodes, rowptr, status, stream)) return rc;
+  return fc_tp_fwd(desc, in1, in2, weights, rowptr, idx_j, n_nodes, n_nodes, out, status, stream);
 }
 
 }  // extern "C"

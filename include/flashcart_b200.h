@@ -101,6 +101,23 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
               const int64_t* rowptr, const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows,
               void* out, int32_t* status, fc_stream_t stream);
 
+/* Allocation-free convolution forward. No counterpart in the reference: an extra
+ * entry point for callers that cannot allocate device memory themselves, e.g. code
+ * running inside a CUDA-graph capture that must not call cudaMalloc, or a host
+ * integration (a simulation engine plugin) whose allocator owns all device memory.
+ * Same result as fc_build_rowptr + fc_tp_fwd (convolution), but the receiver CSR is
+ * built into a fixed workspace inside the library's own device memory (2 MiB per
+ * device, held until process exit), so at most 262,144 receiver nodes are accepted;
+ * larger n_nodes returns FC_ERR_CAPACITY without launching anything. The call itself
+ * never allocates or frees. The first call on a device looks the workspace up
+ * (cudaGetSymbolAddress) with that device current: make it before any stream capture.
+ * All calls share the one workspace: calls that can overlap on the GPU (different
+ * streams without ordering) race and must be serialised by the caller. */
+int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* in2,
+                           const void* weights, const int64_t* idx_i, const int64_t* idx_j,
+                           int64_t n_nodes, int64_t n_edges, void* out, int32_t* status,
+                           fc_stream_t stream);
+
 /* Backward. Replaces flashcart::tp_bwd (o3/_tensor_product.py:588-787).
  * grad_in1 / grad_in2 / grad_weights may be NULL (not requested). n_in2_rows = rows
  * of in2 (edges for a convolution). Scatter targets are zero-filled here. */
