@@ -1,21 +1,23 @@
 // Equivariant linear maps on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // C[r, n] = scale * sum_k A[r, k] * B(k, n) for one rank l, rows r = (node, m).
-// One CTA (128 threads) owns a 128-row x 128-column output tile whose fp32
+// One CTA (256 threads) owns a 128-row x 128-column output tile whose fp32
 // accumulator lives in tensor memory (128 lanes x 128 columns). The k dimension is
-// consumed in 32-element slabs (one 128-byte swizzle row): every thread loads one
-// 128-byte row of A (rows are addressed through the (node, m) strides of the layout,
-// so no tensor map is needed), splits it into tf32 hi + lo parts in registers and
-// writes both into 128B-swizzled K-major shared-memory tiles; the weight slab is
-// split the same way. One thread issues, per 8-wide k step,
+// consumed in 32-element slabs (one 128-byte swizzle row): threads 0-127 load one
+// 128-byte row of A each (rows are addressed through the (node, m) strides of the
+// layout, so no tensor map is needed), threads 128-255 one row of the weight slab;
+// every row is split into tf32 hi + lo parts in registers and written into
+// 128B-swizzled K-major shared-memory tiles. The next slab is loaded into registers
+// before the barrier and the MMAs of the current one, hiding the global latency. One thread issues, per 8-wide k step,
 //     D += A_hi B_hi,  D += A_hi B_lo,  D += A_lo B_hi        ("3xTF32")
 // which keeps the result at fp32 accuracy (the dropped lo*lo term is ~2^-22 relative).
 // Two smem stages let the loads of slab k+1 overlap the MMAs of slab k; a stage is
 // reused only after tcgen05.commit has signalled (through an mbarrier) that the MMAs
 // reading it completed. Every wait is bounded: on expiry the kernel flags an error in
 // the status word, still drains, frees its tensor memory and returns.
-// The epilogue reads the accumulator with tcgen05.ld (warp w owns lanes 32w..32w+31,
-// i.e. tile rows 32w..32w+31), applies the scale and stores whole rows.
+// The epilogue reads the accumulator with tcgen05.ld (warp w owns lanes 32*(w%4)..,
+// column half w/4), transposes through shared memory (the operand stages are free by
+// then) and stores whole rows with coalesced 16-byte stores, applying the scale.
 #include "linear.cuh"
 
 namespace fc {
@@ -114,7 +116,7 @@ __device__ __forceinline__ void split_store(uint8_t* hi_tile, uint8_t* lo_tile, 
 }
 
 template <bool SPLIT>
-__global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, int* status) {
+__global__ void __launch_bounds__(256, 1) lin_tc_kernel(LinGemmArgs<float> a, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE);
@@ -141,15 +143,37 @@ __global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, in
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
 
-  // this thread's A row (tile row = tid) and its B rows (tile rows tid for BN = 128)
-  const int64_t ar = row0 + tid;
-  const bool a_ok = ar < a.R;
-  const float* arow = a_ok ? a.a.row(ar) : a.a.p;
-  const int bn = col0 + tid;
-  const bool b_ok = bn < a.N;
+  // Threads 0..127 load row tid of the A tile, threads 128..255 row tid-128 of the B tile.
+  const bool is_a = tid < BM;
+  const int trow = is_a ? tid : tid - BM;
+  const int64_t ar = row0 + trow;
+  const int bn = col0 + trow;
+  const bool ok = is_a ? (ar < a.R) : (bn < a.N);
+  const float* src = nullptr;
+  if (is_a) src = ok ? a.a.row(ar) : a.a.p;
+  else if (a.trans_b) src = a.w + (int64_t)(ok ? bn : 0) * a.ldw;
+  const bool strided = !is_a && !a.trans_b;  // B(k, n) = W[k*ldw + n]: coalesced across threads
+
+  auto load_slab = [&](int k0, float* x) {
+    if (strided) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) x[k] = (ok && k0 + k < a.K) ? __ldg(a.w + (int64_t)(k0 + k) * a.ldw + bn) : 0.f;
+    } else if (ok && k0 + BK <= a.K && ((reinterpret_cast<uintptr_t>(src + k0) & 15) == 0)) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(src + k0) + c);
+        x[4 * c] = q.x; x[4 * c + 1] = q.y; x[4 * c + 2] = q.z; x[4 * c + 3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) x[k] = (ok && k0 + k < a.K) ? __ldg(src + k0 + k) : 0.f;
+    }
+  };
 
   const int nk = (a.K + BK - 1) / BK;
   bool healthy = true;
+  float x[32];
+  if (nk > 0) load_slab(0, x);
   for (int kt = 0; kt < nk; ++kt) {
     const int s = kt & 1;
     uint8_t* st = smem + s * STAGE;
@@ -161,38 +185,9 @@ __global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, in
         fc_flag(status, FC_DEV_TIMEOUT);
       }
     }
-    const int k0 = kt * BK;
-    float x[32];
-    // A: one row of 32 k values
-    if (a_ok && k0 + BK <= a.K && ((reinterpret_cast<uintptr_t>(arow + k0) & 15) == 0)) {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 q = __ldg(reinterpret_cast<const float4*>(arow + k0) + c);
-        x[4 * c] = q.x; x[4 * c + 1] = q.y; x[4 * c + 2] = q.z; x[4 * c + 3] = q.w;
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 32; ++k) x[k] = (a_ok && k0 + k < a.K) ? __ldg(arow + k0 + k) : 0.f;
-    }
-    split_store<SPLIT>(a_hi, a_lo, tid, x);
-    // B: tile row n = output column col0 + tid, 32 k values
-    if (a.trans_b) {
-      const float* wrow = a.w + (int64_t)(b_ok ? bn : 0) * a.ldw;
-      if (b_ok && k0 + BK <= a.K && ((reinterpret_cast<uintptr_t>(wrow + k0) & 15) == 0)) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float4 q = __ldg(reinterpret_cast<const float4*>(wrow + k0) + c);
-          x[4 * c] = q.x; x[4 * c + 1] = q.y; x[4 * c + 2] = q.z; x[4 * c + 3] = q.w;
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 32; ++k) x[k] = (b_ok && k0 + k < a.K) ? __ldg(wrow + k0 + k) : 0.f;
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 32; ++k) x[k] = (b_ok && k0 + k < a.K) ? __ldg(a.w + (int64_t)(k0 + k) * a.ldw + bn) : 0.f;
-    }
-    split_store<SPLIT>(b_hi, b_lo, tid, x);
+    if (is_a) split_store<SPLIT>(a_hi, a_lo, trow, x);
+    else split_store<SPLIT>(b_hi, b_lo, trow, x);
+    if (kt + 1 < nk) load_slab((kt + 1) * BK, x);  // in flight during the barrier and the MMAs
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (tid == 0 && healthy) {
@@ -211,7 +206,7 @@ __global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, in
       commit(smem_u32(&mbar[s]));
     }
   }
-  // wait for the last commit (covers every earlier MMA of this thread's chain)
+  // wait for the last commit (covers every earlier MMA of the issuing thread)
   if (healthy && nk > 0) {
     const int s = (nk - 1) & 1;
     if (!wait_parity(smem_u32(&mbar[s]), ((nk - 1) / NSTAGE) & 1)) {
@@ -219,22 +214,20 @@ __global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, in
       fc_flag(status, FC_DEV_TIMEOUT);
     }
   }
+  // warp-collective tcgen05.ld below: make the outcome of the bounded waits block-uniform
+  healthy = __syncthreads_and(healthy ? 1 : 0) != 0;
   asm volatile("tcgen05.fence::after_thread_sync;");
-  if (nk == 0) {
-    // empty contraction: the product is zero (the accumulator was never written)
-    const int64_t r = row0 + warp * 32 + lane;
-    if (r < a.R) {
-      float* crow = const_cast<float*>(a.c.row(r));
-      for (int j = col0; j < a.N && j < col0 + BN; ++j) crow[j] = 0.f;
-    }
-  } else if (healthy) {
-    const float sc = *a.scale;
-    const int64_t r = row0 + warp * 32 + lane;
-    float* crow = (r < a.R) ? const_cast<float*>(a.c.row(r)) : nullptr;
+  // Epilogue: TMEM -> registers -> shared-memory transpose -> coalesced row stores.
+  // Warp w reads TMEM lanes 32*(w%4).. (tile rows) and column half w/4.
+  float* tr = reinterpret_cast<float*>(smem);  // [BM][TSTRIDE], reuses the operand stages
+  constexpr int TSTRIDE = BN + 1;
+  const int q = warp & 3, half = warp >> 2;
+  const int trow_e = q * 32 + lane;
 #pragma unroll 1
-    for (int cb = 0; cb < BN; cb += 32) {
-      uint32_t v[32];
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cb;
+  for (int cb = half * (BN / 2); cb < (half + 1) * (BN / 2); cb += 32) {
+    uint32_t v[32];
+    if (nk > 0 && healthy) {
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cb;
       asm volatile(
           "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
           "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -245,23 +238,32 @@ __global__ void __launch_bounds__(128, 1) lin_tc_kernel(LinGemmArgs<float> a, in
             "=r"(v[30]), "=r"(v[31])
           : "r"(taddr));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (crow) {
-        const int cg = col0 + cb;
-        if (cg + 32 <= a.N && ((reinterpret_cast<uintptr_t>(crow + cg) & 15) == 0)) {
+    } else {
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            reinterpret_cast<float4*>(crow + cg)[c] =
-                make_float4(sc * __uint_as_float(v[4 * c]), sc * __uint_as_float(v[4 * c + 1]),
-                            sc * __uint_as_float(v[4 * c + 2]), sc * __uint_as_float(v[4 * c + 3]));
-        } else {
+      for (int j = 0; j < 32; ++j) v[j] = 0u;  // empty contraction (or an expired wait): zero
+    }
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (cg + j < a.N) crow[cg + j] = sc * __uint_as_float(v[j]);
-        }
+    for (int j = 0; j < 32; ++j) tr[trow_e * TSTRIDE + cb + j] = __uint_as_float(v[j]);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  {
+    const float sc = *a.scale;
+    const int ncol = min(BN, a.N - col0);
+    // each warp stores whole rows: lane l writes columns 4l..4l+3
+    for (int r = warp; r < BM; r += 8) {
+      const int64_t gr = row0 + r;
+      if (gr >= a.R) break;
+      float* crow = const_cast<float*>(a.c.row(gr)) + col0;
+      const int c = 4 * lane;
+      if (c + 4 <= ncol && ((reinterpret_cast<uintptr_t>(crow + c) & 15) == 0)) {
+        const float* t = tr + r * TSTRIDE + c;
+        *reinterpret_cast<float4*>(crow + c) = make_float4(sc * t[0], sc * t[1], sc * t[2], sc * t[3]);
+      } else {
+        for (int j = c; j < c + 4 && j < ncol; ++j) crow[j] = sc * tr[r * TSTRIDE + j];
       }
     }
   }
-  asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;");
@@ -289,9 +291,9 @@ int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream
     configured[dev][split ? 1 : 0] = true;
   }
   if (split)
-    tc::lin_tc_kernel<true><<<grid, 128, tc::SMEM_BYTES, s>>>(a, status);
+    tc::lin_tc_kernel<true><<<grid, 256, tc::SMEM_BYTES, s>>>(a, status);
   else
-    tc::lin_tc_kernel<false><<<grid, 128, tc::SMEM_BYTES, s>>>(a, status);
+    tc::lin_tc_kernel<false><<<grid, 256, tc::SMEM_BYTES, s>>>(a, status);
   return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
 }
 
