@@ -5,7 +5,8 @@ interaction-layer case of the receiver-CSR convolution: ``in2_features == 1`` an
 ``in1_features == F`` (= blockDim, a multiple of 32, at most 256), per-edge weights,
 paths not reduced.
 
-Structure of one CTA (receiver ``blockIdx.x``, path group ``blockIdx.y``):
+Structure of one CTA (receiver ``blockIdx.x / groups``, path group ``blockIdx.x % groups``, so
+the groups of a receiver run side by side and share its senders' rows in L2):
 
 * the signature's paths are split into consecutive *groups* whose accumulators fit a
   register budget, so a thread never holds all outputs of a large signature;
@@ -232,7 +233,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("template <typename T>")
         w(f"__device__ __forceinline__ void fwd2_g{gi}(const TpParams<T>& P, T* sm) {{")
         w("  const int F = P.F, tid = threadIdx.x, c = tid;")
-        w("  const int64_t row = blockIdx.x;")
+        w("  const int64_t row = blockIdx.x / FWD2_GROUPS;")
         w(f"  T acc[{gs.nacc}];")
         w(f"  for (int k = 0; k < {gs.nacc}; ++k) acc[k] = T(0);")
         w("  const int64_t e0 = P.rowptr[row], e1 = P.rowptr[row + 1];")
@@ -274,7 +275,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("__global__ void __launch_bounds__(256, 2) fwd2_kernel(TpParams<T> P) {")
     w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
     w("  T* sm = reinterpret_cast<T*>(fc_smem_raw);")
-    w("  switch (blockIdx.y) {")
+    w("  switch (blockIdx.x % FWD2_GROUPS) {  // the groups of one receiver run side by side (shared x1 in L2)")
     for gi in range(len(fwd_groups)):
         w(f"    case {gi}: fwd2_g{gi}<T>(P, sm); break;")
     w("  }")
@@ -285,7 +286,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w(f"__device__ __forceinline__ void bwd2_g{gi}(const TpBwdParams<T>& P, T* sm, bool multi) {{")
         w("  const int F = P.F, tid = threadIdx.x, c = tid;")
         w("  const bool NEED_1 = P.g_in1 != nullptr, NEED_2 = P.g_in2 != nullptr, NEED_W = P.g_w != nullptr;")
-        w("  const int64_t row = blockIdx.x;")
+        w("  const int64_t row = blockIdx.x / BWD2_GROUPS;")
         w(f"  T* gsm = sm + {gs.nmp * EC};  // [EC][D2P] grad_in2 partial sums")
         w(f"  T g[{gs.nacc}];")
         w("  {")
@@ -350,8 +351,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("__global__ void __launch_bounds__(256, 2) bwd2_kernel(TpBwdParams<T> P) {")
     w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
     w("  T* sm = reinterpret_cast<T*>(fc_smem_raw);")
-    w(f"  const bool multi = gridDim.y > 1;")
-    w("  switch (blockIdx.y) {")
+    w("  const bool multi = BWD2_GROUPS > 1;")
+    w("  switch (blockIdx.x % BWD2_GROUPS) {")
     for gi in range(len(bwd_groups)):
         w(f"    case {gi}: bwd2_g{gi}<T>(P, sm, multi); break;")
     w("  }")
@@ -361,7 +362,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("  if (P.n_rows == 0) return 0;")
     w("  const size_t smem = FWD2_SMEM_ELEMS * sizeof(T);")
     w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(fwd2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
-    w("  fwd2_kernel<T><<<dim3((unsigned)P.n_rows, FWD2_GROUPS), P.F, smem, s>>>(P);")
+    w("  if (P.n_rows * FWD2_GROUPS > 0x7fffffffLL) return FC_ERR_UNSUPPORTED;")
+    w("  fwd2_kernel<T><<<(unsigned)(P.n_rows * FWD2_GROUPS), P.F, smem, s>>>(P);")
     w("  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;")
     w("}")
     w("template <typename T>")
@@ -369,7 +371,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("  if (P.n_rows == 0) return 0;")
     w("  const size_t smem = BWD2_SMEM_ELEMS * sizeof(T);")
     w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(bwd2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
-    w("  bwd2_kernel<T><<<dim3((unsigned)P.n_rows, BWD2_GROUPS), P.F, smem, s>>>(P);")
+    w("  if (P.n_rows * BWD2_GROUPS > 0x7fffffffLL) return FC_ERR_UNSUPPORTED;")
+    w("  bwd2_kernel<T><<<(unsigned)(P.n_rows * BWD2_GROUPS), P.F, smem, s>>>(P);")
     w("  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;")
     w("}")
     return "\n".join(L) + "\n"

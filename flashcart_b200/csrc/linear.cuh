@@ -44,6 +44,8 @@ template <typename T>
 int lin_gemm(const LinGemmArgs<T>& a, cudaStream_t s);
 // fp32 on tcgen05 tensor cores: split = 3xTF32 (fp32 accuracy), else one tf32 product.
 int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s);
+// TMA-fed persistent variant; returns 1 (nothing launched) when the layout is not eligible.
+int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s);
 template <typename T>
 int lin_wgrad(LinWgradArgs<T> a, cudaStream_t s);
 

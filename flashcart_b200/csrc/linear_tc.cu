@@ -1,11 +1,12 @@
 // Equivariant linear maps on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // C[r, n] = scale * sum_k A[r, k] * B(k, n) for one rank l, rows r = (node, m).
-// One CTA (256 threads) owns a 128-row x 128-column output tile whose fp32
-// accumulator lives in tensor memory (128 lanes x 128 columns). The k dimension is
+// One CTA (256 threads) owns a 128-row x 64-column output tile whose fp32
+// accumulator lives in tensor memory (128 lanes x 64 columns); 96 KB of shared memory
+// per CTA lets two CTAs share an SM and overlap their load / MMA / store phases. The k dimension is
 // consumed in 32-element slabs (one 128-byte swizzle row): threads 0-127 load one
 // 128-byte row of A each (rows are addressed through the (node, m) strides of the
-// layout, so no tensor map is needed), threads 128-255 one row of the weight slab;
+// layout, so no tensor map is needed), threads 128-191 one row of the weight slab;
 // every row is split into tf32 hi + lo parts in registers and written into
 // 128B-swizzled K-major shared-memory tiles. The next slab is loaded into registers
 // before the barrier and the MMAs of the current one, hiding the global latency. One thread issues, per 8-wide k step,
@@ -27,13 +28,14 @@ namespace fc {
 namespace tc {
 
 constexpr int BM = 128;   // rows per tile (TMEM lanes)
-constexpr int BN = 128;   // output columns per tile (TMEM columns)
+constexpr int BN = 64;    // output columns per tile (TMEM columns); 64 keeps smem at 96 KB -> 2 CTAs/SM
 constexpr int BK = 32;    // k per stage: one 128-byte swizzle row of fp32/tf32
 constexpr int TILE_A = BM * BK * 4;  // bytes of one A tile (16 KB)
 constexpr int TILE_B = BN * BK * 4;  // bytes of one B tile (16 KB)
 constexpr int STAGE = 2 * TILE_A + 2 * TILE_B;  // hi + lo of A and B
 constexpr int NSTAGE = 2;
 constexpr int SMEM_BYTES = NSTAGE * STAGE + 1024 /* alignment slack */ + 64;
+static_assert(BM * (BN + 1) * 4 <= NSTAGE * STAGE, "epilogue transpose must fit in the operand stages");
 constexpr long long WAIT_LIMIT = 1ll << 20;  // polls of try_wait (each may suspend briefly): ~0.1-1 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -116,7 +118,7 @@ __device__ __forceinline__ void split_store(uint8_t* hi_tile, uint8_t* lo_tile, 
 }
 
 template <bool SPLIT>
-__global__ void __launch_bounds__(256, 1) lin_tc_kernel(LinGemmArgs<float> a, int* status) {
+__global__ void __launch_bounds__(256, 2) lin_tc_kernel(LinGemmArgs<float> a, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE);
@@ -146,9 +148,10 @@ __global__ void __launch_bounds__(256, 1) lin_tc_kernel(LinGemmArgs<float> a, in
   // Threads 0..127 load row tid of the A tile, threads 128..255 row tid-128 of the B tile.
   const bool is_a = tid < BM;
   const int trow = is_a ? tid : tid - BM;
+  const bool b_slot = !is_a && trow < BN;  // threads BM+BN.. have no B row (BN < BM)
   const int64_t ar = row0 + trow;
   const int bn = col0 + trow;
-  const bool ok = is_a ? (ar < a.R) : (bn < a.N);
+  const bool ok = is_a ? (ar < a.R) : (b_slot && bn < a.N);
   const float* src = nullptr;
   if (is_a) src = ok ? a.a.row(ar) : a.a.p;
   else if (a.trans_b) src = a.w + (int64_t)(ok ? bn : 0) * a.ldw;
@@ -173,7 +176,7 @@ __global__ void __launch_bounds__(256, 1) lin_tc_kernel(LinGemmArgs<float> a, in
   const int nk = (a.K + BK - 1) / BK;
   bool healthy = true;
   float x[32];
-  if (nk > 0) load_slab(0, x);
+  if (nk > 0 && (is_a || b_slot)) load_slab(0, x);
   for (int kt = 0; kt < nk; ++kt) {
     const int s = kt & 1;
     uint8_t* st = smem + s * STAGE;
@@ -186,8 +189,8 @@ __global__ void __launch_bounds__(256, 1) lin_tc_kernel(LinGemmArgs<float> a, in
       }
     }
     if (is_a) split_store<SPLIT>(a_hi, a_lo, trow, x);
-    else split_store<SPLIT>(b_hi, b_lo, trow, x);
-    if (kt + 1 < nk) load_slab((kt + 1) * BK, x);  // in flight during the barrier and the MMAs
+    else if (b_slot) split_store<SPLIT>(b_hi, b_lo, trow, x);
+    if (kt + 1 < nk && (is_a || b_slot)) load_slab((kt + 1) * BK, x);  // in flight during the barrier and MMAs
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (tid == 0 && healthy) {
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(256, 1) lin_tc_kernel(LinGemmArgs<float> a, in
   const int q = warp & 3, half = warp >> 2;
   const int trow_e = q * 32 + lane;
 #pragma unroll 1
-  for (int cb = half * (BN / 2); cb < (half + 1) * (BN / 2); cb += 32) {
+  for (int cb = half * (BN / 2); cb < (half + 1) * (BN / 2); cb += 32) {  // BN/2 = 32: one load
     uint32_t v[32];
     if (nk > 0 && healthy) {
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cb;
@@ -250,17 +253,20 @@ __global__ void __launch_bounds__(256, 1) lin_tc_kernel(LinGemmArgs<float> a, in
   {
     const float sc = *a.scale;
     const int ncol = min(BN, a.N - col0);
-    // each warp stores whole rows: lane l writes columns 4l..4l+3
-    for (int r = warp; r < BM; r += 8) {
+    // each warp stores two rows per step: half-warp h writes row r + h, lane l columns 4(l%16)..+3
+    constexpr int LPR = BN / 4;  // lanes per row
+    for (int r0 = warp * (32 / LPR); r0 < BM; r0 += 8 * (32 / LPR)) {
+      const int r = r0 + lane / LPR;
       const int64_t gr = row0 + r;
-      if (gr >= a.R) break;
-      float* crow = const_cast<float*>(a.c.row(gr)) + col0;
-      const int c = 4 * lane;
-      if (c + 4 <= ncol && ((reinterpret_cast<uintptr_t>(crow + c) & 15) == 0)) {
-        const float* t = tr + r * TSTRIDE + c;
-        *reinterpret_cast<float4*>(crow + c) = make_float4(sc * t[0], sc * t[1], sc * t[2], sc * t[3]);
-      } else {
-        for (int j = c; j < c + 4 && j < ncol; ++j) crow[j] = sc * tr[r * TSTRIDE + j];
+      if (gr < a.R) {
+        float* crow = const_cast<float*>(a.c.row(gr)) + col0;
+        const int c = 4 * (lane % LPR);
+        if (c + 4 <= ncol && ((reinterpret_cast<uintptr_t>(crow + c) & 15) == 0)) {
+          const float* t = tr + r * TSTRIDE + c;
+          *reinterpret_cast<float4*>(crow + c) = make_float4(sc * t[0], sc * t[1], sc * t[2], sc * t[3]);
+        } else {
+          for (int j = c; j < c + 4 && j < ncol; ++j) crow[j] = sc * tr[r * TSTRIDE + j];
+        }
       }
     }
   }
@@ -275,6 +281,9 @@ __global__ void __launch_bounds__(256, 1) lin_tc_kernel(LinGemmArgs<float> a, in
 
 int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s) {
   if (a.R == 0 || a.N == 0) return 0;
+  // TMA-fed persistent kernel where the layout allows it, else this one
+  const int rc = lin_gemm_tma(a, split, status, s);
+  if (rc != 1) return rc;
   const int64_t tiles = ((a.R + tc::BM - 1) / tc::BM) * ((a.N + tc::BN - 1) / tc::BN);
   if (tiles > 0x7fffffff) return FC_ERR_UNSUPPORTED;
   dim3 grid((unsigned)tiles);

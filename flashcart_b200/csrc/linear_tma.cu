@@ -1,0 +1,606 @@
+// fp32 equivariant linear maps on tcgen05 tensor cores, fed by TMA (sm_100a).
+//
+// C[(m, node), n] = scale * sum_k A[(m, node), k] * B(k, n) for one rank l. The rows of
+// A and C are the (node, m) rows of the rank block; for a fixed m they form a plain
+// strided matrix, so A and C are described to the TMA unit as 3-D tensors
+// (k | n, node, m) and one tile covers 128 nodes of one m. The weights B are split once
+// per call into tf32 hi / lo parts, stored n-major (k contiguous) in a stream-ordered
+// workspace, and fetched by TMA as well.
+//
+// One persistent CTA per SM (320 threads) walks its share of the output tiles:
+//   warp 0     TMA producer: fp32 A slab (128 x 32) + B hi / lo slabs (BN x 32)
+//   warp 1     MMA issue (one thread): D += Ahi Bhi + Ahi Blo + Alo Bhi  ("3xTF32")
+//   warps 2-5  splitters: round the A slab to tf32 in place and write its residual
+//   warps 6-9  epilogue: TMEM -> registers -> scale -> swizzled staging -> TMA store
+// Operand stages cycle through full (TMA landed) -> split (hi / lo ready) -> empty (MMAs
+// done, tcgen05.commit) mbarriers. The k range of a tile is cut into units of 64; each
+// unit accumulates into the next of a ring of TMEM accumulators (acc_full / acc_empty)
+// and the epilogue adds the units in fp32 registers, so the epilogue of one unit
+// overlaps the MMAs of the next. Every wait is bounded: on expiry
+// the CTA raises FC_DEV_TIMEOUT in the status word, all roles stop, outstanding TMA
+// loads and MMAs are drained, tensor memory is freed and the kernel returns.
+//
+// The 128-byte swizzle TMA applies to a 32-float box row (16-byte chunk c of row r at
+// c ^ (r & 7)) is the K-major SW128 layout the UMMA descriptors describe, so the tiles
+// go to the tensor cores as they land. Operand boxes start at k = 32 * slab (128-byte
+// aligned x coordinate); store boxes start at n = 32 * chunk.
+#include "linear.cuh"
+
+#ifndef FC_HOST_EMU
+
+#include <cuda.h>  // CUtensorMap and the driver enums (header only; the entry point is fetched at run time)
+
+#include <algorithm>
+#include <mutex>
+
+namespace fc {
+namespace tma {
+
+constexpr int BM = 128;
+constexpr int BK = 32;
+constexpr int THREADS = 320;
+constexpr int RING_BYTES = 192 * 1024;
+constexpr int EPI_BYTES = 4 * 2 * 32 * 128;  // two 4 KB staging buffers per epilogue warp
+constexpr int BAR_BYTES = 256;
+constexpr long long WAIT_LIMIT = 1ll << 22;
+// k slabs per accumulation unit. The tensor cores accumulate in fp32 but not with
+// IEEE round-to-nearest at every step; over thousands of k the error grows beyond
+// what an fp32 dot product shows. Each unit of KG slabs (64 k) therefore starts a
+// fresh TMEM accumulator, and the epilogue sums the units in fp32 registers.
+constexpr int KG = 2;
+
+template <int BN>
+struct Cfg {
+  static constexpr int TILE_A = BM * BK * 4;  // 16 KB
+  static constexpr int TILE_B = BN * BK * 4;
+  static constexpr int STAGE = 2 * TILE_A + 2 * TILE_B;
+  static constexpr int STAGES = RING_BYTES / STAGE;
+  static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + BAR_BYTES + 1024;
+  static constexpr int NACC = 512 / BN;  // TMEM accumulators in the ring (all 512 columns)
+  static constexpr int TMEM_COLS = 512;
+  static_assert(STAGES >= 2 && STAGES <= 8, "operand ring");
+  static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
+};
+
+struct Args {
+  int64_t nodes;          // rows per m
+  int M;                  // number of m (2l+1)
+  int K, N, nk;           // reduction length, output columns, 32-wide k slabs
+  int nu;                 // accumulation units per tile (ceil(nk / KG))
+  int n_col_tiles;
+  int64_t row_tiles;      // 128-node tiles per m
+  int64_t n_tiles;
+  const float* scale;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ float round_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr) {
+  // K-major, 128-byte swizzle, descriptor version 1; 1024 B between 8-row groups.
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+template <int BN>
+__host__ __device__ constexpr uint32_t idesc_tf32() {
+  // D f32, A / B tf32, both K-major, M = 128, N = BN.
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+template <int BN>
+__device__ __forceinline__ void mma(uint32_t d, uint64_t da, uint64_t db, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
+      :
+      : "r"(d), "l"(da), "l"(db), "r"(idesc_tf32<BN>()), "r"(acc));
+}
+
+__device__ __forceinline__ void commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar) : "memory");
+}
+
+__device__ __forceinline__ void arrive(uint32_t mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(mbar) : "memory");
+}
+
+__device__ __forceinline__ void arrive_tx(uint32_t mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool test_parity(uint32_t mbar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(mbar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase of the given parity. Gives up early (returning false)
+// once another role has raised the CTA's abort flag.
+__device__ __forceinline__ bool wait_parity(uint32_t mbar, uint32_t parity, volatile int* abort_flag,
+                                            int* status) {
+  for (long long it = 0; it < WAIT_LIMIT; ++it) {
+    if (test_parity(mbar, parity)) return true;
+    if ((it & 255) == 255 && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  fc_flag(status, FC_DEV_TIMEOUT);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(mbar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+struct TileCoord {
+  int col0, node0, m;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const Args& a, int64_t t) {
+  const int ct = (int)(t % a.n_col_tiles);
+  const int64_t rt = t / a.n_col_tiles;
+  TileCoord c;
+  c.col0 = ct;
+  c.m = (int)(rt / a.row_tiles);
+  c.node0 = (int)((rt - (int64_t)c.m * a.row_tiles) * BM);
+  return c;
+}
+
+template <int BN, bool SPLIT>
+__global__ void __launch_bounds__(THREADS, 1)
+    lin_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
+                   const __grid_constant__ CUtensorMap map_blo, const __grid_constant__ CUtensorMap map_c,
+                   const Args a) {
+  using C = Cfg<BN>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* epi = smem + S * C::STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + EPI_BYTES);
+  uint64_t* split = full + S;
+  uint64_t* empty = split + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + C::NACC;
+  uint64_t* drain = acc_empty + C::NACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < S; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 128;" ::"r"(smem_u32(&split[s])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&empty[s])));
+    }
+    for (int b = 0; b < C::NACC; ++b) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&acc_full[b])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(smem_u32(&acc_empty[b])));
+    }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(drain)));
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+  const int64_t my_tiles = (a.n_tiles > blockIdx.x) ? (a.n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_bhi)) : "memory");
+      if (SPLIT) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_blo)) : "memory");
+      constexpr uint32_t bytes = C::TILE_A + (SPLIT ? 2 : 1) * C::TILE_B;
+      int64_t g = 0;
+      for (int64_t i = 0; i < my_tiles && !*abort_flag; ++i) {
+        const TileCoord tc = tile_coord(a, blockIdx.x + i * gridDim.x);
+        for (int kt = 0; kt < a.nk; ++kt, ++g) {
+          const int s = (int)(g % S);
+          if (g >= S && !wait_parity(smem_u32(&empty[s]), (uint32_t)(((g / S) - 1) & 1), abort_flag, a.status))
+            break;
+          uint8_t* st = smem + s * C::STAGE;
+          const uint32_t fb = smem_u32(&full[s]);
+          arrive_tx(fb, bytes);
+          tma_load_3d(smem_u32(st), &map_a, kt * BK, tc.node0, tc.m, fb);
+          tma_load_2d(smem_u32(st + 2 * C::TILE_A), &map_bhi, kt * BK, tc.col0 * BN, fb);
+          if (SPLIT) tma_load_2d(smem_u32(st + 2 * C::TILE_A + C::TILE_B), &map_blo, kt * BK, tc.col0 * BN, fb);
+        }
+      }
+      // drain: the last load issued into every stage must have landed before the CTA exits
+      for (int s = 0; s < S; ++s) {
+        const int64_t uses = g > s ? (g - 1 - s) / S + 1 : 0;
+        if (uses > 0) {
+          for (long long it = 0; it < WAIT_LIMIT; ++it)
+            if (test_parity(smem_u32(&full[s]), (uint32_t)((uses - 1) & 1))) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      int64_t g = 0, u = 0;  // slab and accumulation-unit counters of this CTA
+      bool ok = true;
+      for (int64_t i = 0; i < my_tiles && ok && !*abort_flag; ++i) {
+        for (int j = 0; j < a.nu && ok; ++j, ++u) {
+          const int b = (int)(u % C::NACC);
+          const int64_t v = u / C::NACC;
+          if (v >= 1 && !wait_parity(smem_u32(&acc_empty[b]), (uint32_t)((v - 1) & 1), abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;");
+          const uint32_t d = tmem + (uint32_t)(b * BN);
+          const int k_end = min(a.nk, (j + 1) * KG);
+          for (int kt = j * KG; kt < k_end; ++kt, ++g) {
+            const int s = (int)(g % S);
+            if (!wait_parity(smem_u32(&split[s]), (uint32_t)((g / S) & 1), abort_flag, a.status)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            uint8_t* st = smem + s * C::STAGE;
+            const uint64_t dah = make_desc(smem_u32(st)), dal = make_desc(smem_u32(st + C::TILE_A));
+            const uint64_t dbh = make_desc(smem_u32(st + 2 * C::TILE_A));
+            const uint64_t dbl = make_desc(smem_u32(st + 2 * C::TILE_A + C::TILE_B));
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint64_t off = (uint64_t)((kk * 32) >> 4);
+              const uint32_t acc = (kt > j * KG || kk > 0) ? 1u : 0u;
+              if (SPLIT) {
+                mma<BN>(d, dal + off, dbh + off, acc);
+                mma<BN>(d, dah + off, dbl + off, 1u);
+                mma<BN>(d, dah + off, dbh + off, 1u);
+              } else {
+                mma<BN>(d, dah + off, dbh + off, acc);
+              }
+            }
+            commit(smem_u32(&empty[s]));  // the stage is free once these MMAs have completed
+          }
+          if (ok) commit(smem_u32(&acc_full[b]));  // this unit's partial accumulator is complete
+        }
+      }
+      // drain: every MMA issued by this thread completes before tensor memory is freed
+      commit(smem_u32(drain));
+      for (long long it = 0; it < WAIT_LIMIT; ++it)
+        if (test_parity(smem_u32(drain), 0)) break;
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------------ splitters
+    const int t = threadIdx.x - 64;  // 0..127
+    int64_t g = 0;
+    for (int64_t i = 0; i < my_tiles && !*abort_flag; ++i) {
+      bool ok = true;
+      for (int kt = 0; kt < a.nk; ++kt, ++g) {
+        const int s = (int)(g % S);
+        if (!wait_parity(smem_u32(&full[s]), (uint32_t)((g / S) & 1), abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        float4* hi = reinterpret_cast<float4*>(smem + s * C::STAGE);
+        float4* lo = reinterpret_cast<float4*>(smem + s * C::STAGE + C::TILE_A);
+#pragma unroll
+        for (int j = 0; j < C::TILE_A / 16 / 128; ++j) {
+          const int q = t + 128 * j;
+          const float4 x = hi[q];
+          const float4 h = make_float4(round_tf32(x.x), round_tf32(x.y), round_tf32(x.z), round_tf32(x.w));
+          hi[q] = h;
+          if (SPLIT)
+            lo[q] = make_float4(round_tf32(x.x - h.x), round_tf32(x.y - h.y), round_tf32(x.z - h.z),
+                                round_tf32(x.w - h.w));
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        arrive(smem_u32(&split[s]));
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const float sc = *a.scale;
+    uint8_t* stage0 = epi + (warp - 6) * 2 * 4096;
+    int nbuf = 0;
+    int64_t u = 0;
+    // one staged TMA store of 32 columns (this warp's 32 rows) from registers
+    auto store_chunk = [&](const float* vals, int col, const TileCoord& tc) {
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // buffer used two stores ago
+      __syncwarp();
+      uint8_t* buf = stage0 + nbuf * 4096;
+      uint8_t* row = buf + lane * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<float4*>(row + ((c ^ (lane & 7)) << 4)) =
+            make_float4(sc * vals[4 * c], sc * vals[4 * c + 1], sc * vals[4 * c + 2], sc * vals[4 * c + 3]);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&map_c, smem_u32(buf), col, tc.node0 + q * 32, tc.m);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+      nbuf ^= 1;
+    };
+    auto load32 = [&](uint32_t taddr, float* f) {
+      uint32_t v[32];
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+            "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+            "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+            "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+          : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int c = 0; c < 32; ++c) f[c] = __uint_as_float(v[c]);
+    };
+    for (int64_t i = 0; i < my_tiles && !*abort_flag; ++i) {
+      const TileCoord tc = tile_coord(a, blockIdx.x + i * gridDim.x);
+      const int col0 = tc.col0 * BN;
+      const int nchunks = min(BN, a.N - col0 + 31) / 32;
+      bool ok = true;
+      if (a.nu == 1) {
+        // one unit: stream the accumulator out chunk by chunk
+        const int b = (int)(u % C::NACC);
+        if (!wait_parity(smem_u32(&acc_full[b]), (uint32_t)((u / C::NACC) & 1), abort_flag, a.status)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        for (int cb = 0; cb < nchunks; ++cb) {
+          float f[32];
+          load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + cb * 32), f);
+          store_chunk(f, col0 + cb * 32, tc);
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;");
+        __syncwarp();
+        if (lane == 0) arrive(smem_u32(&acc_empty[b]));
+        ++u;
+      } else if constexpr (BN <= 128) {
+        // several units: sum their partial accumulators in fp32 registers
+        float acc[BN];
+#pragma unroll
+        for (int c = 0; c < BN; ++c) acc[c] = 0.f;
+        for (int j = 0; j < a.nu; ++j, ++u) {
+          const int b = (int)(u % C::NACC);
+          if (!wait_parity(smem_u32(&acc_full[b]), (uint32_t)((u / C::NACC) & 1), abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+          for (int cb = 0; cb < BN / 32; ++cb) {
+            float f[32];
+            load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + cb * 32), f);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) acc[cb * 32 + c] += f[c];
+          }
+          asm volatile("tcgen05.fence::before_thread_sync;");
+          __syncwarp();
+          if (lane == 0) arrive(smem_u32(&acc_empty[b]));
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int cb = 0; cb < BN / 32; ++cb)
+          if (cb < nchunks) store_chunk(acc + cb * 32, col0 + cb * 32, tc);
+      }
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
+  }
+}
+
+// Weights -> n-major (k contiguous, row length kp) tf32 hi / lo parts; k >= K is zero.
+__global__ void presplit_kernel(const float* __restrict__ w, int ldw, int trans_b, int K, int N, int kp,
+                                float* __restrict__ hi, float* __restrict__ lo) {
+  const int64_t total = (int64_t)N * kp;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int n = (int)(i / kp), k = (int)(i - (int64_t)n * kp);
+    const float x = k < K ? (trans_b ? w[(int64_t)n * ldw + k] : w[(int64_t)k * ldw + n]) : 0.f;
+    const float h = round_tf32(x);
+    hi[i] = h;
+    if (lo) lo[i] = round_tf32(x - h);
+  }
+}
+
+// ---------------------------------------------------------------------------------- host
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct DeviceState {
+  bool ready = false;
+  int sms = 0;
+  cudaMemPool_t pool = nullptr;
+  bool attr_set[3][2] = {};
+};
+
+static std::mutex g_mu;
+static EncodeTiledFn g_encode = nullptr;
+static DeviceState g_dev[64];
+
+static EncodeTiledFn encode_fn() {
+  if (g_encode) return g_encode;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  return g_encode;
+}
+
+static DeviceState* device_state(int dev) {
+  DeviceState& d = g_dev[dev];
+  if (d.ready) return &d;
+  if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return nullptr;
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = dev;
+  if (cudaMemPoolCreate(&d.pool, &props) != cudaSuccess) return nullptr;
+  uint64_t keep = ~uint64_t(0);  // the pool keeps its memory for reuse by later calls of this process
+  cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  d.ready = true;
+  return &d;
+}
+
+// 3-D map over (inner, node, m) rows of a LinRows block; SW128 box (32, box_rows, 1).
+static bool encode_rows(CUtensorMap* map, const float* base, int64_t inner, int64_t nodes, int M, int64_t ld,
+                        int64_t ms, int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld & 3) || (M > 1 && (ms & 3)) || inner <= 0 || nodes <= 0)
+    return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)nodes, (cuuint64_t)M};
+  const cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(M > 1 ? ms : ld * nodes) * 4};
+  const cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool encode_b(CUtensorMap* map, const float* base, int kp, int N, int box_n) {
+  const cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)N};
+  const cuuint64_t strides[1] = {(cuuint64_t)kp * 4};
+  const cuuint32_t box[2] = {32, (cuuint32_t)box_n};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, bool SPLIT>
+static int launch(const CUtensorMap& ma, const CUtensorMap& mbh, const CUtensorMap& mbl, const CUtensorMap& mc,
+                  const Args& args, DeviceState* ds, int grid, cudaStream_t s) {
+  constexpr int bi = BN == 64 ? 0 : BN == 128 ? 1 : 2;
+  if (!ds->attr_set[bi][SPLIT]) {
+    if (cudaFuncSetAttribute(lin_tma_kernel<BN, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg<BN>::SMEM) != cudaSuccess)
+      return FC_ERR_LAUNCH;
+    ds->attr_set[bi][SPLIT] = true;
+  }
+  lin_tma_kernel<BN, SPLIT><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ma, mbh, mbl, mc, args);
+  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+}
+
+}  // namespace tma
+
+// Returns 1 when the shape / layout is not eligible (the caller uses the non-TMA kernel).
+int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s) {
+  using namespace tma;
+  if (a.K <= 0 || a.R <= 0 || a.N <= 0 || a.a.M != a.c.M || a.R % a.a.M) return 1;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!encode_fn()) return 1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FC_ERR_LAUNCH;
+  DeviceState* ds = device_state(dev);
+  if (!ds) return FC_ERR_LAUNCH;
+  const int M = a.a.M;
+  const int64_t nodes = a.R / M;
+  const int nk = (a.K + BK - 1) / BK;
+  const int nu = (nk + KG - 1) / KG;
+  // 256-column tiles only when one unit covers k (their sum would need 256 registers)
+  const int BN = (a.N > 128 && nu == 1) ? 256 : a.N > 64 ? 128 : 64;
+  const int kp = (a.K + 3) & ~3;
+  if (nodes > 0x7fffffffLL) return 1;
+
+  CUtensorMap ma, mbh, mbl, mc;
+  if (!encode_rows(&ma, a.a.p + a.a.off, a.K, nodes, M, a.a.ld, a.a.ms, BM)) return 1;
+  if (!encode_rows(&mc, a.c.p + a.c.off, a.N, nodes, M, a.c.ld, a.c.ms, 32)) return 1;
+
+  float* ws = nullptr;
+  const size_t wbytes = (size_t)a.N * kp * 4 * (split ? 2 : 1);
+  if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), wbytes, ds->pool, s) != cudaSuccess) return FC_ERR_LAUNCH;
+  float* bhi = ws;
+  float* blo = split ? ws + (size_t)a.N * kp : nullptr;
+  int rc = 0;
+  if (!encode_b(&mbh, bhi, kp, a.N, BN) || (split && !encode_b(&mbl, blo, kp, a.N, BN))) rc = 1;
+  if (!split) mbl = mbh;
+  if (rc == 0) {
+    const int64_t total = (int64_t)a.N * kp;
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * ds->sms);
+    presplit_kernel<<<blocks, 256, 0, s>>>(a.w, a.ldw, a.trans_b, a.K, a.N, kp, bhi, blo);
+    if (cudaGetLastError() != cudaSuccess) rc = FC_ERR_LAUNCH;
+  }
+  if (rc == 0) {
+    Args args;
+    args.nodes = nodes;
+    args.M = M;
+    args.K = a.K;
+    args.N = a.N;
+    args.nk = nk;
+    args.nu = nu;
+    args.n_col_tiles = (a.N + BN - 1) / BN;
+    args.row_tiles = (nodes + BM - 1) / BM;
+    args.n_tiles = args.row_tiles * M * args.n_col_tiles;
+    args.scale = a.scale;
+    args.status = status;
+    const int grid = (int)std::min<int64_t>(args.n_tiles, ds->sms);
+    if (BN == 64)
+      rc = split ? launch<64, true>(ma, mbh, mbl, mc, args, ds, grid, s)
+                 : launch<64, false>(ma, mbh, mbl, mc, args, ds, grid, s);
+    else if (BN == 128)
+      rc = split ? launch<128, true>(ma, mbh, mbl, mc, args, ds, grid, s)
+                 : launch<128, false>(ma, mbh, mbl, mc, args, ds, grid, s);
+    else
+      rc = split ? launch<256, true>(ma, mbh, mbl, mc, args, ds, grid, s)
+                 : launch<256, false>(ma, mbh, mbl, mc, args, ds, grid, s);
+  }
+  // stream-ordered: the workspace returns to the pool after the kernels that read it
+  if (cudaFreeAsync(ws, s) != cudaSuccess && rc == 0) rc = FC_ERR_LAUNCH;
+  return rc;
+}
+
+}  // namespace fc
+
+#endif  // FC_HOST_EMU

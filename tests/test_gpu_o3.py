@@ -229,6 +229,30 @@ def test_gpu_fp32_linear_tensor_cores_vs_float64(cuda_device, shape):
     check_device_status(cuda_device)
 
 
+@pytest.mark.parametrize("shape", [(64, 2944, 1000), (8, 64, 4099), (2944, 64, 300), (64, 64, 129), (7, 50, 77)])
+def test_gpu_fp32_dense_layer_shapes_vs_float64(cuda_device, shape):
+    """Radial-MLP shapes (edge rows x 64 -> paths*F and back) on the TMA-fed tensor-core GEMM."""
+    from flashcart_b200.nn.layers import LinearLayer
+
+    k, n, rows = shape
+    torch.manual_seed(11)
+    lay = LinearLayer(k, n).to(cuda_device)
+    x = torch.randn(rows, k, device=cuda_device, requires_grad=True)
+    out = lay(x)
+    g = torch.randn_like(out)
+    (gx,) = torch.autograd.grad(out, [x], g)
+    w = lay.weight.detach().double().cpu()
+    sc = float(lay.scale)
+    xd = x.detach().double().cpu()
+    ref = sc * xd @ w.t()
+    rgx = sc * g.double().cpu() @ w
+    err = (out.detach().double().cpu() - ref).abs().max().item()
+    assert err < 2e-5 * max(1.0, ref.abs().max().item()), err
+    err_g = (gx.double().cpu() - rgx).abs().max().item()
+    assert err_g < 2e-5 * max(1.0, rgx.abs().max().item()), err_g
+    check_device_status(cuda_device)
+
+
 def test_gpu_tf32_mode_is_single_tf32_product(cuda_device):
     """With TF32 matmuls allowed (the reference's "tf32" dot precision) one tf32 product is used."""
     torch.manual_seed(6)
