@@ -1,21 +1,29 @@
-"""Second-generation convolution kernels for edge attributes shared by all channels.
+"""Convolution kernels for edge attributes shared by all channels.
 
 Emitted into each signature file by :mod:`flashcart_b200.codegen.emit`; used for the
 interaction-layer case of the receiver-CSR convolution: ``in2_features == 1`` and
 ``in1_features == F`` (= blockDim, a multiple of 32, at most 256), per-edge weights,
 paths not reduced.
 
-Structure of one CTA (receiver ``blockIdx.x / groups``, path group ``blockIdx.x % groups``, so
-the groups of a receiver run side by side and share its senders' rows in L2):
+Structure of one CTA (one receiver ``blockIdx.x`` of one path group's launch):
 
-* the signature's paths are split into consecutive *groups* whose accumulators fit a
-  register budget, so a thread never holds all outputs of a large signature;
-* the receiver's edges are walked in chunks of ``EC`` = 32. Phase 1: the CTA computes
-  for every edge of the chunk the channel-independent edge matrices
-  ``M_p[a, i] = sum_j K_p[a, i, j] x2_j`` of the group's paths into shared memory
-  (lane = edge, warp = a quarter of the entries). Phase 2: every thread (one channel)
-  gathers ``x1`` of the sender and forms ``t_a = sum_i M_p[a, i] x1_i`` from broadcast
-  shared-memory reads, accumulating ``w_p * t_a``.
+* the signature's paths are split into *groups* whose accumulators fit a register
+  budget; paths are taken in order of their in1 rank, so a group reads (and in the
+  backward scatters) only a contiguous range of in1 components;
+* every group is its own kernel launch (one code path per launch, so the instruction
+  cache holds it, and its own register allocation); groups touch disjoint in1
+  components, weights and outputs, so nothing is re-read across launches;
+* a prefetch ring of ``RING`` slots streams, per edge, the group's in1 components of
+  the sender row and the group's path weights of the edge into shared memory with
+  1-D bulk async copies issued by thread 0 (completion on a per-slot mbarrier). After
+  edge k thread 0 refills the slot of edge k-LAG+1, which the other warps have
+  normally released already, so the gathers run RING-LAG+1 edges ahead of the
+  arithmetic without a per-edge rendezvous of the warps;
+* the receiver's edges are walked in chunks of ``EC``. Phase 1: the CTA computes for
+  every edge of the chunk the channel-independent edge matrices
+  ``M_p[a, i] = sum_j K_p[a, i, j] x2_j`` of the group's paths into shared memory.
+  Phase 2: every thread (one channel) forms ``t_a = sum_i M_p[a, i] x1_i`` from
+  broadcast shared-memory reads and accumulates ``w_p * t_a``.
 
 Backward (same grouping, same M): ``h_i = sum_a g_a M_p[a, i]`` gives
 ``grad_w_p = sum_i x1_i h_i`` (stored per edge) and ``grad_x1_i += w_p h_i``
@@ -32,8 +40,10 @@ from typing import Dict, List, Sequence, Tuple
 
 from flashcart_b200.codegen import stf
 
-EC = 32       # edges per chunk (one per lane in phase 1)
-NPART = 4     # phase-1 work split (one part per warp of a 128-thread CTA)
+EC = 16       # edges per chunk of phase 1
+NPART = 4     # phase-1 work split (EC x NPART threads)
+RING = 4      # prefetch slots per CTA
+LAG = 2       # a slot is refilled once the edge LAG-1 before the current one is released
 
 
 def _const(fr: Fraction) -> str:
@@ -64,17 +74,19 @@ def _q(r: int, i: int) -> int:
 
 
 def make_groups(sig, budget: int) -> List[List[int]]:
-    """Consecutive path groups whose accumulator count (sum of 2lo+1) stays within budget."""
+    """Path groups (accumulator count, the sum of 2lo+1, within budget), filled in order of
+    decreasing in1 rank so that each group touches a contiguous range of in1 components."""
+    order = sorted(range(len(sig.paths)), key=lambda p: (-sig.paths[p][0], p))
     groups, cur, used = [], [], 0
-    for p, (r1, r2, o) in enumerate(sig.paths):
-        n = 2 * o + 1
+    for p in order:
+        n = 2 * sig.paths[p][2] + 1
         if cur and used + n > budget:
-            groups.append(cur)
+            groups.append(sorted(cur))
             cur, used = [], 0
         cur.append(p)
         used += n
     if cur:
-        groups.append(cur)
+        groups.append(sorted(cur))
     return groups
 
 
@@ -102,6 +114,17 @@ class GroupSlots:
         self.nm = len(self.slots)
         self.nmp = max(4, (self.nm + 3) // 4 * 4)  # padded row stride (16-byte multiple for float)
         self.nacc = sum(2 * sig.paths[p][2] + 1 for p in paths)
+        ranks = [sig.paths[p][0] for p in paths]
+        self.x_lo = min(ranks) ** 2                    # first in1 component read by the group
+        self.x_n = (max(ranks) + 1) ** 2 - self.x_lo   # contiguous in1 components read
+        self.w_pos = {p: k for k, p in enumerate(paths)}  # row of path p in the weight slice
+        self.w_runs: List[Tuple[int, int, int]] = []   # (first path, count, first slice row)
+        for k, p in enumerate(paths):
+            if self.w_runs and self.w_runs[-1][0] + self.w_runs[-1][1] == p:
+                f, n, r = self.w_runs[-1]
+                self.w_runs[-1] = (f, n + 1, r)
+            else:
+                self.w_runs.append((p, 1, k))
 
     def m_expr(self, s: int, x2: str = "x2") -> str:
         if self.slots[s] is None:
@@ -154,9 +177,9 @@ def _fwd_group_body(gs: GroupSlots, ind: str) -> List[str]:
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
         L.extend(_path_mload(gs, p, ind + "  "))
-        L.append(f"{ind}  const T wp = fc_ldg(wr + {p} * F);")
+        L.append(f"{ind}  const T wp = sw[{gs.w_pos[p]} * F];")
         for a in range(2 * o + 1):
-            terms = [f"mv[{gs.index[(p, a, i)] - s0}]*x1[{_q(r1, i)}]" for i in range(2 * r1 + 1)
+            terms = [f"mv[{gs.index[(p, a, i)] - s0}]*x1[{_q(r1, i) - gs.x_lo}]" for i in range(2 * r1 + 1)
                      if (p, a, i) in gs.index]
             expr = " + ".join(terms) if terms else "T(0)"
             L.append(f"{ind}  acc[{acc_base + a}] += wp * ({expr});")
@@ -175,7 +198,7 @@ def _bwd_group_body(gs: GroupSlots, ind: str) -> List[str]:
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
         L.extend(_path_mload(gs, p, ind + "  "))
-        L.append(f"{ind}  const T wp = fc_ldg(wr + {p} * F);")
+        L.append(f"{ind}  const T wp = sw[{gs.w_pos[p]} * F];")
         hs = []
         for i in range(2 * r1 + 1):
             terms = [f"g[{base + a}]*mv[{gs.index[(p, a, i)] - s0}]" for a in range(2 * o + 1)
@@ -183,18 +206,18 @@ def _bwd_group_body(gs: GroupSlots, ind: str) -> List[str]:
             if terms:
                 L.append(f"{ind}  const T h{i} = {' + '.join(terms)};")
                 hs.append(i)
-        gw = " + ".join(f"x1[{_q(r1, i)}]*h{i}" for i in hs) or "T(0)"
+        gw = " + ".join(f"x1[{_q(r1, i) - gs.x_lo}]*h{i}" for i in hs) or "T(0)"
         L.append(f"{ind}  if (NEED_W) gwr[{p} * F] = {gw};")
         if hs:
             L.append(f"{ind}  if (NEED_1) {{")
             for i in hs:
-                L.append(f"{ind}    gx1[{_q(r1, i)}] += wp * h{i};")
+                L.append(f"{ind}    gx1[{_q(r1, i) - gs.x_lo}] += wp * h{i};")
             L.append(f"{ind}  }}")
         body2 = []
         for j in range(2 * r2 + 1):
             pairs = []
             for a in range(2 * o + 1):
-                n = _lin([(K[a][i][j], f"x1[{_q(r1, i)}]") for i in range(2 * r1 + 1)])
+                n = _lin([(K[a][i][j], f"x1[{_q(r1, i) - gs.x_lo}]") for i in range(2 * r1 + 1)])
                 if n != "T(0)":
                     pairs.append(f"g[{base + a}]*({n})")
             if pairs:
@@ -208,20 +231,114 @@ def _bwd_group_body(gs: GroupSlots, ind: str) -> List[str]:
     return L
 
 
+def _ring_setup(gs: GroupSlots, extra_elems: str, ind: str) -> List[str]:
+    """Shared-memory carve-up (M | ring slots | [extra] | mbarriers) and the first copies."""
+    return [
+        f"{ind}constexpr int XLO = {gs.x_lo}, XN = {gs.x_n}, NW = {len(gs.paths)}, NMP = {gs.nmp};",
+        f"{ind}const int F = P.F, c = threadIdx.x, lane = c & 31;",
+        f"{ind}T* sm = reinterpret_cast<T*>(smem);",
+        f"{ind}T* ring = sm + NMP * {EC};",
+        f"{ind}const int SLOT = (XN + NW) * F;",
+        f"{ind}T* extra = ring + {RING} * SLOT;",
+        f"{ind}uint64_t* full = reinterpret_cast<uint64_t*>(extra + {extra_elems});",
+        f"{ind}uint64_t* empty = full + {RING};",
+        f"{ind}volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + {RING});",
+        f"{ind}const int64_t e0 = P.rowptr[row], ne_all = P.rowptr[row + 1] - e0;",
+        f"{ind}if (c == 0) {{",
+        f"{ind}  for (int s = 0; s < {RING}; ++s) {{ fc_mbar_init(&full[s], 1); fc_mbar_init(&empty[s], F >> 5); }}",
+        f"{ind}  *abort_flag = 0;",
+        f"{ind}  fc_mbar_init_fence();",
+        f"{ind}}}",
+        f"{ind}__syncthreads();",
+    ]
+
+
+def _issue_fn(gs: GroupSlots, ind: str) -> List[str]:
+    """Thread 0: bulk copies of edge e0+kk (sender's in1 components, the group's weights)."""
+    L = [f"{ind}int64_t issued = 0;",
+         f"{ind}auto issue = [&](int64_t kk) {{",
+         f"{ind}  issued = kk + 1;",
+         f"{ind}  const int s = (int)(kk % {RING});",
+         f"{ind}  const int64_t e = e0 + kk;",
+         f"{ind}  const int64_t j = P.idx_j[e];",
+         f"{ind}  const bool ok = (uint64_t)j < (uint64_t)P.n_in1;",
+         f"{ind}  T* dst = ring + s * SLOT;",
+         f"{ind}  fc_mbar_arrive_tx(&full[s], (uint32_t)(((ok ? XN : 0) + NW) * F * sizeof(T)));",
+         f"{ind}  if (ok) fc_bulk_g2s(dst, P.in1 + j * (int64_t)(D1 * F) + XLO * F, (uint32_t)(XN * F * sizeof(T)), &full[s]);",
+         f"{ind}  const T* wrow = P.w + e * (int64_t)(NP * F);"]
+    for (p0, n, r) in gs.w_runs:
+        L.append(f"{ind}  fc_bulk_g2s(dst + (XN + {r}) * F, wrow + {p0} * F, (uint32_t)({n} * F * sizeof(T)), &full[s]);")
+    L.append(f"{ind}}};")
+    L.append(f"{ind}if (c == 0) for (int64_t kk = 0; kk < ne_all && kk < {RING}; ++kk) issue(kk);")
+    return L
+
+
+def _ring_edge_begin(ind: str) -> List[str]:
+    return [f"{ind}const int64_t kk = eb + k;",
+            f"{ind}const int s = (int)(kk % {RING});",
+            f"{ind}const bool landed = fc_mbar_wait(&full[s], (uint32_t)((kk / {RING}) & 1), abort_flag, P.status);",
+            f"{ind}const int64_t e = e0 + kk;",
+            f"{ind}const int64_t j = P.idx_j[e];",
+            f"{ind}const bool valid = landed && (uint64_t)j < (uint64_t)P.n_in1;",
+            f"{ind}if (landed && !valid && c == 0) fc_flag(P.status, FC_DEV_BAD_INDEX);"]
+
+
+def _ring_edge_end(ind: str) -> List[str]:
+    return [f"{ind}__syncwarp();",
+            f"{ind}if (lane == 0) fc_mbar_arrive(&empty[s]);",
+            f"{ind}if (c == 0) {{",
+            f"{ind}  const int64_t r = kk - {LAG - 1};  // edge whose slot is refilled",
+            f"{ind}  if (r >= 0 && r + {RING} < ne_all &&",
+            f"{ind}      fc_mbar_wait(&empty[r % {RING}], (uint32_t)((r / {RING}) & 1), abort_flag, P.status))",
+            f"{ind}    issue(r + {RING});",
+            f"{ind}}}"]
+
+
+def _ring_drain(ind: str) -> List[str]:
+    """Thread 0: every issued copy has landed before the CTA exits (only an aborted
+    CTA can have copies that no consumer waited for)."""
+    return [f"{ind}if (c == 0 && *abort_flag) {{",
+            f"{ind}  for (int64_t kk = issued > {RING} ? issued - {RING} : 0; kk < issued; ++kk)",
+            f"{ind}    for (long long it = 0; it < FC_RING_WAIT_LIMIT; ++it)",
+            f"{ind}      if (fc_mbar_test(&full[kk % {RING}], (uint32_t)((kk / {RING}) & 1))) break;",
+            f"{ind}}}"]
+
+
+def _phase1_loop(gs: GroupSlots, ind: str) -> List[str]:
+    return [f"{ind}for (int t = c; t < {EC * NPART}; t += blockDim.x) {{",
+            f"{ind}  const int le = t % {EC}, part = t / {EC};",
+            f"{ind}  if (le < ne) {{",
+            f"{ind}    T x2[D2];",
+            f"{ind}    const T* __restrict__ a2 = P.in2 + (e0 + eb + le) * (int64_t)D2;",
+            f"{ind}    for (int q = 0; q < D2; ++q) x2[q] = fc_ldg(a2 + q);",
+            f"{ind}    T* m = sm + le * NMP;",
+            *_phase1(gs, ind + "    "),
+            f"{ind}  }}",
+            f"{ind}}}",
+            f"{ind}__syncthreads();"]
+
+
 def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
-    """Conv-v2 kernels of one signature (appended inside its namespace)."""
-    fwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, 64)]
+    """Shared-attribute convolution kernels of one signature (appended inside its namespace)."""
+    fwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, 40)]
     bwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, 40)]
     d2p = 1
     while d2p < sig.d2:
         d2p *= 2
     L = []
     w = L.append
-    w(f"// ---- conv v2 (shared edge attributes): {len(fwd_groups)} forward / {len(bwd_groups)} backward path groups")
+    w(f"// ---- shared-attribute convolution: {len(fwd_groups)} forward / {len(bwd_groups)} backward path groups")
     w(f"constexpr int FWD2_GROUPS = {len(fwd_groups)}, BWD2_GROUPS = {len(bwd_groups)};")
-    w(f"constexpr int FWD2_SMEM_ELEMS = {max(g.nmp for g in fwd_groups) * EC};")
-    w(f"constexpr int BWD2_SMEM_ELEMS = {max(g.nmp for g in bwd_groups) * EC + EC * d2p};")
-    # accumulator index -> output offset (non reduced), per path
+    # shared memory per group (elements of T, F-dependent ring) + mbarriers / abort flag
+    for kind, groups, extra in (("fwd", fwd_groups, 0), ("bwd", bwd_groups, EC * d2p)):
+        w(f"inline size_t {kind}2_smem(int g, int F, size_t es) {{")
+        w("  switch (g) {")
+        for gi, gs in enumerate(groups):
+            w(f"    case {gi}: return (size_t)({gs.nmp * EC} + {RING} * ({gs.x_n} + {len(gs.paths)}) * F + {extra}) * es"
+              f" + {2 * RING * 8 + 16};")
+        w("  }")
+        w("  return 0;")
+        w("}")
     acc_out = {}
     k = 0
     for p, (r1, r2, o) in enumerate(sig.paths):
@@ -231,38 +348,30 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     # ---------------- forward
     for gi, gs in enumerate(fwd_groups):
         w("template <typename T>")
-        w(f"__device__ __forceinline__ void fwd2_g{gi}(const TpParams<T>& P, T* sm) {{")
-        w("  const int F = P.F, tid = threadIdx.x, c = tid;")
-        w("  const int64_t row = blockIdx.x / FWD2_GROUPS;")
+        w(f"__device__ __forceinline__ void fwd2_g{gi}(const TpParams<T>& P, unsigned char* smem) {{")
+        w("  const int64_t row = blockIdx.x;")
+        L.extend(_ring_setup(gs, "0", "  "))
+        L.extend(_issue_fn(gs, "  "))
         w(f"  T acc[{gs.nacc}];")
-        w(f"  for (int k = 0; k < {gs.nacc}; ++k) acc[k] = T(0);")
-        w("  const int64_t e0 = P.rowptr[row], e1 = P.rowptr[row + 1];")
-        w(f"  for (int64_t eb = e0; eb < e1; eb += {EC}) {{")
-        w(f"    const int ne = (int)min((int64_t){EC}, e1 - eb);")
-        w(f"    for (int t = tid; t < {EC * NPART}; t += blockDim.x) {{")
-        w(f"      const int le = t % {EC}, part = t / {EC};")
-        w("      if (le < ne) {")
-        w("        T x2[D2];")
-        w("        const T* __restrict__ a2 = P.in2 + (eb + le) * (int64_t)D2;")
-        w("        for (int q = 0; q < D2; ++q) x2[q] = fc_ldg(a2 + q);")
-        w(f"        T* m = sm + le * {gs.nmp};")
-        L.extend(_phase1(gs, "        "))
-        w("      }")
-        w("    }")
-        w("    __syncthreads();")
+        w(f"  for (int q = 0; q < {gs.nacc}; ++q) acc[q] = T(0);")
+        w(f"  for (int64_t eb = 0; eb < ne_all; eb += {EC}) {{")
+        w(f"    const int ne = (int)min((int64_t){EC}, ne_all - eb);")
+        L.extend(_phase1_loop(gs, "    "))
         w("    for (int k = 0; k < ne; ++k) {")
-        w("      const int64_t e = eb + k;")
-        w("      const int64_t j = P.idx_j[e];")
-        w("      if ((uint64_t)j >= (uint64_t)P.n_in1) { if (c == 0) fc_flag(P.status, FC_DEV_BAD_INDEX); continue; }")
-        w("      const T* __restrict__ a1 = P.in1 + j * (int64_t)(D1 * F) + c;")
-        w("      T x1[D1];")
-        w("      for (int q = 0; q < D1; ++q) x1[q] = fc_ldg(a1 + q * F);")
-        w("      const T* __restrict__ wr = P.w + e * (int64_t)(NP * F) + c;")
-        w(f"      const T* m = sm + k * {gs.nmp};")
-        L.extend(_fwd_group_body(gs, "      "))
+        L.extend(_ring_edge_begin("      "))
+        w("      if (valid) {")
+        w("        const T* sx = ring + s * SLOT + c;")
+        w("        T x1[XN];")
+        w("        for (int q = 0; q < XN; ++q) x1[q] = sx[q * F];")
+        w("        const T* sw = sx + XN * F;")
+        w("        const T* m = sm + k * NMP;")
+        L.extend(_fwd_group_body(gs, "        "))
+        w("      }")
+        L.extend(_ring_edge_end("      "))
         w("    }")
         w("    __syncthreads();")
         w("  }")
+        L.extend(_ring_drain("  "))
         w("  T* __restrict__ o = P.out + row * (int64_t)(OUT_COMPS * F) + c;")
         k = 0
         for p in gs.paths:
@@ -271,23 +380,21 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
                 w(f"  o[{acc_out[(p, a)]} * F] = acc[{k}];")
                 k += 1
         w("}")
-    w("template <typename T>")
+    w("template <typename T, int G>")
     w("__global__ void __launch_bounds__(256, 2) fwd2_kernel(TpParams<T> P) {")
     w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
-    w("  T* sm = reinterpret_cast<T*>(fc_smem_raw);")
-    w("  switch (blockIdx.x % FWD2_GROUPS) {  // the groups of one receiver run side by side (shared x1 in L2)")
     for gi in range(len(fwd_groups)):
-        w(f"    case {gi}: fwd2_g{gi}<T>(P, sm); break;")
-    w("  }")
+        w(f"  if constexpr (G == {gi}) fwd2_g{gi}<T>(P, fc_smem_raw);")
     w("}")
     # ---------------- backward
     for gi, gs in enumerate(bwd_groups):
         w("template <typename T>")
-        w(f"__device__ __forceinline__ void bwd2_g{gi}(const TpBwdParams<T>& P, T* sm, bool multi) {{")
-        w("  const int F = P.F, tid = threadIdx.x, c = tid;")
+        w(f"__device__ __forceinline__ void bwd2_g{gi}(const TpBwdParams<T>& P, unsigned char* smem, bool multi) {{")
         w("  const bool NEED_1 = P.g_in1 != nullptr, NEED_2 = P.g_in2 != nullptr, NEED_W = P.g_w != nullptr;")
-        w("  const int64_t row = blockIdx.x / BWD2_GROUPS;")
-        w(f"  T* gsm = sm + {gs.nmp * EC};  // [EC][D2P] grad_in2 partial sums")
+        w("  const int64_t row = blockIdx.x;")
+        L.extend(_ring_setup(gs, str(EC * d2p), "  "))
+        w("  T* gsm = extra;  // [EC][D2P] grad_in2 partial sums")
+        L.extend(_issue_fn(gs, "  "))
         w(f"  T g[{gs.nacc}];")
         w("  {")
         w("    const T* __restrict__ go = P.g_out + row * (int64_t)(OUT_COMPS * F) + c;")
@@ -298,81 +405,68 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
                 w(f"    g[{k}] = fc_ldg(go + {acc_out[(p, a)]} * F);")
                 k += 1
         w("  }")
-        w("  const int64_t e0 = P.rowptr[row], e1 = P.rowptr[row + 1];")
-        w(f"  for (int64_t eb = e0; eb < e1; eb += {EC}) {{")
-        w(f"    const int ne = (int)min((int64_t){EC}, e1 - eb);")
-        w(f"    for (int t = tid; t < {EC * d2p}; t += blockDim.x) gsm[t] = T(0);")
-        w(f"    for (int t = tid; t < {EC * NPART}; t += blockDim.x) {{")
-        w(f"      const int le = t % {EC}, part = t / {EC};")
-        w("      if (le < ne) {")
-        w("        T x2[D2];")
-        w("        const T* __restrict__ a2 = P.in2 + (eb + le) * (int64_t)D2;")
-        w("        for (int q = 0; q < D2; ++q) x2[q] = fc_ldg(a2 + q);")
-        w(f"        T* m = sm + le * {gs.nmp};")
-        L.extend(_phase1(gs, "        "))
-        w("      }")
-        w("    }")
-        w("    __syncthreads();")
+        w(f"  for (int64_t eb = 0; eb < ne_all; eb += {EC}) {{")
+        w(f"    const int ne = (int)min((int64_t){EC}, ne_all - eb);")
+        w(f"    for (int t = c; t < {EC * d2p}; t += blockDim.x) gsm[t] = T(0);")
+        L.extend(_phase1_loop(gs, "    "))
         w("    for (int k = 0; k < ne; ++k) {")
-        w("      const int64_t e = eb + k;")
-        w("      const int64_t j = P.idx_j[e];")
-        w("      if ((uint64_t)j >= (uint64_t)P.n_in1) { if (c == 0) fc_flag(P.status, FC_DEV_BAD_INDEX); continue; }")
-        w("      const T* __restrict__ a1 = P.in1 + j * (int64_t)(D1 * F) + c;")
-        w("      T x1[D1], gx1[D1];")
-        w(f"      T gx2[{d2p}];")
-        w("      for (int q = 0; q < D1; ++q) { x1[q] = fc_ldg(a1 + q * F); gx1[q] = T(0); }")
-        w(f"      for (int q = 0; q < {d2p}; ++q) gx2[q] = T(0);")
-        w("      const T* __restrict__ wr = P.w + e * (int64_t)(NP * F) + c;")
-        w("      T* __restrict__ gwr = NEED_W ? P.g_w + e * (int64_t)(NP * F) + c : nullptr;")
-        w(f"      const T* m = sm + k * {gs.nmp};")
-        L.extend(_bwd_group_body(gs, "      "))
-        w("      if (NEED_1) {")
-        w("        T* __restrict__ t1 = P.g_in1 + j * (int64_t)(D1 * F) + c;")
-        w("        for (int q = 0; q < D1; ++q) fc_atomic_add(t1 + q * F, gx1[q]);")
+        L.extend(_ring_edge_begin("      "))
+        w("      if (valid) {")
+        w("        const T* sx = ring + s * SLOT + c;")
+        w("        T x1[XN], gx1[XN];")
+        w(f"        T gx2[{d2p}];")
+        w("        for (int q = 0; q < XN; ++q) { x1[q] = sx[q * F]; gx1[q] = T(0); }")
+        w(f"        for (int q = 0; q < {d2p}; ++q) gx2[q] = T(0);")
+        w("        const T* sw = sx + XN * F;")
+        w("        T* __restrict__ gwr = NEED_W ? P.g_w + e * (int64_t)(NP * F) + c : nullptr;")
+        w("        const T* m = sm + k * NMP;")
+        L.extend(_bwd_group_body(gs, "        "))
+        w("        if (NEED_1) {")
+        w("          T* __restrict__ t1 = P.g_in1 + j * (int64_t)(D1 * F) + XLO * F + c;")
+        w("          for (int q = 0; q < XN; ++q) fc_atomic_add(t1 + q * F, gx1[q]);")
+        w("        }")
+        w("        if (NEED_2) {")
+        w(f"          const int comp = fc_warp_transpose_reduce<T, {d2p}>(gx2);")
+        w(f"          if ((lane & {32 // d2p - 1}) == 0 && comp < D2) atomicAdd(gsm + k * {d2p} + comp, gx2[0]);")
+        w("        }")
         w("      }")
-        w("      if (NEED_2) {")
-        w(f"        const int comp = fc_warp_transpose_reduce<T, {d2p}>(gx2);")
-        w(f"        if ((threadIdx.x & {32 // d2p - 1}) == 0 && comp < D2) atomicAdd(gsm + k * {d2p} + comp, gx2[0]);")
-        w("      }")
+        L.extend(_ring_edge_end("      "))
         w("    }")
         w("    __syncthreads();")
         w("    if (NEED_2) {")
-        w(f"      for (int t = tid; t < ne * D2; t += blockDim.x) {{")
+        w(f"      for (int t = c; t < ne * D2; t += blockDim.x) {{")
         w("        const int k = t / D2, q = t % D2;")
-        w(f"        T* dst = P.g_in2 + (eb + k) * (int64_t)D2 + q;")
+        w(f"        T* dst = P.g_in2 + (e0 + eb + k) * (int64_t)D2 + q;")
         w(f"        const T v = gsm[k * {d2p} + q];")
         w("        if (multi) atomicAdd(dst, v); else *dst = v;")
         w("      }")
         w("    }")
         w("    __syncthreads();")
         w("  }")
+        L.extend(_ring_drain("  "))
         w("}")
-    w("template <typename T>")
+    w("template <typename T, int G>")
     w("__global__ void __launch_bounds__(256, 2) bwd2_kernel(TpBwdParams<T> P) {")
     w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
-    w("  T* sm = reinterpret_cast<T*>(fc_smem_raw);")
-    w("  const bool multi = BWD2_GROUPS > 1;")
-    w("  switch (blockIdx.x % BWD2_GROUPS) {")
     for gi in range(len(bwd_groups)):
-        w(f"    case {gi}: bwd2_g{gi}<T>(P, sm, multi); break;")
-    w("  }")
+        w(f"  if constexpr (G == {gi}) bwd2_g{gi}<T>(P, fc_smem_raw, BWD2_GROUPS > 1);")
     w("}")
-    w("template <typename T>")
-    w("int launch_fwd2(const TpParams<T>& P, cudaStream_t s) {")
-    w("  if (P.n_rows == 0) return 0;")
-    w("  const size_t smem = FWD2_SMEM_ELEMS * sizeof(T);")
-    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(fwd2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
-    w("  if (P.n_rows * FWD2_GROUPS > 0x7fffffffLL) return FC_ERR_UNSUPPORTED;")
-    w("  fwd2_kernel<T><<<(unsigned)(P.n_rows * FWD2_GROUPS), P.F, smem, s>>>(P);")
-    w("  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;")
-    w("}")
-    w("template <typename T>")
-    w("int launch_bwd2(const TpBwdParams<T>& P, cudaStream_t s) {")
-    w("  if (P.n_rows == 0) return 0;")
-    w("  const size_t smem = BWD2_SMEM_ELEMS * sizeof(T);")
-    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(bwd2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
-    w("  if (P.n_rows * BWD2_GROUPS > 0x7fffffffLL) return FC_ERR_UNSUPPORTED;")
-    w("  bwd2_kernel<T><<<(unsigned)(P.n_rows * BWD2_GROUPS), P.F, smem, s>>>(P);")
-    w("  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;")
-    w("}")
+    for kind, params, groups in (("fwd", "TpParams", fwd_groups), ("bwd", "TpBwdParams", bwd_groups)):
+        w("template <typename T, int G>")
+        w(f"int launch_{kind}2_group(const {params}<T>& P, cudaStream_t s) {{")
+        w(f"  const size_t smem = {kind}2_smem(G, P.F, sizeof(T));")
+        w("  if (smem > 227 * 1024) return FC_ERR_UNSUPPORTED;")
+        w(f"  if (smem > 48 * 1024 && cudaFuncSetAttribute({kind}2_kernel<T, G>, "
+          "cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
+        w(f"  {kind}2_kernel<T, G><<<(unsigned)P.n_rows, P.F, smem, s>>>(P);")
+        w("  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;")
+        w("}")
+        w("template <typename T>")
+        w(f"int launch_{kind}2(const {params}<T>& P, cudaStream_t s) {{")
+        w("  if (P.n_rows == 0) return 0;")
+        w("  if (P.n_rows > 0x7fffffffLL) return FC_ERR_UNSUPPORTED;")
+        for gi in range(len(groups)):
+            w(f"  if (int rc = launch_{kind}2_group<T, {gi}>(P, s)) return rc;")
+        w("  return 0;")
+        w("}")
     return "\n".join(L) + "\n"

@@ -110,12 +110,14 @@ static int64_t out_dim(const fc_tp_desc* d) {
   return s;
 }
 
-// The second-generation convolution kernels: edge attributes shared by every channel,
+// The shared-attribute convolution kernels: edge attributes shared by every channel,
 // one thread per channel (F a multiple of 32, at most 256), per-edge weights, paths kept.
-static bool conv2_eligible(const fc_tp_desc* d, bool conv) {
+// Their bulk copies of in1 rows and weight rows need 16-byte aligned base pointers.
+static bool conv2_eligible(const fc_tp_desc* d, bool conv, const void* in1, const void* w) {
   const int F = d->in1_features > d->in2_features ? d->in1_features : d->in2_features;
-  return conv && d->in2_features == 1 && d->in1_features == F && F % 32 == 0 && F <= 256 && !d->shared_weights &&
-         !d->reduce_paths;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(in1) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  return conv && aligned && d->in2_features == 1 && d->in1_features == F && F % 32 == 0 && F <= 256 &&
+         !d->shared_weights && !d->reduce_paths;
 }
 
 template <typename P>
@@ -340,7 +342,7 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
     return FC_OK;
   }
   cudaStream_t s = (cudaStream_t)stream;
-  const bool v2 = conv2_eligible(desc, rowptr != nullptr) && sig->table->fwd2_f32 != nullptr;
+  const bool v2 = conv2_eligible(desc, rowptr != nullptr, in1, weights) && sig->table->fwd2_f32 != nullptr;
   if (desc->dtype == FC_F32) {
     TpParams<float> p;
     fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
@@ -379,7 +381,7 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
   if (rc) return launch_status(FC_ERR_LAUNCH, "fc_tp_bwd (zero fill)");
   if (n_out_rows == 0 || np == 0) return FC_OK;
   if (!grad_out || !in1 || !in2 || !weights) return fail(FC_ERR_INVALID, "fc_tp_bwd: null tensor");
-  const bool v2 = conv2_eligible(desc, conv) && sig->table->bwd2_f32 != nullptr;
+  const bool v2 = conv2_eligible(desc, conv, in1, weights) && sig->table->bwd2_f32 != nullptr;
   if (desc->dtype == FC_F32) {
     TpBwdParams<float> p;
     fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);

@@ -90,6 +90,58 @@ __device__ __forceinline__ void ld4(const double* p, double* v) {
   v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
 }
 
+// ---- prefetch ring of the convolution kernels: 1-D bulk async copies (global -> this
+// CTA's shared memory, no multicast) completing on an mbarrier per slot.
+constexpr long long FC_RING_WAIT_LIMIT = 1ll << 22;
+
+__device__ __forceinline__ uint32_t fc_smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void fc_mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(fc_smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fc_mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fc_mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fc_smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void fc_mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fc_smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool fc_mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(fc_smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of the given parity; false on expiry (FC_DEV_TIMEOUT is
+// raised and the CTA's abort flag set) or once another thread has set the abort flag.
+__device__ __forceinline__ bool fc_mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  for (long long it = 0; it < FC_RING_WAIT_LIMIT; ++it) {
+    if (fc_mbar_test(bar, parity)) return true;
+    if ((it & 63) == 63 && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  fc_flag(status, FC_DEV_TIMEOUT);
+  return false;
+}
+// Bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) into this CTA's
+// shared memory, completing as transaction bytes on `bar`.
+__device__ __forceinline__ void fc_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          fc_smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(fc_smem_addr(bar))
+      : "memory");
+}
+
 // Sum N values (N a power of two <= 32) over the 32 lanes of a warp with log2(N) halving
 // exchanges: at offset o a lane keeps the upper half when its bit o is set and receives
 // the partner's copy of that half. Afterwards v[0] of a lane holds the warp total of one
