@@ -49,6 +49,8 @@ def _args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--op-case", choices=["conv", "gemm"], default=None,
+                    help="run one small operator case (for ncu captures) instead of the benchmark")
     return ap.parse_args()
 
 
@@ -149,6 +151,23 @@ def _peaks():
         return float(p["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def _count_own_launches(step, graph) -> int:
+    """Kernels of this library's shared object launched by one step, counted from the CUDA
+    activity trace of one extra (untimed) step."""
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step(graph)
+        torch.cuda.synchronize()
+    own = re.compile(r"(^|[^A-Za-z_])(fc::|tma::)|sig_[0-9]{3}[ns]::")
+    n = 0
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA and own.search(ev.name):
+            n += 1
+    return n
 
 
 def _profile_traffic(kernel: str):
@@ -257,6 +276,8 @@ def run_b200(args):
     if world > 1:
         dist.barrier()
 
+    own_per_step = _count_own_launches(step, graph)
+
     # end to end: host graph in pinned memory -> device, predict, results -> pinned host
     keys = ["positions", "cell", "atom_types", "edge_index", "shifts", "batch", "n_atoms", "pbc"]
     host = {k: graph[k].cpu().pin_memory() for k in keys}
@@ -313,7 +334,7 @@ def run_b200(args):
             "cpu_baseline": cpu_base,
             "e2e": {"value": world * n_atoms / (e2e_max * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": timer.launches,
+            "gpu_launches": own_per_step * args.steps,
             "clocks": clock_info,
             "kernels_ms_per_step": {k: sum(v) / args.steps for k, v in sorted(durs.items(),
                                                                                key=lambda kv: -sum(kv[1]))},
@@ -324,9 +345,51 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_op_case(case: str):
+    """Small single-operator cases with the benchmark's shapes, sized for ncu captures (a few GB):
+    ``conv``: conv products (3,3)->3 and (0,3)->3, C=128, forward + backward, on a 3,456-atom water
+    box; ``gemm``: the radial-MLP output layer 64 -> 23*128 and its input gradient on 200,000 rows."""
+    from flashcart_b200 import o3
+    from flashcart_b200.data import neighbors, synthetic
+    from flashcart_b200.nn.layers import LinearLayer
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    if case == "conv":
+        s = synthetic.water_box(12, 12, 8, seed=0)
+        ei, sh = neighbors.neighbor_list(s["positions"], s["cell"], s["pbc"], 5.0, device="cuda")
+        pos = torch.as_tensor(s["positions"], device=dev, dtype=torch.float32)
+        ei = torch.as_tensor(ei, device=dev)
+        cell = torch.as_tensor(s["cell"], device=dev, dtype=torch.float32)
+        vec = pos[ei[1]] - pos[ei[0]] + torch.as_tensor(sh, device=dev, dtype=torch.float32) @ cell
+        x2 = o3.Irreps(3)(vec)
+        n, c = pos.shape[0], 128
+        for (l1, l2, lo) in [(3, 3, 3), (0, 3, 3)]:
+            tp = o3.TensorProduct(l1, l2, lo, c, 1)
+            in1 = torch.randn(n, tp.in1_dim, device=dev, generator=g)
+            w = torch.randn(ei.shape[1], tp.n_total_paths * c, device=dev, generator=g)
+            out = tp(in1, x2, w, ei[0], ei[1])
+            torch.ops.flashcart.tp_bwd(torch.randn_like(out), in1, x2, w, ei[0], ei[1], l1, l2, lo, c, 1, False,
+                                       False, tp._in1_offs, tp._in2_offs, tp._out_sizes, tp._n_paths_per_l,
+                                       tp.n_total_paths, False, l1 > 0, True, True)
+    else:
+        lay = LinearLayer(64, 23 * 128).to(dev)
+        for p_ in lay.parameters():
+            p_.requires_grad_(False)
+        h = torch.randn(200_000, 64, device=dev, generator=g, requires_grad=True)
+        out = lay(h)
+        torch.autograd.grad(out, [h], torch.randn_like(out))
+    torch.cuda.synchronize()
+    from flashcart_b200.ops import check_device_status
+    check_device_status(dev)
+    print(json.dumps({"op_case": case, "ok": True}))
+
+
 def main():
     args = _args()
-    if args.impl == "reference":
+    if args.op_case is not None:
+        run_op_case(args.op_case)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

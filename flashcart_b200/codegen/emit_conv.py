@@ -41,7 +41,7 @@ from typing import Dict, List, Sequence, Tuple
 from flashcart_b200.codegen import stf
 
 EC = 16       # edges per chunk of phase 1
-NPART = 4     # phase-1 work split (EC x NPART threads)
+NPART = 8     # phase-1 work split (EC x NPART = 128 threads)
 RING = 4      # prefetch slots per CTA
 LAG = 2       # a slot is refilled once the edge LAG-1 before the current one is released
 
@@ -459,7 +459,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w(f"  if (smem > 48 * 1024 && cudaFuncSetAttribute({kind}2_kernel<T, G>, "
           "cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
         w(f"  {kind}2_kernel<T, G><<<(unsigned)P.n_rows, P.F, smem, s>>>(P);")
-        w("  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;")
+        w("  return fc_check_launch();")
         w("}")
         w("template <typename T>")
         w(f"int launch_{kind}2(const {params}<T>& P, cudaStream_t s) {{")

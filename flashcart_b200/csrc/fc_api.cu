@@ -36,7 +36,12 @@ static int fail(int code, const char* fmt, ...) {
 static int launch_status(int rc, const char* what) {
   if (rc == 0) return FC_OK;
 #ifndef FC_HOST_EMU
-  if (rc == FC_ERR_LAUNCH) return fail(FC_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(cudaGetLastError()));
+  if (rc == FC_ERR_LAUNCH) {
+    cudaError_t e = fc_noted_error();
+    fc_noted_error() = cudaSuccess;
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return fail(FC_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  }
 #endif
   return fail(rc, "%s failed with status %d", what, rc);
 }

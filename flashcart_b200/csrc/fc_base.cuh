@@ -31,6 +31,22 @@ typedef void* cudaStream_t;
 
 namespace fc {
 
+#ifndef FC_HOST_EMU
+// The CUDA error behind the last failed launch of this thread, kept for the message of
+// the entry point (cudaGetLastError clears it when the launcher checks it).
+inline cudaError_t& fc_noted_error() {
+  static thread_local cudaError_t e = cudaSuccess;
+  return e;
+}
+// Launcher epilogue: FC_OK, or FC_ERR_LAUNCH with the CUDA error noted.
+inline int fc_check_launch() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return 0;
+  fc_noted_error() = e;
+  return FC_ERR_LAUNCH;
+}
+#endif
+
 // Device-side data errors, OR-ed into the caller's status word (if any).
 FC_HD FC_INLINE void fc_flag(int* status, int code) {
   if (status == nullptr) return;

@@ -101,7 +101,7 @@ int irreps_fwd_launch(const T* x, T* out, int64_t n, cudaStream_t s) {
 #else
   if (n == 0) return 0;
   irreps_fwd_kernel<T, L><<<elem_grid(n, 256), 256, 0, s>>>(x, out, n);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 #endif
 }
 template <typename T, int L>
@@ -112,7 +112,7 @@ int irreps_bwd_launch(const T* g, const T* x, T* gx, int64_t n, cudaStream_t s) 
 #else
   if (n == 0) return 0;
   irreps_bwd_kernel<T, L><<<elem_grid(n, 256), 256, 0, s>>>(g, x, gx, n);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 #endif
 }
 template <typename T, int L>
@@ -123,7 +123,7 @@ int irreps_dbwd_launch(const T* g, const T* x, const T* v, T* dgo, T* dx, int64_
 #else
   if (n == 0) return 0;
   irreps_dbwd_kernel<T, L><<<elem_grid(n, 256), 256, 0, s>>>(g, x, v, dgo, dx, n);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 #endif
 }
 
@@ -206,7 +206,7 @@ int build_rowptr(const int64_t* idx, int64_t n_edges, int64_t n_nodes, int64_t* 
 #else
   const int64_t work = n_edges > n_nodes + 1 ? n_edges : n_nodes + 1;
   rowptr_kernel<<<elem_grid(work, 256), 256, 0, s>>>(idx, n_edges, n_nodes, rowptr, status);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 #endif
 }
 

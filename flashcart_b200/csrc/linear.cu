@@ -150,7 +150,7 @@ int lin_gemm(const LinGemmArgs<T>& a, cudaStream_t s) {
   if (gx > 0x7fffffff) return FC_ERR_UNSUPPORTED;
   dim3 grid((unsigned)gx, (unsigned)((a.N + LB - 1) / LB));
   lin_gemm_kernel<T><<<grid, 256, 0, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 #endif
 }
 
@@ -179,7 +179,7 @@ int lin_wgrad(LinWgradArgs<T> a, cudaStream_t s) {
   splits = (a.R + a.rows_per_split - 1) / a.rows_per_split;
   dim3 grid(to, tf, (unsigned)splits);
   lin_wgrad_kernel<T><<<grid, 256, 0, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 #endif
 }
 

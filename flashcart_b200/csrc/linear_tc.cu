@@ -303,7 +303,7 @@ int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream
     tc::lin_tc_kernel<true><<<grid, 256, tc::SMEM_BYTES, s>>>(a, status);
   else
     tc::lin_tc_kernel<false><<<grid, 256, tc::SMEM_BYTES, s>>>(a, status);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 }
 
 #else

@@ -8,7 +8,9 @@
 // workspace, and fetched by TMA as well.
 //
 // One persistent CTA per SM (320 threads) walks its share of the output tiles:
-//   warp 0     TMA producer: fp32 A slab (128 x 32) + B hi / lo slabs (BN x 32)
+//   warp 0     TMA producer: fp32 A slab (128 x 32) + B hi / lo slabs (BN x 32); optional L2
+//              prefetch of A slabs further ahead (FC_TMA_PF_AHEAD, off: it did not raise the
+//              measured rate)
 //   warp 1     MMA issue (one thread): D += Ahi Bhi + Ahi Blo + Alo Bhi  ("3xTF32")
 //   warps 2-5  splitters: round the A slab to tf32 in place and write its residual
 //   warps 6-9  epilogue: TMEM -> registers -> scale -> swizzled staging -> TMA store
@@ -38,7 +40,13 @@ namespace tma {
 
 constexpr int BM = 128;
 constexpr int BK = 32;
-constexpr int THREADS = 320;
+#ifndef FC_TMA_SPLIT_WARPS
+#define FC_TMA_SPLIT_WARPS 4
+#endif
+constexpr int SPLIT_WARPS = FC_TMA_SPLIT_WARPS;
+constexpr int EPI_WARP0 = 2 + SPLIT_WARPS;
+// 10 warps by default (4 splitters: splitting, not the MMAs, limited the slab rate with 2)
+constexpr int THREADS = (EPI_WARP0 + 4) * 32;
 constexpr int RING_BYTES = 192 * 1024;
 constexpr int EPI_BYTES = 4 * 2 * 32 * 128;  // two 4 KB staging buffers per epilogue warp
 constexpr int BAR_BYTES = 256;
@@ -48,6 +56,11 @@ constexpr long long WAIT_LIMIT = 1ll << 22;
 // what an fp32 dot product shows. Each unit of KG slabs (64 k) therefore starts a
 // fresh TMEM accumulator, and the epilogue sums the units in fp32 registers.
 constexpr int KG = 2;
+constexpr int PF_SLABS = 4;   // k slabs per L2 prefetch box (512 bytes of each row)
+#ifndef FC_TMA_PF_AHEAD
+#define FC_TMA_PF_AHEAD 0
+#endif
+constexpr int PF_AHEAD = FC_TMA_PF_AHEAD;  // slabs between the prefetch cursor and the loads
 
 template <int BN>
 struct Cfg {
@@ -78,10 +91,23 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+#ifndef FC_TMA_INT_ROUND
+#define FC_TMA_INT_ROUND 1
+#endif
+// fp32 -> tf32 (10 explicit mantissa bits), round to nearest with ties away from zero:
+// add half a tf32 unit in the last place to the magnitude bits and clear the 13 dropped
+// bits (integer add + and; a carry into the exponent is the correct rounding up to the
+// next binade). Infinities are kept; a NaN whose payload sits only in the dropped bits
+// becomes an infinity, and in the 3xTF32 split the residual x - hi is then NaN, so NaN
+// still reaches the result.
 __device__ __forceinline__ float round_tf32(float x) {
+#if FC_TMA_INT_ROUND
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+#else
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
+#endif
 }
 
 __device__ __forceinline__ uint64_t make_desc(uint32_t saddr) {
@@ -165,6 +191,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// L2 prefetch of a box of A (no shared-memory destination): keeps more HBM traffic in
+// flight than the shared-memory ring alone can hold.
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
@@ -190,7 +225,7 @@ template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
     lin_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
                    const __grid_constant__ CUtensorMap map_blo, const __grid_constant__ CUtensorMap map_c,
-                   const Args a) {
+                   const __grid_constant__ CUtensorMap map_pf, const Args a) {
   using C = Cfg<BN>;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -214,7 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 32) {
     for (int s = 0; s < S; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 128;" ::"r"(smem_u32(&split[s])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&split[s])), "r"(SPLIT_WARPS * 32));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&empty[s])));
     }
     for (int b = 0; b < C::NACC; ++b) {
@@ -235,13 +270,30 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_pf)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_bhi)) : "memory");
       if (SPLIT) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_blo)) : "memory");
       constexpr uint32_t bytes = C::TILE_A + (SPLIT ? 2 : 1) * C::TILE_B;
+      // prefetch cursor: PF_AHEAD slabs ahead of the loads, one L2 prefetch per PF_SLABS slabs
+      int64_t pi = 0;
+      int pk = 0;
+      auto advance_prefetch = [&]() {
+        if (PF_AHEAD == 0 || pi >= my_tiles) return;
+        if (pk % PF_SLABS == 0) {
+          const TileCoord pc = tile_coord(a, blockIdx.x + pi * gridDim.x);
+          tma_prefetch_3d(&map_pf, pk * BK, pc.node0, pc.m);
+        }
+        if (++pk == a.nk) {
+          pk = 0;
+          ++pi;
+        }
+      };
+      for (int q = 0; q < PF_AHEAD; ++q) advance_prefetch();  // (no-op loop when PF_AHEAD is 0)
       int64_t g = 0;
       for (int64_t i = 0; i < my_tiles && !*abort_flag; ++i) {
         const TileCoord tc = tile_coord(a, blockIdx.x + i * gridDim.x);
         for (int kt = 0; kt < a.nk; ++kt, ++g) {
+          advance_prefetch();
           const int s = (int)(g % S);
           if (g >= S && !wait_parity(smem_u32(&empty[s]), (uint32_t)(((g / S) - 1) & 1), abort_flag, a.status))
             break;
@@ -311,9 +363,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (long long it = 0; it < WAIT_LIMIT; ++it)
         if (test_parity(smem_u32(drain), 0)) break;
     }
-  } else if (warp < 6) {
+  } else if (warp < EPI_WARP0) {
     // ------------------------------------------------------------------ splitters
-    const int t = threadIdx.x - 64;  // 0..127
+    const int t = threadIdx.x - 64;  // 0 .. 32 * SPLIT_WARPS - 1
     int64_t g = 0;
     for (int64_t i = 0; i < my_tiles && !*abort_flag; ++i) {
       bool ok = true;
@@ -326,8 +378,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         float4* hi = reinterpret_cast<float4*>(smem + s * C::STAGE);
         float4* lo = reinterpret_cast<float4*>(smem + s * C::STAGE + C::TILE_A);
 #pragma unroll
-        for (int j = 0; j < C::TILE_A / 16 / 128; ++j) {
-          const int q = t + 128 * j;
+        for (int j = 0; j < C::TILE_A / 16 / (32 * SPLIT_WARPS); ++j) {
+          const int q = t + 32 * SPLIT_WARPS * j;
           const float4 x = hi[q];
           const float4 h = make_float4(round_tf32(x.x), round_tf32(x.y), round_tf32(x.z), round_tf32(x.w));
           hi[q] = h;
@@ -344,7 +396,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const float sc = *a.scale;
-    uint8_t* stage0 = epi + (warp - 6) * 2 * 4096;
+    uint8_t* stage0 = epi + (warp - EPI_WARP0) * 2 * 4096;
     int nbuf = 0;
     int64_t u = 0;
     // one staged TMA store of 32 columns (this warp's 32 rows) from registers
@@ -495,18 +547,20 @@ static DeviceState* device_state(int dev) {
   return &d;
 }
 
-// 3-D map over (inner, node, m) rows of a LinRows block; SW128 box (32, box_rows, 1).
+// 3-D map over (inner, node, m) rows of a LinRows block; box (box_inner, box_rows, 1), 128-byte
+// swizzle for operand / store boxes (box_inner 32) or none for L2 prefetch boxes.
 static bool encode_rows(CUtensorMap* map, const float* base, int64_t inner, int64_t nodes, int M, int64_t ld,
-                        int64_t ms, int box_rows) {
+                        int64_t ms, int box_rows, int box_inner = 32) {
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld & 3) || (M > 1 && (ms & 3)) || inner <= 0 || nodes <= 0)
     return false;
   const cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)nodes, (cuuint64_t)M};
   const cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(M > 1 ? ms : ld * nodes) * 4};
-  const cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+  const cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     box_inner == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 static bool encode_b(CUtensorMap* map, const float* base, int kp, int N, int box_n) {
@@ -521,7 +575,7 @@ static bool encode_b(CUtensorMap* map, const float* base, int kp, int N, int box
 
 template <int BN, bool SPLIT>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mbh, const CUtensorMap& mbl, const CUtensorMap& mc,
-                  const Args& args, DeviceState* ds, int grid, cudaStream_t s) {
+                  const CUtensorMap& mpf, const Args& args, DeviceState* ds, int grid, cudaStream_t s) {
   constexpr int bi = BN == 64 ? 0 : BN == 128 ? 1 : 2;
   if (!ds->attr_set[bi][SPLIT]) {
     if (cudaFuncSetAttribute(lin_tma_kernel<BN, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -529,8 +583,8 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mbh, const CUtensorM
       return FC_ERR_LAUNCH;
     ds->attr_set[bi][SPLIT] = true;
   }
-  lin_tma_kernel<BN, SPLIT><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ma, mbh, mbl, mc, args);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  lin_tma_kernel<BN, SPLIT><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ma, mbh, mbl, mc, mpf, args);
+  return fc_check_launch();
 }
 
 }  // namespace tma
@@ -554,8 +608,9 @@ int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStrea
   const int kp = (a.K + 3) & ~3;
   if (nodes > 0x7fffffffLL) return 1;
 
-  CUtensorMap ma, mbh, mbl, mc;
+  CUtensorMap ma, mbh, mbl, mc, mpf;
   if (!encode_rows(&ma, a.a.p + a.a.off, a.K, nodes, M, a.a.ld, a.a.ms, BM)) return 1;
+  if (!encode_rows(&mpf, a.a.p + a.a.off, a.K, nodes, M, a.a.ld, a.a.ms, BM, PF_SLABS * BK)) return 1;
   if (!encode_rows(&mc, a.c.p + a.c.off, a.N, nodes, M, a.c.ld, a.c.ms, 32)) return 1;
 
   float* ws = nullptr;
@@ -587,14 +642,14 @@ int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStrea
     args.status = status;
     const int grid = (int)std::min<int64_t>(args.n_tiles, ds->sms);
     if (BN == 64)
-      rc = split ? launch<64, true>(ma, mbh, mbl, mc, args, ds, grid, s)
-                 : launch<64, false>(ma, mbh, mbl, mc, args, ds, grid, s);
+      rc = split ? launch<64, true>(ma, mbh, mbl, mc, mpf, args, ds, grid, s)
+                 : launch<64, false>(ma, mbh, mbl, mc, mpf, args, ds, grid, s);
     else if (BN == 128)
-      rc = split ? launch<128, true>(ma, mbh, mbl, mc, args, ds, grid, s)
-                 : launch<128, false>(ma, mbh, mbl, mc, args, ds, grid, s);
+      rc = split ? launch<128, true>(ma, mbh, mbl, mc, mpf, args, ds, grid, s)
+                 : launch<128, false>(ma, mbh, mbl, mc, mpf, args, ds, grid, s);
     else
-      rc = split ? launch<256, true>(ma, mbh, mbl, mc, args, ds, grid, s)
-                 : launch<256, false>(ma, mbh, mbl, mc, args, ds, grid, s);
+      rc = split ? launch<256, true>(ma, mbh, mbl, mc, mpf, args, ds, grid, s)
+                 : launch<256, false>(ma, mbh, mbl, mc, mpf, args, ds, grid, s);
   }
   // stream-ordered: the workspace returns to the pool after the kernels that read it
   if (cudaFreeAsync(ws, s) != cudaSuccess && rc == 0) rc = FC_ERR_LAUNCH;

@@ -225,19 +225,19 @@ template <typename T, typename S>
 int tp_fwd_launch(const TpParams<T>& P, cudaStream_t s) {
   if (P.n_rows == 0) return 0;
   tp_fwd_kernel<T, S><<<tp_grid_for(P.n_rows, false), tp_block_for(P.F), 0, s>>>(P);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 }
 template <typename T, typename S>
 int tp_bwd_launch(const TpBwdParams<T>& P, cudaStream_t s) {
   if (P.n_rows == 0) return 0;
   tp_bwd_kernel<T, S><<<tp_grid_for(P.n_rows, P.shared_w && P.g_w), tp_block_for(P.F), 0, s>>>(P);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 }
 template <typename T, typename S>
 int tp_dbwd_launch(const TpDbwdParams<T>& P, cudaStream_t s) {
   if (P.n_rows == 0) return 0;
   tp_dbwd_kernel<T, S><<<tp_grid_for(P.n_rows, P.shared_w && P.d_w), tp_block_for(P.F), 0, s>>>(P);
-  return cudaGetLastError() == cudaSuccess ? 0 : FC_ERR_LAUNCH;
+  return fc_check_launch();
 }
 
 #else

@@ -212,8 +212,8 @@ class InteractionLayer(nn.Module):
         aggregated = self.tp(node_feats, edge_attrs, weights, idx_i, idx_j)
         if out_nodes is not None:
             aggregated = aggregated[:out_nodes]
-        aggregated = aggregated / self.sqrt_avg_neighbors
-        out = self.linear_second(aggregated)
+        # aggregated / sqrt(avg_neighbors), folded into the scales of the linear map
+        out = self.linear_second(aggregated, input_scale=1.0 / self.sqrt_avg_neighbors)
         if self.skip_projection is not None:
             skip = self.skip_projection(residual)
             if self.in1_l_max == 0:

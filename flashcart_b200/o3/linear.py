@@ -72,15 +72,18 @@ class LinearLayer(nn.Module):
         for l in range(self.common_l_max + 1):
             self.weight.append(nn.Parameter(torch.randn(out_features, in_features * self.in_paths[l])))
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, input_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``input_scale`` (optional, 0-d tensor) multiplies the input: the map is linear, so
+        it is applied to the per-rank scales instead of to every element of ``x``."""
         if x.shape[-1] != self.in_dim:
             raise RuntimeError(f"Incorrect last dimension for x. Expected {self.in_dim}, got {x.shape[-1]}.")
         if x.dim() != 2:
             raise ValueError(f"x must be 2D [N, packed_dim], got shape {tuple(x.shape)}.")
         use_fp64, precision = get_linear_triton_kernel_options(x.dtype)
         weights = [w if w.dtype == x.dtype else w.to(x.dtype) for w in self.weight]
+        scale = self.scale if input_scale is None else self.scale * input_scale
         return torch.ops.flashcart.linear_fwd(x, weights, self.meta, self.out_dim, use_fp64, precision,
-                                              *self.meta_lists, self.scale)
+                                              *self.meta_lists, scale)
 
     def extra_repr(self) -> str:
         return (f"in_l_max={self.in_l_max}, out_l_max={self.out_l_max}, in_features={self.in_features}, "
