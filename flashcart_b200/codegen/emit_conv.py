@@ -43,6 +43,8 @@ from flashcart_b200.codegen import stf
 EC = 16       # edges per chunk of phase 1
 NPART = 8     # phase-1 work split (EC x NPART = 128 threads)
 RING = 4      # prefetch slots per CTA
+BUDGET = 32   # accumulators (sum of 2lo+1) per path group when a signature is split
+SINGLE_MAX = 40  # a signature with at most this many accumulators stays one group
 LAG = 2       # a slot is refilled once the edge LAG-1 before the current one is released
 
 
@@ -73,14 +75,22 @@ def _q(r: int, i: int) -> int:
     return r * r + i
 
 
+PURE_RANKS = True  # split a large signature at every change of in1 rank (measured fastest at C=128, l<=3)
+
+
 def make_groups(sig, budget: int) -> List[List[int]]:
     """Path groups (accumulator count, the sum of 2lo+1, within budget), filled in order of
-    decreasing in1 rank so that each group touches a contiguous range of in1 components."""
+    decreasing in1 rank so that each group touches a contiguous range of in1 components.
+    Small signatures stay one group: their per-edge work is too small to pay for a launch
+    and an edge walk per group."""
+    if sum(2 * o + 1 for (_, _, o) in sig.paths) <= SINGLE_MAX:
+        return [list(range(len(sig.paths)))]
     order = sorted(range(len(sig.paths)), key=lambda p: (-sig.paths[p][0], p))
     groups, cur, used = [], [], 0
     for p in order:
         n = 2 * sig.paths[p][2] + 1
-        if cur and used + n > budget:
+        rank_change = PURE_RANKS and cur and sig.paths[cur[-1]][0] != sig.paths[p][0]
+        if cur and (used + n > budget or rank_change):
             groups.append(sorted(cur))
             cur, used = [], 0
         cur.append(p)
@@ -320,8 +330,13 @@ def _phase1_loop(gs: GroupSlots, ind: str) -> List[str]:
 
 def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     """Shared-attribute convolution kernels of one signature (appended inside its namespace)."""
-    fwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, 40)]
-    bwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, 40)]
+    fwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, BUDGET)]
+    bwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, BUDGET)]
+
+    def min_ctas(gs: GroupSlots) -> int:
+        # __launch_bounds__(256, m): m = 3 caps a thread at 85 registers (5 CTAs of 128 threads
+        # per SM), enough for up to 32 accumulators; larger groups keep 128 registers (m = 2)
+        return 3 if gs.nacc <= BUDGET else 2
     d2p = 1
     while d2p < sig.d2:
         d2p *= 2
@@ -380,8 +395,11 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
                 w(f"  o[{acc_out[(p, a)]} * F] = acc[{k}];")
                 k += 1
         w("}")
+    w("template <int G> struct Fwd2MinCtas;")
+    for gi, gs in enumerate(fwd_groups):
+        w(f"template <> struct Fwd2MinCtas<{gi}> {{ static constexpr int value = {min_ctas(gs)}; }};")
     w("template <typename T, int G>")
-    w("__global__ void __launch_bounds__(256, 2) fwd2_kernel(TpParams<T> P) {")
+    w("__global__ void __launch_bounds__(256, Fwd2MinCtas<G>::value) fwd2_kernel(TpParams<T> P) {")
     w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
     for gi in range(len(fwd_groups)):
         w(f"  if constexpr (G == {gi}) fwd2_g{gi}<T>(P, fc_smem_raw);")
@@ -445,8 +463,11 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("  }")
         L.extend(_ring_drain("  "))
         w("}")
+    w("template <int G> struct Bwd2MinCtas;")
+    for gi, gs in enumerate(bwd_groups):
+        w(f"template <> struct Bwd2MinCtas<{gi}> {{ static constexpr int value = {min_ctas(gs)}; }};")
     w("template <typename T, int G>")
-    w("__global__ void __launch_bounds__(256, 2) bwd2_kernel(TpBwdParams<T> P) {")
+    w("__global__ void __launch_bounds__(256, Bwd2MinCtas<G>::value) bwd2_kernel(TpBwdParams<T> P) {")
     w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
     for gi in range(len(bwd_groups)):
         w(f"  if constexpr (G == {gi}) bwd2_g{gi}<T>(P, fc_smem_raw, BWD2_GROUPS > 1);")
