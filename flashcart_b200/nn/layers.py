@@ -64,16 +64,39 @@ class LinearLayer(nn.Module):
         self._meta = torch.zeros(1, 6, dtype=torch.int64)
         self._lists = ([0], [0], [0], [1], [in_features], [out_features])
 
-    def forward(self, x):
+    def forward(self, x, input_scale: Optional[torch.Tensor] = None):
+        """``input_scale`` (optional 0-d tensor) multiplies the input; the map is linear, so it
+        is applied to the layer's scale instead of to every element of ``x``."""
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.in_features)
         use_fp64, precision = o3.utils.get_linear_triton_kernel_options(x.dtype)
         w = self.weight if self.weight.dtype == x.dtype else self.weight.to(x.dtype)
+        scale = self.scale.reshape(1) if input_scale is None else self.scale.reshape(1) * input_scale
         y = torch.ops.flashcart.linear_fwd(x2, [w], self._meta, self.out_features, use_fp64, precision,
-                                           *self._lists, self.scale.reshape(1))
+                                           *self._lists, scale)
         if self.bias is not None:
             y = y + self.bias
         return y.reshape(*lead, self.out_features)
+
+
+class _MLP(nn.Sequential):
+    """Linear / rescaled-SiLU stack (the reference's ``nn.Sequential``, same state_dict keys).
+    The constant of each rescaled SiLU is handed to the next linear layer's scale instead of
+    being multiplied into the activations (one pass over the edge rows less per layer)."""
+
+    def forward(self, x):
+        mods = list(self)
+        pending = None
+        for k, m in enumerate(mods):
+            if isinstance(m, RescaledSiLULayer) and k + 1 < len(mods) and isinstance(mods[k + 1], LinearLayer):
+                x = F.silu(x)
+                pending = m.scale
+            elif isinstance(m, LinearLayer):
+                x = m(x, input_scale=pending)
+                pending = None
+            else:
+                x = m(x)
+        return x
 
 
 def _mlp(widths: List[int]) -> nn.Sequential:
@@ -81,7 +104,7 @@ def _mlp(widths: List[int]) -> nn.Sequential:
     for a, b in zip(widths[:-1], widths[1:]):
         layers.append(LinearLayer(a, b))
         layers.append(RescaledSiLULayer())
-    return nn.Sequential(*layers[:-1])
+    return _MLP(*layers[:-1])
 
 
 class RMSLayerNorm(nn.Module):
