@@ -11,7 +11,7 @@ xx, yy, zz, yz, xz, xy and ``virials = -stress * volume``.
 from __future__ import annotations
 
 from collections.abc import Mapping
-from typing import Any, Dict, List, Optional
+from typing import Callable, Any, Dict, List, Optional
 
 import torch
 import torch.nn as nn
@@ -143,6 +143,13 @@ class FlashCartPotential(nn.Module):
         """
         if not isinstance(graph, Mapping):
             raise TypeError(f"{self.__class__.__name__}.forward expects a tensor dictionary. Use predict() for Data.")
+        return self._forward_impl(graph)
+
+    def _forward_impl(self, graph: Dict[str, Any], n_out: Optional[int] = None,
+                      halo_fn: Optional[Callable[[torch.Tensor], torch.Tensor]] = None) -> torch.Tensor:
+        """Site energies; with ``n_out`` only the first ``n_out`` atoms are receivers (the
+        atoms a domain owns, the rest are its ghosts) and ``halo_fn`` maps the owned rows of
+        a layer's output to the ghost rows that the next layer reads."""
         edge_index = graph["edge_index"]
         batch = graph["batch"]
         atom_types = graph["atom_types"]
@@ -159,19 +166,23 @@ class FlashCartPotential(nn.Module):
         edge_feats = self.radial_basis(distances)
         envelope = self.cutoff_fn(distances)
         node_feats = self.embedding(atom_types)
+        own_types = atom_types if n_out is None else atom_types[:n_out]
         outputs = []
         for i, interaction in enumerate(self.interactions):
             feats = interaction(node_feats, edge_attrs, edge_feats, edge_index, envelope,
-                                atom_types=atom_types if not self.element_agnostic_interaction else None)
+                                atom_types=atom_types if not self.element_agnostic_interaction else None,
+                                out_nodes=n_out)
             if self.nonlinearity:
                 feats = self.nonlinearities[i](feats)
             if self.use_products:
-                node_feats = self.products[i](feats, None if self.element_agnostic_product else atom_types)
+                node_feats = self.products[i](feats, None if self.element_agnostic_product else own_types)
             else:
                 node_feats = feats
             outputs.append(node_feats[:, :self.n_hidden_feats])
+            if halo_fn is not None and i + 1 < len(self.interactions):
+                node_feats = torch.cat([node_feats, halo_fn(node_feats)], dim=0)
         energies = self.readout(outputs)
-        return self.scale_shift(energies, atom_types)
+        return self.scale_shift(energies, own_types)
 
     # ------------------------------------------------------------------ predict
 
@@ -238,6 +249,28 @@ class FlashCartPotential(nn.Module):
                 out["node_energies"] = out["node_energies"].detach()
                 out["energy"] = out["energy"].detach()
         return out
+
+    def predict_domain(self, graph, plan, group=None, compute_forces: bool = True,
+                       compute_stress: bool = True) -> Dict[str, torch.Tensor]:
+        """Energy, forces of the owned atoms and stress of one periodic cell evaluated by
+        atom-domain decomposition (one rank's share; every rank of ``group`` calls this with
+        its own ``plan`` from :func:`flashcart_b200.domain.build_plans`).
+
+        Positions of the owned atoms go through the virtual strain, then to the ranks that
+        hold them as ghosts (:class:`flashcart_b200.domain.HaloExchange`); the backward
+        returns the ghosts' position and feature gradients to their owners, so ``forces``
+        are complete for the owned atoms. ``energy`` and ``stress`` are summed over ranks.
+        """
+        from flashcart_b200.domain import evaluate_domain
+
+        frozen = [p for p in self.parameters() if p.requires_grad]
+        for p in frozen:
+            p.requires_grad_(False)
+        try:
+            return evaluate_domain(self._forward_impl, graph, plan, group, compute_forces, compute_stress)
+        finally:
+            for p in frozen:
+                p.requires_grad_(True)
 
     # ------------------------------------------------------------------ config
 
