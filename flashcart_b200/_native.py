@@ -27,6 +27,7 @@ FC_DEV_UNSORTED = 2
 FC_DEV_TIMEOUT = 4
 FC_F32 = 0
 FC_F64 = 1
+FC_BF16 = 2
 FC_PREC_IEEE = 0
 FC_PREC_TF32 = 1
 FC_MAX_L = 3
@@ -34,7 +35,7 @@ FC_MAX_L = 3
 EXPORTED_SYMBOLS = (
     "fc_version", "fc_last_error", "fc_build_rowptr", "fc_tp_num_paths", "fc_tp_out_dim",
     "fc_tp_fwd", "fc_tp_bwd", "fc_tp_dbwd", "fc_irreps_fwd", "fc_irreps_bwd", "fc_irreps_dbwd",
-    "fc_linear_fwd", "fc_linear_bwd", "fc_tp_conv_fwd_noalloc",
+    "fc_linear_fwd", "fc_linear_bwd", "fc_tp_conv_fwd_noalloc", "fc_newton_schulz",
 )
 
 
@@ -98,6 +99,8 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_tp_conv_fwd_noalloc.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P]
     lib.fc_linear_bwd.restype = ctypes.c_int
     lib.fc_linear_bwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P, _P]
+    lib.fc_newton_schulz.restype = ctypes.c_int
+    lib.fc_newton_schulz.argtypes = [_P, _I32, _I64, _I32, _I32, _P, _I32, _P, _I32, ctypes.c_float, _P, _P, _P]
     return lib
 
 

@@ -296,6 +296,14 @@ static int noalloc_rowptr(int64_t** out) {
 
 using namespace fc;
 
+#ifndef FC_HOST_EMU
+namespace fc {
+int ns_orthogonalize(const void* update, int dtype_in, int64_t batch, int rows_in, int cols_in, const float* coeffs,
+                     int steps, const float* polish, int polish_steps, float eps, void* out, int32_t* status,
+                     cudaStream_t s);
+}
+#endif
+
 extern "C" {
 
 const char* fc_version(void) {
@@ -558,6 +566,29 @@ int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* 
   // the workspace is fully rewritten by this call, so nothing needs clearing
   if (int rc = fc_build_rowptr(idx_i, n_edges, n_nodes, rowptr, status, stream)) return rc;
   return fc_tp_fwd(desc, in1, in2, weights, rowptr, idx_j, n_nodes, n_nodes, out, status, stream);
+}
+
+// Muon Newton-Schulz orthogonalisation (see the header).
+int fc_newton_schulz(const void* update, int dtype, int64_t batch, int rows, int cols, const float* coeffs,
+                     int steps, const float* polish, int polish_steps, float eps, void* out, int32_t* status,
+                     fc_stream_t stream) {
+  if (batch < 0 || rows <= 0 || cols <= 0 || steps < 0 || polish_steps < 0)
+    return fail(FC_ERR_INVALID, "fc_newton_schulz: invalid sizes");
+  if (dtype != FC_F32 && dtype != FC_BF16) return fail(FC_ERR_INVALID, "fc_newton_schulz: dtype must be f32 or bf16");
+  if (batch == 0) return FC_OK;
+  if (!update || !out || !coeffs || (polish_steps > 0 && !polish))
+    return fail(FC_ERR_INVALID, "fc_newton_schulz: null pointer");
+  if (rows % 8 != 0 || cols % 8 != 0)
+    return fail(FC_ERR_UNSUPPORTED, "fc_newton_schulz: rows and cols must be multiples of 8 (got %d x %d)", rows,
+                cols);
+#ifdef FC_HOST_EMU
+  (void)eps; (void)status; (void)stream;
+  return fail(FC_ERR_UNSUPPORTED, "fc_newton_schulz: tensor-core kernel only");
+#else
+  return launch_status(ns_orthogonalize(update, dtype, batch, rows, cols, coeffs, steps, polish, polish_steps, eps,
+                                        out, status, (cudaStream_t)stream),
+                       "fc_newton_schulz");
+#endif
 }
 
 }  // extern "C"

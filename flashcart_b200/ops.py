@@ -711,3 +711,35 @@ def _linear_bwd_backward(ctx, v_gx, v_gw):
 
 linear_fwd.register_autograd(_linear_backward, setup_context=_linear_setup)
 linear_bwd.register_autograd(_linear_bwd_backward, setup_context=_linear_bwd_setup)
+
+
+# --------------------------------------------------------------------------- Muon Newton-Schulz
+
+@torch.library.custom_op("flashcart::newton_schulz", mutates_args=())
+def newton_schulz(update: Tensor, coeffs: List[float], steps: int, polish: List[float], polish_steps: int,
+                  eps: float) -> Tensor:
+    """Batched Newton-Schulz orthogonalisation in bf16 on the tensor cores
+    (reference ``training/muon.py:27-61`` ``_batched_newtonschulz``): ``update`` is
+    ``(batch, rows, cols)`` float32 or bfloat16; returns bfloat16 of the same shape."""
+    _require_cuda(update)
+    if update.dim() != 3:
+        raise ValueError(f"update must be (batch, rows, cols), got shape {tuple(update.shape)}")
+    if update.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"update must be float32 or bfloat16, got {update.dtype}")
+    lib = N.lib()
+    u = update.contiguous()
+    out = torch.empty(u.shape, dtype=torch.bfloat16, device=u.device)
+    cf = (ctypes.c_float * 3)(*[float(v) for v in coeffs])
+    pl = (ctypes.c_float * 3)(*[float(v) for v in (list(polish) + [0.0, 0.0, 0.0])[:3]])
+    code = N.FC_F32 if u.dtype == torch.float32 else N.FC_BF16
+    with _timed("newton_schulz", 4 * (int(steps) + int(polish_steps)) + 2, _nbytes(u, out)):
+        rc = lib.fc_newton_schulz(_p(u), code, u.shape[0], u.shape[1], u.shape[2], cf, int(steps), pl,
+                                  int(polish_steps), float(eps), _p(out),
+                                  ctypes.c_void_p(status_word(u.device).data_ptr()), _stream(u.device))
+    _after(lib, rc, "fc_newton_schulz", u.device)
+    return out
+
+
+@newton_schulz.register_fake
+def _(update, coeffs, steps, polish, polish_steps, eps):
+    return torch.empty(update.shape, dtype=torch.bfloat16, device=update.device)

@@ -50,6 +50,7 @@ typedef void* fc_stream_t;
 /* dtypes */
 #define FC_F32 0
 #define FC_F64 1
+#define FC_BF16 2  /* fc_newton_schulz input only */
 
 /* linear-map arithmetic */
 #define FC_PREC_IEEE 0 /* fp32-accurate: fp64 FMA, or fp32 on tensor cores as 3xTF32 (hi*hi+hi*lo+lo*hi) */
@@ -117,6 +118,18 @@ int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* 
                            const void* weights, const int64_t* idx_i, const int64_t* idx_j,
                            int64_t n_nodes, int64_t n_edges, void* out, int32_t* status,
                            fc_stream_t stream);
+
+/* Newton-Schulz orthogonalisation of a batch of Muon updates on the tensor cores (bf16).
+ * Replaces _batched_newtonschulz (training/muon.py:27-61). update: (batch, rows, cols),
+ * row-major, dtype FC_F32 or FC_BF16; out: (batch, rows, cols) bf16. A tall matrix
+ * (rows > cols) is iterated transposed, as in the reference. X <- X / max(||X||_F, eps),
+ * then `steps` iterations with coeffs = (a, b, c) and `polish_steps` with polish = (a, b, c):
+ * G = X X^T, U = b G + c G G, X = a X + U X, each product in fp32 and rounded to bf16.
+ * min(rows, cols) and max(rows, cols) must be multiples of 8. Uses a stream-ordered
+ * workspace of 2 bytes x batch x (2 rows cols + 2 min(rows, cols)^2). */
+int fc_newton_schulz(const void* update, int dtype, int64_t batch, int rows, int cols, const float* coeffs,
+                     int steps, const float* polish, int polish_steps, float eps, void* out, int32_t* status,
+                     fc_stream_t stream);
 
 /* Backward. Replaces flashcart::tp_bwd (o3/_tensor_product.py:588-787).
  * grad_in1 / grad_in2 / grad_weights may be NULL (not requested). n_in2_rows = rows
