@@ -274,6 +274,19 @@ class FlashCartPotential(nn.Module):
 
     # ------------------------------------------------------------------ config
 
+    def non_decayable_parameters(self):
+        """Child-layer hooks and the element embedding (reference ``model/flashcart.py:366-382``)."""
+        from flashcart_b200.nn.layers import iter_child_special_parameters
+
+        yield from iter_child_special_parameters(self, "non_decayable_parameters")
+        yield from self.embedding.parameters()
+
+    def non_muon_parameters(self):
+        from flashcart_b200.nn.layers import iter_child_special_parameters
+
+        yield from iter_child_special_parameters(self, "non_muon_parameters")
+        yield from self.embedding.parameters()
+
     def to_model_config(self) -> Dict[str, Any]:
         return {
             "elements": list(self.elements), "r_max": self.r_max, "r_min": self.r_min,

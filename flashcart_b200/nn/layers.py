@@ -8,7 +8,7 @@ weights); every equivariant operation (tensor products, linear maps) goes throug
 radial / readout MLPs and gates (as one-rank linear maps on the tensor cores).
 """
 
-from typing import List, Optional
+from typing import Iterator, List, Optional
 
 import torch
 import torch.nn as nn
@@ -17,7 +17,40 @@ import torch.nn.functional as F
 from flashcart_b200 import o3
 
 
-class RescaledSiLULayer(nn.Module):
+def iter_child_special_parameters(module: nn.Module, method_name: str) -> Iterator[nn.Parameter]:
+    """Each parameter reported by the ``method_name`` hook of any nested child (not the
+    module itself), once (reference ``utils/parameter_groups.py:6-30``). The hooks route
+    parameters away from Muon / weight decay in the optimizer factory."""
+    seen = set()
+    for child in module.modules():
+        if child is module:
+            continue
+        method = getattr(child, method_name, None)
+        if method is None:
+            continue
+        for p in method():
+            if id(p) not in seen:
+                seen.add(id(p))
+                yield p
+
+
+class _NoSpecialParameters:
+    def non_decayable_parameters(self) -> Iterator[nn.Parameter]:
+        return iter(())
+
+    def non_muon_parameters(self) -> Iterator[nn.Parameter]:
+        return iter(())
+
+
+class _ChildSpecialParameters:
+    def non_decayable_parameters(self) -> Iterator[nn.Parameter]:
+        yield from iter_child_special_parameters(self, "non_decayable_parameters")
+
+    def non_muon_parameters(self) -> Iterator[nn.Parameter]:
+        yield from iter_child_special_parameters(self, "non_muon_parameters")
+
+
+class RescaledSiLULayer(_NoSpecialParameters, nn.Module):
     """scale * silu(x); default scale 1/sqrt(E[silu(z)^2]), z ~ N(0,1) (reference ``nn/layers.py:12-44``)."""
 
     def __init__(self, scale: Optional[float] = None):
@@ -29,7 +62,7 @@ class RescaledSiLULayer(nn.Module):
         return self.scale * F.silu(x)
 
 
-class RescaledSigmoidLayer(nn.Module):
+class RescaledSigmoidLayer(_NoSpecialParameters, nn.Module):
     """scale * sigmoid(x); default scale 1/sqrt(E[sigmoid(z)^2]) (reference ``nn/layers.py:47-79``)."""
 
     def __init__(self, scale: Optional[float] = None):
@@ -79,6 +112,15 @@ class LinearLayer(nn.Module):
         return y.reshape(*lead, self.out_features)
 
 
+def _linear_non_decayable(self) -> Iterator[nn.Parameter]:
+    if self.bias is not None:
+        yield self.bias
+
+
+LinearLayer.non_decayable_parameters = _linear_non_decayable
+LinearLayer.non_muon_parameters = _linear_non_decayable
+
+
 class _MLP(nn.Sequential):
     """Linear / rescaled-SiLU stack (the reference's ``nn.Sequential``, same state_dict keys).
     The constant of each rescaled SiLU is handed to the next linear layer's scale instead of
@@ -114,6 +156,12 @@ class RMSLayerNorm(nn.Module):
     product (shared unit weights), weighted 1/((2l+1)(l_max+1)) and averaged over
     channels; per-rank gains (and an l=0 bias with centering) follow.
     """
+
+    def non_decayable_parameters(self) -> Iterator[nn.Parameter]:
+        yield from self.parameters()
+
+    def non_muon_parameters(self) -> Iterator[nn.Parameter]:
+        yield from self.parameters()
 
     def __init__(self, l_max: int, n_features: int, eps: float = 1.0e-12, affine: bool = True,
                  centering: bool = False, use_triton: bool = False):
@@ -174,6 +222,15 @@ class InteractionLayer(nn.Module):
     radial_mlp(basis * envelope) -> / sqrt(avg_neighbors) -> linear_second
     (+ skip projection) (-> RMS layer norm).
     """
+
+    def non_decayable_parameters(self) -> Iterator[nn.Parameter]:
+        yield from iter_child_special_parameters(self, "non_decayable_parameters")
+
+    def non_muon_parameters(self) -> Iterator[nn.Parameter]:
+        yield from iter_child_special_parameters(self, "non_muon_parameters")
+        if self.emb_i is not None:
+            yield from self.emb_i.parameters()
+            yield from self.emb_j.parameters()
 
     def __init__(self, in1_l_max: int, in2_l_max: int, out_l_max: int, in1_features: int, out_features: int,
                  n_radial: int, hidden_radial: Optional[List[int]] = None, n_elements: Optional[int] = None,
@@ -253,7 +310,7 @@ class InteractionLayer(nn.Module):
         self.sqrt_avg_neighbors.fill_(float(avg_neighbors) ** 0.5)
 
 
-class EquivariantGatedLayer(nn.Module):
+class EquivariantGatedLayer(_ChildSpecialParameters, nn.Module):
     """Gated residual update, identity at initialisation (reference ``nn/layers.py:543-648``)."""
 
     def __init__(self, l_max: int, in_features: int, hidden_features: Optional[int] = None,
@@ -293,7 +350,7 @@ class EquivariantGatedLayer(nn.Module):
         return node_feats + self.output_linear(torch.cat(parts, dim=-1))
 
 
-class IrrepsSelector(nn.Module):
+class IrrepsSelector(_NoSpecialParameters, nn.Module):
     """Keep the leading rank blocks up to out_l_max (reference ``nn/layers.py:651-698``)."""
 
     def __init__(self, in_l_max: int, out_l_max: int, in_features: int, in_paths: Optional[List[int]] = None):
@@ -313,6 +370,17 @@ class IrrepsSelector(nn.Module):
 
 class ProductPathWeights(nn.Module):
     """Per-path multiplicative weights 1 + delta (reference ``nn/layers.py:701-765``)."""
+
+    def non_decayable_parameters(self) -> Iterator[nn.Parameter]:
+        return iter(())
+
+    def non_muon_parameters(self) -> Iterator[nn.Parameter]:
+        if not self.learnable:
+            return
+        if self.element_dependent:
+            yield from self.delta.parameters()
+        else:
+            yield self.delta
 
     def __init__(self, n_weights: int, n_elements: Optional[int] = None, learnable: bool = False):
         super().__init__()
@@ -338,7 +406,7 @@ class ProductPathWeights(nn.Module):
         return 1.0 + self.delta
 
 
-class ProductLayer(nn.Module):
+class ProductLayer(_ChildSpecialParameters, nn.Module):
     """Repeated node-local products up to the correlation order (reference ``nn/layers.py:768-1018``)."""
 
     def __init__(self, in_l_max: int, out_l_max: int, in_features: int, n_elements: Optional[int] = None,
@@ -432,6 +500,14 @@ class ProductLayer(nn.Module):
 class EnergyReadoutLayer(nn.Module):
     """MLP on the scalar channels of every layer (reference ``nn/layers.py:1021-1077``)."""
 
+    def non_decayable_parameters(self) -> Iterator[nn.Parameter]:
+        yield from iter_child_special_parameters(self, "non_decayable_parameters")
+
+    def non_muon_parameters(self) -> Iterator[nn.Parameter]:
+        # the last (single-output) layer goes to AdamW (reference nn/layers.py:1068-1070)
+        yield from iter_child_special_parameters(self, "non_muon_parameters")
+        yield self.readout_mlp[-1].weight
+
     def __init__(self, in_features: int, n_layers: int, hidden_readout: Optional[List[int]] = None):
         super().__init__()
         self.in_features = in_features
@@ -447,7 +523,7 @@ class EnergyReadoutLayer(nn.Module):
         return self.readout_mlp(scalars).squeeze(-1)
 
 
-class ScaleShiftEnergyLayer(nn.Module):
+class ScaleShiftEnergyLayer(_NoSpecialParameters, nn.Module):
     """Per-element energy scale; shifts stored for calculators (reference ``nn/layers.py:1080-1138``)."""
 
     def __init__(self, n_elements: int):
