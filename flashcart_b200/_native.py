@@ -81,7 +81,7 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_tp_out_dim.restype = ctypes.c_int64
     lib.fc_tp_out_dim.argtypes = [ctypes.POINTER(TpDesc)]
     lib.fc_tp_fwd.restype = ctypes.c_int
-    lib.fc_tp_fwd.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P]
+    lib.fc_tp_fwd.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P]
     lib.fc_tp_bwd.restype = ctypes.c_int
     lib.fc_tp_bwd.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P]
     lib.fc_tp_dbwd.restype = ctypes.c_int

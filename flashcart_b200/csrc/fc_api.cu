@@ -340,10 +340,10 @@ int64_t fc_tp_out_dim(const fc_tp_desc* desc) {
 }
 
 int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const void* weights, const int64_t* rowptr,
-              const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows, void* out, int32_t* status,
-              fc_stream_t stream) {
+              const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows, int64_t n_in2_rows, void* out,
+              int32_t* status, fc_stream_t stream) {
   if (int rc = check_desc(desc)) return rc;
-  if (n_out_rows < 0 || n_in1_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_fwd: negative size");
+  if (n_out_rows < 0 || n_in1_rows < 0 || n_in2_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_fwd: negative size");
   if (rowptr == nullptr && n_out_rows != n_in1_rows)
     return fail(FC_ERR_INVALID, "fc_tp_fwd: dense product needs n_out_rows == n_in1_rows");
   if (rowptr != nullptr && idx_j == nullptr) return fail(FC_ERR_INVALID, "fc_tp_fwd: convolution needs idx_j");
@@ -367,6 +367,7 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
   p.in1 = (const double*)in1; p.in2 = (const double*)in2; p.w = (const double*)weights; p.out = (double*)out;
   return launch_status(v2 ? sig->table->fwd2_f64(p, s) : sig->table->fwd_f64(p, s), "fc_tp_fwd");
 }
+
 
 int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2, const void* weights,
               const int64_t* rowptr, const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows,
@@ -565,7 +566,7 @@ int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* 
   if (int rc = noalloc_rowptr(&rowptr)) return rc;
   // the workspace is fully rewritten by this call, so nothing needs clearing
   if (int rc = fc_build_rowptr(idx_i, n_edges, n_nodes, rowptr, status, stream)) return rc;
-  return fc_tp_fwd(desc, in1, in2, weights, rowptr, idx_j, n_nodes, n_nodes, out, status, stream);
+  return fc_tp_fwd(desc, in1, in2, weights, rowptr, idx_j, n_nodes, n_nodes, n_edges, out, status, stream);
 }
 
 // Muon Newton-Schulz orthogonalisation (see the header).

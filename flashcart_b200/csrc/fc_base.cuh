@@ -38,6 +38,9 @@ inline cudaError_t& fc_noted_error() {
   static thread_local cudaError_t e = cudaSuccess;
   return e;
 }
+// Stream-ordered device workspace from the library's per-device pool (pool.cu).
+int fc_pool_alloc(void** ptr, size_t bytes, cudaStream_t s);
+int fc_pool_free(void* ptr, cudaStream_t s);
 // Launcher epilogue: FC_OK, or FC_ERR_LAUNCH with the CUDA error noted.
 inline int fc_check_launch() {
   const cudaError_t e = cudaGetLastError();

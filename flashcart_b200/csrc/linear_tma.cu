@@ -513,7 +513,6 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 struct DeviceState {
   bool ready = false;
   int sms = 0;
-  cudaMemPool_t pool = nullptr;
   bool attr_set[3][2] = {};
 };
 
@@ -536,13 +535,6 @@ static DeviceState* device_state(int dev) {
   DeviceState& d = g_dev[dev];
   if (d.ready) return &d;
   if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return nullptr;
-  cudaMemPoolProps props = {};
-  props.allocType = cudaMemAllocationTypePinned;
-  props.location.type = cudaMemLocationTypeDevice;
-  props.location.id = dev;
-  if (cudaMemPoolCreate(&d.pool, &props) != cudaSuccess) return nullptr;
-  uint64_t keep = ~uint64_t(0);  // the pool keeps its memory for reuse by later calls of this process
-  cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
   d.ready = true;
   return &d;
 }
@@ -615,7 +607,7 @@ int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStrea
 
   float* ws = nullptr;
   const size_t wbytes = (size_t)a.N * kp * 4 * (split ? 2 : 1);
-  if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), wbytes, ds->pool, s) != cudaSuccess) return FC_ERR_LAUNCH;
+  if (fc_pool_alloc(reinterpret_cast<void**>(&ws), wbytes, s)) return FC_ERR_LAUNCH;
   float* bhi = ws;
   float* blo = split ? ws + (size_t)a.N * kp : nullptr;
   int rc = 0;
@@ -652,7 +644,7 @@ int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStrea
                  : launch<256, false>(ma, mbh, mbl, mc, mpf, args, ds, grid, s);
   }
   // stream-ordered: the workspace returns to the pool after the kernels that read it
-  if (cudaFreeAsync(ws, s) != cudaSuccess && rc == 0) rc = FC_ERR_LAUNCH;
+  if (fc_pool_free(ws, s) && rc == 0) rc = FC_ERR_LAUNCH;
   return rc;
 }
 

@@ -235,14 +235,15 @@ def tp_fwd(in1: Tensor, in2: Tensor, weights: Tensor, idx_i: Optional[Tensor], i
         nb = _nbytes(in1, in2, weights, out, idx_j, rowptr)
         with _timed(f"tp_fwd_conv_{in1_l_max}{in2_l_max}{out_l_max}", 1, nb):
             rc = lib.fc_tp_fwd(ctypes.byref(desc), _p(in1), _p(in2), _p(weights),
-                               ctypes.c_void_p(rowptr.data_ptr()), _p(idx_j), n_out, n_out, _p(out), status, stream)
+                               ctypes.c_void_p(rowptr.data_ptr()), _p(idx_j), n_out, n_out, in2.shape[0], _p(out),
+                               status, stream)
     else:
         if in1.shape[0] != in2.shape[0]:
             raise ValueError("idx_i and idx_j must be provided when in1 and in2 have different batch sizes. "
                              f"Got in1_batch={in1.shape[0]}, in2_batch={in2.shape[0]}.")
         with _timed(f"tp_fwd_dense_{in1_l_max}{in2_l_max}{out_l_max}", 1, _nbytes(in1, in2, weights, out)):
             rc = lib.fc_tp_fwd(ctypes.byref(desc), _p(in1), _p(in2), _p(weights), None, None, n_out, n_out,
-                               _p(out), status, stream)
+                               n_out, _p(out), status, stream)
     _after(lib, rc, "fc_tp_fwd", dev)
     return out
 

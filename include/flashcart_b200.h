@@ -95,12 +95,12 @@ int64_t fc_tp_out_dim(const fc_tp_desc* desc);
  * Convolution when rowptr != NULL: out[i] = sum over edges e of receiver i of
  *   W[e] (.) TP(in1[idx_j[e]], in2[e]);  in2/weights have one row per edge,
  *   rowptr from fc_build_rowptr, n_out_rows = number of receivers, n_in1_rows =
- *   rows of in1 (idx_j range).
+ *   rows of in1 (idx_j range), n_in2_rows = edges (rows of in2 and weights).
  * Dense when rowptr == NULL: row r of out from row r of in1, in2 and weights;
- *   n_out_rows = n_in1_rows = rows. */
+ *   n_out_rows = n_in1_rows = n_in2_rows = rows. */
 int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const void* weights,
               const int64_t* rowptr, const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows,
-              void* out, int32_t* status, fc_stream_t stream);
+              int64_t n_in2_rows, void* out, int32_t* status, fc_stream_t stream);
 
 /* Allocation-free convolution forward. No counterpart in the reference: an extra
  * entry point for callers that cannot allocate device memory themselves, e.g. code

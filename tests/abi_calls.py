@@ -45,7 +45,7 @@ def tp_fwd(lib, meta, in1, in2, w, idx_i=None, idx_j=None, status=None):
     n = in1.shape[0]
     out = torch.full((n, odim), float("nan"), dtype=in1.dtype, device=in1.device)
     rp = rowptr(lib, idx_i, n, status) if idx_i is not None else None
-    rc = lib.fc_tp_fwd(ctypes.byref(d), p(in1), p(in2), p(w), p(rp), p(idx_j), n, n, p(out), p(status),
+    rc = lib.fc_tp_fwd(ctypes.byref(d), p(in1), p(in2), p(w), p(rp), p(idx_j), n, n, in2.shape[0], p(out), p(status),
                        stream_of(in1))
     N.check(lib, rc, "fc_tp_fwd")
     return out
