@@ -43,6 +43,9 @@ from flashcart_b200.codegen import stf
 EC = 16       # edges per chunk of phase 1
 NPART = 8     # phase-1 work split (EC x NPART = 128 threads)
 RING = 4      # prefetch slots per CTA
+# Forward gathers: a signature kept as one path group streams its edges through the ring of
+# bulk copies; a signature split into several groups loads sender rows and weights per
+# thread (coalesced over channels), which measured faster there (C = 128, l <= 3).
 BUDGET = 32   # accumulators (sum of 2lo+1) per path group when a signature is split
 SINGLE_MAX = 40  # a signature with at most this many accumulators stays one group
 LAG = 2       # a slot is refilled once the edge LAG-1 before the current one is released
@@ -178,7 +181,7 @@ def _path_mload(gs: GroupSlots, p: int, ind: str) -> List[str]:
     return L
 
 
-def _fwd_group_body(gs: GroupSlots, ind: str) -> List[str]:
+def _fwd_group_body(gs: GroupSlots, ind: str, direct: bool = False) -> List[str]:
     sig = gs.sig
     L = []
     acc_base = 0
@@ -187,7 +190,8 @@ def _fwd_group_body(gs: GroupSlots, ind: str) -> List[str]:
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
         L.extend(_path_mload(gs, p, ind + "  "))
-        L.append(f"{ind}  const T wp = sw[{gs.w_pos[p]} * F];")
+        wsrc = f"fc_ldg(wr + {p} * F)" if direct else f"sw[{gs.w_pos[p]} * F]"
+        L.append(f"{ind}  const T wp = {wsrc};")
         for a in range(2 * o + 1):
             terms = [f"mv[{gs.index[(p, a, i)] - s0}]*x1[{_q(r1, i) - gs.x_lo}]" for i in range(2 * r1 + 1)
                      if (p, a, i) in gs.index]
@@ -332,6 +336,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     """Shared-attribute convolution kernels of one signature (appended inside its namespace)."""
     fwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, BUDGET)]
     bwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, BUDGET)]
+    FWD_RING = len(fwd_groups) == 1
 
     def min_ctas(gs: GroupSlots) -> int:
         # __launch_bounds__(256, m): m = 3 caps a thread at 85 registers (5 CTAs of 128 threads
@@ -343,12 +348,15 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     L = []
     w = L.append
     w(f"// ---- shared-attribute convolution: {len(fwd_groups)} forward / {len(bwd_groups)} backward path groups")
-    w(f"constexpr int FWD2_GROUPS = {len(fwd_groups)}, BWD2_GROUPS = {len(bwd_groups)};")
+    w(f"constexpr int BWD2_GROUPS = {len(bwd_groups)};")
     # shared memory per group (elements of T, F-dependent ring) + mbarriers / abort flag
     for kind, groups, extra in (("fwd", fwd_groups, 0), ("bwd", bwd_groups, EC * d2p)):
         w(f"inline size_t {kind}2_smem(int g, int F, size_t es) {{")
         w("  switch (g) {")
         for gi, gs in enumerate(groups):
+            if kind == "fwd" and not FWD_RING:
+                w(f"    case {gi}: return (size_t){gs.nmp * EC} * es;")
+                continue
             w(f"    case {gi}: return (size_t)({gs.nmp * EC} + {RING} * ({gs.x_n} + {len(gs.paths)}) * F + {extra}) * es"
               f" + {2 * RING * 8 + 16};")
         w("  }")
@@ -365,28 +373,46 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("template <typename T>")
         w(f"__device__ __forceinline__ void fwd2_g{gi}(const TpParams<T>& P, unsigned char* smem) {{")
         w("  const int64_t row = blockIdx.x;")
-        L.extend(_ring_setup(gs, "0", "  "))
-        L.extend(_issue_fn(gs, "  "))
+        if FWD_RING:
+            L.extend(_ring_setup(gs, "0", "  "))
+            L.extend(_issue_fn(gs, "  "))
+        else:
+            w(f"  constexpr int XLO = {gs.x_lo}, XN = {gs.x_n}, NMP = {gs.nmp};")
+            w("  const int F = P.F, c = threadIdx.x;")
+            w("  T* sm = reinterpret_cast<T*>(smem);")
+            w("  const int64_t e0 = P.rowptr[row], ne_all = P.rowptr[row + 1] - e0;")
         w(f"  T acc[{gs.nacc}];")
         w(f"  for (int q = 0; q < {gs.nacc}; ++q) acc[q] = T(0);")
         w(f"  for (int64_t eb = 0; eb < ne_all; eb += {EC}) {{")
         w(f"    const int ne = (int)min((int64_t){EC}, ne_all - eb);")
         L.extend(_phase1_loop(gs, "    "))
         w("    for (int k = 0; k < ne; ++k) {")
-        L.extend(_ring_edge_begin("      "))
-        w("      if (valid) {")
-        w("        const T* sx = ring + s * SLOT + c;")
-        w("        T x1[XN];")
-        w("        for (int q = 0; q < XN; ++q) x1[q] = sx[q * F];")
-        w("        const T* sw = sx + XN * F;")
-        w("        const T* m = sm + k * NMP;")
-        L.extend(_fwd_group_body(gs, "        "))
-        w("      }")
-        L.extend(_ring_edge_end("      "))
+        if FWD_RING:
+            L.extend(_ring_edge_begin("      "))
+            w("      if (valid) {")
+            w("        const T* sx = ring + s * SLOT + c;")
+            w("        T x1[XN];")
+            w("        for (int q = 0; q < XN; ++q) x1[q] = sx[q * F];")
+            w("        const T* sw = sx + XN * F;")
+            w("        const T* m = sm + k * NMP;")
+            L.extend(_fwd_group_body(gs, "        "))
+            w("      }")
+            L.extend(_ring_edge_end("      "))
+        else:
+            w("      const int64_t e = e0 + eb + k;")
+            w("      const int64_t j = P.idx_j[e];")
+            w("      if ((uint64_t)j >= (uint64_t)P.n_in1) { if (c == 0) fc_flag(P.status, FC_DEV_BAD_INDEX); continue; }")
+            w("      const T* __restrict__ a1 = P.in1 + j * (int64_t)(D1 * F) + XLO * F + c;")
+            w("      T x1[XN];")
+            w("      for (int q = 0; q < XN; ++q) x1[q] = fc_ldg(a1 + q * F);")
+            w("      const T* __restrict__ wr = P.w + e * (int64_t)(NP * F) + c;")
+            w("      const T* m = sm + k * NMP;")
+            L.extend(_fwd_group_body(gs, "      ", direct=True))
         w("    }")
         w("    __syncthreads();")
         w("  }")
-        L.extend(_ring_drain("  "))
+        if FWD_RING:
+            L.extend(_ring_drain("  "))
         w("  T* __restrict__ o = P.out + row * (int64_t)(OUT_COMPS * F) + c;")
         k = 0
         for p in gs.paths:
