@@ -43,6 +43,8 @@ from flashcart_b200.codegen import stf
 EC = 16       # edges per chunk of phase 1
 NPART = 8     # phase-1 work split (EC x NPART = 128 threads)
 RING = 4      # prefetch slots per CTA
+BWD_RING_DEFAULT = True  # backward gathers through the prefetch ring (per-thread gathers measured 10% slower)
+
 # Forward gathers: a signature kept as one path group streams its edges through the ring of
 # bulk copies; a signature split into several groups loads sender rows and weights per
 # thread (coalesced over channels), which measured faster there (C = 128, l <= 3).
@@ -202,7 +204,7 @@ def _fwd_group_body(gs: GroupSlots, ind: str, direct: bool = False) -> List[str]
     return L
 
 
-def _bwd_group_body(gs: GroupSlots, ind: str) -> List[str]:
+def _bwd_group_body(gs: GroupSlots, ind: str, direct: bool = False) -> List[str]:
     sig = gs.sig
     L = []
     base = 0
@@ -212,7 +214,8 @@ def _bwd_group_body(gs: GroupSlots, ind: str) -> List[str]:
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
         L.extend(_path_mload(gs, p, ind + "  "))
-        L.append(f"{ind}  const T wp = sw[{gs.w_pos[p]} * F];")
+        wsrc = f"fc_ldg(wr + {p} * F)" if direct else f"sw[{gs.w_pos[p]} * F]"
+        L.append(f"{ind}  const T wp = {wsrc};")
         hs = []
         for i in range(2 * r1 + 1):
             terms = [f"g[{base + a}]*mv[{gs.index[(p, a, i)] - s0}]" for a in range(2 * o + 1)
@@ -337,6 +340,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     fwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, BUDGET)]
     bwd_groups = [GroupSlots(sig, g) for g in make_groups(sig, BUDGET)]
     FWD_RING = len(fwd_groups) == 1
+    BWD_RING = BWD_RING_DEFAULT
 
     def min_ctas(gs: GroupSlots) -> int:
         # __launch_bounds__(256, m): m = 3 caps a thread at 85 registers (5 CTAs of 128 threads
@@ -354,8 +358,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w(f"inline size_t {kind}2_smem(int g, int F, size_t es) {{")
         w("  switch (g) {")
         for gi, gs in enumerate(groups):
-            if kind == "fwd" and not FWD_RING:
-                w(f"    case {gi}: return (size_t){gs.nmp * EC} * es;")
+            if (kind == "fwd" and not FWD_RING) or (kind == "bwd" and not BWD_RING):
+                w(f"    case {gi}: return (size_t)({gs.nmp * EC} + {extra}) * es;")
                 continue
             w(f"    case {gi}: return (size_t)({gs.nmp * EC} + {RING} * ({gs.x_n} + {len(gs.paths)}) * F + {extra}) * es"
               f" + {2 * RING * 8 + 16};")
@@ -436,9 +440,16 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w(f"__device__ __forceinline__ void bwd2_g{gi}(const TpBwdParams<T>& P, unsigned char* smem, bool multi) {{")
         w("  const bool NEED_1 = P.g_in1 != nullptr, NEED_2 = P.g_in2 != nullptr, NEED_W = P.g_w != nullptr;")
         w("  const int64_t row = blockIdx.x;")
-        L.extend(_ring_setup(gs, str(EC * d2p), "  "))
-        w("  T* gsm = extra;  // [EC][D2P] grad_in2 partial sums")
-        L.extend(_issue_fn(gs, "  "))
+        if BWD_RING:
+            L.extend(_ring_setup(gs, str(EC * d2p), "  "))
+            w("  T* gsm = extra;  // [EC][D2P] grad_in2 partial sums")
+            L.extend(_issue_fn(gs, "  "))
+        else:
+            w(f"  constexpr int XLO = {gs.x_lo}, XN = {gs.x_n}, NMP = {gs.nmp};")
+            w("  const int F = P.F, c = threadIdx.x, lane = c & 31;")
+            w("  T* sm = reinterpret_cast<T*>(smem);")
+            w(f"  T* gsm = sm + NMP * {EC};  // [EC][D2P] grad_in2 partial sums")
+            w("  const int64_t e0 = P.rowptr[row], ne_all = P.rowptr[row + 1] - e0;")
         w(f"  T g[{gs.nacc}];")
         w("  {")
         w("    const T* __restrict__ go = P.g_out + row * (int64_t)(OUT_COMPS * F) + c;")
@@ -454,17 +465,29 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w(f"    for (int t = c; t < {EC * d2p}; t += blockDim.x) gsm[t] = T(0);")
         L.extend(_phase1_loop(gs, "    "))
         w("    for (int k = 0; k < ne; ++k) {")
-        L.extend(_ring_edge_begin("      "))
-        w("      if (valid) {")
-        w("        const T* sx = ring + s * SLOT + c;")
-        w("        T x1[XN], gx1[XN];")
-        w(f"        T gx2[{d2p}];")
-        w("        for (int q = 0; q < XN; ++q) { x1[q] = sx[q * F]; gx1[q] = T(0); }")
-        w(f"        for (int q = 0; q < {d2p}; ++q) gx2[q] = T(0);")
-        w("        const T* sw = sx + XN * F;")
+        if BWD_RING:
+            L.extend(_ring_edge_begin("      "))
+            w("      if (valid) {")
+            w("        const T* sx = ring + s * SLOT + c;")
+            w("        T x1[XN], gx1[XN];")
+            w(f"        T gx2[{d2p}];")
+            w("        for (int q = 0; q < XN; ++q) { x1[q] = sx[q * F]; gx1[q] = T(0); }")
+            w(f"        for (int q = 0; q < {d2p}; ++q) gx2[q] = T(0);")
+            w("        const T* sw = sx + XN * F;")
+        else:
+            w("      const int64_t kk = eb + k, e = e0 + kk;")
+            w("      const int64_t j = P.idx_j[e];")
+            w("      if ((uint64_t)j >= (uint64_t)P.n_in1) { if (c == 0) fc_flag(P.status, FC_DEV_BAD_INDEX); continue; }")
+            w("      {")
+            w("        const T* __restrict__ a1 = P.in1 + j * (int64_t)(D1 * F) + XLO * F + c;")
+            w("        T x1[XN], gx1[XN];")
+            w(f"        T gx2[{d2p}];")
+            w("        for (int q = 0; q < XN; ++q) { x1[q] = fc_ldg(a1 + q * F); gx1[q] = T(0); }")
+            w(f"        for (int q = 0; q < {d2p}; ++q) gx2[q] = T(0);")
+            w("        const T* __restrict__ wr = P.w + e * (int64_t)(NP * F) + c;")
         w("        T* __restrict__ gwr = NEED_W ? P.g_w + e * (int64_t)(NP * F) + c : nullptr;")
         w("        const T* m = sm + k * NMP;")
-        L.extend(_bwd_group_body(gs, "        "))
+        L.extend(_bwd_group_body(gs, "        ", direct=not BWD_RING))
         w("        if (NEED_1) {")
         w("          T* __restrict__ t1 = P.g_in1 + j * (int64_t)(D1 * F) + XLO * F + c;")
         w("          for (int q = 0; q < XN; ++q) fc_atomic_add(t1 + q * F, gx1[q]);")
@@ -474,7 +497,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w(f"          if ((lane & {32 // d2p - 1}) == 0 && comp < D2) atomicAdd(gsm + k * {d2p} + comp, gx2[0]);")
         w("        }")
         w("      }")
-        L.extend(_ring_edge_end("      "))
+        if BWD_RING:
+            L.extend(_ring_edge_end("      "))
         w("    }")
         w("    __syncthreads();")
         w("    if (NEED_2) {")
@@ -487,7 +511,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("    }")
         w("    __syncthreads();")
         w("  }")
-        L.extend(_ring_drain("  "))
+        if BWD_RING:
+            L.extend(_ring_drain("  "))
         w("}")
     w("template <int G> struct Bwd2MinCtas;")
     for gi, gs in enumerate(bwd_groups):
