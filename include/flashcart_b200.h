@@ -103,9 +103,10 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
               int64_t n_in2_rows, void* out, int32_t* status, fc_stream_t stream);
 
 /* Allocation-free convolution forward. No counterpart in the reference: an extra
- * entry point for callers that cannot allocate device memory themselves, e.g. code
- * running inside a CUDA-graph capture that must not call cudaMalloc, or a host
- * integration (a simulation engine plugin) whose allocator owns all device memory.
+ * entry point for callers that cannot allocate device memory themselves, e.g. a
+ * simulation engine plug-in (an MD code whose own memory manager owns every device
+ * byte and hands out only pointers into its buffers), or a time-step loop that may not
+ * call cudaMalloc because it can synchronise the device and stall the step.
  * Same result as fc_build_rowptr + fc_tp_fwd (convolution), but the receiver CSR is
  * built into a fixed workspace inside the library's own device memory (2 MiB per
  * device, held until process exit), so at most 262,144 receiver nodes are accepted;

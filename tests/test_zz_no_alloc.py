@@ -1,8 +1,8 @@
 """The allocation-free convolution entry point (fc_tp_conv_fwd_noalloc).
 
-Some callers cannot allocate device memory themselves -- code that runs while a CUDA
-graph is being captured, or a host engine whose own allocator owns every device byte.
-For them the library offers one convolution forward that keeps its receiver-CSR
+Some callers cannot allocate device memory themselves -- an MD engine plug-in whose
+memory manager owns every device byte, or a time-step loop that may not call cudaMalloc
+because it can synchronise the device. For them the library offers one convolution forward that keeps its receiver-CSR
 workspace in a fixed array of its own device memory. This file is collected last so
 that a failure here cannot hide the rest of the suite; it passes both alone and after
 the other tests (the workspace keeps whatever the previous call left, and the entry
