@@ -436,9 +436,12 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("}")
     # ---------------- backward
     for gi, gs in enumerate(bwd_groups):
-        w("template <typename T>")
+        w("template <typename T, int NM>")
         w(f"__device__ __forceinline__ void bwd2_g{gi}(const TpBwdParams<T>& P, unsigned char* smem, bool multi) {{")
-        w("  const bool NEED_1 = P.g_in1 != nullptr, NEED_2 = P.g_in2 != nullptr, NEED_W = P.g_w != nullptr;")
+        w("  // NM: requested gradients as a compile-time mask (1 in1, 2 in2, 4 weights), 0 = read the pointers")
+        w("  const bool NEED_1 = NM ? (NM & 1) != 0 : P.g_in1 != nullptr;")
+        w("  const bool NEED_2 = NM ? (NM & 2) != 0 : P.g_in2 != nullptr;")
+        w("  const bool NEED_W = NM ? (NM & 4) != 0 : P.g_w != nullptr;")
         w("  const int64_t row = blockIdx.x;")
         if BWD_RING:
             L.extend(_ring_setup(gs, str(EC * d2p), "  "))
@@ -517,22 +520,39 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("template <int G> struct Bwd2MinCtas;")
     for gi, gs in enumerate(bwd_groups):
         w(f"template <> struct Bwd2MinCtas<{gi}> {{ static constexpr int value = {min_ctas(gs)}; }};")
-    w("template <typename T, int G>")
+    w("template <typename T, int G, int NM>")
     w("__global__ void __launch_bounds__(256, Bwd2MinCtas<G>::value) bwd2_kernel(TpBwdParams<T> P) {")
     w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
     for gi in range(len(bwd_groups)):
-        w(f"  if constexpr (G == {gi}) bwd2_g{gi}<T>(P, fc_smem_raw, BWD2_GROUPS > 1);")
+        w(f"  if constexpr (G == {gi}) bwd2_g{gi}<T, NM>(P, fc_smem_raw, BWD2_GROUPS > 1);")
+    w("}")
+    w("template <typename T, int G>")
+    w("int launch_fwd2_group(const TpParams<T>& P, cudaStream_t s) {")
+    w("  const size_t smem = fwd2_smem(G, P.F, sizeof(T));")
+    w("  if (smem > 227 * 1024) return FC_ERR_UNSUPPORTED;")
+    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(fwd2_kernel<T, G>, "
+      "cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
+    w("  fwd2_kernel<T, G><<<(unsigned)P.n_rows, P.F, smem, s>>>(P);")
+    w("  return fc_check_launch();")
+    w("}")
+    w("template <typename T, int G, int NM>")
+    w("int launch_bwd2_variant(const TpBwdParams<T>& P, size_t smem, cudaStream_t s) {")
+    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(bwd2_kernel<T, G, NM>, "
+      "cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
+    w("  bwd2_kernel<T, G, NM><<<(unsigned)P.n_rows, P.F, smem, s>>>(P);")
+    w("  return fc_check_launch();")
+    w("}")
+    w("template <typename T, int G>")
+    w("int launch_bwd2_group(const TpBwdParams<T>& P, cudaStream_t s) {")
+    w("  const size_t smem = bwd2_smem(G, P.F, sizeof(T));")
+    w("  if (smem > 227 * 1024) return FC_ERR_UNSUPPORTED;")
+    w("  // the gradient sets of the force / stress and training passes get their own code path")
+    w("  const int nm = (P.g_in1 ? 1 : 0) | (P.g_in2 ? 2 : 0) | (P.g_w ? 4 : 0);")
+    w("  if (nm == 7) return launch_bwd2_variant<T, G, 7>(P, smem, s);")
+    w("  if (nm == 6) return launch_bwd2_variant<T, G, 6>(P, smem, s);")
+    w("  return launch_bwd2_variant<T, G, 0>(P, smem, s);")
     w("}")
     for kind, params, groups in (("fwd", "TpParams", fwd_groups), ("bwd", "TpBwdParams", bwd_groups)):
-        w("template <typename T, int G>")
-        w(f"int launch_{kind}2_group(const {params}<T>& P, cudaStream_t s) {{")
-        w(f"  const size_t smem = {kind}2_smem(G, P.F, sizeof(T));")
-        w("  if (smem > 227 * 1024) return FC_ERR_UNSUPPORTED;")
-        w(f"  if (smem > 48 * 1024 && cudaFuncSetAttribute({kind}2_kernel<T, G>, "
-          "cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
-        w(f"  {kind}2_kernel<T, G><<<(unsigned)P.n_rows, P.F, smem, s>>>(P);")
-        w("  return fc_check_launch();")
-        w("}")
         w("template <typename T>")
         w(f"int launch_{kind}2(const {params}<T>& P, cudaStream_t s) {{")
         w("  if (P.n_rows == 0) return 0;")

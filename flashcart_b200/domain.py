@@ -199,7 +199,7 @@ def evaluate_domain(energy_fn, graph, plan: DomainPlan, group=None, compute_forc
     to their owners. ``energy`` and the strain derivative are summed over the group;
     ``forces`` are those of the owned atoms (``plan.owned`` order).
     """
-    from flashcart_b200.model.flashcart import to_voigt6
+    from flashcart_b200.model.flashcart import rows_times_3x3, to_voigt6
 
     g = dict(graph.to_dict() if hasattr(graph, "to_dict") else graph)
     cell = g["cell"].detach().reshape(1, 3, 3)
@@ -207,7 +207,7 @@ def evaluate_domain(energy_fn, graph, plan: DomainPlan, group=None, compute_forc
     displacement = torch.zeros_like(cell).requires_grad_(compute_stress)
     sym = 0.5 * (displacement + displacement.transpose(-1, -2))
     scaling = torch.eye(3, device=cell.device, dtype=cell.dtype).unsqueeze(0) + sym
-    pos_s = pos_leaf @ scaling[0]
+    pos_s = rows_times_3x3(pos_leaf, scaling[0])
     cell_s = cell @ scaling
     pos_local = torch.cat([pos_s, HaloExchange.apply(pos_s, plan, group)], dim=0)
     local = plan.local_atoms

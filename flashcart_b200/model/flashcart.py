@@ -24,6 +24,14 @@ from flashcart_b200.nn.radial import ChebyshevBasis, PolynomialCutoff
 MIN_EDGE_LENGTH = 1.0e-4
 
 
+def rows_times_3x3(x, m):
+    """``x @ m`` for rows x (R, 3) and one 3 x 3 matrix m, as a broadcast product summed
+    over the inner index. Its gradient with respect to m is a reduction over the R rows;
+    the GEMM form's gradient is an (3 x R) x (R x 3) product that cuBLAS runs as a
+    single-tile SIMT kernel (0.2-0.35 ms at R = 1.5 M)."""
+    return (x.unsqueeze(-1) * m).sum(-2)
+
+
 def get_edge_vectors(positions, cell, shifts, edge_index, batch, use_shifts: bool = True):
     """v_e = r_j - r_i + S_e . cell (row 0 receivers i, row 1 senders j; reference ``utils/geometry.py:25-53``).
 
@@ -38,7 +46,7 @@ def get_edge_vectors(positions, cell, shifts, edge_index, batch, use_shifts: boo
         return vec
     s = shifts.to(cell.dtype)
     if cell.shape[0] == 1:
-        return vec + s @ cell[0]
+        return vec + rows_times_3x3(s, cell[0])
     per_edge_cell = cell.index_select(0, batch.index_select(0, idx_i))
     return vec + torch.bmm(s.unsqueeze(1), per_edge_cell).squeeze(1)
 
@@ -219,7 +227,7 @@ class FlashCartPotential(nn.Module):
             sym = 0.5 * (displacement + displacement.transpose(-1, -2))
             scaling = torch.eye(3, device=cell.device, dtype=cell.dtype).unsqueeze(0) + sym
             if scaling.shape[0] == 1:
-                positions = positions @ scaling[0]
+                positions = rows_times_3x3(positions, scaling[0])
             else:
                 per_atom = scaling.index_select(0, g["batch"])
                 positions = torch.bmm(positions.unsqueeze(-2), per_atom).squeeze(-2)
