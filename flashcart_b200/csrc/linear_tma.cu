@@ -12,7 +12,9 @@
 //              prefetch of A slabs further ahead (FC_TMA_PF_AHEAD, off: it did not raise the
 //              measured rate)
 //   warp 1     MMA issue (one thread): D += Ahi Bhi + Ahi Blo + Alo Bhi  ("3xTF32")
-//   warps 2-5  splitters: round the A slab to tf32 in place and write its residual
+//   warps 2-5  splitters: round the A slab to tf32 and form its residual; for BN = 128
+//              tiles both parts go to tensor memory (one lane quarter per warp) and the
+//              MMAs read A from there, otherwise they go back to shared memory
 //   warps 6-9  epilogue: TMEM -> registers -> scale -> swizzled staging -> TMA store
 // Operand stages cycle through full (TMA landed) -> split (hi / lo ready) -> empty (MMAs
 // done, tcgen05.commit) mbarriers. The k range of a tile is cut into units of 64; each
@@ -66,12 +68,21 @@ template <int BN>
 struct Cfg {
   static constexpr int TILE_A = BM * BK * 4;  // 16 KB
   static constexpr int TILE_B = BN * BK * 4;
-  static constexpr int STAGE = 2 * TILE_A + 2 * TILE_B;
-  static constexpr int STAGES = RING_BYTES / STAGE;
+  // ATM: the splitters write the tf32 hi / lo parts of A into tensor memory and the MMAs
+  // read A from there, so shared memory carries A once (TMA in, splitters out) instead of
+  // five times (TMA in, splitters in / hi out / lo out, three MMA reads). Taken for
+  // BN = 128 (the node-level maps: measured 10-38% faster). BN = 64 (long k, the radial
+  // input gradient) measured 6% slower with it, with 4 or 6 stages; BN = 256 tiles
+  // (k <= 64) keep A in shared memory and all of tensor memory for accumulators.
+  static constexpr bool ATM = BN == 128;
+  static constexpr int STAGE = ATM ? TILE_A + 2 * TILE_B : 2 * TILE_A + 2 * TILE_B;
+  static constexpr int STAGES = ATM ? 4 : RING_BYTES / STAGE;
+  static constexpr int A_COLS = ATM ? STAGES * 2 * BK : 0;  // tensor-memory A stages: hi | lo columns
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + BAR_BYTES + 1024;
-  static constexpr int NACC = 512 / BN;  // TMEM accumulators in the ring (all 512 columns)
+  static constexpr int NACC = (512 - A_COLS) / BN;  // TMEM accumulators in the ring (the other columns)
   static constexpr int TMEM_COLS = 512;
   static_assert(STAGES >= 2 && STAGES <= 8, "operand ring");
+  static_assert(NACC >= 2, "accumulator ring");
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
 
@@ -89,6 +100,18 @@ struct Args {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 32 consecutive tensor-memory columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
 
 #ifndef FC_TMA_INT_ROUND
@@ -125,6 +148,17 @@ template <int BN>
 __host__ __device__ constexpr uint32_t idesc_tf32() {
   // D f32, A / B tf32, both K-major, M = 128, N = BN.
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// D (tensor memory) += A (tensor memory: row m in lane m, 8 k in consecutive columns) x B.
+template <int BN>
+__device__ __forceinline__ void mma_ta(uint32_t d, uint32_t ta, uint64_t db, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n"
+      :
+      : "r"(d), "r"(ta), "l"(db), "r"(idesc_tf32<BN>()), "r"(acc));
 }
 
 template <int BN>
@@ -228,6 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                    const __grid_constant__ CUtensorMap map_pf, const Args a) {
   using C = Cfg<BN>;
   constexpr int S = C::STAGES;
+  constexpr int B_OFF = C::ATM ? C::TILE_A : 2 * C::TILE_A;  // B hi | lo after the A slab (and its lo half)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi = smem + S * C::STAGE;
@@ -301,8 +336,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t fb = smem_u32(&full[s]);
           arrive_tx(fb, bytes);
           tma_load_3d(smem_u32(st), &map_a, kt * BK, tc.node0, tc.m, fb);
-          tma_load_2d(smem_u32(st + 2 * C::TILE_A), &map_bhi, kt * BK, tc.col0 * BN, fb);
-          if (SPLIT) tma_load_2d(smem_u32(st + 2 * C::TILE_A + C::TILE_B), &map_blo, kt * BK, tc.col0 * BN, fb);
+          tma_load_2d(smem_u32(st + B_OFF), &map_bhi, kt * BK, tc.col0 * BN, fb);
+          if (SPLIT) tma_load_2d(smem_u32(st + B_OFF + C::TILE_B), &map_blo, kt * BK, tc.col0 * BN, fb);
         }
       }
       // drain: the last load issued into every stage must have landed before the CTA exits
@@ -328,7 +363,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;");
-          const uint32_t d = tmem + (uint32_t)(b * BN);
+          const uint32_t d = tmem + (uint32_t)(C::A_COLS + b * BN);
           const int k_end = min(a.nk, (j + 1) * KG);
           for (int kt = j * KG; kt < k_end; ++kt, ++g) {
             const int s = (int)(g % S);
@@ -338,19 +373,35 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             asm volatile("tcgen05.fence::after_thread_sync;");
             uint8_t* st = smem + s * C::STAGE;
-            const uint64_t dah = make_desc(smem_u32(st)), dal = make_desc(smem_u32(st + C::TILE_A));
-            const uint64_t dbh = make_desc(smem_u32(st + 2 * C::TILE_A));
-            const uint64_t dbl = make_desc(smem_u32(st + 2 * C::TILE_A + C::TILE_B));
+            const uint64_t dbh = make_desc(smem_u32(st + B_OFF));
+            const uint64_t dbl = make_desc(smem_u32(st + B_OFF + C::TILE_B));
+            if constexpr (C::ATM) {
+              const uint32_t tah = tmem + (uint32_t)(s * 2 * BK), tal = tah + (uint32_t)BK;
 #pragma unroll
-            for (int kk = 0; kk < BK / 8; ++kk) {
-              const uint64_t off = (uint64_t)((kk * 32) >> 4);
-              const uint32_t acc = (kt > j * KG || kk > 0) ? 1u : 0u;
-              if (SPLIT) {
-                mma<BN>(d, dal + off, dbh + off, acc);
-                mma<BN>(d, dah + off, dbl + off, 1u);
-                mma<BN>(d, dah + off, dbh + off, 1u);
-              } else {
-                mma<BN>(d, dah + off, dbh + off, acc);
+              for (int kk = 0; kk < BK / 8; ++kk) {
+                const uint64_t off = (uint64_t)((kk * 32) >> 4);
+                const uint32_t acc = (kt > j * KG || kk > 0) ? 1u : 0u;
+                if (SPLIT) {
+                  mma_ta<BN>(d, tal + kk * 8, dbh + off, acc);
+                  mma_ta<BN>(d, tah + kk * 8, dbl + off, 1u);
+                  mma_ta<BN>(d, tah + kk * 8, dbh + off, 1u);
+                } else {
+                  mma_ta<BN>(d, tah + kk * 8, dbh + off, acc);
+                }
+              }
+            } else {
+              const uint64_t dah = make_desc(smem_u32(st)), dal = make_desc(smem_u32(st + C::TILE_A));
+#pragma unroll
+              for (int kk = 0; kk < BK / 8; ++kk) {
+                const uint64_t off = (uint64_t)((kk * 32) >> 4);
+                const uint32_t acc = (kt > j * KG || kk > 0) ? 1u : 0u;
+                if (SPLIT) {
+                  mma<BN>(d, dal + off, dbh + off, acc);
+                  mma<BN>(d, dah + off, dbl + off, 1u);
+                  mma<BN>(d, dah + off, dbh + off, 1u);
+                } else {
+                  mma<BN>(d, dah + off, dbh + off, acc);
+                }
               }
             }
             commit(smem_u32(&empty[s]));  // the stage is free once these MMAs have completed
@@ -375,19 +426,43 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        float4* hi = reinterpret_cast<float4*>(smem + s * C::STAGE);
-        float4* lo = reinterpret_cast<float4*>(smem + s * C::STAGE + C::TILE_A);
+        if constexpr (C::ATM) {
+          // this warp's lane quarter: row r of the slab (128-byte swizzled, 16-byte chunk c
+          // at c ^ (r & 7)) -> 32 hi and 32 lo columns of lane r in tensor-memory stage s
+          const int r = (warp & 3) * 32 + lane;
+          const uint8_t* row = smem + s * C::STAGE + r * 128;
+          uint32_t h[32], l[32];
 #pragma unroll
-        for (int j = 0; j < C::TILE_A / 16 / (32 * SPLIT_WARPS); ++j) {
-          const int q = t + 32 * SPLIT_WARPS * j;
-          const float4 x = hi[q];
-          const float4 h = make_float4(round_tf32(x.x), round_tf32(x.y), round_tf32(x.z), round_tf32(x.w));
-          hi[q] = h;
-          if (SPLIT)
-            lo[q] = make_float4(round_tf32(x.x - h.x), round_tf32(x.y - h.y), round_tf32(x.z - h.z),
-                                round_tf32(x.w - h.w));
+          for (int c = 0; c < 8; ++c) {
+            const float4 x = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+            const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float hv = round_tf32(xs[e]);
+              h[4 * c + e] = __float_as_uint(hv);
+              l[4 * c + e] = __float_as_uint(SPLIT ? round_tf32(xs[e] - hv) : 0.f);
+            }
+          }
+          const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(s * 2 * BK);
+          tmem_st32(ta, h);
+          if (SPLIT) tmem_st32(ta + BK, l);
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        } else {
+          float4* hi = reinterpret_cast<float4*>(smem + s * C::STAGE);
+          float4* lo = reinterpret_cast<float4*>(smem + s * C::STAGE + C::TILE_A);
+#pragma unroll
+          for (int j = 0; j < C::TILE_A / 16 / (32 * SPLIT_WARPS); ++j) {
+            const int q = t + 32 * SPLIT_WARPS * j;
+            const float4 x = hi[q];
+            const float4 h = make_float4(round_tf32(x.x), round_tf32(x.y), round_tf32(x.z), round_tf32(x.w));
+            hi[q] = h;
+            if (SPLIT)
+              lo[q] = make_float4(round_tf32(x.x - h.x), round_tf32(x.y - h.y), round_tf32(x.z - h.z),
+                                  round_tf32(x.w - h.w));
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         arrive(smem_u32(&split[s]));
       }
       if (!ok) break;
@@ -444,7 +519,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("tcgen05.fence::after_thread_sync;");
         for (int cb = 0; cb < nchunks; ++cb) {
           float f[32];
-          load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + cb * 32), f);
+          load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COLS + b * BN + cb * 32), f);
           store_chunk(f, col0 + cb * 32, tc);
         }
         asm volatile("tcgen05.fence::before_thread_sync;");
@@ -466,7 +541,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int cb = 0; cb < BN / 32; ++cb) {
             float f[32];
-            load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + cb * 32), f);
+            load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COLS + b * BN + cb * 32), f);
 #pragma unroll
             for (int c = 0; c < 32; ++c) acc[cb * 32 + c] += f[c];
           }
