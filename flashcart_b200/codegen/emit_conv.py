@@ -204,6 +204,32 @@ def _fwd_group_body(gs: GroupSlots, ind: str, direct: bool = False) -> List[str]
     return L
 
 
+def _fwd_group_body_cpt(gs: GroupSlots, ind: str) -> List[str]:
+    """Forward of one edge for CPT channels per thread (c + u*H, u < CPT): the edge matrix
+    entries are loaded from shared memory once and used for every channel of the thread."""
+    sig = gs.sig
+    L = []
+    acc_base = 0
+    for p in gs.paths:
+        r1, r2, o = sig.paths[p]
+        s0 = gs.range[p][0]
+        L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
+        L.extend(_path_mload(gs, p, ind + "  "))
+        L.append(f"{ind}  T wp[CPT];")
+        L.append(f"{ind}  for (int u = 0; u < CPT; ++u) wp[u] = fc_ldg(wr + {p} * F + u * H);")
+        L.append(f"{ind}#pragma unroll")
+        L.append(f"{ind}  for (int u = 0; u < CPT; ++u) {{")
+        for a in range(2 * o + 1):
+            terms = [f"mv[{gs.index[(p, a, i)] - s0}]*x1[u][{_q(r1, i) - gs.x_lo}]" for i in range(2 * r1 + 1)
+                     if (p, a, i) in gs.index]
+            expr = " + ".join(terms) if terms else "T(0)"
+            L.append(f"{ind}    acc[u][{acc_base + a}] += wp[u] * ({expr});")
+        L.append(f"{ind}  }}")
+        L.append(f"{ind}}}")
+        acc_base += 2 * o + 1
+    return L
+
+
 def _bwd_group_body(gs: GroupSlots, ind: str, direct: bool = False) -> List[str]:
     sig = gs.sig
     L = []
@@ -374,19 +400,23 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
             k += 1
     # ---------------- forward
     for gi, gs in enumerate(fwd_groups):
-        w("template <typename T>")
+        w("template <typename T, int CPT>")
         w(f"__device__ __forceinline__ void fwd2_g{gi}(const TpParams<T>& P, unsigned char* smem) {{")
         w("  const int64_t row = blockIdx.x;")
         if FWD_RING:
+            w("  static_assert(CPT == 1, \"the prefetch ring maps one thread to one channel\");")
             L.extend(_ring_setup(gs, "0", "  "))
             L.extend(_issue_fn(gs, "  "))
+            w(f"  T acc[{gs.nacc}];")
+            w(f"  for (int q = 0; q < {gs.nacc}; ++q) acc[q] = T(0);")
         else:
             w(f"  constexpr int XLO = {gs.x_lo}, XN = {gs.x_n}, NMP = {gs.nmp};")
-            w("  const int F = P.F, c = threadIdx.x;")
+            w("  const int F = P.F, c = threadIdx.x, H = F / CPT;  // channels c + u*H, u < CPT")
             w("  T* sm = reinterpret_cast<T*>(smem);")
             w("  const int64_t e0 = P.rowptr[row], ne_all = P.rowptr[row + 1] - e0;")
-        w(f"  T acc[{gs.nacc}];")
-        w(f"  for (int q = 0; q < {gs.nacc}; ++q) acc[q] = T(0);")
+            w(f"  T acc[CPT][{gs.nacc}];")
+            w("  for (int u = 0; u < CPT; ++u)")
+            w(f"    for (int q = 0; q < {gs.nacc}; ++q) acc[u][q] = T(0);")
         w(f"  for (int64_t eb = 0; eb < ne_all; eb += {EC}) {{")
         w(f"    const int ne = (int)min((int64_t){EC}, ne_all - eb);")
         L.extend(_phase1_loop(gs, "    "))
@@ -407,11 +437,12 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
             w("      const int64_t j = P.idx_j[e];")
             w("      if ((uint64_t)j >= (uint64_t)P.n_in1) { if (c == 0) fc_flag(P.status, FC_DEV_BAD_INDEX); continue; }")
             w("      const T* __restrict__ a1 = P.in1 + j * (int64_t)(D1 * F) + XLO * F + c;")
-            w("      T x1[XN];")
-            w("      for (int q = 0; q < XN; ++q) x1[q] = fc_ldg(a1 + q * F);")
+            w("      T x1[CPT][XN];")
+            w("      for (int u = 0; u < CPT; ++u)")
+            w("        for (int q = 0; q < XN; ++q) x1[u][q] = fc_ldg(a1 + u * H + q * F);")
             w("      const T* __restrict__ wr = P.w + e * (int64_t)(NP * F) + c;")
             w("      const T* m = sm + k * NMP;")
-            L.extend(_fwd_group_body(gs, "      ", direct=True))
+            L.extend(_fwd_group_body_cpt(gs, "      "))
         w("    }")
         w("    __syncthreads();")
         w("  }")
@@ -419,20 +450,30 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
             L.extend(_ring_drain("  "))
         w("  T* __restrict__ o = P.out + row * (int64_t)(OUT_COMPS * F) + c;")
         k = 0
+        if not FWD_RING:
+            w("  for (int u = 0; u < CPT; ++u) {")
         for p in gs.paths:
             o_ = sig.paths[p][2]
             for a in range(2 * o_ + 1):
-                w(f"  o[{acc_out[(p, a)]} * F] = acc[{k}];")
+                if FWD_RING:
+                    w(f"  o[{acc_out[(p, a)]} * F] = acc[{k}];")
+                else:
+                    w(f"    o[{acc_out[(p, a)]} * F + u * H] = acc[u][{k}];")
                 k += 1
+        if not FWD_RING:
+            w("  }")
         w("}")
     w("template <int G> struct Fwd2MinCtas;")
     for gi, gs in enumerate(fwd_groups):
         w(f"template <> struct Fwd2MinCtas<{gi}> {{ static constexpr int value = {min_ctas(gs)}; }};")
-    w("template <typename T, int G>")
-    w("__global__ void __launch_bounds__(256, Fwd2MinCtas<G>::value) fwd2_kernel(TpParams<T> P) {")
+    # two channels per thread (64-thread CTAs at C = 128) when the signature is split into
+    # groups: 128 registers (2 x the accumulators), the edge-matrix loads shared by both
+    w(f"constexpr bool FWD2_CPT2 = {'false' if FWD_RING else 'true'};")
+    w("template <typename T, int G, int CPT>")
+    w("__global__ void __launch_bounds__(256, CPT == 1 ? Fwd2MinCtas<G>::value : 2) fwd2_kernel(TpParams<T> P) {")
     w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
     for gi in range(len(fwd_groups)):
-        w(f"  if constexpr (G == {gi}) fwd2_g{gi}<T>(P, fc_smem_raw);")
+        w(f"  if constexpr (G == {gi}) fwd2_g{gi}<T, CPT>(P, fc_smem_raw);")
     w("}")
     # ---------------- backward
     for gi, gs in enumerate(bwd_groups):
@@ -526,14 +567,21 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     for gi in range(len(bwd_groups)):
         w(f"  if constexpr (G == {gi}) bwd2_g{gi}<T, NM>(P, fc_smem_raw, BWD2_GROUPS > 1);")
     w("}")
+    w("template <typename T, int G, int CPT>")
+    w("int launch_fwd2_variant(const TpParams<T>& P, size_t smem, cudaStream_t s) {")
+    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(fwd2_kernel<T, G, CPT>, "
+      "cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
+    w("  fwd2_kernel<T, G, CPT><<<(unsigned)P.n_rows, P.F / CPT, smem, s>>>(P);")
+    w("  return fc_check_launch();")
+    w("}")
     w("template <typename T, int G>")
     w("int launch_fwd2_group(const TpParams<T>& P, cudaStream_t s) {")
     w("  const size_t smem = fwd2_smem(G, P.F, sizeof(T));")
     w("  if (smem > 227 * 1024) return FC_ERR_UNSUPPORTED;")
-    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(fwd2_kernel<T, G>, "
-      "cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
-    w("  fwd2_kernel<T, G><<<(unsigned)P.n_rows, P.F, smem, s>>>(P);")
-    w("  return fc_check_launch();")
+    w("  if constexpr (FWD2_CPT2) {")
+    w("    if (P.F % 64 == 0) return launch_fwd2_variant<T, G, 2>(P, smem, s);")
+    w("  }")
+    w("  return launch_fwd2_variant<T, G, 1>(P, smem, s);")
     w("}")
     w("template <typename T, int G, int NM>")
     w("int launch_bwd2_variant(const TpBwdParams<T>& P, size_t smem, cudaStream_t s) {")

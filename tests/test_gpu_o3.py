@@ -272,10 +272,13 @@ def test_gpu_tf32_mode_is_single_tf32_product(cuda_device):
     assert 0 < rel < 3e-3, rel
 
 
-@pytest.mark.parametrize("sig", [(3, 3, 3, 32), (2, 2, 2, 64), (0, 3, 3, 32), (1, 2, 2, 96), (3, 2, 1, 32)])
+@pytest.mark.parametrize("sig", [(3, 3, 3, 32), (2, 2, 2, 64), (0, 3, 3, 32), (1, 2, 2, 96), (3, 2, 1, 32),
+                                 (3, 3, 3, 64), (2, 3, 3, 128)])
 def test_gpu_fp64_shared_attribute_convolution_vs_oracle(cuda_device, sig):
     """The shared-edge-attribute convolution kernels (path groups, edge matrices in shared
-    memory) in float64 against the oracle, forward and all three gradients."""
+    memory) in float64 against the oracle, forward and all three gradients. (3,3,3,64) and
+    (2,3,3,128) are split into path groups with a channel count divisible by 64, so their
+    forward runs two channels per thread."""
     l1, l2, lo, C = sig
     dev = cuda_device
     idx_i, idx_j, in1, in2 = _conv_inputs(40, 700, C, l1, l2, 9, torch.float64, dev)
