@@ -487,6 +487,38 @@ def _poly_expr(poly: Dict[Tuple[int, int, int], Fraction]) -> str:
     return lin(terms)
 
 
+def emit_rms(l_max: int = L_MAX) -> str:
+    """Invariant squared norms of stored rank blocks: rms_quad_l(x) = sum_ij K_l[i][j] x_i x_j
+    with K_l the (l, l) -> 0 coupling of the tensor product (what the symmetric scalar
+    product of the reference's RMS layer norm computes per channel), and its gradient
+    (K_l + K_l^T) x."""
+    L = []
+    w = L.append
+    w("// Generated by flashcart_b200/codegen/emit.py -- (l, l) -> 0 quadratic forms of stored STF")
+    w(f"// components for l <= {l_max} (exact couplings of codegen/stf.py) and their gradients.")
+    w('#include "../fc_base.cuh"')
+    w("namespace fc {")
+    for l in range(l_max + 1):
+        K = stf.oriented_path_tensor(l, l, 0)
+        n = 2 * l + 1
+        terms = []
+        for i in range(n):
+            for j in range(i, n):
+                c = K[0][i][j] if i == j else K[0][i][j] + K[0][j][i]
+                if c != 0:
+                    terms.append((c, f"x[{i}]*x[{j}]"))
+        w("template <typename T>")
+        w(f"FC_HD FC_INLINE T rms_quad_l{l}(const T* x) {{ return {lin(terms)}; }}")
+        w("template <typename T>")
+        w(f"FC_HD FC_INLINE void rms_quad_grad_l{l}(const T* x, T* g) {{")
+        for m in range(n):
+            gt = [(K[0][m][j] + K[0][j][m], f"x[{j}]") for j in range(n)]
+            w(f"  g[{m}] = {lin(gt)};")
+        w("}")
+    w("}  // namespace fc")
+    return "\n".join(L) + "\n"
+
+
 def emit_irreps(l_max: int = L_MAX) -> str:
     L = []
     w = L.append
@@ -576,6 +608,7 @@ def write_all(out_dir: str = GEN_DIR) -> List[str]:
         written.append(path)
     _write_if_changed(os.path.join(out_dir, "tp_dispatch.inc"), emit_dispatch(sigs))
     _write_if_changed(os.path.join(out_dir, "irreps_poly.cuh"), emit_irreps())
+    _write_if_changed(os.path.join(out_dir, "rms_quad.cuh"), emit_rms())
     return written
 
 

@@ -20,6 +20,10 @@ template <typename T> int irreps_bwd_dispatch(const T*, const T*, T*, int64_t, i
 template <typename T>
 int irreps_dbwd_dispatch(const T*, const T*, const T*, T*, T*, int64_t, int, cudaStream_t);
 int build_rowptr(const int64_t*, int64_t, int64_t, int64_t*, int*, cudaStream_t);
+template <typename T>
+int rms_norm_fwd_dispatch(int, const T*, const T*, const T*, T, int, int64_t, T*, T*, cudaStream_t);
+template <typename T>
+int rms_norm_bwd_dispatch(int, const T*, const T*, const T*, const T*, const T*, int, int64_t, T*, cudaStream_t);
 
 static thread_local std::string g_last_error;
 
@@ -567,6 +571,54 @@ int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* 
   // the workspace is fully rewritten by this call, so nothing needs clearing
   if (int rc = fc_build_rowptr(idx_i, n_edges, n_nodes, rowptr, status, stream)) return rc;
   return fc_tp_fwd(desc, in1, in2, weights, rowptr, idx_j, n_nodes, n_nodes, n_edges, out, status, stream);
+}
+
+// ------------------------------------------------------------------ RMS layer norm
+
+static int rms_check(int l_max, int features, int dtype, int64_t n_rows, const char* what) {
+  if (l_max < 0 || l_max > FC_MAX_L)
+    return fail(FC_ERR_UNSUPPORTED, "%s: l_max %d outside 0..%d", what, l_max, FC_MAX_L);
+  if (features <= 0 || features > 1024)
+    return fail(FC_ERR_UNSUPPORTED, "%s: features must be in 1..1024 (got %d)", what, features);
+  if (dtype != FC_F32 && dtype != FC_F64) return fail(FC_ERR_INVALID, "%s: dtype must be f32 or f64", what);
+  if (n_rows < 0) return fail(FC_ERR_INVALID, "%s: negative row count", what);
+  return FC_OK;
+}
+
+int fc_rms_norm_fwd(int32_t l_max, int32_t features, int32_t dtype, const void* x, const void* gains,
+                    const void* l_weights, double eps, int64_t n_rows, void* y, void* rstd, fc_stream_t stream) {
+  if (int rc = rms_check(l_max, features, dtype, n_rows, "fc_rms_norm_fwd")) return rc;
+  if (n_rows == 0) return FC_OK;
+  if (!x || !gains || !l_weights || !y || !rstd) return fail(FC_ERR_INVALID, "fc_rms_norm_fwd: null pointer");
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == FC_F32)
+    return launch_status(rms_norm_fwd_dispatch<float>(l_max, (const float*)x, (const float*)gains,
+                                                      (const float*)l_weights, (float)eps, features, n_rows,
+                                                      (float*)y, (float*)rstd, s),
+                         "fc_rms_norm_fwd");
+  return launch_status(rms_norm_fwd_dispatch<double>(l_max, (const double*)x, (const double*)gains,
+                                                     (const double*)l_weights, eps, features, n_rows, (double*)y,
+                                                     (double*)rstd, s),
+                       "fc_rms_norm_fwd");
+}
+
+int fc_rms_norm_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* grad_y, const void* x,
+                    const void* gains, const void* l_weights, const void* rstd, int64_t n_rows, void* grad_x,
+                    fc_stream_t stream) {
+  if (int rc = rms_check(l_max, features, dtype, n_rows, "fc_rms_norm_bwd")) return rc;
+  if (n_rows == 0) return FC_OK;
+  if (!grad_y || !x || !gains || !l_weights || !rstd || !grad_x)
+    return fail(FC_ERR_INVALID, "fc_rms_norm_bwd: null pointer");
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == FC_F32)
+    return launch_status(rms_norm_bwd_dispatch<float>(l_max, (const float*)grad_y, (const float*)x,
+                                                      (const float*)gains, (const float*)l_weights,
+                                                      (const float*)rstd, features, n_rows, (float*)grad_x, s),
+                         "fc_rms_norm_bwd");
+  return launch_status(rms_norm_bwd_dispatch<double>(l_max, (const double*)grad_y, (const double*)x,
+                                                     (const double*)gains, (const double*)l_weights,
+                                                     (const double*)rstd, features, n_rows, (double*)grad_x, s),
+                       "fc_rms_norm_bwd");
 }
 
 // Muon Newton-Schulz orthogonalisation (see the header).

@@ -1,0 +1,229 @@
+// Fused RMS layer norm of Cartesian node features (forward and first-order backward).
+//
+// One node row holds the rank blocks l = 0..L of F channels each, component axis outer
+// and channels contiguous (row length (L+1)^2 F). Per row:
+//   q_c  = sum_l w_l * x_{l,.,c}^T K_l x_{l,.,c}     (K_l the (l,l)->0 coupling)
+//   ms   = (1/F) sum_c q_c,   r = (ms + eps)^(-1/2)
+//   y    = x * r * gain_{l,c}
+// and, for the backward with S = sum_{l,m,c} g x gain,
+//   dx   = r gain g - (r^3 / 2) S (w_l / F) (K_l + K_l^T) x .
+// One CTA per row and one thread per channel: each thread reads its (L+1)^2 components
+// (coalesced over channels), the per-row sums are block reductions in a fixed order, so
+// every thread sees the same r and S and the result does not depend on timing.
+#include "fc_base.cuh"
+#include "gen/rms_quad.cuh"
+
+namespace fc {
+
+template <typename T, int L>
+FC_HD FC_INLINE T rms_row_quad(const T* v, const T* lw) {
+  T q = lw[0] * rms_quad_l0<T>(v);
+  if constexpr (L >= 1) q += lw[1] * rms_quad_l1<T>(v + 1);
+  if constexpr (L >= 2) q += lw[2] * rms_quad_l2<T>(v + 4);
+  if constexpr (L >= 3) q += lw[3] * rms_quad_l3<T>(v + 9);
+  return q;
+}
+
+template <typename T, int L>
+FC_HD FC_INLINE void rms_row_quad_grad(const T* v, T* gq) {
+  rms_quad_grad_l0<T>(v, gq);
+  if constexpr (L >= 1) rms_quad_grad_l1<T>(v + 1, gq + 1);
+  if constexpr (L >= 2) rms_quad_grad_l2<T>(v + 4, gq + 4);
+  if constexpr (L >= 3) rms_quad_grad_l3<T>(v + 9, gq + 9);
+}
+
+FC_HD FC_INLINE int rms_rank_of(int comp) { return comp < 1 ? 0 : comp < 4 ? 1 : comp < 9 ? 2 : 3; }
+
+FC_HD FC_INLINE float rms_rsqrt(float x) {
+#if defined(__CUDA_ARCH__)
+  return rsqrtf(x);
+#else
+  return 1.0f / std::sqrt(x);
+#endif
+}
+FC_HD FC_INLINE double rms_rsqrt(double x) {
+#if defined(__CUDA_ARCH__)
+  return rsqrt(x);
+#else
+  return 1.0 / std::sqrt(x);
+#endif
+}
+
+#ifndef FC_HOST_EMU
+
+// Sum over the CTA (blockDim a multiple of 32, at most 1024); every thread gets the total.
+template <typename T>
+__device__ __forceinline__ T rms_block_sum(T v, T* sh) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) sh[warp] = v;
+  __syncthreads();
+  T t = T(0);
+  for (int k = 0; k < nw; ++k) t += sh[k];
+  __syncthreads();
+  return t;
+}
+
+template <typename T, int L>
+__global__ void __launch_bounds__(1024) rms_fwd_kernel(const T* __restrict__ x, const T* __restrict__ gains,
+                                                      const T* __restrict__ lw, T eps, int F, int64_t n_rows,
+                                                      T* __restrict__ y, T* __restrict__ rstd) {
+  constexpr int NC = (L + 1) * (L + 1);
+  __shared__ T sh[32];
+  const int c = threadIdx.x;
+  const bool on = c < F;
+  T lwv[L + 1];
+  for (int l = 0; l <= L; ++l) lwv[l] = lw[l];
+  for (int64_t row = blockIdx.x; row < n_rows; row += gridDim.x) {
+    const T* xr = x + row * (int64_t)(NC * F) + c;
+    T v[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) v[k] = on ? fc_ldg(xr + k * F) : T(0);
+    const T tot = rms_block_sum<T>(on ? rms_row_quad<T, L>(v, lwv) : T(0), sh);
+    const T r = rms_rsqrt(tot / T(F) + eps);
+    if (on) {
+      T* yr = y + row * (int64_t)(NC * F) + c;
+#pragma unroll
+      for (int k = 0; k < NC; ++k) yr[k * F] = v[k] * r * fc_ldg(gains + rms_rank_of(k) * F + c);
+    }
+    if (c == 0) rstd[row] = r;
+  }
+}
+
+template <typename T, int L>
+__global__ void __launch_bounds__(1024) rms_bwd_kernel(const T* __restrict__ g, const T* __restrict__ x,
+                                                      const T* __restrict__ gains, const T* __restrict__ lw,
+                                                      const T* __restrict__ rstd, int F, int64_t n_rows,
+                                                      T* __restrict__ gx) {
+  constexpr int NC = (L + 1) * (L + 1);
+  __shared__ T sh[32];
+  const int c = threadIdx.x;
+  const bool on = c < F;
+  T lwv[L + 1], gn[L + 1];
+  for (int l = 0; l <= L; ++l) {
+    lwv[l] = lw[l];
+    gn[l] = on ? fc_ldg(gains + l * F + c) : T(0);
+  }
+  for (int64_t row = blockIdx.x; row < n_rows; row += gridDim.x) {
+    const T* xr = x + row * (int64_t)(NC * F) + c;
+    const T* gr = g + row * (int64_t)(NC * F) + c;
+    T v[NC], gv[NC];
+    T s = T(0);
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+      v[k] = on ? fc_ldg(xr + k * F) : T(0);
+      gv[k] = on ? fc_ldg(gr + k * F) : T(0);
+      s += gv[k] * v[k] * gn[rms_rank_of(k)];
+    }
+    const T S = rms_block_sum<T>(s, sh);
+    const T r = fc_ldg(rstd + row);
+    const T coef = T(0.5) * r * r * r * S / T(F);
+    if (on) {
+      T gq[NC];
+      rms_row_quad_grad<T, L>(v, gq);
+      T* o = gx + row * (int64_t)(NC * F) + c;
+#pragma unroll
+      for (int k = 0; k < NC; ++k) {
+        const int l = rms_rank_of(k);
+        o[k * F] = r * gn[l] * gv[k] - coef * lwv[l] * gq[k];
+      }
+    }
+  }
+}
+
+template <typename T, int L>
+static int rms_fwd_launch(const T* x, const T* gains, const T* lw, T eps, int F, int64_t n, T* y, T* rstd,
+                          cudaStream_t s) {
+  const int block = fc_round_up(F, 32);
+  const int grid = (int)(n < ((int64_t)1 << 30) ? n : ((int64_t)1 << 30));
+  rms_fwd_kernel<T, L><<<grid, block, 0, s>>>(x, gains, lw, eps, F, n, y, rstd);
+  return fc_check_launch();
+}
+template <typename T, int L>
+static int rms_bwd_launch(const T* g, const T* x, const T* gains, const T* lw, const T* rstd, int F, int64_t n,
+                          T* gx, cudaStream_t s) {
+  const int block = fc_round_up(F, 32);
+  const int grid = (int)(n < ((int64_t)1 << 30) ? n : ((int64_t)1 << 30));
+  rms_bwd_kernel<T, L><<<grid, block, 0, s>>>(g, x, gains, lw, rstd, F, n, gx);
+  return fc_check_launch();
+}
+
+#else  // host emulation: the same per-channel arithmetic, rows and channels in loops
+
+template <typename T, int L>
+static int rms_fwd_launch(const T* x, const T* gains, const T* lw, T eps, int F, int64_t n, T* y, T* rstd,
+                          cudaStream_t) {
+  constexpr int NC = (L + 1) * (L + 1);
+  for (int64_t row = 0; row < n; ++row) {
+    T tot = T(0);
+    for (int c = 0; c < F; ++c) {
+      T v[NC];
+      for (int k = 0; k < NC; ++k) v[k] = x[row * NC * F + k * F + c];
+      tot += rms_row_quad<T, L>(v, lw);
+    }
+    const T r = rms_rsqrt(tot / T(F) + eps);
+    for (int c = 0; c < F; ++c)
+      for (int k = 0; k < NC; ++k)
+        y[row * NC * F + k * F + c] = x[row * NC * F + k * F + c] * r * gains[rms_rank_of(k) * F + c];
+    rstd[row] = r;
+  }
+  return 0;
+}
+template <typename T, int L>
+static int rms_bwd_launch(const T* g, const T* x, const T* gains, const T* lw, const T* rstd, int F, int64_t n,
+                          T* gx, cudaStream_t) {
+  constexpr int NC = (L + 1) * (L + 1);
+  for (int64_t row = 0; row < n; ++row) {
+    T S = T(0);
+    for (int c = 0; c < F; ++c)
+      for (int k = 0; k < NC; ++k)
+        S += g[row * NC * F + k * F + c] * x[row * NC * F + k * F + c] * gains[rms_rank_of(k) * F + c];
+    const T r = rstd[row];
+    const T coef = T(0.5) * r * r * r * S / T(F);
+    for (int c = 0; c < F; ++c) {
+      T v[NC], gq[NC];
+      for (int k = 0; k < NC; ++k) v[k] = x[row * NC * F + k * F + c];
+      rms_row_quad_grad<T, L>(v, gq);
+      for (int k = 0; k < NC; ++k) {
+        const int l = rms_rank_of(k);
+        gx[row * NC * F + k * F + c] = r * gains[l * F + c] * g[row * NC * F + k * F + c] - coef * lw[l] * gq[k];
+      }
+    }
+  }
+  return 0;
+}
+
+#endif
+
+template <typename T>
+int rms_norm_fwd_dispatch(int l_max, const T* x, const T* gains, const T* lw, T eps, int F, int64_t n, T* y, T* rstd,
+                          cudaStream_t s) {
+  switch (l_max) {
+    case 0: return rms_fwd_launch<T, 0>(x, gains, lw, eps, F, n, y, rstd, s);
+    case 1: return rms_fwd_launch<T, 1>(x, gains, lw, eps, F, n, y, rstd, s);
+    case 2: return rms_fwd_launch<T, 2>(x, gains, lw, eps, F, n, y, rstd, s);
+    default: return rms_fwd_launch<T, 3>(x, gains, lw, eps, F, n, y, rstd, s);
+  }
+}
+template <typename T>
+int rms_norm_bwd_dispatch(int l_max, const T* g, const T* x, const T* gains, const T* lw, const T* rstd, int F,
+                          int64_t n, T* gx, cudaStream_t s) {
+  switch (l_max) {
+    case 0: return rms_bwd_launch<T, 0>(g, x, gains, lw, rstd, F, n, gx, s);
+    case 1: return rms_bwd_launch<T, 1>(g, x, gains, lw, rstd, F, n, gx, s);
+    case 2: return rms_bwd_launch<T, 2>(g, x, gains, lw, rstd, F, n, gx, s);
+    default: return rms_bwd_launch<T, 3>(g, x, gains, lw, rstd, F, n, gx, s);
+  }
+}
+
+template int rms_norm_fwd_dispatch<float>(int, const float*, const float*, const float*, float, int, int64_t, float*,
+                                          float*, cudaStream_t);
+template int rms_norm_fwd_dispatch<double>(int, const double*, const double*, const double*, double, int, int64_t,
+                                           double*, double*, cudaStream_t);
+template int rms_norm_bwd_dispatch<float>(int, const float*, const float*, const float*, const float*, const float*,
+                                          int, int64_t, float*, cudaStream_t);
+template int rms_norm_bwd_dispatch<double>(int, const double*, const double*, const double*, const double*,
+                                           const double*, int, int64_t, double*, cudaStream_t);
+
+}  // namespace fc

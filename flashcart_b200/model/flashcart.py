@@ -10,13 +10,14 @@ xx, yy, zz, yz, xz, xy and ``virials = -stress * volume``.
 
 from __future__ import annotations
 
+import contextlib
 from collections.abc import Mapping
 from typing import Callable, Any, Dict, List, Optional
 
 import torch
 import torch.nn as nn
 
-from flashcart_b200 import o3
+from flashcart_b200 import o3, ops
 from flashcart_b200.nn.layers import (EnergyReadoutLayer, EquivariantGatedLayer, InteractionLayer, ProductLayer,
                                       ScaleShiftEnergyLayer)
 from flashcart_b200.nn.radial import ChebyshevBasis, PolynomialCutoff
@@ -236,14 +237,17 @@ class FlashCartPotential(nn.Module):
             positions.requires_grad_(True)
         g["positions"] = positions
         g["cell"] = cell
-        node_energies = self(g)
-        n_graphs = int(g["n_atoms"].shape[0]) if "n_atoms" in g else int(g["batch"].max().item()) + 1
-        energy = torch.zeros(n_graphs, dtype=node_energies.dtype, device=node_energies.device)
-        energy = energy.index_add(0, g["batch"], node_energies)
-        out = {"node_energies": node_energies, "energy": energy}
-        inputs = ([positions] if compute_forces else []) + ([displacement] if compute_stress else [])
+        # without create_graph the graph is differentiated once: fused first-order kernels
+        # (RMS layer norm) may replace their composed, twice-differentiable forms
+        with ops.first_order_only() if not create_graph else contextlib.nullcontext():
+            node_energies = self(g)
+            n_graphs = int(g["n_atoms"].shape[0]) if "n_atoms" in g else int(g["batch"].max().item()) + 1
+            energy = torch.zeros(n_graphs, dtype=node_energies.dtype, device=node_energies.device)
+            energy = energy.index_add(0, g["batch"], node_energies)
+            out = {"node_energies": node_energies, "energy": energy}
+            inputs = ([positions] if compute_forces else []) + ([displacement] if compute_stress else [])
+            grads = torch.autograd.grad(energy.sum(), inputs, create_graph=create_graph) if inputs else None
         if inputs:
-            grads = torch.autograd.grad(energy.sum(), inputs, create_graph=create_graph)
             k = 0
             if compute_forces:
                 out["forces"] = -grads[0]
@@ -275,7 +279,8 @@ class FlashCartPotential(nn.Module):
         for p in frozen:
             p.requires_grad_(False)
         try:
-            return evaluate_domain(self._forward_impl, graph, plan, group, compute_forces, compute_stress)
+            with ops.first_order_only():
+                return evaluate_domain(self._forward_impl, graph, plan, group, compute_forces, compute_stress)
         finally:
             for p in frozen:
                 p.requires_grad_(True)

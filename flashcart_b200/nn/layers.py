@@ -14,7 +14,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from flashcart_b200 import o3
+from flashcart_b200 import o3, ops
 
 
 def iter_child_special_parameters(module: nn.Module, method_name: str) -> Iterator[nn.Parameter]:
@@ -194,10 +194,22 @@ class RMSLayerNorm(nn.Module):
             self.weights = nn.ParameterList()
             self.register_parameter("bias", None)
 
+    def _fused_ok(self, node_feats: torch.Tensor) -> bool:
+        """The fused kernel pair (one pass forward, one backward) replaces the composition
+        when the graph is differentiated at most once, without centering, with constant
+        gains (parameters frozen, as in force / stress evaluation)."""
+        return (ops.first_order_only_active() and node_feats.is_cuda and node_feats.dim() == 2
+                and not self.centering and node_feats.dtype in (torch.float32, torch.float64)
+                and not any(w.requires_grad for w in self.weights))
+
     def forward(self, node_feats: torch.Tensor) -> torch.Tensor:
         if node_feats.shape[-1] != self.dim:
             raise RuntimeError(f"Incorrect last dimension for node_feats. Expected {self.dim}, "
                                f"got {node_feats.shape[-1]}.")
+        if self._fused_ok(node_feats):
+            gains = (torch.stack(tuple(self.weights)) if self.affine else
+                     node_feats.new_ones((self.l_max + 1, self.n_features)))
+            return ops.rms_norm(node_feats, gains, self.l_weights, self.l_max, self.n_features, self.eps)
         n = node_feats.shape[0]
         feats = node_feats
         if self.centering:

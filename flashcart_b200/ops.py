@@ -14,8 +14,10 @@ on the current stream. There is no CPU path: a CPU tensor raises.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
+import threading
 from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
@@ -23,7 +25,7 @@ from torch import Tensor
 
 from flashcart_b200 import _native as N
 
-__all__ = ["check_device_status", "status_word", "KernelTimer", "set_kernel_timer"]
+__all__ = ["check_device_status", "status_word", "KernelTimer", "set_kernel_timer", "first_order_only", "rms_norm"]
 
 _DEBUG_CHECK = os.environ.get("FLASHCART_B200_CHECK", "0") not in ("", "0", "false", "False")
 
@@ -744,3 +746,112 @@ def newton_schulz(update: Tensor, coeffs: List[float], steps: int, polish: List[
 @newton_schulz.register_fake
 def _(update, coeffs, steps, polish, polish_steps, eps):
     return torch.empty(update.shape, dtype=torch.bfloat16, device=update.device)
+
+
+# --------------------------------------------------------------------------- fused RMS layer norm
+
+_FIRST_ORDER = threading.local()
+
+
+@contextlib.contextmanager
+def first_order_only():
+    """Mark a region whose graph is differentiated at most once (energy -> forces and
+    stress without ``create_graph``). Inside it, modules may use fused operators that
+    have a first derivative but no second one (:func:`rms_norm`); a second derivative
+    through them raises. ``FlashCartPotential.predict`` enters it when ``create_graph``
+    is false."""
+    prev = getattr(_FIRST_ORDER, "on", False)
+    _FIRST_ORDER.on = True
+    try:
+        yield
+    finally:
+        _FIRST_ORDER.on = prev
+
+
+def first_order_only_active() -> bool:
+    return getattr(_FIRST_ORDER, "on", False)
+
+
+def _rms_args(x: Tensor, gains: Tensor, l_weights: Tensor, l_max: int, features: int):
+    if x.dim() != 2 or x.shape[1] != (l_max + 1) ** 2 * features:
+        raise RuntimeError(f"Incorrect last dimension for node_feats. Expected {(l_max + 1) ** 2 * features}, "
+                           f"got {x.shape[-1]}.")
+    if x.dtype not in (torch.float32, torch.float64):
+        raise ValueError(f"rms_norm supports float32 / float64, got {x.dtype}")
+    g = gains.to(x.dtype).contiguous()
+    lw = l_weights.to(device=x.device, dtype=x.dtype).contiguous()
+    if g.numel() != (l_max + 1) * features or lw.numel() != l_max + 1:
+        raise ValueError("rms_norm: gains must be (l_max+1, features) and l_weights (l_max+1,)")
+    return x.contiguous(), g, lw
+
+
+@torch.library.custom_op("flashcart::rms_norm_fwd", mutates_args=())
+def rms_norm_fwd(x: Tensor, gains: Tensor, l_weights: Tensor, l_max: int, features: int,
+                 eps: float) -> Tuple[Tensor, Tensor]:
+    """Fused ``RMSLayerNorm`` forward (reference ``nn/layers.py:413-540``, affine, no
+    centering): returns ``y`` and the per-row ``rstd = (mean_sq + eps)^-1/2``."""
+    _require_cuda(x, gains, l_weights)
+    x, g, lw = _rms_args(x, gains, l_weights, l_max, features)
+    lib = N.lib()
+    y = torch.empty_like(x)
+    rstd = x.new_empty((x.shape[0],))
+    with _timed("rms_norm_fwd", 1, _nbytes(x, y, rstd)):
+        rc = lib.fc_rms_norm_fwd(int(l_max), int(features), _code(x.dtype), _p(x), _p(g), _p(lw), float(eps),
+                                 x.shape[0], _p(y), _p(rstd), _stream(x.device))
+    _after(lib, rc, "fc_rms_norm_fwd", x.device)
+    return y, rstd
+
+
+@rms_norm_fwd.register_fake
+def _(x, gains, l_weights, l_max, features, eps):
+    return torch.empty_like(x), x.new_empty((x.shape[0],))
+
+
+@torch.library.custom_op("flashcart::rms_norm_bwd", mutates_args=())
+def rms_norm_bwd(grad_y: Tensor, x: Tensor, gains: Tensor, l_weights: Tensor, rstd: Tensor, l_max: int,
+                 features: int) -> Tensor:
+    """First-order backward of :func:`rms_norm_fwd` with respect to ``x``."""
+    _require_cuda(grad_y, x, gains, l_weights, rstd)
+    x, g, lw = _rms_args(x, gains, l_weights, l_max, features)
+    gy, r = grad_y.contiguous(), rstd.contiguous()
+    lib = N.lib()
+    gx = torch.empty_like(x)
+    with _timed("rms_norm_bwd", 1, _nbytes(gy, x, r, gx)):
+        rc = lib.fc_rms_norm_bwd(int(l_max), int(features), _code(x.dtype), _p(gy), _p(x), _p(g), _p(lw), _p(r),
+                                 x.shape[0], _p(gx), _stream(x.device))
+    _after(lib, rc, "fc_rms_norm_bwd", x.device)
+    return gx
+
+
+@rms_norm_bwd.register_fake
+def _(grad_y, x, gains, l_weights, rstd, l_max, features):
+    return torch.empty_like(x)
+
+
+def _rms_setup(ctx, inputs, output):
+    x, gains, l_weights, l_max, features, _ = inputs
+    ctx.save_for_backward(x, gains, l_weights, output[1])
+    ctx.l_max, ctx.features = l_max, features
+
+
+def _rms_backward(ctx, grad_y, grad_rstd):
+    if torch.is_grad_enabled():
+        raise RuntimeError("flashcart::rms_norm_fwd was evaluated inside first_order_only(); its backward "
+                           "cannot build a graph for a second derivative (use create_graph=False, or "
+                           "evaluate the model outside first_order_only())")
+    if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
+        raise RuntimeError("flashcart::rms_norm_fwd: gradients of gains / l_weights are not provided")
+    x, gains, l_weights, rstd = ctx.saved_tensors
+    gx = None
+    if ctx.needs_input_grad[0]:
+        gx = rms_norm_bwd(grad_y.contiguous(), x, gains, l_weights, rstd, ctx.l_max, ctx.features)
+    return gx, None, None, None, None, None
+
+
+rms_norm_fwd.register_autograd(_rms_backward, setup_context=_rms_setup)
+
+
+def rms_norm(x: Tensor, gains: Tensor, l_weights: Tensor, l_max: int, features: int, eps: float) -> Tensor:
+    """``y = x * (mean_c sum_l l_weights[l] inv_l + eps)^-1/2 * gains[l, c]`` per row (first
+    derivative only, see :func:`first_order_only`)."""
+    return rms_norm_fwd(x, gains, l_weights, l_max, features, eps)[0]

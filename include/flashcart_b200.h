@@ -195,6 +195,22 @@ int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* 
                   const void* const* weights, const void* scale, int64_t n, void* grad_x,
                   void* const* grad_weights, int32_t* status, fc_stream_t stream);
 
+/* ---------------------------------------------------------------- RMS layer norm
+ * Fused forward and first-order backward of RMSLayerNorm (nn/layers.py:413-540, affine,
+ * without centering): per row, q_c = sum_l l_weights[l] * inv_l[c] with inv_l the
+ * (l,l)->0 symmetric scalar tensor product of the row with itself (nn/layers.py:456-466,
+ * 517), r = (mean_c q_c + eps)^(-1/2), y = x * r * gains[l, c]. x, y, grad_y, grad_x:
+ * (n_rows, (l_max+1)^2 * features) rows; gains: (l_max+1, features); l_weights: l_max+1
+ * values; rstd: n_rows values written by the forward and read by the backward.
+ * dtype FC_F32 or FC_F64 for every array. The backward returns grad_x only (gains and
+ * l_weights are constants of the call). */
+int fc_rms_norm_fwd(int32_t l_max, int32_t features, int32_t dtype, const void* x, const void* gains,
+                    const void* l_weights, double eps, int64_t n_rows, void* y, void* rstd,
+                    fc_stream_t stream);
+int fc_rms_norm_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* grad_y, const void* x,
+                    const void* gains, const void* l_weights, const void* rstd, int64_t n_rows,
+                    void* grad_x, fc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,108 @@
+"""Fused RMS layer norm (fc_rms_norm_fwd / fc_rms_norm_bwd, flashcart::rms_norm_*).
+
+The fused kernels replace the composition of the reference's RMSLayerNorm
+(nn/layers.py:413-540: symmetric scalar tensor product of the features with
+themselves, per-rank weights 1/((2l+1)(l_max+1)), channel mean, (mean_sq + eps)^-1/2,
+per-rank gains) when the graph is differentiated once. The oracle here is that
+composition on the oracle tensor product, differentiated by autograd.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+import abi_calls as A
+from flashcart_b200 import _native as N
+from oracle import stf_oracle as O
+
+
+def _composed(x, gains, l_max, C, eps):
+    """RMSLayerNorm.forward of the reference, on the oracle tensor product (float64)."""
+    n = x.shape[0]
+    npaths = l_max + 1
+    ones = torch.ones(npaths * C, dtype=x.dtype)
+    inv = O.tensor_product(x, x, ones, None, None, l_max, l_max, 0, C, C, True, True, False).view(n, l_max + 1, C)
+    lw = torch.tensor([1.0 / ((2 * l + 1) * (l_max + 1)) for l in range(l_max + 1)], dtype=torch.float64)
+    mean_sq = (inv * lw.to(inv.dtype).view(1, -1, 1)).sum(1).mean(-1, keepdim=True)
+    scaled = x * torch.pow(mean_sq + eps, -0.5)
+    g = torch.cat([gains[l].repeat(2 * l + 1) for l in range(l_max + 1)])
+    return scaled * g, lw
+
+
+@pytest.mark.parametrize("l_max,C", [(0, 8), (1, 5), (2, 32), (3, 16)])
+def test_emu_rms_norm_matches_composed_oracle(emu_lib, l_max, C):
+    g = torch.Generator().manual_seed(7 + l_max)
+    n, eps = 9, 1e-6
+    x = torch.randn(n, (l_max + 1) ** 2 * C, generator=g, dtype=torch.float64)
+    gains = 1.0 + 0.3 * torch.randn(l_max + 1, C, generator=g, dtype=torch.float64)
+    xr = x.clone().requires_grad_(True)
+    ref, lw = _composed(xr, gains, l_max, C, eps)
+    gy = torch.randn_like(ref)
+    (ref_gx,) = torch.autograd.grad(ref, [xr], gy)
+
+    y = torch.empty_like(x)
+    rstd = torch.empty(n, dtype=torch.float64)
+    rc = emu_lib.fc_rms_norm_fwd(l_max, C, N.FC_F64, A.p(x), A.p(gains), A.p(lw), eps, n, A.p(y), A.p(rstd), None)
+    N.check(emu_lib, rc, "fc_rms_norm_fwd")
+    gx = torch.empty_like(x)
+    rc = emu_lib.fc_rms_norm_bwd(l_max, C, N.FC_F64, A.p(gy), A.p(x), A.p(gains), A.p(lw), A.p(rstd), n, A.p(gx),
+                                 None)
+    N.check(emu_lib, rc, "fc_rms_norm_bwd")
+    assert (y - ref.detach()).abs().max().item() < 1e-12 * max(1.0, ref.abs().max().item())
+    assert (gx - ref_gx).abs().max().item() < 1e-12 * max(1.0, ref_gx.abs().max().item())
+
+
+def test_emu_rms_norm_rejects_bad_arguments(emu_lib):
+    x = torch.zeros(2, 16 * 4, dtype=torch.float64)
+    rc = emu_lib.fc_rms_norm_fwd(4, 4, N.FC_F64, A.p(x), A.p(x), A.p(x), 1e-6, 2, A.p(x), A.p(x), None)
+    assert rc == N.FC_ERR_UNSUPPORTED
+    rc = emu_lib.fc_rms_norm_fwd(3, 4, 7, A.p(x), A.p(x), A.p(x), 1e-6, 2, A.p(x), A.p(x), None)
+    assert rc == N.FC_ERR_INVALID
+    rc = emu_lib.fc_rms_norm_bwd(3, 4, N.FC_F64, None, A.p(x), A.p(x), A.p(x), A.p(x), 2, A.p(x), None)
+    assert rc == N.FC_ERR_INVALID
+    assert b"null" in emu_lib.fc_last_error()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-12), (torch.float32, 2e-6)])
+@pytest.mark.parametrize("l_max,C", [(3, 128), (2, 64), (1, 96)])
+def test_gpu_fused_rms_norm_matches_composed(cuda_device, dtype, tol, l_max, C):
+    """RMSLayerNorm inside first_order_only (fused kernels) against the same module outside
+    it (composed tensor-product path), forward and input gradient."""
+    from flashcart_b200 import ops
+    from flashcart_b200.nn.layers import RMSLayerNorm
+
+    torch.manual_seed(3)
+    norm = RMSLayerNorm(l_max, C, eps=1e-6).to(cuda_device, dtype)
+    with torch.no_grad():
+        for w in norm.weights:
+            w.add_(0.3 * torch.randn_like(w))
+    for p in norm.parameters():
+        p.requires_grad_(False)
+    x = torch.randn(1000, (l_max + 1) ** 2 * C, device=cuda_device, dtype=dtype, requires_grad=True)
+    gy = torch.randn_like(x)
+    ref = norm(x)
+    (ref_gx,) = torch.autograd.grad(ref, [x], gy)
+    with ops.first_order_only():
+        assert norm._fused_ok(x)
+        out = norm(x)
+        (gx,) = torch.autograd.grad(out, [x], gy)
+    ops.check_device_status(cuda_device)
+    assert (out - ref).abs().max().item() < tol * ref.abs().max().item()
+    assert (gx - ref_gx).abs().max().item() < tol * ref_gx.abs().max().item()
+
+
+@pytest.mark.gpu
+def test_gpu_fused_rms_norm_refuses_second_derivative(cuda_device):
+    from flashcart_b200 import ops
+    from flashcart_b200.nn.layers import RMSLayerNorm
+
+    norm = RMSLayerNorm(2, 32).to(cuda_device)
+    for p in norm.parameters():
+        p.requires_grad_(False)
+    x = torch.randn(10, 9 * 32, device=cuda_device, requires_grad=True)
+    with ops.first_order_only():
+        y = norm(x)
+        with pytest.raises(RuntimeError, match="second derivative"):
+            torch.autograd.grad(y.square().sum(), [x], create_graph=True)
