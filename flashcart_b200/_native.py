@@ -36,7 +36,7 @@ EXPORTED_SYMBOLS = (
     "fc_version", "fc_last_error", "fc_build_rowptr", "fc_tp_num_paths", "fc_tp_out_dim",
     "fc_tp_fwd", "fc_tp_bwd", "fc_tp_dbwd", "fc_irreps_fwd", "fc_irreps_bwd", "fc_irreps_dbwd",
     "fc_linear_fwd", "fc_linear_bwd", "fc_tp_conv_fwd_noalloc", "fc_newton_schulz",
-    "fc_rms_norm_fwd", "fc_rms_norm_bwd",
+    "fc_rms_norm_fwd", "fc_rms_norm_bwd", "fc_gate_fwd", "fc_gate_bwd",
 )
 
 
@@ -106,6 +106,10 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_rms_norm_fwd.argtypes = [_I32, _I32, _I32, _P, _P, _P, ctypes.c_double, _I64, _P, _P, _P]
     lib.fc_rms_norm_bwd.restype = ctypes.c_int
     lib.fc_rms_norm_bwd.argtypes = [_I32, _I32, _I32, _P, _P, _P, _P, _P, _I64, _P, _P]
+    lib.fc_gate_fwd.restype = ctypes.c_int
+    lib.fc_gate_fwd.argtypes = [_I32, _I32, _I32, _P, _P, _I64, _P, _P]
+    lib.fc_gate_bwd.restype = ctypes.c_int
+    lib.fc_gate_bwd.argtypes = [_I32, _I32, _I32, _P, _P, _P, _I64, _P, _P, _P]
     return lib
 
 

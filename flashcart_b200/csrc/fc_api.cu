@@ -24,6 +24,10 @@ template <typename T>
 int rms_norm_fwd_dispatch(int, const T*, const T*, const T*, T, int, int64_t, T*, T*, cudaStream_t);
 template <typename T>
 int rms_norm_bwd_dispatch(int, const T*, const T*, const T*, const T*, const T*, int, int64_t, T*, cudaStream_t);
+template <typename T>
+int gate_fwd_dispatch(int, const T*, const T*, T*, int, int64_t, cudaStream_t);
+template <typename T>
+int gate_bwd_dispatch(int, const T*, const T*, const T*, T*, T*, int, int64_t, cudaStream_t);
 
 static thread_local std::string g_last_error;
 
@@ -619,6 +623,40 @@ int fc_rms_norm_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* 
                                                      (const double*)gains, (const double*)l_weights,
                                                      (const double*)rstd, features, n_rows, (double*)grad_x, s),
                        "fc_rms_norm_bwd");
+}
+
+// ------------------------------------------------------------------ equivariant gate
+
+int fc_gate_fwd(int32_t l_max, int32_t features, int32_t dtype, const void* values, const void* gates,
+                int64_t n_rows, void* y, fc_stream_t stream) {
+  if (int rc = rms_check(l_max, features, dtype, n_rows, "fc_gate_fwd")) return rc;
+  if (n_rows == 0) return FC_OK;
+  if (!values || !gates || !y) return fail(FC_ERR_INVALID, "fc_gate_fwd: null pointer");
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == FC_F32)
+    return launch_status(gate_fwd_dispatch<float>(l_max, (const float*)values, (const float*)gates, (float*)y,
+                                                  features, n_rows, s),
+                         "fc_gate_fwd");
+  return launch_status(gate_fwd_dispatch<double>(l_max, (const double*)values, (const double*)gates, (double*)y,
+                                                 features, n_rows, s),
+                       "fc_gate_fwd");
+}
+
+int fc_gate_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* grad_y, const void* values,
+                const void* gates, int64_t n_rows, void* grad_values, void* grad_gates, fc_stream_t stream) {
+  if (int rc = rms_check(l_max, features, dtype, n_rows, "fc_gate_bwd")) return rc;
+  if (n_rows == 0) return FC_OK;
+  if (!grad_y || !values || !gates) return fail(FC_ERR_INVALID, "fc_gate_bwd: null pointer");
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == FC_F32)
+    return launch_status(gate_bwd_dispatch<float>(l_max, (const float*)grad_y, (const float*)values,
+                                                  (const float*)gates, (float*)grad_values, (float*)grad_gates,
+                                                  features, n_rows, s),
+                         "fc_gate_bwd");
+  return launch_status(gate_bwd_dispatch<double>(l_max, (const double*)grad_y, (const double*)values,
+                                                 (const double*)gates, (double*)grad_values, (double*)grad_gates,
+                                                 features, n_rows, s),
+                       "fc_gate_bwd");
 }
 
 // Muon Newton-Schulz orthogonalisation (see the header).

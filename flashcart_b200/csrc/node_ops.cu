@@ -1,4 +1,5 @@
-// Fused RMS layer norm of Cartesian node features (forward and first-order backward).
+// Fused RMS layer norm and equivariant gate of Cartesian node features (forward and
+// first-order backward).
 //
 // One node row holds the rank blocks l = 0..L of F channels each, component axis outer
 // and channels contiguous (row length (L+1)^2 F). Per row:
@@ -225,5 +226,122 @@ template int rms_norm_bwd_dispatch<float>(int, const float*, const float*, const
                                           int, int64_t, float*, cudaStream_t);
 template int rms_norm_bwd_dispatch<double>(int, const double*, const double*, const double*, const double*,
                                            const double*, int, int64_t, double*, cudaStream_t);
+
+}  // namespace fc
+
+// ------------------------------------------------------------------ equivariant gate
+// y[n, (l, m), c] = v[n, (l, m), c] * gate[n, l, c] over the rank blocks of a row, and its
+// first-order backward: grad_v = g * gate, grad_gate[n, l, c] = sum_m g v. One thread per
+// (row, channel) walks the (L+1)^2 components, so every access is coalesced over channels.
+namespace fc {
+
+template <typename T, int L>
+FC_HD FC_INLINE void gate_fwd_one(const T* __restrict__ v, const T* __restrict__ gate, T* __restrict__ y, int F,
+                                  int64_t row, int c) {
+  constexpr int NC = (L + 1) * (L + 1);
+  const T* vr = v + row * (int64_t)(NC * F) + c;
+  T* yr = y + row * (int64_t)(NC * F) + c;
+  const T* gr = gate + row * (int64_t)((L + 1) * F) + c;
+  T gl[L + 1];
+  for (int l = 0; l <= L; ++l) gl[l] = fc_ldg(gr + l * F);
+#ifdef __CUDA_ARCH__
+#pragma unroll
+#endif
+  for (int k = 0; k < NC; ++k) yr[k * F] = fc_ldg(vr + k * F) * gl[rms_rank_of(k)];
+}
+
+template <typename T, int L>
+FC_HD FC_INLINE void gate_bwd_one(const T* __restrict__ g, const T* __restrict__ v, const T* __restrict__ gate,
+                                  T* __restrict__ gv, T* __restrict__ ggate, int F, int64_t row, int c) {
+  constexpr int NC = (L + 1) * (L + 1);
+  const int64_t o = row * (int64_t)(NC * F) + c;
+  const T* gr = gate + row * (int64_t)((L + 1) * F) + c;
+  T gl[L + 1], acc[L + 1];
+  for (int l = 0; l <= L; ++l) {
+    gl[l] = fc_ldg(gr + l * F);
+    acc[l] = T(0);
+  }
+#ifdef __CUDA_ARCH__
+#pragma unroll
+#endif
+  for (int k = 0; k < NC; ++k) {
+    const int l = rms_rank_of(k);
+    const T gk = fc_ldg(g + o + k * F);
+    if (gv) gv[o + k * F] = gk * gl[l];
+    acc[l] += gk * fc_ldg(v + o + k * F);
+  }
+  if (ggate)
+    for (int l = 0; l <= L; ++l) ggate[row * (int64_t)((L + 1) * F) + l * F + c] = acc[l];
+}
+
+#ifndef FC_HOST_EMU
+template <typename T, int L>
+__global__ void gate_fwd_kernel(const T* v, const T* gate, T* y, int F, int64_t n) {
+  const int64_t total = n * F;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x)
+    gate_fwd_one<T, L>(v, gate, y, F, t / F, (int)(t % F));
+}
+template <typename T, int L>
+__global__ void gate_bwd_kernel(const T* g, const T* v, const T* gate, T* gv, T* ggate, int F, int64_t n) {
+  const int64_t total = n * F;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x)
+    gate_bwd_one<T, L>(g, v, gate, gv, ggate, F, t / F, (int)(t % F));
+}
+static int gate_grid(int64_t threads) {
+  const int64_t b = (threads + 255) / 256;
+  return (int)(b < 148 * 64 ? (b < 1 ? 1 : b) : 148 * 64);
+}
+template <typename T, int L>
+static int gate_fwd_launch(const T* v, const T* gate, T* y, int F, int64_t n, cudaStream_t s) {
+  gate_fwd_kernel<T, L><<<gate_grid(n * F), 256, 0, s>>>(v, gate, y, F, n);
+  return fc_check_launch();
+}
+template <typename T, int L>
+static int gate_bwd_launch(const T* g, const T* v, const T* gate, T* gv, T* ggate, int F, int64_t n,
+                           cudaStream_t s) {
+  gate_bwd_kernel<T, L><<<gate_grid(n * F), 256, 0, s>>>(g, v, gate, gv, ggate, F, n);
+  return fc_check_launch();
+}
+#else
+template <typename T, int L>
+static int gate_fwd_launch(const T* v, const T* gate, T* y, int F, int64_t n, cudaStream_t) {
+  for (int64_t r = 0; r < n; ++r)
+    for (int c = 0; c < F; ++c) gate_fwd_one<T, L>(v, gate, y, F, r, c);
+  return 0;
+}
+template <typename T, int L>
+static int gate_bwd_launch(const T* g, const T* v, const T* gate, T* gv, T* ggate, int F, int64_t n, cudaStream_t) {
+  for (int64_t r = 0; r < n; ++r)
+    for (int c = 0; c < F; ++c) gate_bwd_one<T, L>(g, v, gate, gv, ggate, F, r, c);
+  return 0;
+}
+#endif
+
+template <typename T>
+int gate_fwd_dispatch(int l_max, const T* v, const T* gate, T* y, int F, int64_t n, cudaStream_t s) {
+  switch (l_max) {
+    case 0: return gate_fwd_launch<T, 0>(v, gate, y, F, n, s);
+    case 1: return gate_fwd_launch<T, 1>(v, gate, y, F, n, s);
+    case 2: return gate_fwd_launch<T, 2>(v, gate, y, F, n, s);
+    default: return gate_fwd_launch<T, 3>(v, gate, y, F, n, s);
+  }
+}
+template <typename T>
+int gate_bwd_dispatch(int l_max, const T* g, const T* v, const T* gate, T* gv, T* ggate, int F, int64_t n,
+                      cudaStream_t s) {
+  switch (l_max) {
+    case 0: return gate_bwd_launch<T, 0>(g, v, gate, gv, ggate, F, n, s);
+    case 1: return gate_bwd_launch<T, 1>(g, v, gate, gv, ggate, F, n, s);
+    case 2: return gate_bwd_launch<T, 2>(g, v, gate, gv, ggate, F, n, s);
+    default: return gate_bwd_launch<T, 3>(g, v, gate, gv, ggate, F, n, s);
+  }
+}
+
+template int gate_fwd_dispatch<float>(int, const float*, const float*, float*, int, int64_t, cudaStream_t);
+template int gate_fwd_dispatch<double>(int, const double*, const double*, double*, int, int64_t, cudaStream_t);
+template int gate_bwd_dispatch<float>(int, const float*, const float*, const float*, float*, float*, int, int64_t,
+                                      cudaStream_t);
+template int gate_bwd_dispatch<double>(int, const double*, const double*, const double*, double*, double*, int,
+                                       int64_t, cudaStream_t);
 
 }  // namespace fc

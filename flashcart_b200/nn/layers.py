@@ -355,6 +355,10 @@ class EquivariantGatedLayer(_ChildSpecialParameters, nn.Module):
         values = self.value_linear(node_feats)
         gates = self.gate_activation(self.gate_linear(node_feats[:, :self.in_features]))
         gates = gates.view(n, self.l_max + 1, self.hidden_features)
+        if ops.first_order_only_active() and values.is_cuda and values.dtype in (torch.float32, torch.float64):
+            # one fused pass over the rank blocks (first derivative only)
+            gated = ops.gate_fwd(values, gates, self.l_max, self.hidden_features)
+            return node_feats + self.output_linear(gated)
         parts = []
         for l, (a, b) in enumerate(self.hidden_slices):
             parts.append((values[:, a:b].view(n, 2 * l + 1, self.hidden_features) * gates[:, l].unsqueeze(1))
@@ -481,7 +485,7 @@ class ProductLayer(_ChildSpecialParameters, nn.Module):
             self.step0_weight_index = None
 
     def forward(self, node_feats, atom_types=None):
-        out = node_feats.new_zeros(node_feats.shape[0], self.out_dim)
+        out = None  # sum of the selected products (the reference starts from zeros; 0 + x == x)
         prod = node_feats
         for step in range(self.correlation):
             if step == 0:
@@ -499,7 +503,8 @@ class ProductLayer(_ChildSpecialParameters, nn.Module):
                     prod = prod * getattr(self, name)
             else:
                 prod = self.product_linears[step](prod)
-            out = out + self.irreps_selectors[step](prod)
+            sel = self.irreps_selectors[step](prod)
+            out = sel if out is None else out + sel
         if self.path_reduced:
             out = self.final_linear(out)
         if self.skip_projection is not None:

@@ -855,3 +855,69 @@ def rms_norm(x: Tensor, gains: Tensor, l_weights: Tensor, l_max: int, features: 
     """``y = x * (mean_c sum_l l_weights[l] inv_l + eps)^-1/2 * gains[l, c]`` per row (first
     derivative only, see :func:`first_order_only`)."""
     return rms_norm_fwd(x, gains, l_weights, l_max, features, eps)[0]
+
+
+# --------------------------------------------------------------------------- fused equivariant gate
+
+
+@torch.library.custom_op("flashcart::gate_fwd", mutates_args=())
+def gate_fwd(values: Tensor, gates: Tensor, l_max: int, features: int) -> Tensor:
+    """``y[n, (l, m), c] = values[n, (l, m), c] * gates[n, l, c]`` over every rank block
+    (the per-rank products and concatenation of ``EquivariantGatedLayer.forward``,
+    reference ``nn/layers.py:609-635``)."""
+    _require_cuda(values, gates)
+    v, g = values.contiguous(), gates.contiguous()
+    if v.dim() != 2 or v.shape[1] != (l_max + 1) ** 2 * features or g.numel() != v.shape[0] * (l_max + 1) * features:
+        raise ValueError("gate: values must be (n, (l_max+1)^2 features) and gates (n, l_max+1, features)")
+    if g.dtype != v.dtype or v.dtype not in (torch.float32, torch.float64):
+        raise ValueError("gate: values and gates must share a float32 / float64 dtype")
+    lib = N.lib()
+    y = torch.empty_like(v)
+    with _timed("gate_fwd", 1, _nbytes(v, g, y)):
+        rc = lib.fc_gate_fwd(int(l_max), int(features), _code(v.dtype), _p(v), _p(g), v.shape[0], _p(y),
+                             _stream(v.device))
+    _after(lib, rc, "fc_gate_fwd", v.device)
+    return y
+
+
+@gate_fwd.register_fake
+def _(values, gates, l_max, features):
+    return torch.empty_like(values)
+
+
+@torch.library.custom_op("flashcart::gate_bwd", mutates_args=())
+def gate_bwd(grad_y: Tensor, values: Tensor, gates: Tensor, l_max: int, features: int) -> Tuple[Tensor, Tensor]:
+    """First-order backward of :func:`gate_fwd`: (grad_values, grad_gates)."""
+    _require_cuda(grad_y, values, gates)
+    gy, v, g = grad_y.contiguous(), values.contiguous(), gates.contiguous()
+    lib = N.lib()
+    gv = torch.empty_like(v)
+    gg = torch.empty(g.shape, dtype=g.dtype, device=g.device)
+    with _timed("gate_bwd", 1, _nbytes(gy, v, g, gv, gg)):
+        rc = lib.fc_gate_bwd(int(l_max), int(features), _code(v.dtype), _p(gy), _p(v), _p(g), v.shape[0], _p(gv),
+                             _p(gg), _stream(v.device))
+    _after(lib, rc, "fc_gate_bwd", v.device)
+    return gv, gg
+
+
+@gate_bwd.register_fake
+def _(grad_y, values, gates, l_max, features):
+    return torch.empty_like(values), torch.empty_like(gates)
+
+
+def _gate_setup(ctx, inputs, output):
+    values, gates, l_max, features = inputs
+    ctx.save_for_backward(values, gates)
+    ctx.l_max, ctx.features = l_max, features
+
+
+def _gate_backward(ctx, grad_y):
+    if torch.is_grad_enabled():
+        raise RuntimeError("flashcart::gate_fwd was evaluated inside first_order_only(); its backward cannot "
+                           "build a graph for a second derivative")
+    values, gates = ctx.saved_tensors
+    gv, gg = gate_bwd(grad_y.contiguous(), values, gates, ctx.l_max, ctx.features)
+    return (gv if ctx.needs_input_grad[0] else None), (gg if ctx.needs_input_grad[1] else None), None, None
+
+
+gate_fwd.register_autograd(_gate_backward, setup_context=_gate_setup)

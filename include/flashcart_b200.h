@@ -211,6 +211,17 @@ int fc_rms_norm_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* 
                     const void* gains, const void* l_weights, const void* rstd, int64_t n_rows,
                     void* grad_x, fc_stream_t stream);
 
+/* ---------------------------------------------------------------- equivariant gate
+ * The gating product of EquivariantGatedLayer.forward (nn/layers.py:609-635):
+ * y[n, (l, m), c] = values[n, (l, m), c] * gates[n, l, c] for every rank block of a row
+ * (the reference's per-rank multiply and concatenation), and its first-order backward.
+ * values, y, grad_y, grad_values: (n_rows, (l_max+1)^2 * features) rows; gates,
+ * grad_gates: (n_rows, l_max+1, features). grad_values or grad_gates may be NULL. */
+int fc_gate_fwd(int32_t l_max, int32_t features, int32_t dtype, const void* values, const void* gates,
+                int64_t n_rows, void* y, fc_stream_t stream);
+int fc_gate_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* grad_y, const void* values,
+                const void* gates, int64_t n_rows, void* grad_values, void* grad_gates, fc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

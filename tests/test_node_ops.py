@@ -1,10 +1,12 @@
-"""Fused RMS layer norm (fc_rms_norm_fwd / fc_rms_norm_bwd, flashcart::rms_norm_*).
+"""Fused node-level operators: RMS layer norm (fc_rms_norm_*, flashcart::rms_norm_*) and
+the equivariant gate (fc_gate_*, flashcart::gate_*).
 
-The fused kernels replace the composition of the reference's RMSLayerNorm
-(nn/layers.py:413-540: symmetric scalar tensor product of the features with
-themselves, per-rank weights 1/((2l+1)(l_max+1)), channel mean, (mean_sq + eps)^-1/2,
-per-rank gains) when the graph is differentiated once. The oracle here is that
-composition on the oracle tensor product, differentiated by autograd.
+The fused kernels replace compositions of the reference when the graph is
+differentiated once: RMSLayerNorm (nn/layers.py:413-540: symmetric scalar tensor
+product of the features with themselves, per-rank weights 1/((2l+1)(l_max+1)), channel
+mean, (mean_sq + eps)^-1/2, per-rank gains) and the per-rank gating products of
+EquivariantGatedLayer (nn/layers.py:609-635). The oracles are those compositions (on the
+oracle tensor product), differentiated by autograd.
 """
 
 import ctypes
@@ -106,3 +108,60 @@ def test_gpu_fused_rms_norm_refuses_second_derivative(cuda_device):
         y = norm(x)
         with pytest.raises(RuntimeError, match="second derivative"):
             torch.autograd.grad(y.square().sum(), [x], create_graph=True)
+
+
+def _gate_composed(values, gates, l_max, H):
+    n = values.shape[0]
+    parts, a = [], 0
+    for l in range(l_max + 1):
+        b = a + (2 * l + 1) * H
+        parts.append((values[:, a:b].view(n, 2 * l + 1, H) * gates[:, l].unsqueeze(1)).flatten(1))
+        a = b
+    return torch.cat(parts, dim=-1)
+
+
+@pytest.mark.parametrize("l_max,H", [(0, 4), (2, 7), (3, 16)])
+def test_emu_gate_matches_composition(emu_lib, l_max, H):
+    g = torch.Generator().manual_seed(11 + l_max)
+    n = 6
+    v = torch.randn(n, (l_max + 1) ** 2 * H, generator=g, dtype=torch.float64)
+    gt = torch.randn(n, l_max + 1, H, generator=g, dtype=torch.float64)
+    vr, gr = v.clone().requires_grad_(True), gt.clone().requires_grad_(True)
+    ref = _gate_composed(vr, gr, l_max, H)
+    gy = torch.randn_like(ref)
+    ref_gv, ref_gg = torch.autograd.grad(ref, [vr, gr], gy)
+    y = torch.empty_like(v)
+    N.check(emu_lib, emu_lib.fc_gate_fwd(l_max, H, N.FC_F64, A.p(v), A.p(gt), n, A.p(y), None), "fc_gate_fwd")
+    gv, gg = torch.empty_like(v), torch.empty_like(gt)
+    N.check(emu_lib, emu_lib.fc_gate_bwd(l_max, H, N.FC_F64, A.p(gy), A.p(v), A.p(gt), n, A.p(gv), A.p(gg), None),
+            "fc_gate_bwd")
+    assert torch.equal(y, ref.detach())
+    assert (gv - ref_gv).abs().max().item() < 1e-14 * ref_gv.abs().max().item()
+    assert (gg - ref_gg).abs().max().item() < 1e-12 * ref_gg.abs().max().item()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-12), (torch.float32, 2e-6)])
+def test_gpu_fused_gated_layer_matches_composed(cuda_device, dtype, tol):
+    """EquivariantGatedLayer inside first_order_only (fused gate) against the same layer
+    outside it, forward and input gradient."""
+    from flashcart_b200 import ops
+    from flashcart_b200.nn.layers import EquivariantGatedLayer
+
+    torch.manual_seed(5)
+    layer = EquivariantGatedLayer(3, 128, gate_activation="sigmoid").to(cuda_device, dtype)
+    with torch.no_grad():
+        for w in layer.output_linear.weight:
+            w.normal_()
+    for p in layer.parameters():
+        p.requires_grad_(False)
+    x = torch.randn(700, 16 * 128, device=cuda_device, dtype=dtype, requires_grad=True)
+    gy = torch.randn_like(x)
+    ref = layer(x)
+    (ref_gx,) = torch.autograd.grad(ref, [x], gy)
+    with ops.first_order_only():
+        out = layer(x)
+        (gx,) = torch.autograd.grad(out, [x], gy)
+    ops.check_device_status(cuda_device)
+    assert (out - ref).abs().max().item() < tol * ref.abs().max().item()
+    assert (gx - ref_gx).abs().max().item() < tol * ref_gx.abs().max().item()
