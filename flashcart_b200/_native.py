@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "fc_tp_fwd", "fc_tp_bwd", "fc_tp_dbwd", "fc_irreps_fwd", "fc_irreps_bwd", "fc_irreps_dbwd",
     "fc_linear_fwd", "fc_linear_bwd", "fc_tp_conv_fwd_noalloc", "fc_newton_schulz",
     "fc_rms_norm_fwd", "fc_rms_norm_bwd", "fc_gate_fwd", "fc_gate_bwd",
+    "fc_neighbor_workspace_bytes", "fc_neighbor_count", "fc_neighbor_fill",
 )
 
 
@@ -57,6 +58,12 @@ class LinearDesc(ctypes.Structure):
         ("f_in_values", ctypes.c_int32 * (FC_MAX_L + 1)),
         ("f_out_values", ctypes.c_int32 * (FC_MAX_L + 1)),
     ]
+
+
+class NlDesc(ctypes.Structure):
+    _fields_ = [("lengths", ctypes.c_double * 3), ("inv_lengths", ctypes.c_double * 3),
+                ("bin_widths", ctypes.c_double * 3), ("r_max_sq", ctypes.c_double),
+                ("bins", ctypes.c_int32 * 3), ("reserved", ctypes.c_int32)]
 
 
 class NativeError(RuntimeError):
@@ -106,6 +113,12 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_rms_norm_fwd.argtypes = [_I32, _I32, _I32, _P, _P, _P, ctypes.c_double, _I64, _P, _P, _P]
     lib.fc_rms_norm_bwd.restype = ctypes.c_int
     lib.fc_rms_norm_bwd.argtypes = [_I32, _I32, _I32, _P, _P, _P, _P, _P, _I64, _P, _P]
+    lib.fc_neighbor_workspace_bytes.restype = ctypes.c_int64
+    lib.fc_neighbor_workspace_bytes.argtypes = [ctypes.POINTER(NlDesc), _I64]
+    lib.fc_neighbor_count.restype = ctypes.c_int
+    lib.fc_neighbor_count.argtypes = [ctypes.POINTER(NlDesc), _P, _I64, _P, _P, _P, _P]
+    lib.fc_neighbor_fill.restype = ctypes.c_int
+    lib.fc_neighbor_fill.argtypes = [ctypes.POINTER(NlDesc), _I64, _P, _P, _I64, _P, _P, _P, _P]
     lib.fc_gate_fwd.restype = ctypes.c_int
     lib.fc_gate_fwd.argtypes = [_I32, _I32, _I32, _P, _P, _I64, _P, _P]
     lib.fc_gate_bwd.restype = ctypes.c_int

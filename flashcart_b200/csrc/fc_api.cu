@@ -24,6 +24,11 @@ template <typename T>
 int rms_norm_fwd_dispatch(int, const T*, const T*, const T*, T, int, int64_t, T*, T*, cudaStream_t);
 template <typename T>
 int rms_norm_bwd_dispatch(int, const T*, const T*, const T*, const T*, const T*, int, int64_t, T*, cudaStream_t);
+int64_t nl_workspace_bytes(int64_t n, int64_t nbins);
+#ifndef FC_HOST_EMU
+int nl_count(const fc_nl_desc*, const double*, int64_t, void*, int64_t*, int*, cudaStream_t);
+int nl_fill(const fc_nl_desc*, int64_t, const void*, const int64_t*, int64_t, int64_t*, int32_t*, int*, cudaStream_t);
+#endif
 template <typename T>
 int gate_fwd_dispatch(int, const T*, const T*, T*, int, int64_t, cudaStream_t);
 template <typename T>
@@ -657,6 +662,67 @@ int fc_gate_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* grad
                                                  (const double*)gates, (double*)grad_values, (double*)grad_gates,
                                                  features, n_rows, s),
                        "fc_gate_bwd");
+}
+
+// ------------------------------------------------------------------ neighbour list
+
+static int nl_check(const fc_nl_desc* d, int64_t n, const char* what) {
+  if (!d) return fail(FC_ERR_INVALID, "%s: null descriptor", what);
+  if (n < 0 || n > 0x7fffffffLL) return fail(FC_ERR_INVALID, "%s: atom count %lld outside 0..2^31-1", what,
+                                             (long long)n);
+  if (!(d->r_max_sq > 0.0)) return fail(FC_ERR_INVALID, "%s: r_max must be positive", what);
+  for (int k = 0; k < 3; ++k) {
+    if (!(d->lengths[k] > 0.0) || !(d->inv_lengths[k] > 0.0))
+      return fail(FC_ERR_INVALID, "%s: cell lengths must be positive", what);
+    if (d->bins[k] < 3)
+      return fail(FC_ERR_UNSUPPORTED, "%s: %d bins on axis %d; the cell list needs at least 3 (use the host list)",
+                  what, d->bins[k], k);
+    if (!(d->bin_widths[k] * d->bin_widths[k] >= d->r_max_sq))
+      return fail(FC_ERR_INVALID, "%s: bin width below r_max on axis %d", what, k);
+  }
+  if ((int64_t)d->bins[0] * d->bins[1] * d->bins[2] > (int64_t)1 << 30)
+    return fail(FC_ERR_UNSUPPORTED, "%s: too many bins", what);
+  return FC_OK;
+}
+
+int64_t fc_neighbor_workspace_bytes(const fc_nl_desc* desc, int64_t n_atoms) {
+  if (int rc = nl_check(desc, n_atoms, "fc_neighbor_workspace_bytes")) return rc;
+  return nl_workspace_bytes(n_atoms, (int64_t)desc->bins[0] * desc->bins[1] * desc->bins[2]);
+}
+
+int fc_neighbor_count(const fc_nl_desc* desc, const double* positions, int64_t n_atoms, void* workspace,
+                      int64_t* rowptr, int32_t* status, fc_stream_t stream) {
+  if (int rc = nl_check(desc, n_atoms, "fc_neighbor_count")) return rc;
+  if (!rowptr || (n_atoms > 0 && (!positions || !workspace)))
+    return fail(FC_ERR_INVALID, "fc_neighbor_count: null pointer");
+#ifdef FC_HOST_EMU
+  (void)status; (void)stream;
+  return fail(FC_ERR_UNSUPPORTED, "fc_neighbor_count: GPU kernel only");
+#else
+  if (n_atoms == 0)
+    return cudaMemsetAsync(rowptr, 0, sizeof(int64_t), (cudaStream_t)stream) == cudaSuccess
+               ? FC_OK
+               : fail(FC_ERR_LAUNCH, "fc_neighbor_count: memset failed");
+  return launch_status(nl_count(desc, positions, n_atoms, workspace, rowptr, reinterpret_cast<int*>(status),
+                                (cudaStream_t)stream),
+                       "fc_neighbor_count");
+#endif
+}
+
+int fc_neighbor_fill(const fc_nl_desc* desc, int64_t n_atoms, const void* workspace, const int64_t* rowptr,
+                     int64_t n_edges, int64_t* edge_index, int32_t* shifts, int32_t* status, fc_stream_t stream) {
+  if (int rc = nl_check(desc, n_atoms, "fc_neighbor_fill")) return rc;
+  if (n_edges < 0) return fail(FC_ERR_INVALID, "fc_neighbor_fill: negative edge count");
+  if (n_atoms == 0 || n_edges == 0) return FC_OK;
+  if (!workspace || !rowptr || !edge_index || !shifts) return fail(FC_ERR_INVALID, "fc_neighbor_fill: null pointer");
+#ifdef FC_HOST_EMU
+  (void)status; (void)stream;
+  return fail(FC_ERR_UNSUPPORTED, "fc_neighbor_fill: GPU kernel only");
+#else
+  return launch_status(nl_fill(desc, n_atoms, workspace, rowptr, n_edges, edge_index, shifts,
+                               reinterpret_cast<int*>(status), (cudaStream_t)stream),
+                       "fc_neighbor_fill");
+#endif
 }
 
 // Muon Newton-Schulz orthogonalisation (see the header).

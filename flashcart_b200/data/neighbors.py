@@ -10,9 +10,12 @@ order -- lexicographic in (i, j, S_x, S_y, S_z) -- with the distance test in flo
 * ``neighbor_list_bruteforce``: every (i, j) against every periodic image that can be
   within r_max (small systems, and the oracle of the cell list);
 * ``neighbor_list``: a binned cell list for orthorhombic cells of at least three bins
-  per periodic axis, falling back to the brute force otherwise.
-Both evaluate the identical expression for the distance, so their edge sets agree
-exactly.
+  per periodic axis, falling back to the brute force otherwise;
+* ``neighbor_list_device``: the same cell list as sm_100a kernels (``fc_neighbor_count``
+  / ``fc_neighbor_fill``), the edges built and sorted on the GPU and returned as device
+  tensors (``neighbor_list(device="cuda")`` uses it when the cell qualifies).
+All evaluate the same float64 expressions for the wrap, the bins and the distance, so
+their edge sets and orders agree exactly.
 """
 
 from __future__ import annotations
@@ -77,20 +80,88 @@ def neighbor_list_bruteforce(positions, cell, pbc, r_max: float, chunk: int = 51
     return _canonical(i, j, s)
 
 
+def _cell_list_geometry(cell: np.ndarray, pbc, r_max: float):
+    """(lengths, bins) of the binned search, or None when the cell does not qualify
+    (not orthorhombic, not periodic on every axis, fewer than three bins on an axis)."""
+    lengths = np.diag(cell)
+    ortho = np.allclose(cell, np.diag(lengths))
+    nb = np.floor(lengths / r_max).astype(np.int64)
+    if not ortho or not all(pbc) or (nb < 3).any():
+        return None
+    return lengths, nb
+
+
+def neighbor_list_device(positions, cell, pbc, r_max: float, device="cuda"):
+    """Cell list on the GPU: ``(edge_index (2, E) int64, shifts (E, 3) int32)`` as tensors on
+    ``device``, equal to :func:`neighbor_list` element for element. ``positions`` may be a
+    host array or a tensor (float64 is used). Raises ``NotImplementedError`` for cells the
+    binned search does not cover (use :func:`neighbor_list`)."""
+    import ctypes
+
+    from flashcart_b200 import _native as N
+    from flashcart_b200.ops import _after, _stream, status_word
+
+    cell = np.asarray(cell, dtype=np.float64)
+    geo = _cell_list_geometry(cell, pbc, r_max)
+    if geo is None:
+        raise NotImplementedError("neighbor_list_device needs an orthorhombic periodic cell with at least three "
+                                  "bins of r_max per axis")
+    lengths, nb = geo
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        raise RuntimeError("neighbor_list_device runs on CUDA devices only")
+    pos = torch.as_tensor(positions, dtype=torch.float64).to(dev).contiguous()
+    n = pos.shape[0]
+    d = N.NlDesc()
+    inv = np.linalg.inv(cell)
+    width = lengths / nb
+    for k in range(3):
+        d.lengths[k] = float(lengths[k])
+        d.inv_lengths[k] = float(inv[k, k])
+        d.bin_widths[k] = float(width[k])
+        d.bins[k] = int(nb[k])
+    d.r_max_sq = float(r_max) * float(r_max)
+    lib = N.lib()
+    nbytes = lib.fc_neighbor_workspace_bytes(ctypes.byref(d), n)
+    N.check(lib, int(nbytes) if nbytes < 0 else 0, "fc_neighbor_workspace_bytes")
+    ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
+    rowptr = torch.empty(n + 1, dtype=torch.int64, device=dev)
+    status = ctypes.c_void_p(status_word(dev).data_ptr())
+    stream = _stream(dev)
+    rc = lib.fc_neighbor_count(ctypes.byref(d), ctypes.c_void_p(pos.data_ptr()), n, ctypes.c_void_p(ws.data_ptr()),
+                               ctypes.c_void_p(rowptr.data_ptr()), status, stream)
+    _after(lib, rc, "fc_neighbor_count", dev)
+    n_edges = int(rowptr[-1].item())
+    edge_index = torch.empty((2, n_edges), dtype=torch.int64, device=dev)
+    shifts = torch.empty((n_edges, 3), dtype=torch.int32, device=dev)
+    rc = lib.fc_neighbor_fill(ctypes.byref(d), n, ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(rowptr.data_ptr()),
+                              n_edges, ctypes.c_void_p(edge_index.data_ptr()) if n_edges else None,
+                              ctypes.c_void_p(shifts.data_ptr()) if n_edges else None, status, stream)
+    _after(lib, rc, "fc_neighbor_fill", dev)
+    from flashcart_b200.ops import check_device_status
+
+    check_device_status(dev)
+    return edge_index, shifts
+
+
 def neighbor_list(positions, cell, pbc, r_max: float, device: str = "cpu"):
     """Cell-list neighbour search (orthorhombic periodic cells), canonical order.
 
     Atoms are binned on the wrapped positions into >= r_max cubes; each bin is padded
     to the largest occupancy and compared with its 27 neighbouring bins in one batched
-    float64 distance evaluation (torch, on ``device``).
+    float64 distance evaluation (torch on the host). With a CUDA ``device`` the list is
+    built by the GPU kernels of :func:`neighbor_list_device` (same arithmetic, same
+    order) and returned as host arrays.
     """
     positions = np.asarray(positions, dtype=np.float64)
     cell = np.asarray(cell, dtype=np.float64)
-    lengths = np.diag(cell)
-    ortho = np.allclose(cell, np.diag(lengths))
-    nb = np.floor(lengths / r_max).astype(np.int64)
-    if not ortho or not all(pbc) or (nb < 3).any():
+    geo = _cell_list_geometry(cell, pbc, r_max)
+    if geo is None:
         return neighbor_list_bruteforce(positions, cell, pbc, r_max)
+    if torch.device(device).type == "cuda":
+        ei, sh = neighbor_list_device(positions, cell, pbc, r_max, device)
+        return ei.cpu().numpy(), sh.cpu().numpy()
+    lengths, nb = geo
     pw, wrap = _wrap(positions, cell, pbc)
     n = len(pw)
     b3 = np.minimum((pw / (lengths / nb)).astype(np.int64), nb - 1)

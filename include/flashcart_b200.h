@@ -222,6 +222,32 @@ int fc_gate_fwd(int32_t l_max, int32_t features, int32_t dtype, const void* valu
 int fc_gate_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* grad_y, const void* values,
                 const void* gates, int64_t n_rows, void* grad_values, void* grad_gates, fc_stream_t stream);
 
+/* ---------------------------------------------------------------- neighbour list
+ * Periodic cell list of an orthorhombic cell on the GPU. Replaces the host neighbour
+ * search that feeds the model (data/neighbors.py:120-143, matscipy neighbour_list("ijS"):
+ * pairs |r_j - r_i + S . cell| < r_max, self pair removed, row 0 = receiver i, row 1 =
+ * sender j, receivers ascending) with the canonical order (i, j, S) of
+ * flashcart_b200/data/neighbors.py and the same float64 arithmetic, so the two lists are
+ * equal element for element. Two calls: fc_neighbor_count bins the atoms into the
+ * caller's workspace (fc_neighbor_workspace_bytes) and writes the receiver CSR rowptr
+ * (n_atoms + 1 int64, rowptr[n_atoms] = number of edges); after reading n_edges the
+ * caller allocates edge_index (2, n_edges) int64 and shifts (n_edges, 3) int32 and calls
+ * fc_neighbor_fill with the same workspace. */
+typedef struct fc_nl_desc {
+  double lengths[3];     /* cell edge lengths (diagonal of the cell matrix) */
+  double inv_lengths[3]; /* diagonal of the inverse cell matrix (as the host list computes it) */
+  double bin_widths[3];  /* lengths / bins, each >= r_max */
+  double r_max_sq;       /* cutoff squared */
+  int32_t bins[3];       /* cell-list bins per axis, each >= 3 */
+  int32_t reserved;
+} fc_nl_desc;
+int64_t fc_neighbor_workspace_bytes(const fc_nl_desc* desc, int64_t n_atoms);
+int fc_neighbor_count(const fc_nl_desc* desc, const double* positions, int64_t n_atoms, void* workspace,
+                      int64_t* rowptr, int32_t* status, fc_stream_t stream);
+int fc_neighbor_fill(const fc_nl_desc* desc, int64_t n_atoms, const void* workspace, const int64_t* rowptr,
+                     int64_t n_edges, int64_t* edge_index, int32_t* shifts, int32_t* status,
+                     fc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
