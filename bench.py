@@ -53,6 +53,9 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--op-case", choices=["conv", "gemm"], default=None,
                     help="run one small operator case (for ncu captures) instead of the benchmark")
+    ap.add_argument("--config", type=int, choices=[1, 2, 3], default=3,
+                    help="3: the headline E+F+S step; 1: the isolated TP convolution microbenchmark; "
+                         "2: edge expansion + equivariant linear map (one GPU, one JSON line)")
     return ap.parse_args()
 
 
@@ -434,9 +437,127 @@ def run_op_case(case: str):
     print(json.dumps({"op_case": case, "ok": True}))
 
 
+def _event_ms(fn, reps: int, warmup: int) -> float:
+    for _ in range(max(warmup, 1)):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def _roof(nbytes: int, ms: float, peak: float, peak_src: str, traffic=None):
+    ach = nbytes / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "traffic": traffic,
+            "peak_source": f"{peak_src} (hbm_gbs)", "bytes_per_launch": nbytes, "ms_per_launch": ms}
+
+
+def run_config1(args):
+    """TensorProduct(2, 2, 2, 64, 1) convolution, E = 2^20 edges over
+    N = 2^16 nodes (receiver-sorted uniform indices), unit-vector moments scaled by
+    N(0,1) radial weights as in2, N(0,1) node features and path weights, forward and
+    backward with respect to in1, in2 and the weights; fp32."""
+    from flashcart_b200 import o3, ops
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    n, e, c = 65536, 1048576, 64
+    idx_i = torch.sort(torch.randint(0, n, (e,), device=dev, generator=g)).values
+    idx_j = torch.randint(0, n, (e,), device=dev, generator=g)
+    u = torch.randn(e, 3, device=dev, generator=g)
+    in2 = (o3.Irreps(2).forward_normalized(u / u.norm(dim=-1, keepdim=True))
+           * torch.randn(e, 1, device=dev, generator=g)).contiguous()
+    tp = o3.TensorProduct(2, 2, 2, c, 1)
+    in1 = torch.randn(n, tp.in1_dim, device=dev, generator=g)
+    w = torch.randn(e, tp.n_total_paths * c, device=dev, generator=g)
+    a = (idx_i, idx_j, 2, 2, 2, c, 1, False, False, tp._in1_offs, tp._in2_offs, tp._out_sizes, tp._n_paths_per_l,
+         tp.n_total_paths, False)
+    out = torch.ops.flashcart.tp_fwd(in1, in2, w, *a)
+    gout = torch.randn_like(out)
+    fwd = lambda: torch.ops.flashcart.tp_fwd(in1, in2, w, *a)
+    bwd = lambda: torch.ops.flashcart.tp_bwd(gout, in1, in2, w, *a, True, True, True)
+    reps = max(args.steps, 1)
+    fwd_ms, bwd_ms = _event_ms(fwd, reps, args.warmup), _event_ms(bwd, reps, args.warmup)
+    ops.check_device_status(dev)
+    idx = 8 * (2 * e + n + 1)
+    fwd_b = 4 * (in1.numel() + in2.numel() + w.numel() + out.numel()) + idx
+    bwd_b = 4 * (gout.numel() + 2 * in1.numel() + 2 * in2.numel() + 2 * w.numel()) + idx
+    peak, src = _peaks()
+    ms = fwd_ms + bwd_ms
+    print(json.dumps({
+        "metric": "TP convolution (2,2)->2 forward + backward, E=2^20, N=2^16, C=64 (BASELINE config 1)",
+        "value": e / (ms * 1e-3), "unit": "edges/s", "n_gpus": 1, "steps": reps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config1", "edges": e, "nodes": n, "channels": c, "paths": tp.n_total_paths,
+                   "l2": "inputs larger than L2 (weights 2.9 GB)"},
+        "roofline": {"fwd": _roof(fwd_b, fwd_ms, peak, src), "bwd": _roof(bwd_b, bwd_ms, peak, src)},
+    }), flush=True)
+
+
+def run_config2(args):
+    """2,000,000 edge vectors uniform in a 5 A ball; moments T^l(r^),
+    l <= 3, times h = Linear(8 -> 128)(Bessel(8, 5 A)(r) * cutoff_6(r)) laid out as
+    (E, 2048), then o3.LinearLayer(3, 3, 128, 128) with Xavier-normal weights and
+    weight_scale 1 (3xTF32 tensor-core path); forward, fp32."""
+    from flashcart_b200 import o3, ops
+    from flashcart_b200.nn.layers import LinearLayer
+    from flashcart_b200.nn.radial import BesselBasis, PolynomialCutoff
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    e, C = 2_000_000, 128
+    d = torch.randn(e, 3, device=dev, generator=g)
+    d = d / d.norm(dim=-1, keepdim=True)
+    r = 5.0 * torch.rand(e, device=dev, generator=g) ** (1.0 / 3.0)
+    v = d * r.unsqueeze(-1)
+    v = v[v.norm(dim=-1) >= 1e-4].contiguous()
+    e = v.shape[0]
+    torch.manual_seed(0)
+    lay = LinearLayer(8, C).to(dev)
+    lin = o3.LinearLayer(3, 3, C, C, weight_scale=1.0).to(dev)
+    with torch.no_grad():
+        for wl in lin.weight:
+            wl.normal_(0.0, (2.0 / (C + C)) ** 0.5)
+    basis, cut, irr = BesselBasis(8, 5.0).to(dev), PolynomialCutoff(5.0, 6).to(dev), o3.Irreps(3)
+    sizes = [(2 * l + 1) for l in range(4)]
+
+    def expand():
+        rr = v.norm(dim=-1)
+        T = irr.forward_normalized(v / rr.unsqueeze(-1))
+        h = lay(basis(rr) * cut(rr).unsqueeze(-1))
+        blocks = torch.split(T, sizes, dim=1)
+        return torch.cat([(b.unsqueeze(-1) * h.unsqueeze(1)).reshape(e, -1) for b in blocks], dim=-1)
+
+    with torch.no_grad():
+        x = expand()
+        reps = max(args.steps, 1)
+        exp_ms = _event_ms(expand, reps, args.warmup)
+        lin_ms = _event_ms(lambda: lin(x), reps, args.warmup)
+    ops.check_device_status(dev)
+    peak, src = _peaks()
+    ms = exp_ms + lin_ms
+    xb = x.numel() * 4
+    print(json.dumps({
+        "metric": "edge expansion + equivariant linear map 128->128, l<=3, 2,000,000 edges (BASELINE config 2)",
+        "value": e / (ms * 1e-3), "unit": "edges/s", "n_gpus": 1, "steps": reps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "dtype": "f32 (linear map: 3xTF32 tensor cores)",
+        "data": "synthetic", "config": {"workload": "config2", "edges": e, "channels": C,
+                                         "expansion": "unfused reference composition (torch) writing (E, 2048)"},
+        "roofline": {"expansion": _roof(e * 12 + xb, exp_ms, peak, src), "linear": _roof(2 * xb, lin_ms, peak, src)},
+    }), flush=True)
+
+
 def main():
     args = _args()
-    if args.op_case is not None:
+    if args.config == 1:
+        run_config1(args)
+    elif args.config == 2:
+        run_config2(args)
+    elif args.op_case is not None:
         run_op_case(args.op_case)
     elif args.impl == "reference":
         run_reference(args)
