@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "fc_linear_fwd", "fc_linear_bwd", "fc_tp_conv_fwd_noalloc", "fc_newton_schulz",
     "fc_rms_norm_fwd", "fc_rms_norm_bwd", "fc_gate_fwd", "fc_gate_bwd",
     "fc_neighbor_workspace_bytes", "fc_neighbor_count", "fc_neighbor_fill",
+    "fc_edge_expand_fwd", "fc_edge_expand_bwd",
 )
 
 
@@ -119,6 +120,10 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_neighbor_count.argtypes = [ctypes.POINTER(NlDesc), _P, _I64, _P, _P, _P, _P]
     lib.fc_neighbor_fill.restype = ctypes.c_int
     lib.fc_neighbor_fill.argtypes = [ctypes.POINTER(NlDesc), _I64, _P, _P, _I64, _P, _P, _P, _P]
+    lib.fc_edge_expand_fwd.restype = ctypes.c_int
+    lib.fc_edge_expand_fwd.argtypes = [_I32, _I32, _I32, _I32, _P, _P, _I64, _P, _P]
+    lib.fc_edge_expand_bwd.restype = ctypes.c_int
+    lib.fc_edge_expand_bwd.argtypes = [_I32, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _P, _P]
     lib.fc_gate_fwd.restype = ctypes.c_int
     lib.fc_gate_fwd.argtypes = [_I32, _I32, _I32, _P, _P, _I64, _P, _P]
     lib.fc_gate_bwd.restype = ctypes.c_int

@@ -30,6 +30,10 @@ int nl_count(const fc_nl_desc*, const double*, int64_t, void*, int64_t*, int*, c
 int nl_fill(const fc_nl_desc*, int64_t, const void*, const int64_t*, int64_t, int64_t*, int32_t*, int*, cudaStream_t);
 #endif
 template <typename T>
+int edge_expand_fwd_dispatch(int, const T*, const T*, int, int, int64_t, T*, cudaStream_t);
+template <typename T>
+int edge_expand_bwd_dispatch(int, const T*, const T*, const T*, int, int, int64_t, T*, T*, cudaStream_t);
+template <typename T>
 int gate_fwd_dispatch(int, const T*, const T*, T*, int, int64_t, cudaStream_t);
 template <typename T>
 int gate_bwd_dispatch(int, const T*, const T*, const T*, T*, T*, int, int64_t, cudaStream_t);
@@ -662,6 +666,43 @@ int fc_gate_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* grad
                                                  (const double*)gates, (double*)grad_values, (double*)grad_gates,
                                                  features, n_rows, s),
                        "fc_gate_bwd");
+}
+
+// ------------------------------------------------------------------ edge expansion
+
+int fc_edge_expand_fwd(int32_t l_max, int32_t features, int32_t per_rank, int32_t dtype, const void* moments,
+                       const void* h, int64_t n_rows, void* out, fc_stream_t stream) {
+  if (int rc = rms_check(l_max, features, dtype, n_rows, "fc_edge_expand_fwd")) return rc;
+  if (n_rows == 0) return FC_OK;
+  if (!moments || !h || !out) return fail(FC_ERR_INVALID, "fc_edge_expand_fwd: null pointer");
+  const cudaStream_t s = (cudaStream_t)stream;
+  const int pr = per_rank ? 1 : 0;
+  if (dtype == FC_F32)
+    return launch_status(edge_expand_fwd_dispatch<float>(l_max, (const float*)moments, (const float*)h, features, pr,
+                                                         n_rows, (float*)out, s),
+                         "fc_edge_expand_fwd");
+  return launch_status(edge_expand_fwd_dispatch<double>(l_max, (const double*)moments, (const double*)h, features, pr,
+                                                        n_rows, (double*)out, s),
+                       "fc_edge_expand_fwd");
+}
+
+int fc_edge_expand_bwd(int32_t l_max, int32_t features, int32_t per_rank, int32_t dtype, const void* grad_out,
+                       const void* moments, const void* h, int64_t n_rows, void* grad_moments, void* grad_h,
+                       fc_stream_t stream) {
+  if (int rc = rms_check(l_max, features, dtype, n_rows, "fc_edge_expand_bwd")) return rc;
+  if (n_rows == 0) return FC_OK;
+  if (!grad_out || !moments || !h) return fail(FC_ERR_INVALID, "fc_edge_expand_bwd: null pointer");
+  const cudaStream_t s = (cudaStream_t)stream;
+  const int pr = per_rank ? 1 : 0;
+  if (dtype == FC_F32)
+    return launch_status(edge_expand_bwd_dispatch<float>(l_max, (const float*)grad_out, (const float*)moments,
+                                                         (const float*)h, features, pr, n_rows, (float*)grad_moments,
+                                                         (float*)grad_h, s),
+                         "fc_edge_expand_bwd");
+  return launch_status(edge_expand_bwd_dispatch<double>(l_max, (const double*)grad_out, (const double*)moments,
+                                                        (const double*)h, features, pr, n_rows,
+                                                        (double*)grad_moments, (double*)grad_h, s),
+                       "fc_edge_expand_bwd");
 }
 
 // ------------------------------------------------------------------ neighbour list

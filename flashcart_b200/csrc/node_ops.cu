@@ -13,6 +13,7 @@
 // every thread sees the same r and S and the result does not depend on timing.
 #include "fc_base.cuh"
 #include "gen/rms_quad.cuh"
+#include "tp_common.cuh"  // fc_warp_transpose_reduce
 
 namespace fc {
 
@@ -343,5 +344,152 @@ template int gate_bwd_dispatch<float>(int, const float*, const float*, const flo
                                       cudaStream_t);
 template int gate_bwd_dispatch<double>(int, const double*, const double*, const double*, double*, double*, int,
                                        int64_t, cudaStream_t);
+
+}  // namespace fc
+
+// ------------------------------------------------------------------ edge expansion
+// out[e, k, c] = T[e, k] * h[e, r, c] for the (L+1)^2 stored components k of the
+// direction moments T (rows of Irreps(L)), r = 0 when h is shared by all ranks (h: (E, C))
+// or r = rank of k when h holds one row per rank (h: (E, L+1, C), the factorised form
+// T_l (x) (h W_l^T) of an equivariant linear map applied to T (x) h). The output rows are
+// the rank-block layout (rank l at l^2 C, component axis outer, channels contiguous).
+// Backward: grad_h[e, r, c] = sum_{k of r} g[e, k, c] T[e, k] and grad_T[e, k] =
+// sum_c g[e, k, c] h[e, r(k), c], the channel sum reduced over a warp (transpose-reduce).
+namespace fc {
+
+#ifndef FC_HOST_EMU
+template <typename T, int L>
+__global__ void edge_expand_fwd_kernel(const T* __restrict__ tm, const T* __restrict__ h, int F, int per_rank,
+                                       int64_t n, T* __restrict__ out) {
+  constexpr int NC = (L + 1) * (L + 1);
+  const int64_t total = n * F;
+  const int R = per_rank ? L + 1 : 1;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = t / F;
+    const int c = (int)(t - e * F);
+    T hv[L + 1];
+    for (int r = 0; r <= L; ++r) hv[r] = r < R ? fc_ldg(h + (e * R + r) * F + c) : hv[0];
+    T* o = out + e * (int64_t)(NC * F) + c;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) o[k * F] = fc_ldg(tm + e * NC + k) * hv[per_rank ? rms_rank_of(k) : 0];
+  }
+}
+
+// One warp per edge row; lane handles channels lane, lane + 32, ...
+template <typename T, int L>
+__global__ void edge_expand_bwd_kernel(const T* __restrict__ g, const T* __restrict__ tm, const T* __restrict__ h,
+                                       int F, int per_rank, int64_t n, T* __restrict__ gt, T* __restrict__ gh) {
+  constexpr int NC = (L + 1) * (L + 1);
+  constexpr int NP = NC <= 1 ? 1 : NC <= 4 ? 4 : NC <= 8 ? 8 : NC <= 16 ? 16 : 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int R = per_rank ? L + 1 : 1;
+  for (int64_t e = warp0; e < n; e += nwarps) {
+    T tv[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) tv[k] = fc_ldg(tm + e * NC + k);
+    T acc[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) acc[k] = T(0);
+    const T* gr = g + e * (int64_t)(NC * F);
+    for (int c = lane; c < F; c += 32) {
+      T hv[L + 1], ghv[L + 1];
+      for (int r = 0; r <= L; ++r) {
+        hv[r] = r < R ? fc_ldg(h + (e * R + r) * F + c) : hv[0];
+        ghv[r] = T(0);
+      }
+#pragma unroll
+      for (int k = 0; k < NC; ++k) {
+        const int r = per_rank ? rms_rank_of(k) : 0;
+        const T gk = fc_ldg(gr + k * F + c);
+        acc[k] += gk * hv[r];
+        ghv[r] += gk * tv[k];
+      }
+      if (gh)
+        for (int r = 0; r < R; ++r) gh[(e * R + r) * F + c] = ghv[r];
+    }
+    if (gt) {
+      const int comp = fc_warp_transpose_reduce<T, NP>(acc);
+      if ((lane & (32 / NP - 1)) == 0 && comp < NC) gt[e * NC + comp] = acc[0];
+    }
+  }
+}
+
+template <typename T, int L>
+static int edge_expand_fwd_launch(const T* tm, const T* h, int F, int per_rank, int64_t n, T* out, cudaStream_t s) {
+  edge_expand_fwd_kernel<T, L><<<gate_grid(n * F), 256, 0, s>>>(tm, h, F, per_rank, n, out);
+  return fc_check_launch();
+}
+template <typename T, int L>
+static int edge_expand_bwd_launch(const T* g, const T* tm, const T* h, int F, int per_rank, int64_t n, T* gt, T* gh,
+                                  cudaStream_t s) {
+  edge_expand_bwd_kernel<T, L><<<gate_grid(n * 32), 256, 0, s>>>(g, tm, h, F, per_rank, n, gt, gh);
+  return fc_check_launch();
+}
+#else
+template <typename T, int L>
+static int edge_expand_fwd_launch(const T* tm, const T* h, int F, int per_rank, int64_t n, T* out, cudaStream_t) {
+  constexpr int NC = (L + 1) * (L + 1);
+  const int R = per_rank ? L + 1 : 1;
+  for (int64_t e = 0; e < n; ++e)
+    for (int k = 0; k < NC; ++k)
+      for (int c = 0; c < F; ++c)
+        out[e * NC * F + k * F + c] = tm[e * NC + k] * h[(e * R + (per_rank ? rms_rank_of(k) : 0)) * F + c];
+  return 0;
+}
+template <typename T, int L>
+static int edge_expand_bwd_launch(const T* g, const T* tm, const T* h, int F, int per_rank, int64_t n, T* gt, T* gh,
+                                  cudaStream_t) {
+  constexpr int NC = (L + 1) * (L + 1);
+  const int R = per_rank ? L + 1 : 1;
+  for (int64_t e = 0; e < n; ++e) {
+    if (gh)
+      for (int r = 0; r < R; ++r)
+        for (int c = 0; c < F; ++c) gh[(e * R + r) * F + c] = T(0);
+    for (int k = 0; k < NC; ++k) {
+      const int r = per_rank ? rms_rank_of(k) : 0;
+      T a = T(0);
+      for (int c = 0; c < F; ++c) {
+        const T gk = g[e * NC * F + k * F + c];
+        a += gk * h[(e * R + r) * F + c];
+        if (gh) gh[(e * R + r) * F + c] += gk * tm[e * NC + k];
+      }
+      if (gt) gt[e * NC + k] = a;
+    }
+  }
+  return 0;
+}
+#endif
+
+template <typename T>
+int edge_expand_fwd_dispatch(int l_max, const T* tm, const T* h, int F, int per_rank, int64_t n, T* out,
+                             cudaStream_t s) {
+  switch (l_max) {
+    case 0: return edge_expand_fwd_launch<T, 0>(tm, h, F, per_rank, n, out, s);
+    case 1: return edge_expand_fwd_launch<T, 1>(tm, h, F, per_rank, n, out, s);
+    case 2: return edge_expand_fwd_launch<T, 2>(tm, h, F, per_rank, n, out, s);
+    default: return edge_expand_fwd_launch<T, 3>(tm, h, F, per_rank, n, out, s);
+  }
+}
+template <typename T>
+int edge_expand_bwd_dispatch(int l_max, const T* g, const T* tm, const T* h, int F, int per_rank, int64_t n, T* gt,
+                             T* gh, cudaStream_t s) {
+  switch (l_max) {
+    case 0: return edge_expand_bwd_launch<T, 0>(g, tm, h, F, per_rank, n, gt, gh, s);
+    case 1: return edge_expand_bwd_launch<T, 1>(g, tm, h, F, per_rank, n, gt, gh, s);
+    case 2: return edge_expand_bwd_launch<T, 2>(g, tm, h, F, per_rank, n, gt, gh, s);
+    default: return edge_expand_bwd_launch<T, 3>(g, tm, h, F, per_rank, n, gt, gh, s);
+  }
+}
+
+template int edge_expand_fwd_dispatch<float>(int, const float*, const float*, int, int, int64_t, float*,
+                                             cudaStream_t);
+template int edge_expand_fwd_dispatch<double>(int, const double*, const double*, int, int, int64_t, double*,
+                                              cudaStream_t);
+template int edge_expand_bwd_dispatch<float>(int, const float*, const float*, const float*, int, int, int64_t,
+                                             float*, float*, cudaStream_t);
+template int edge_expand_bwd_dispatch<double>(int, const double*, const double*, const double*, int, int, int64_t,
+                                              double*, double*, cudaStream_t);
 
 }  // namespace fc

@@ -921,3 +921,83 @@ def _gate_backward(ctx, grad_y):
 
 
 gate_fwd.register_autograd(_gate_backward, setup_context=_gate_setup)
+
+
+# --------------------------------------------------------------------------- fused edge expansion
+
+
+def _expand_index(l_max: int, device) -> Tensor:
+    return torch.cat([torch.full((2 * l + 1,), l, dtype=torch.int64) for l in range(l_max + 1)]).to(device)
+
+
+@torch.library.custom_op("flashcart::edge_expand_fwd", mutates_args=())
+def edge_expand_fwd(moments: Tensor, h: Tensor, l_max: int, features: int, per_rank: bool) -> Tensor:
+    """``out[e, k, c] = moments[e, k] * h[e, r, c]`` as rank-block rows (E, (l_max+1)^2 *
+    features): ``h`` (E, features) shared by every rank, or (E, l_max+1, features) with
+    ``per_rank`` (the factorised equivariant linear map of the expansion)."""
+    _require_cuda(moments, h)
+    t, hh = moments.contiguous(), h.contiguous()
+    nc = (l_max + 1) ** 2
+    if t.dim() != 2 or t.shape[1] != nc:
+        raise ValueError(f"edge_expand: moments must be (E, {nc}), got {tuple(t.shape)}")
+    if hh.numel() != t.shape[0] * (l_max + 1 if per_rank else 1) * features or hh.dtype != t.dtype:
+        raise ValueError("edge_expand: h must be (E, features) or (E, l_max+1, features) with per_rank, same dtype")
+    lib = N.lib()
+    out = t.new_empty((t.shape[0], nc * features))
+    with _timed("edge_expand_fwd", 1, _nbytes(t, hh, out)):
+        rc = lib.fc_edge_expand_fwd(int(l_max), int(features), int(bool(per_rank)), _code(t.dtype), _p(t), _p(hh),
+                                    t.shape[0], _p(out), _stream(t.device))
+    _after(lib, rc, "fc_edge_expand_fwd", t.device)
+    return out
+
+
+@edge_expand_fwd.register_fake
+def _(moments, h, l_max, features, per_rank):
+    return moments.new_empty((moments.shape[0], (l_max + 1) ** 2 * features))
+
+
+@torch.library.custom_op("flashcart::edge_expand_bwd", mutates_args=())
+def edge_expand_bwd(grad_out: Tensor, moments: Tensor, h: Tensor, l_max: int, features: int,
+                    per_rank: bool) -> Tuple[Tensor, Tensor]:
+    """First-order backward of :func:`edge_expand_fwd`: (grad_moments, grad_h)."""
+    _require_cuda(grad_out, moments, h)
+    g, t, hh = grad_out.contiguous(), moments.contiguous(), h.contiguous()
+    lib = N.lib()
+    gt = torch.empty_like(t)
+    gh = torch.empty_like(hh)
+    with _timed("edge_expand_bwd", 1, _nbytes(g, t, hh, gt, gh)):
+        rc = lib.fc_edge_expand_bwd(int(l_max), int(features), int(bool(per_rank)), _code(t.dtype), _p(g), _p(t),
+                                    _p(hh), t.shape[0], _p(gt), _p(gh), _stream(t.device))
+    _after(lib, rc, "fc_edge_expand_bwd", t.device)
+    return gt, gh
+
+
+@edge_expand_bwd.register_fake
+def _(grad_out, moments, h, l_max, features, per_rank):
+    return torch.empty_like(moments), torch.empty_like(h)
+
+
+def _expand_setup(ctx, inputs, output):
+    moments, h, l_max, features, per_rank = inputs
+    ctx.save_for_backward(moments, h)
+    ctx.l_max, ctx.features, ctx.per_rank = l_max, features, per_rank
+
+
+def _expand_backward(ctx, grad_out):
+    moments, h = ctx.saved_tensors
+    L, F, pr = ctx.l_max, ctx.features, ctx.per_rank
+    if torch.is_grad_enabled():
+        # building a graph for a second derivative: the same gradient from differentiable ops
+        e, nc = moments.shape
+        g = grad_out.reshape(e, nc, F)
+        hr = h.reshape(e, L + 1 if pr else 1, F)
+        hx = hr.index_select(1, _expand_index(L, h.device)) if pr else hr
+        gt = (g * hx).sum(-1)
+        gm = g * moments.unsqueeze(-1)
+        gh = (torch.zeros_like(hr).index_add(1, _expand_index(L, h.device), gm) if pr else gm.sum(1, keepdim=True))
+        return gt, gh.reshape(h.shape), None, None, None
+    gt, gh = edge_expand_bwd(grad_out.contiguous(), moments, h, L, F, pr)
+    return (gt if ctx.needs_input_grad[0] else None), (gh if ctx.needs_input_grad[1] else None), None, None, None
+
+
+edge_expand_fwd.register_autograd(_expand_backward, setup_context=_expand_setup)

@@ -222,6 +222,22 @@ int fc_gate_fwd(int32_t l_max, int32_t features, int32_t dtype, const void* valu
 int fc_gate_bwd(int32_t l_max, int32_t features, int32_t dtype, const void* grad_y, const void* values,
                 const void* gates, int64_t n_rows, void* grad_values, void* grad_gates, fc_stream_t stream);
 
+/* ---------------------------------------------------------------- edge expansion
+ * Cartesian expansion of edge features: out[e, k, c] = moments[e, k] * h[e, r, c] over the
+ * (l_max+1)^2 stored components k of the direction moments (rows of fc_irreps_fwd), laid
+ * out as rank blocks (rank l at l^2 * features). per_rank = 0: h is (n_rows, features),
+ * shared by all ranks -- the composition T^l(r^) (x) radial features of the reference's
+ * pieces (o3/irreps.py:54-72, nn/radial.py, nn/layers.py:84-131), which it materialises
+ * with broadcast products and a concatenation; per_rank = 1: h is (n_rows, l_max+1,
+ * features) -- the factorised form T_l (x) (h W_l^T) of an equivariant linear map
+ * (o3/linear.py:88-128) applied to that expansion. The backward returns grad_moments
+ * (n_rows, (l_max+1)^2) and grad_h (h's shape); either may be NULL. */
+int fc_edge_expand_fwd(int32_t l_max, int32_t features, int32_t per_rank, int32_t dtype, const void* moments,
+                       const void* h, int64_t n_rows, void* out, fc_stream_t stream);
+int fc_edge_expand_bwd(int32_t l_max, int32_t features, int32_t per_rank, int32_t dtype, const void* grad_out,
+                       const void* moments, const void* h, int64_t n_rows, void* grad_moments, void* grad_h,
+                       fc_stream_t stream);
+
 /* ---------------------------------------------------------------- neighbour list
  * Periodic cell list of an orthorhombic cell on the GPU. Replaces the host neighbour
  * search that feeds the model (data/neighbors.py:120-143, matscipy neighbour_list("ijS"):

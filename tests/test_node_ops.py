@@ -165,3 +165,64 @@ def test_gpu_fused_gated_layer_matches_composed(cuda_device, dtype, tol):
     ops.check_device_status(cuda_device)
     assert (out - ref).abs().max().item() < tol * ref.abs().max().item()
     assert (gx - ref_gx).abs().max().item() < tol * ref_gx.abs().max().item()
+
+
+def _expand_ref(T, h, l_max, C, per_rank):
+    blocks, off = [], 0
+    for l in range(l_max + 1):
+        n = 2 * l + 1
+        hl = h[:, l] if per_rank else h
+        blocks.append((T[:, off:off + n].unsqueeze(-1) * hl.unsqueeze(1)).reshape(T.shape[0], n * C))
+        off += n
+    return torch.cat(blocks, dim=-1)
+
+
+@pytest.mark.parametrize("l_max,C,per_rank", [(3, 8, False), (3, 5, True), (2, 33, True), (0, 4, False)])
+def test_emu_edge_expand_matches_composition(emu_lib, l_max, C, per_rank):
+    g = torch.Generator().manual_seed(21 + l_max)
+    n, nc = 7, (l_max + 1) ** 2
+    T = torch.randn(n, nc, generator=g, dtype=torch.float64)
+    h = torch.randn(*((n, l_max + 1, C) if per_rank else (n, C)), generator=g, dtype=torch.float64)
+    Tr, hr = T.clone().requires_grad_(True), h.clone().requires_grad_(True)
+    ref = _expand_ref(Tr, hr, l_max, C, per_rank)
+    gy = torch.randn_like(ref)
+    ref_gt, ref_gh = torch.autograd.grad(ref, [Tr, hr], gy)
+    out = torch.empty_like(ref)
+    N.check(emu_lib, emu_lib.fc_edge_expand_fwd(l_max, C, int(per_rank), N.FC_F64, A.p(T), A.p(h), n, A.p(out), None),
+            "fc_edge_expand_fwd")
+    gt, gh = torch.empty_like(T), torch.empty_like(h)
+    N.check(emu_lib, emu_lib.fc_edge_expand_bwd(l_max, C, int(per_rank), N.FC_F64, A.p(gy), A.p(T), A.p(h), n, A.p(gt),
+                                                A.p(gh), None), "fc_edge_expand_bwd")
+    assert torch.equal(out, ref.detach())
+    assert (gt - ref_gt).abs().max().item() < 1e-12 * ref_gt.abs().max().item()
+    assert (gh - ref_gh).abs().max().item() < 1e-12 * ref_gh.abs().max().item()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("per_rank", [False, True])
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-12), (torch.float32, 1e-5)])
+def test_gpu_edge_expand_matches_composition(cuda_device, per_rank, dtype, tol):
+    """Forward, first derivative (kernels) and second derivative (composed backward)."""
+    from flashcart_b200 import ops
+
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    n, L, C = 5000, 3, 128
+    T = torch.randn(n, 16, device=cuda_device, dtype=dtype, generator=g, requires_grad=True)
+    h = torch.randn(*((n, L + 1, C) if per_rank else (n, C)), device=cuda_device, dtype=dtype, generator=g,
+                    requires_grad=True)
+    ref = _expand_ref(T, h, L, C, per_rank)
+    out = ops.edge_expand_fwd(T, h, L, C, per_rank)
+    assert torch.equal(out, ref)
+    gy = torch.randn_like(ref)
+    r_gt, r_gh = torch.autograd.grad(ref, [T, h], gy, create_graph=True)
+    gt, gh = torch.autograd.grad(out, [T, h], gy, create_graph=True)
+    assert (gt - r_gt).abs().max().item() < tol * r_gt.abs().max().item()
+    assert (gh - r_gh).abs().max().item() < tol * r_gh.abs().max().item()
+    (a,) = torch.autograd.grad((gt.square().sum() + gh.square().sum()), [T])
+    (b,) = torch.autograd.grad((r_gt.square().sum() + r_gh.square().sum()), [T])
+    assert (a - b).abs().max().item() < 10 * tol * b.abs().max().item()
+    with torch.no_grad():
+        gt1, gh1 = torch.ops.flashcart.edge_expand_bwd(gy, T, h, L, C, per_rank)
+    assert (gt1 - r_gt).abs().max().item() < tol * r_gt.abs().max().item()
+    assert (gh1 - r_gh).abs().max().item() < tol * r_gh.abs().max().item()
+    ops.check_device_status(cuda_device)
