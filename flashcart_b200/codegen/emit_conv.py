@@ -240,10 +240,18 @@ def _fwd_group_body_cpt(gs: GroupSlots, ind: str) -> List[str]:
     return L
 
 
-def _bwd_group_body(gs: GroupSlots, ind: str, direct: bool = False) -> List[str]:
+def _bwd_group_body(gs: GroupSlots, ind: str, d2p: int, direct: bool = False) -> List[str]:
+    """Backward of one edge. The first contribution to a gradient register assigns it, so
+    the registers need no zeroing per edge; components no path touches are zeroed last."""
     sig = gs.sig
     L = []
     base = 0
+    set1, set2 = set(), set()
+
+    def acc(name: str, k: int, expr: str, seen: set) -> str:
+        op = "+=" if k in seen else "="
+        seen.add(k)
+        return f"{name}[{k}] {op} {expr};"
     for p in gs.paths:
         r1, r2, o = sig.paths[p]
         K = stf.oriented_path_tensor(r1, r2, o)
@@ -264,7 +272,7 @@ def _bwd_group_body(gs: GroupSlots, ind: str, direct: bool = False) -> List[str]
         if hs:
             L.append(f"{ind}  if (NEED_1) {{")
             for i in hs:
-                L.append(f"{ind}    gx1[{_q(r1, i) - gs.x_lo}] += wp * h{i};")
+                L.append(f"{ind}    " + acc("gx1", _q(r1, i) - gs.x_lo, f"wp * h{i}", set1))
             L.append(f"{ind}  }}")
         body2 = []
         for j in range(2 * r2 + 1):
@@ -274,13 +282,19 @@ def _bwd_group_body(gs: GroupSlots, ind: str, direct: bool = False) -> List[str]
                 if n != "T(0)":
                     pairs.append(f"g[{base + a}]*({n})")
             if pairs:
-                body2.append(f"{ind}    gx2[{_q(r2, j)}] += wp * ({' + '.join(pairs)});")
+                body2.append(f"{ind}    " + acc("gx2", _q(r2, j), f"wp * ({' + '.join(pairs)})", set2))
         if body2:
             L.append(f"{ind}  if (NEED_2) {{")
             L.extend(body2)
             L.append(f"{ind}  }}")
         L.append(f"{ind}}}")
         base += 2 * o + 1
+    for q in range(gs.x_n):
+        if q not in set1:
+            L.append(f"{ind}gx1[{q}] = T(0);")
+    for q in range(d2p):
+        if q not in set2:
+            L.append(f"{ind}gx2[{q}] = T(0);")
     return L
 
 
@@ -525,8 +539,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
             w("        const T* sx = ring + s * SLOT + c;")
             w("        T x1[XN], gx1[XN];")
             w(f"        T gx2[{d2p}];")
-            w("        for (int q = 0; q < XN; ++q) { x1[q] = sx[q * F]; gx1[q] = T(0); }")
-            w(f"        for (int q = 0; q < {d2p}; ++q) gx2[q] = T(0);")
+            w("        for (int q = 0; q < XN; ++q) x1[q] = sx[q * F];")
             w("        const T* sw = sx + XN * F;")
         else:
             w("      const int64_t kk = eb + k, e = e0 + kk;")
@@ -536,12 +549,11 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
             w("        const T* __restrict__ a1 = P.in1 + j * (int64_t)(D1 * F) + XLO * F + c;")
             w("        T x1[XN], gx1[XN];")
             w(f"        T gx2[{d2p}];")
-            w("        for (int q = 0; q < XN; ++q) { x1[q] = fc_ldg(a1 + q * F); gx1[q] = T(0); }")
-            w(f"        for (int q = 0; q < {d2p}; ++q) gx2[q] = T(0);")
+            w("        for (int q = 0; q < XN; ++q) x1[q] = fc_ldg(a1 + q * F);")
             w("        const T* __restrict__ wr = P.w + e * (int64_t)(NP * F) + c;")
         w("        T* __restrict__ gwr = NEED_W ? P.g_w + e * (int64_t)(NP * F) + c : nullptr;")
         w("        const T* m = sm + k * NMP;")
-        L.extend(_bwd_group_body(gs, "        ", direct=not BWD_RING))
+        L.extend(_bwd_group_body(gs, "        ", d2p, direct=not BWD_RING))
         w("        if (NEED_1) {")
         w("          T* __restrict__ t1 = P.g_in1 + j * (int64_t)(D1 * F) + XLO * F + c;")
         w("          for (int q = 0; q < XN; ++q) fc_atomic_add(t1 + q * F, gx1[q]);")
