@@ -53,9 +53,10 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--op-case", choices=["conv", "gemm"], default=None,
                     help="run one small operator case (for ncu captures) instead of the benchmark")
-    ap.add_argument("--config", type=int, choices=[1, 2, 3], default=3,
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4], default=3,
                     help="3: the headline E+F+S step; 1: the isolated TP convolution microbenchmark; "
-                         "2: edge expansion + equivariant linear map (one GPU, one JSON line)")
+                         "2: edge expansion + equivariant linear map (one GPU, one JSON line); "
+                         "4: data-parallel training (32 molecules per GPU, energy + force loss, Muon)")
     return ap.parse_args()
 
 
@@ -573,9 +574,81 @@ def run_config2(args):
     }), flush=True)
 
 
+def run_config4(args):
+    """data-parallel training. Per GPU and step 32 seeded random-walk
+    molecules (20-60 atoms, H/C/N/O 50/30/10/10, seed 1000 rank + step); labels from a
+    random-init teacher (config-0 architecture, elements H/C/N/O, seed 1); the student
+    (seed 0) takes the energy-per-atom + force MSE with forces from create_graph=True (the
+    operators' double backward), one flat NCCL all-reduce of the gradients, then AdamW +
+    Muon (Newton-Schulz on the tensor cores). Batches and labels are built before the
+    timed region; value = molecules (and atoms) of all ranks / max-over-ranks step time."""
+    import torch.distributed as dist
+
+    from flashcart_b200 import ops, training
+    from flashcart_b200.model.flashcart import FlashCartPotential
+
+    rank, world, local = _dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    kw = dict(elements=training.ELEMENTS, r_max=5.0, n_hidden_feats=64, l_max_hidden_feats=2, l_max_edge_attrs=2,
+              n_radial=8, n_interactions=2, correlation=3, layer_norm=True, nonlinearity=True,
+              gate_activation="sigmoid", radial_mapping="cosine", path_reduced_product=False,
+              fit_atomic_shifts=False, atomic_shifts=[0.0] * 4)
+    n_steps = max(args.warmup, 0) + max(args.steps, 1)
+    graphs = [training.batch_graph(training.synthetic_molecules(32, rank=rank, step=st), 5.0, dev)
+              for st in range(n_steps)]
+    avg = graphs[0]["edge_index"].shape[1] / graphs[0]["positions"].shape[0]  # mean degree of the first batch
+    torch.manual_seed(1)
+    teacher = FlashCartPotential(**kw, avg_neighbors=avg).to(dev)
+    torch.manual_seed(0)
+    student = FlashCartPotential(**kw, avg_neighbors=avg).to(dev)
+    opts = training.make_optimizer(student)
+    batches = []
+    for g in graphs:
+        lab = teacher.predict(g, compute_forces=True)
+        batches.append((g, lab["energy"].detach(), lab["forces"].detach()))
+    n_atoms = [int(b[0]["positions"].shape[0]) for b in batches]
+    for st in range(args.warmup):
+        training.train_step(student, *batches[st], opts)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for st in range(args.warmup, n_steps):
+        loss = training.train_step(student, *batches[st], opts)
+    e1.record()
+    torch.cuda.synchronize()
+    ops.check_device_status(dev)
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    t = torch.tensor([ms, float(sum(n_atoms[args.warmup:]))], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t[0:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(t[1:2], op=dist.ReduceOp.SUM)
+    ms_max, atoms = float(t[0]), float(t[1])
+    if rank == 0:
+        mols_per_s = 32 * world / (ms_max * 1e-3)
+        print(json.dumps({
+            "metric": "DP training structures/s (32 molecules of 20-60 atoms per GPU, E+F loss, Muon; BASELINE config 4)",
+            "value": mols_per_s, "unit": "structures/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "dtype": "f32", "data": "synthetic",
+            "atom_steps_per_s": atoms / max(args.steps, 1) / (ms_max * 1e-3), "final_loss": float(loss),
+            "config": {"workload": "config4", "molecules_per_gpu": 32, "parallelism": f"dp{world}",
+                       "model": "config-0 architecture, elements H/C/N/O"},
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = _args()
-    if args.config == 1:
+    if args.config == 4:
+        run_config4(args)
+    elif args.config == 1:
         run_config1(args)
     elif args.config == 2:
         run_config2(args)

@@ -55,9 +55,13 @@ constexpr int BAR_BYTES = 256;
 constexpr long long WAIT_LIMIT = 1ll << 22;
 // k slabs per accumulation unit. The tensor cores accumulate in fp32 but not with
 // IEEE round-to-nearest at every step; over thousands of k the error grows beyond
-// what an fp32 dot product shows. Each unit of KG slabs (64 k) therefore starts a
+// what an fp32 dot product shows. Each unit of KG slabs (128 k; 64 k measured 4-12% slower
+// with the same accuracy against float64) therefore starts a
 // fresh TMEM accumulator, and the epilogue sums the units in fp32 registers.
-constexpr int KG = 2;
+#ifndef FC_TMA_KG
+#define FC_TMA_KG 4
+#endif
+constexpr int KG = FC_TMA_KG;
 constexpr int PF_SLABS = 4;   // k slabs per L2 prefetch box (512 bytes of each row)
 #ifndef FC_TMA_PF_AHEAD
 #define FC_TMA_PF_AHEAD 0
