@@ -675,7 +675,10 @@ int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStrea
   const int nk = (a.K + BK - 1) / BK;
   const int nu = (nk + KG - 1) / KG;
   // 256-column tiles only when one unit covers k (their sum would need 256 registers)
-  const int BN = (a.N > 128 && nu == 1) ? 256 : a.N > 64 ? 128 : 64;
+#ifndef FC_TMA_USE_BN256
+#define FC_TMA_USE_BN256 1
+#endif
+  const int BN = (FC_TMA_USE_BN256 && a.N > 128 && nu == 1) ? 256 : a.N > 64 ? 128 : 64;
   const int kp = (a.K + 3) & ~3;
   if (nodes > 0x7fffffffLL) return 1;
 
