@@ -55,8 +55,8 @@ constexpr int BAR_BYTES = 256;
 constexpr long long WAIT_LIMIT = 1ll << 22;
 // k slabs per accumulation unit. The tensor cores accumulate in fp32 but not with
 // IEEE round-to-nearest at every step; over thousands of k the error grows beyond
-// what an fp32 dot product shows. Each unit of KG slabs (128 k; 64 k measured 4-12% slower
-// with the same accuracy against float64) therefore starts a
+// what an fp32 dot product shows. Each unit of KG slabs (128 k; as accurate against float64
+// as 64 k, with half the epilogue handshakes) therefore starts a
 // fresh TMEM accumulator, and the epilogue sums the units in fp32 registers.
 #ifndef FC_TMA_KG
 #define FC_TMA_KG 4
@@ -675,10 +675,7 @@ int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStrea
   const int nk = (a.K + BK - 1) / BK;
   const int nu = (nk + KG - 1) / KG;
   // 256-column tiles only when one unit covers k (their sum would need 256 registers)
-#ifndef FC_TMA_USE_BN256
-#define FC_TMA_USE_BN256 1
-#endif
-  const int BN = (FC_TMA_USE_BN256 && a.N > 128 && nu == 1) ? 256 : a.N > 64 ? 128 : 64;
+  const int BN = (a.N > 128 && nu == 1) ? 256 : a.N > 64 ? 128 : 64;
   const int kp = (a.K + 3) & ~3;
   if (nodes > 0x7fffffffLL) return 1;
 
