@@ -281,10 +281,6 @@ __global__ void __launch_bounds__(256, 2) lin_tc_kernel(LinGemmArgs<float> a, in
 
 int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s) {
   if (a.R == 0 || a.N == 0) return 0;
-  // k <= 16 (the radial MLP's input layer, k = 8): one k slab per tile leaves the tensor-core
-  // pipeline latency-bound; the SIMT tiles run it at memory speed with exact fp32 FMAs
-  // (at least as accurate as 3xTF32). A requested single-TF32 product keeps the tensor cores.
-  if (split && a.K <= 16) return lin_gemm<float>(a, s);
   // TMA-fed persistent kernel where the layout allows it, else this one
   const int rc = lin_gemm_tma(a, split, status, s);
   if (rc != 1) return rc;
