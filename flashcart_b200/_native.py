@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "fc_rms_norm_fwd", "fc_rms_norm_bwd", "fc_gate_fwd", "fc_gate_bwd",
     "fc_neighbor_workspace_bytes", "fc_neighbor_count", "fc_neighbor_fill",
     "fc_edge_expand_fwd", "fc_edge_expand_bwd",
+    "fc_linear_presplit", "fc_linear_fwd_presplit", "fc_linear_bwd_presplit",
 )
 
 
@@ -120,6 +121,12 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_neighbor_count.argtypes = [ctypes.POINTER(NlDesc), _P, _I64, _P, _P, _P, _P]
     lib.fc_neighbor_fill.restype = ctypes.c_int
     lib.fc_neighbor_fill.argtypes = [ctypes.POINTER(NlDesc), _I64, _P, _P, _I64, _P, _P, _P, _P]
+    lib.fc_linear_presplit.restype = ctypes.c_int
+    lib.fc_linear_presplit.argtypes = [ctypes.POINTER(LinearDesc), _P, _I32, _P, _P]
+    lib.fc_linear_fwd_presplit.restype = ctypes.c_int
+    lib.fc_linear_fwd_presplit.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P]
+    lib.fc_linear_bwd_presplit.restype = ctypes.c_int
+    lib.fc_linear_bwd_presplit.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P]
     lib.fc_edge_expand_fwd.restype = ctypes.c_int
     lib.fc_edge_expand_fwd.argtypes = [_I32, _I32, _I32, _I32, _P, _P, _I64, _P, _P]
     lib.fc_edge_expand_bwd.restype = ctypes.c_int

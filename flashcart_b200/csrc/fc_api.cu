@@ -206,7 +206,7 @@ static int zero_tail(T* p, int64_t rows, int64_t width, int64_t from, cudaStream
 
 template <typename T>
 static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* weights, const T* scale, int64_t n,
-                        T* out, int* status, cudaStream_t s) {
+                        T* out, int* status, cudaStream_t s, const void* const* bsplit = nullptr) {
   int64_t end = 0;
   if (d->n_active > 0) {
     const int l = d->n_active - 1;
@@ -219,6 +219,7 @@ static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* 
     a.w = (const T*)weights[l];
     a.ldw = d->f_in_values[l];
     a.trans_b = 1;
+    a.bsplit = bsplit ? (const T*)bsplit[l] : nullptr;
     a.scale = scale + l;
     a.c = LinRows<T>{out, d->out_dim, d->out_offsets[l], d->f_out_values[l], d->m_values[l]};
     a.R = n * d->m_values[l];
@@ -231,7 +232,8 @@ static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* 
 
 template <typename T>
 static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const void* const* weights, const T* scale,
-                        int64_t n, T* gx, void* const* gw, int* status, cudaStream_t s) {
+                        int64_t n, T* gx, void* const* gw, int* status, cudaStream_t s,
+                        const void* const* bsplit = nullptr) {
   if (gx) {
     // columns of x outside the active ranks get zero gradient
     int64_t prev = 0;
@@ -247,6 +249,7 @@ static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const v
       a.w = (const T*)weights[l];
       a.ldw = d->f_in_values[l];
       a.trans_b = 0;
+      a.bsplit = bsplit ? (const T*)bsplit[l] : nullptr;
       a.scale = scale + l;
       a.c = LinRows<T>{gx, d->in_dim, d->in_offsets[l], d->f_in_values[l], d->m_values[l]};
       a.R = n * d->m_values[l];
@@ -563,6 +566,57 @@ int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* 
                                             (const double*)scale, n, (double*)grad_x, grad_weights,
                                             reinterpret_cast<int*>(status), s),
                        "fc_linear_bwd");
+}
+
+// ------------------------------------------------------------------ linear maps, split weights
+
+static int presplit_check(const fc_linear_desc* desc, const void* const* weights, const void* const* split,
+                          const char* what) {
+  if (int rc = check_linear(desc)) return rc;
+  if (desc->dtype != FC_F32) return fail(FC_ERR_UNSUPPORTED, "%s: split weights are for float32 maps", what);
+  if (desc->n_active > 0 && (!weights || !split)) return fail(FC_ERR_INVALID, "%s: null weight array", what);
+  for (int l = 0; l < desc->n_active; ++l)
+    if (!weights[l] || !split[l]) return fail(FC_ERR_INVALID, "%s: null weight for rank %d", what, l);
+  return FC_OK;
+}
+
+int fc_linear_presplit(const fc_linear_desc* desc, const void* const* weights, int32_t backward,
+                       void* const* split, fc_stream_t stream) {
+  if (int rc = presplit_check(desc, weights, split, "fc_linear_presplit")) return rc;
+  const cudaStream_t s = (cudaStream_t)stream;
+  for (int l = 0; l < desc->n_active; ++l) {
+    const int fi = desc->f_in_values[l], fo = desc->f_out_values[l];
+    // forward B(k, n) = W[n][k] (k = in, n = out); backward B(k, n) = W[k][n] (k = out, n = in)
+    const int rc = backward ? lin_presplit((const float*)weights[l], fi, 0, fo, fi, (float*)split[l], s)
+                            : lin_presplit((const float*)weights[l], fi, 1, fi, fo, (float*)split[l], s);
+    if (rc) return launch_status(rc, "fc_linear_presplit");
+  }
+  return FC_OK;
+}
+
+int fc_linear_fwd_presplit(const fc_linear_desc* desc, const void* x, const void* const* weights,
+                           const void* const* split, const void* scale, int64_t n, void* out, int32_t* status,
+                           fc_stream_t stream) {
+  if (int rc = presplit_check(desc, weights, split, "fc_linear_fwd_presplit")) return rc;
+  if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_fwd_presplit: negative size");
+  if (n == 0 || desc->out_dim == 0) return FC_OK;
+  if (!out || (desc->n_active > 0 && (!x || !scale))) return fail(FC_ERR_INVALID, "fc_linear_fwd_presplit: null tensor");
+  return launch_status(linear_fwd_t<float>(desc, (const float*)x, weights, (const float*)scale, n, (float*)out,
+                                           reinterpret_cast<int*>(status), (cudaStream_t)stream, split),
+                       "fc_linear_fwd_presplit");
+}
+
+int fc_linear_bwd_presplit(const fc_linear_desc* desc, const void* grad_out, const void* x,
+                           const void* const* weights, const void* const* split, const void* scale, int64_t n,
+                           void* grad_x, void* const* grad_weights, int32_t* status, fc_stream_t stream) {
+  if (int rc = presplit_check(desc, weights, split, "fc_linear_bwd_presplit")) return rc;
+  if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_bwd_presplit: negative size");
+  if (desc->n_active > 0 && (!grad_out || !x || !scale))
+    return fail(FC_ERR_INVALID, "fc_linear_bwd_presplit: null tensor");
+  return launch_status(linear_bwd_t<float>(desc, (const float*)grad_out, (const float*)x, weights,
+                                           (const float*)scale, n, (float*)grad_x, grad_weights,
+                                           reinterpret_cast<int*>(status), (cudaStream_t)stream, split),
+                       "fc_linear_bwd_presplit");
 }
 
 // Convolution forward for callers that cannot allocate device memory (see the header).

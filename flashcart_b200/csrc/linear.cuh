@@ -27,6 +27,9 @@ struct LinGemmArgs {
   LinRows<T> c;     // C(r, col), col contiguous
   int64_t R;
   int K, N;
+  // optional: the weights already split into tf32 hi | lo rows (n-major, k padded to a
+  // multiple of 4), as lin_presplit writes them; null = split inside the call
+  const T* bsplit = nullptr;
 };
 
 template <typename T>
@@ -48,5 +51,8 @@ int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream
 int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s);
 template <typename T>
 int lin_wgrad(LinWgradArgs<T> a, cudaStream_t s);
+// B(k, n) of a GEMM (W[n*ldw + k] if trans_b, else W[k*ldw + n]) as tf32 hi rows then lo
+// rows, n-major with k padded to kp = (K + 3) & ~3 (zeros): 2 * N * kp floats at out.
+int lin_presplit(const float* w, int ldw, int trans_b, int K, int N, float* out, cudaStream_t s);
 
 }  // namespace fc

@@ -310,6 +310,27 @@ int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream
 
 int lin_gemm_tc(const LinGemmArgs<float>& a, bool, int*, cudaStream_t s) { return lin_gemm<float>(a, s); }
 
+// host emulation of the split (same integer rounding to tf32 as the kernel)
+int lin_presplit(const float* w, int ldw, int trans_b, int K, int N, float* out, cudaStream_t) {
+  const int kp = (K + 3) & ~3;
+  const int64_t total = (int64_t)N * kp;
+  auto rnd = [](float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    u = (u + 0x1000u) & 0xFFFFE000u;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+  };
+  for (int64_t i = 0; i < total; ++i) {
+    const int n = (int)(i / kp), k = (int)(i - (int64_t)n * kp);
+    const float x = k < K ? (trans_b ? w[(int64_t)n * ldw + k] : w[(int64_t)k * ldw + n]) : 0.f;
+    out[i] = rnd(x);
+    out[total + i] = rnd(x - out[i]);
+  }
+  return 0;
+}
+
 #endif
 
 }  // namespace fc

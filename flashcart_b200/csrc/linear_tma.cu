@@ -685,14 +685,19 @@ int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStrea
   if (!encode_rows(&mc, a.c.p + a.c.off, a.N, nodes, M, a.c.ld, a.c.ms, 32)) return 1;
 
   float* ws = nullptr;
-  const size_t wbytes = (size_t)a.N * kp * 4 * (split ? 2 : 1);
-  if (fc_pool_alloc(reinterpret_cast<void**>(&ws), wbytes, s)) return FC_ERR_LAUNCH;
-  float* bhi = ws;
-  float* blo = split ? ws + (size_t)a.N * kp : nullptr;
+  float* bhi = nullptr;
+  if (a.bsplit) {
+    bhi = const_cast<float*>(a.bsplit);  // split once by the caller (lin_presplit layout)
+  } else {
+    const size_t wbytes = (size_t)a.N * kp * 4 * (split ? 2 : 1);
+    if (fc_pool_alloc(reinterpret_cast<void**>(&ws), wbytes, s)) return FC_ERR_LAUNCH;
+    bhi = ws;
+  }
+  float* blo = split ? bhi + (size_t)a.N * kp : nullptr;
   int rc = 0;
   if (!encode_b(&mbh, bhi, kp, a.N, BN) || (split && !encode_b(&mbl, blo, kp, a.N, BN))) rc = 1;
   if (!split) mbl = mbh;
-  if (rc == 0) {
+  if (rc == 0 && !a.bsplit) {
     const int64_t total = (int64_t)a.N * kp;
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * ds->sms);
     presplit_kernel<<<blocks, 256, 0, s>>>(a.w, a.ldw, a.trans_b, a.K, a.N, kp, bhi, blo);
@@ -723,8 +728,17 @@ int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStrea
                  : launch<256, false>(ma, mbh, mbl, mc, mpf, args, ds, grid, s);
   }
   // stream-ordered: the workspace returns to the pool after the kernels that read it
-  if (fc_pool_free(ws, s) && rc == 0) rc = FC_ERR_LAUNCH;
+  if (ws && fc_pool_free(ws, s) && rc == 0) rc = FC_ERR_LAUNCH;
   return rc;
+}
+
+int lin_presplit(const float* w, int ldw, int trans_b, int K, int N, float* out, cudaStream_t s) {
+  const int kp = (K + 3) & ~3;
+  const int64_t total = (int64_t)N * kp;
+  if (total == 0) return 0;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 4);
+  tma::presplit_kernel<<<blocks, 256, 0, s>>>(w, ldw, trans_b, K, N, kp, out, out + total);
+  return fc_check_launch();
 }
 
 }  // namespace fc

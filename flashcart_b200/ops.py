@@ -18,6 +18,7 @@ import contextlib
 import ctypes
 import os
 import threading
+import weakref
 from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
@@ -535,6 +536,48 @@ def _ptr_array(tensors: Sequence[Optional[Tensor]]):
     return arr
 
 
+class _Split:
+    __slots__ = ("refs", "versions", "bufs", "arr")
+
+
+_SPLITS: Dict[Tuple, _Split] = {}
+
+
+def _split_weights(lib, d: N.LinearDesc, ws: Sequence[Tensor], backward: bool):
+    """tf32 hi / lo splits of frozen float32 weights for the tensor-core maps (the
+    parameters ``predict`` freezes), made once and kept while the same weight tensors are
+    unchanged (tensor identity, storage and ``_version``: in-place updates through torch
+    invalidate them; writes through ``.data`` bypass the version counter and are not
+    seen), so a step does not re-split constant weights. ``None`` when not applicable
+    (the call then splits on its own). Never created during stream capture: a captured
+    step reuses the splits its warm-up made."""
+    if not ws or ws[0].dtype != torch.float32 or not ws[0].is_cuda or any(w.requires_grad for w in ws):
+        return None  # trainable weights change every step: they are split per call
+    key = (bool(backward),) + tuple(id(w) for w in ws) + tuple(tuple(w.shape) for w in ws)
+    vers = tuple((w._version, w.data_ptr()) for w in ws)
+    ent = _SPLITS.get(key)
+    if ent is not None and ent.versions == vers and all(r() is w for r, w in zip(ent.refs, ws)):
+        return ent.arr
+    if torch.cuda.is_current_stream_capturing():
+        return None
+    if len(_SPLITS) > 1024:
+        _SPLITS.clear()
+    bufs = []
+    for l, w in enumerate(ws):
+        k, n = (d.f_out_values[l], d.f_in_values[l]) if backward else (d.f_in_values[l], d.f_out_values[l])
+        bufs.append(torch.empty(2 * int(n) * ((int(k) + 3) // 4 * 4), dtype=torch.float32, device=w.device))
+    arr = _ptr_array(bufs)
+    if _TIMER is not None:
+        _TIMER.launches += len(ws)
+    rc = lib.fc_linear_presplit(ctypes.byref(d), _ptr_array(ws), int(bool(backward)), arr, _stream(ws[0].device))
+    _after(lib, rc, "fc_linear_presplit", ws[0].device)
+    ent = _Split()
+    ent.refs = [weakref.ref(w) for w in ws]
+    ent.versions, ent.bufs, ent.arr = vers, bufs, arr
+    _SPLITS[key] = ent
+    return arr
+
+
 def _linear_fwd_impl(x: Tensor, weights: Sequence[Tensor], out_dim: int, lists, precision: str,
                      scale: Tensor) -> Tensor:
     lib = N.lib()
@@ -544,9 +587,15 @@ def _linear_fwd_impl(x: Tensor, weights: Sequence[Tensor], out_dim: int, lists, 
     sc = scale.to(device=x.device, dtype=x.dtype).contiguous()
     out = x.new_empty((x.shape[0], int(out_dim)))
     d = _linear_desc(x, out_dim, lists[0], lists[1], lists[3], lists[4], lists[5], precision)
+    split = _split_weights(lib, d, ws, False)
     with _timed("linear_fwd", n_active, _nbytes(x, out, *ws)):
-        rc = lib.fc_linear_fwd(ctypes.byref(d), _p(x), _ptr_array(ws), _p(sc), x.shape[0], _p(out),
-                               ctypes.c_void_p(status_word(x.device).data_ptr()), _stream(x.device))
+        if split is not None:
+            rc = lib.fc_linear_fwd_presplit(ctypes.byref(d), _p(x), _ptr_array(ws), split, _p(sc), x.shape[0],
+                                            _p(out), ctypes.c_void_p(status_word(x.device).data_ptr()),
+                                            _stream(x.device))
+        else:
+            rc = lib.fc_linear_fwd(ctypes.byref(d), _p(x), _ptr_array(ws), _p(sc), x.shape[0], _p(out),
+                                   ctypes.c_void_p(status_word(x.device).data_ptr()), _stream(x.device))
     _after(lib, rc, "fc_linear_fwd", x.device)
     return out
 
@@ -565,10 +614,16 @@ def _linear_bwd_impl(grad_out: Tensor, x: Tensor, weights: Sequence[Tensor], nee
             gx.zero_()
         return gx, gws
     d = _linear_desc(x, g.shape[1], lists[0], lists[1], lists[3], lists[4], lists[5], precision)
+    split = _split_weights(lib, d, ws, True) if need_x else None
     with _timed("linear_bwd", n_active * (int(need_x) + int(need_w)), _nbytes(g, x, gx, *ws, *gws)):
-        rc = lib.fc_linear_bwd(ctypes.byref(d), _p(g), _p(x), _ptr_array(ws), _p(sc), x.shape[0],
-                               _p(gx) if need_x else None, _ptr_array(gws) if need_w else None,
-                               ctypes.c_void_p(status_word(x.device).data_ptr()), _stream(x.device))
+        if split is not None:
+            rc = lib.fc_linear_bwd_presplit(ctypes.byref(d), _p(g), _p(x), _ptr_array(ws), split, _p(sc),
+                                            x.shape[0], _p(gx), _ptr_array(gws) if need_w else None,
+                                            ctypes.c_void_p(status_word(x.device).data_ptr()), _stream(x.device))
+        else:
+            rc = lib.fc_linear_bwd(ctypes.byref(d), _p(g), _p(x), _ptr_array(ws), _p(sc), x.shape[0],
+                                   _p(gx) if need_x else None, _ptr_array(gws) if need_w else None,
+                                   ctypes.c_void_p(status_word(x.device).data_ptr()), _stream(x.device))
     _after(lib, rc, "fc_linear_bwd", x.device)
     return gx, gws
 

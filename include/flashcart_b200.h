@@ -195,6 +195,24 @@ int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* 
                   const void* const* weights, const void* scale, int64_t n, void* grad_x,
                   void* const* grad_weights, int32_t* status, fc_stream_t stream);
 
+/* Weights split once. The float32 maps run on the tensor cores as 3xTF32, which needs every
+ * weight matrix as tf32 hi and lo parts; fc_linear_fwd/bwd split them on every call.
+ * fc_linear_presplit writes, per active rank l, the split of weights[l] into split[l]
+ * (2 * N * kp floats, kp = (K + 3) & ~3; forward: K = f_in_values[l], N = f_out_values[l];
+ * backward: K = f_out_values[l], N = f_in_values[l]); fc_linear_fwd_presplit /
+ * fc_linear_bwd_presplit take those buffers next to the weights (which layouts outside
+ * the TMA-fed kernel still read) and skip the split. The caller keeps the buffers valid
+ * and re-splits after changing the weights. float32 only. Replace the same reference ops
+ * as fc_linear_fwd / fc_linear_bwd. */
+int fc_linear_presplit(const fc_linear_desc* desc, const void* const* weights, int32_t backward,
+                       void* const* split, fc_stream_t stream);
+int fc_linear_fwd_presplit(const fc_linear_desc* desc, const void* x, const void* const* weights,
+                           const void* const* split, const void* scale, int64_t n, void* out, int32_t* status,
+                           fc_stream_t stream);
+int fc_linear_bwd_presplit(const fc_linear_desc* desc, const void* grad_out, const void* x,
+                           const void* const* weights, const void* const* split, const void* scale, int64_t n,
+                           void* grad_x, void* const* grad_weights, int32_t* status, fc_stream_t stream);
+
 /* ---------------------------------------------------------------- RMS layer norm
  * Fused forward and first-order backward of RMSLayerNorm (nn/layers.py:413-540, affine,
  * without centering): per row, q_c = sum_l l_weights[l] * inv_l[c] with inv_l the

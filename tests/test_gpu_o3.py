@@ -295,3 +295,34 @@ def test_gpu_fp64_shared_attribute_convolution_vs_oracle(cuda_device, sig):
     for a, b in zip(grads, ref_grads):
         assert (a.cpu() - b).abs().max().item() < 1e-11 * max(1.0, b.abs().max().item())
     check_device_status(dev)
+
+
+def test_gpu_split_weight_cache_follows_in_place_updates(cuda_device):
+    """Frozen float32 weights are split into tf32 hi / lo once and reused; an in-place
+    update of the weights (a new _version) must be seen by the next forward and backward."""
+    from flashcart_b200 import o3 as O3
+
+    torch.manual_seed(2)
+    lin = O3.LinearLayer(2, 2, 64, 64).to(cuda_device)
+    for p in lin.parameters():
+        p.requires_grad_(False)
+    x = torch.randn(500, 9 * 64, device=cuda_device, requires_grad=True)
+
+    def check():
+        y = lin(x)
+        (g,) = torch.autograd.grad(y.square().sum(), [x])
+        xr = x.detach().double().cpu().requires_grad_(True)
+        yr = O.linear(xr, [w.double().cpu() for w in lin.weight], 2, 2, 64, 64)
+        (gr,) = torch.autograd.grad(yr.square().sum(), [xr])
+        assert (y.detach().double().cpu() - yr).abs().max().item() < 2e-5 * yr.abs().max().item()
+        assert (g.double().cpu() - gr).abs().max().item() < 2e-5 * gr.abs().max().item()
+        return y.detach()
+
+    y1 = check()
+    assert torch.equal(y1, lin(x).detach())  # the cached split gives the same result
+    with torch.no_grad():
+        for w in lin.weight:
+            w.mul_(-0.5).add_(0.1)
+    y2 = check()
+    assert not torch.equal(y1, y2)
+    check_device_status(cuda_device)
