@@ -1,8 +1,8 @@
 // Stream-ordered workspace of the library: one memory pool per device, created on first
 // use, that keeps its memory between calls (release threshold = unlimited) so that the
-// per-call workspaces (split weights of the GEMMs, edge matrices of the convolutions) are
-// re-used instead of re-mapped. Under stream capture the allocations become graph
-// allocation nodes.
+// per-call workspace of the GEMMs (their tf32-split weights, when the caller passes no
+// split of its own) is re-used instead of re-mapped. Under stream capture the
+// allocations become graph allocation nodes.
 #include "fc_base.cuh"
 
 #ifndef FC_HOST_EMU

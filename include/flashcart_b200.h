@@ -3,8 +3,11 @@
  *
  * Every entry point takes plain pointers to DEVICE memory (row-major, contiguous),
  * sizes, a POD descriptor and a cudaStream_t, and returns an int status
- * (FC_OK = 0, negative values below). Nothing here allocates device memory, frees
- * caller memory or synchronises the stream; outputs are owned by the caller.
+ * (FC_OK = 0, negative values below). No entry point frees caller memory or
+ * synchronises the stream; outputs are owned by the caller. Device memory is allocated
+ * only as stream-ordered workspace: fc_linear_fwd/bwd (the tf32 split of the weights,
+ * from the library's memory pool) and fc_newton_schulz (see there); the *_presplit
+ * linear entry points and every other entry point allocate nothing.
  * Accumulated outputs (scatter targets) are zero-filled inside the call with
  * cudaMemsetAsync on the given stream. Errors in the DATA (an index out of range,
  * an unsorted receiver list) are OR-ed into the optional device word `status`
