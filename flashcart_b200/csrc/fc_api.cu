@@ -234,6 +234,13 @@ template <typename T>
 static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const void* const* weights, const T* scale,
                         int64_t n, T* gx, void* const* gw, int* status, cudaStream_t s,
                         const void* const* bsplit = nullptr) {
+  if (n == 0) {
+    // no rows: grad_x is empty and every weight gradient is an empty sum
+    for (int l = 0; gw && l < d->n_active; ++l)
+      if (gw[l] && zero_fill(gw[l], (int64_t)d->f_out_values[l] * d->f_in_values[l] * sizeof(T), s))
+        return FC_ERR_LAUNCH;
+    return 0;
+  }
   if (gx) {
     // columns of x outside the active ranks get zero gradient
     int64_t prev = 0;
@@ -366,15 +373,22 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
   if (n_out_rows < 0 || n_in1_rows < 0 || n_in2_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_fwd: negative size");
   if (rowptr == nullptr && n_out_rows != n_in1_rows)
     return fail(FC_ERR_INVALID, "fc_tp_fwd: dense product needs n_out_rows == n_in1_rows");
-  if (rowptr != nullptr && idx_j == nullptr) return fail(FC_ERR_INVALID, "fc_tp_fwd: convolution needs idx_j");
+  if (rowptr != nullptr && idx_j == nullptr && n_in2_rows > 0)
+    return fail(FC_ERR_INVALID, "fc_tp_fwd: convolution needs idx_j");
   if (n_out_rows == 0) return FC_OK;
-  if (!in1 || !in2 || !weights || !out) return fail(FC_ERR_INVALID, "fc_tp_fwd: null tensor");
   const TpSigEntry* sig = find_sig(desc);
   if (sig == nullptr || sig->npaths == 0) {
     // no path: output has zero width
     return FC_OK;
   }
   cudaStream_t s = (cudaStream_t)stream;
+  if (rowptr != nullptr && n_in2_rows == 0) {
+    // convolution over no edges (isolated receivers only): every output row is an empty sum
+    if (!out) return fail(FC_ERR_INVALID, "fc_tp_fwd: null tensor");
+    return launch_status(zero_fill(out, n_out_rows * out_dim(desc) * (desc->dtype == FC_F32 ? 4 : 8), s),
+                         "fc_tp_fwd (zero fill)");
+  }
+  if (!in1 || !in2 || !weights || !out) return fail(FC_ERR_INVALID, "fc_tp_fwd: null tensor");
   const bool v2 = conv2_eligible(desc, rowptr != nullptr, in1, weights) && sig->table->fwd2_f32 != nullptr;
   if (desc->dtype == FC_F32) {
     TpParams<float> p;
@@ -395,7 +409,8 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
               fc_stream_t stream) {
   if (int rc = check_desc(desc)) return rc;
   if (n_out_rows < 0 || n_in1_rows < 0 || n_in2_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_bwd: negative size");
-  if (rowptr != nullptr && idx_j == nullptr) return fail(FC_ERR_INVALID, "fc_tp_bwd: convolution needs idx_j");
+  if (rowptr != nullptr && idx_j == nullptr && n_in2_rows > 0)
+    return fail(FC_ERR_INVALID, "fc_tp_bwd: convolution needs idx_j");
   if (rowptr == nullptr && (n_out_rows != n_in1_rows || n_in2_rows != n_in1_rows))
     return fail(FC_ERR_INVALID, "fc_tp_bwd: dense product needs equal row counts");
   const TpSigEntry* sig = find_sig(desc);
@@ -413,7 +428,8 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
   if (grad_weights && (desc->shared_weights || np == 0 || (conv && n_out_rows == 0)))
     rc |= zero_fill(grad_weights, (desc->shared_weights ? 1 : n_in2_rows) * (int64_t)np * F * esz, s);
   if (rc) return launch_status(FC_ERR_LAUNCH, "fc_tp_bwd (zero fill)");
-  if (n_out_rows == 0 || np == 0) return FC_OK;
+  // no edges: the zero-filled grad_in1 / shared grad_weights are the answer, grad_in2 has no rows
+  if (n_out_rows == 0 || np == 0 || (conv && n_in2_rows == 0)) return FC_OK;
   if (!grad_out || !in1 || !in2 || !weights) return fail(FC_ERR_INVALID, "fc_tp_bwd: null tensor");
   const bool v2 = conv2_eligible(desc, conv, in1, weights) && sig->table->bwd2_f32 != nullptr;
   if (desc->dtype == FC_F32) {
@@ -438,7 +454,8 @@ int fc_tp_dbwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, co
                void* d_in1, void* d_in2, void* d_weights, int32_t* status, fc_stream_t stream) {
   if (int rc = check_desc(desc)) return rc;
   if (n_out_rows < 0 || n_in1_rows < 0 || n_in2_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_dbwd: negative size");
-  if (rowptr != nullptr && idx_j == nullptr) return fail(FC_ERR_INVALID, "fc_tp_dbwd: convolution needs idx_j");
+  if (rowptr != nullptr && idx_j == nullptr && n_in2_rows > 0)
+    return fail(FC_ERR_INVALID, "fc_tp_dbwd: convolution needs idx_j");
   if (rowptr == nullptr && (n_out_rows != n_in1_rows || n_in2_rows != n_in1_rows))
     return fail(FC_ERR_INVALID, "fc_tp_dbwd: dense product needs equal row counts");
   const TpSigEntry* sig = find_sig(desc);
@@ -454,9 +471,10 @@ int fc_tp_dbwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, co
   if (d_in2 && (desc->in2_features == 1 || np == 0)) rc |= zero_fill(d_in2, n_in2_rows * d2 * esz, s);
   if (d_weights && (desc->shared_weights || np == 0 || (conv && n_out_rows == 0)))
     rc |= zero_fill(d_weights, (desc->shared_weights ? 1 : n_in2_rows) * (int64_t)np * F * esz, s);
-  if (d_grad_out && np == 0) rc |= zero_fill(d_grad_out, n_out_rows * out_dim(desc) * esz, s);
+  const bool no_edges = conv && n_in2_rows == 0;
+  if (d_grad_out && (np == 0 || no_edges)) rc |= zero_fill(d_grad_out, n_out_rows * out_dim(desc) * esz, s);
   if (rc) return launch_status(FC_ERR_LAUNCH, "fc_tp_dbwd (zero fill)");
-  if (n_out_rows == 0 || np == 0) return FC_OK;
+  if (n_out_rows == 0 || np == 0 || no_edges) return FC_OK;
   if (!grad_out || !in1 || !in2 || !weights) return fail(FC_ERR_INVALID, "fc_tp_dbwd: null tensor");
   if (desc->dtype == FC_F32) {
     TpDbwdParams<float> p;
@@ -554,7 +572,7 @@ int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* 
                   fc_stream_t stream) {
   if (int rc = check_linear(desc)) return rc;
   if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_bwd: negative size");
-  if (desc->n_active > 0 && (!grad_out || !x || !scale || !weights))
+  if (desc->n_active > 0 && (!scale || !weights || (n > 0 && (!grad_out || !x))))
     return fail(FC_ERR_INVALID, "fc_linear_bwd: null tensor");
   cudaStream_t s = (cudaStream_t)stream;
   if (desc->dtype == FC_F32)
@@ -611,7 +629,7 @@ int fc_linear_bwd_presplit(const fc_linear_desc* desc, const void* grad_out, con
                            void* grad_x, void* const* grad_weights, int32_t* status, fc_stream_t stream) {
   if (int rc = presplit_check(desc, weights, split, "fc_linear_bwd_presplit")) return rc;
   if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_bwd_presplit: negative size");
-  if (desc->n_active > 0 && (!grad_out || !x || !scale))
+  if (desc->n_active > 0 && (!scale || (n > 0 && (!grad_out || !x))))
     return fail(FC_ERR_INVALID, "fc_linear_bwd_presplit: null tensor");
   return launch_status(linear_bwd_t<float>(desc, (const float*)grad_out, (const float*)x, weights,
                                            (const float*)scale, n, (float*)grad_x, grad_weights,

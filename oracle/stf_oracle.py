@@ -255,10 +255,12 @@ def tensor_product(in1, in2, weights, idx_i, idx_j, in1_l_max, in2_l_max, out_l_
     for lo, bucket in enumerate(per_l):
         if not bucket:
             continue
-        if reduce_paths:
-            blocks.append(sum(bucket).reshape(n, -1))
-        else:
-            blocks.append(torch.stack(bucket, dim=2).reshape(n, -1))
+        # explicit widths: with no edges (n = 0) a reshape to (n, -1) is ambiguous and the
+        # reference py path raises there, while its CUDA operator writes every receiver row
+        # as an empty sum (CSR grid over receivers, o3/_tensor_product.py:396-412); the
+        # oracle gives that empty sum
+        t = sum(bucket) if reduce_paths else torch.stack(bucket, dim=2)
+        blocks.append(t.reshape(n, math.prod(t.shape[1:])))
     out = torch.cat(blocks, dim=-1) if blocks else in1.new_zeros(n, 0)
     if conv:
         res = out.new_zeros(n_nodes, out.shape[1])

@@ -6,6 +6,8 @@ GEMMs, receiver CSR) with the host compiler; this suite drives it through the sa
 C entry points and checks every output against the reference's golden vectors.
 """
 
+import ctypes
+
 import pytest
 import torch
 
@@ -137,3 +139,88 @@ def test_emu_tp_out_of_range_sender_is_flagged_not_read(emu_lib):
     out = A.tp_fwd(emu_lib, m, in1, in2, w, idx_i, idx_j, status)
     assert int(status) & N.FC_DEV_BAD_INDEX
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("sig", [(2, 2, 2, 4), (1, 1, 1, 3), (0, 3, 3, 2)])
+def test_emu_tp_convolution_without_edges(emu_lib, sig):
+    """A graph with no edges (isolated atoms only): every receiver sums nothing, the
+    per-edge gradients have no rows, and nothing is read through the empty index arrays
+    (the reference's gather / scatter_sum gives zeros the same way)."""
+    l1, l2, lo, C = sig
+    m = [l1, l2, lo, C, 1, 0, 0, 0]
+    n = 5
+    n_paths = emu_lib.fc_tp_num_paths(ctypes.byref(A.desc(m, torch.float64)))
+    in1 = torch.randn(n, (l1 + 1) ** 2 * C, dtype=torch.float64)
+    in2 = torch.zeros(0, (l2 + 1) ** 2, dtype=torch.float64)
+    w = torch.zeros(0, n_paths * C, dtype=torch.float64)
+    idx = torch.zeros(0, dtype=torch.int64)
+    status = torch.zeros(1, dtype=torch.int32)
+    out = A.tp_fwd(emu_lib, m, in1, in2, w, idx, idx, status)
+    assert out.shape[0] == n and out.shape[1] > 0 and (out == 0).all()
+    g = torch.randn_like(out)
+    g1, g2, gw = A.tp_bwd(emu_lib, m, g, in1, in2, w, idx, idx, status=status)
+    assert (g1 == 0).all() and g2.shape == in2.shape and gw.shape == w.shape
+    v1 = torch.randn_like(in1)
+    dg, d1, d2, dw = A.tp_dbwd(emu_lib, m, g, in1, in2, w, v1, in2, w, idx, idx, status)
+    assert (dg == 0).all() and (d1 == 0).all() and d2.shape == in2.shape and dw.shape == w.shape
+    assert int(status) == 0
+
+
+def _ragged_receivers(n_nodes, degrees, seed):
+    """Receiver-sorted idx_i with the given per-node degree (zeros allowed) and random senders."""
+    g = torch.Generator().manual_seed(seed)
+    idx_i = torch.repeat_interleave(torch.arange(n_nodes), torch.tensor(degrees))
+    idx_j = torch.randint(0, n_nodes, (idx_i.numel(),), generator=g)
+    return idx_i, idx_j, g
+
+
+@pytest.mark.parametrize("sig", [(2, 2, 2, 4), (3, 3, 3, 2), (0, 3, 3, 3)])
+def test_emu_tp_ragged_degrees_vs_oracle(emu_lib, sig):
+    """Isolated receivers at both ends and in the middle, one receiver with many edges
+    (several edge chunks), the rest of degree 1-3: forward and all three gradients
+    against the oracle in float64."""
+    from oracle import stf_oracle as O
+
+    l1, l2, lo, C = sig
+    m = [l1, l2, lo, C, 1, 0, 0, 0]
+    degrees = [0, 0, 3, 137, 0, 1, 2, 0, 3, 1, 0, 0]
+    n = len(degrees)
+    idx_i, idx_j, g = _ragged_receivers(n, degrees, 5)
+    e = idx_i.numel()
+    n_paths = emu_lib.fc_tp_num_paths(ctypes.byref(A.desc(m, torch.float64)))
+    in1 = torch.randn(n, (l1 + 1) ** 2 * C, generator=g, dtype=torch.float64)
+    r = torch.nn.functional.normalize(torch.randn(e, 3, generator=g, dtype=torch.float64), dim=-1)
+    in2 = O.irreps(r, l2)
+    w = torch.randn(e, n_paths * C, generator=g, dtype=torch.float64)
+    out = A.tp_fwd(emu_lib, m, in1, in2, w, idx_i, idx_j)
+    leaves = [t.clone().requires_grad_(True) for t in (in1, in2, w)]
+    ref = O.tensor_product(*leaves, idx_i, idx_j, l1, l2, lo, C, 1)
+    assert (out - ref.detach()).abs().max() < TOL * max(1.0, ref.abs().max().item())
+    for node, deg in enumerate(degrees):
+        if deg == 0:
+            assert (out[node] == 0).all()
+    gout = torch.randn_like(out)
+    grads = A.tp_bwd(emu_lib, m, gout, in1, in2, w, idx_i, idx_j)
+    ref_grads = torch.autograd.grad(ref, leaves, gout)
+    for a, b in zip(grads, ref_grads):
+        assert (a - b).abs().max() < TOL * max(1.0, b.abs().max().item())
+
+
+def test_emu_linear_without_rows(golden, emu_lib):
+    """A map applied to zero rows (e.g. the radial layers of a graph with no edges):
+    empty output, and weight gradients that are zero rather than left unwritten."""
+    name = sorted({k.split("/")[1] for k in golden if k.startswith("linear/")})[0]
+    k = f"linear/{name}"
+    meta = [int(v) for v in golden[k + "/meta"]]
+    li, lo, fi, fo = meta[:4]
+    paths = meta[5:]
+    common = min(li, lo)
+    ws = [golden[f"{k}/w{l}"] for l in range(common + 1)]
+    scale = torch.ones(common + 1, dtype=torch.float64)
+    d = A.linear_desc(li, lo, fi, fo, paths, torch.float64)
+    x = golden[k + "/x"][:0]
+    out = A.linear_fwd(emu_lib, d, x, ws, scale)
+    assert out.shape == (0, d.out_dim)
+    gx, gws = A.linear_bwd(emu_lib, d, out, x, ws, scale)
+    assert gx.shape == x.shape
+    assert all((gw == 0).all() for gw in gws)

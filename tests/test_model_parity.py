@@ -93,3 +93,44 @@ def test_b200_potential_matches_reference(model_golden, name, cuda_device):
     model = _build(name, model_golden).to(cuda_device)
     out = model.predict(_graph(model_golden, torch.float32, cuda_device), compute_forces=True, compute_stress=True)
     _check_f32(out, model_golden, name, n)
+
+
+def _isolated_atom_graph(dtype, device, with_molecule):
+    """A water molecule (6 edges) and a hydrogen atom 20 A away with no neighbour, as two
+    structures of one batch; or the lone atom alone (no edge in the whole batch)."""
+    lone = [[30.0, 30.0, 30.0]]
+    if with_molecule:
+        pos = [[10.0, 10.0, 10.0], [10.96, 10.0, 10.0], [9.76, 10.93, 10.0]] + lone
+        types, batch, counts = [1, 0, 0, 0], [0, 0, 0, 1], [3, 1]
+        edges = [[0, 0, 1, 1, 2, 2], [1, 2, 0, 2, 0, 1]]
+    else:
+        pos, types, batch, counts, edges = lone, [0], [0], [1], [[], []]
+    g = len(counts)
+    return {
+        "positions": torch.tensor(pos, dtype=dtype, device=device),
+        "cell": (40.0 * torch.eye(3, dtype=dtype, device=device)).expand(g, 3, 3).contiguous(),
+        "atom_types": torch.tensor(types, device=device), "edge_index": torch.tensor(edges, dtype=torch.int64,
+                                                                                     device=device),
+        "shifts": torch.zeros(len(edges[0]), 3, dtype=torch.int32, device=device),
+        "batch": torch.tensor(batch, device=device), "n_atoms": torch.tensor(counts, device=device),
+        "pbc": torch.tensor([False, False, False], device=device),
+    }
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("with_molecule", [True, False])
+def test_b200_potential_with_isolated_atoms(model_golden, with_molecule, cuda_device):
+    """Atoms without neighbours (and a batch without a single edge) give the oracle's
+    energies, zero forces on the lone atom and finite stress, in float64."""
+    name = "cfg0"
+    model = _build(name, model_golden)
+    sd = {k: v.double() if v.is_floating_point() else v for k, v in model.state_dict().items()}
+    ref = model_oracle.predict(sd, _kwargs(name, float(model_golden["avg_neighbors"])),
+                               _isolated_atom_graph(torch.float64, "cpu", with_molecule))
+    m64 = model.to(cuda_device, torch.float64)
+    out = m64.predict(_isolated_atom_graph(torch.float64, cuda_device, with_molecule), compute_forces=True,
+                      compute_stress=True)
+    for key in ("energy", "forces", "stress"):
+        r = ref[key]
+        assert (out[key].cpu() - r).abs().max() <= 1e-9 * max(1.0, r.abs().max().item()), key
+    assert (out["forces"][-1] == 0).all()
