@@ -99,6 +99,8 @@ int64_t fc_tp_out_dim(const fc_tp_desc* desc);
  *   W[e] (.) TP(in1[idx_j[e]], in2[e]);  in2/weights have one row per edge,
  *   rowptr from fc_build_rowptr, n_out_rows = number of receivers, n_in1_rows =
  *   rows of in1 (idx_j range), n_in2_rows = edges (rows of in2 and weights).
+ *   With no edges (n_in2_rows == 0) in2, weights and idx_j may be NULL and every
+ *   output row is zero; the same holds for fc_tp_bwd / fc_tp_dbwd.
  * Dense when rowptr == NULL: row r of out from row r of in1, in2 and weights;
  *   n_out_rows = n_in1_rows = n_in2_rows = rows. */
 int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const void* weights,
