@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "fc_neighbor_workspace_bytes", "fc_neighbor_count", "fc_neighbor_fill",
     "fc_edge_expand_fwd", "fc_edge_expand_bwd",
     "fc_linear_presplit", "fc_linear_fwd_presplit", "fc_linear_bwd_presplit",
+    "fc_linear_dbwd", "fc_halo_pack", "fc_halo_unpack",
 )
 
 
@@ -109,6 +110,12 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_tp_conv_fwd_noalloc.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P]
     lib.fc_linear_bwd.restype = ctypes.c_int
     lib.fc_linear_bwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P, _P]
+    lib.fc_linear_dbwd.restype = ctypes.c_int
+    lib.fc_linear_dbwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P]
+    lib.fc_halo_pack.restype = ctypes.c_int
+    lib.fc_halo_pack.argtypes = [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P]
+    lib.fc_halo_unpack.restype = ctypes.c_int
+    lib.fc_halo_unpack.argtypes = [_P, _I64, _I64, _I32, _P, _P, _I64, _I32, _P, _P]
     lib.fc_newton_schulz.restype = ctypes.c_int
     lib.fc_newton_schulz.argtypes = [_P, _I32, _I64, _I32, _I32, _P, _I32, _P, _I32, ctypes.c_float, _P, _P, _P]
     lib.fc_rms_norm_fwd.restype = ctypes.c_int

@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstdarg>
 #include <mutex>
+#include <vector>
 
 #include "tp_common.cuh"
 #include "linear.cuh"
@@ -35,6 +36,12 @@ template <typename T>
 int edge_expand_bwd_dispatch(int, const T*, const T*, const T*, int, int, int64_t, T*, T*, cudaStream_t);
 template <typename T>
 int gate_fwd_dispatch(int, const T*, const T*, T*, int, int64_t, cudaStream_t);
+template <typename T>
+int halo_pack_dispatch(const T*, int64_t, int64_t, const int64_t*, int64_t, T*, int*, cudaStream_t);
+template <typename T>
+int halo_unpack_dispatch(const T*, int64_t, const int64_t*, int64_t, T*, int64_t, int, int*, cudaStream_t);
+template <typename T>
+int add_rows_dispatch(T*, const T*, int64_t, cudaStream_t);
 template <typename T>
 int gate_bwd_dispatch(int, const T*, const T*, const T*, T*, T*, int, int64_t, cudaStream_t);
 
@@ -279,6 +286,56 @@ static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const v
       a.k_in = d->f_in_values[l];
       a.rows_per_split = 0;
       if (int rc = lin_wgrad<T>(a, s)) return rc;
+    }
+  }
+  return 0;
+}
+
+// VJP of linear_bwd_t (see fc_linear_dbwd in the header) from the forward / backward GEMMs.
+template <typename T>
+static int linear_dbwd_t(const fc_linear_desc* d, const T* g, const T* x, const void* const* weights, const T* vx,
+                         const void* const* vw, const T* scale, int64_t n, T* dg, T* dx, void* const* dw, int* status,
+                         cudaStream_t s) {
+  const size_t esz = sizeof(T);
+  if (dg) {
+    if (vx) {
+      if (int rc = linear_fwd_t<T>(d, vx, weights, scale, n, dg, status, s)) return rc;
+    }
+    if (vw) {
+      if (!vx) {
+        if (int rc = linear_fwd_t<T>(d, x, vw, scale, n, dg, status, s)) return rc;
+      } else {
+        const int64_t count = n * d->out_dim;
+#ifndef FC_HOST_EMU
+        void* tmp = nullptr;
+        if (fc_pool_alloc(&tmp, (size_t)count * esz, s)) return FC_ERR_LAUNCH;
+        int rc = linear_fwd_t<T>(d, x, vw, scale, n, (T*)tmp, status, s);
+        if (!rc) rc = add_rows_dispatch<T>(dg, (const T*)tmp, count, s);
+        if (fc_pool_free(tmp, s) && !rc) rc = FC_ERR_LAUNCH;
+#else
+        std::vector<T> tmp((size_t)count);
+        int rc = linear_fwd_t<T>(d, x, vw, scale, n, tmp.data(), status, s);
+        if (!rc) rc = add_rows_dispatch<T>(dg, tmp.data(), count, s);
+#endif
+        if (rc) return rc;
+      }
+    }
+    if (!vx && !vw && zero_fill(dg, n * d->out_dim * (int64_t)esz, s)) return FC_ERR_LAUNCH;
+  }
+  if (dx) {
+    if (vw) {
+      if (int rc = linear_bwd_t<T>(d, g, x, vw, scale, n, dx, nullptr, status, s)) return rc;
+    } else if (zero_fill(dx, n * d->in_dim * (int64_t)esz, s)) {
+      return FC_ERR_LAUNCH;
+    }
+  }
+  if (dw) {
+    if (vx) {
+      if (int rc = linear_bwd_t<T>(d, g, vx, weights, scale, n, nullptr, dw, status, s)) return rc;
+    } else {
+      for (int l = 0; l < d->n_active; ++l)
+        if (dw[l] && zero_fill(dw[l], (int64_t)d->f_out_values[l] * d->f_in_values[l] * (int64_t)esz, s))
+          return FC_ERR_LAUNCH;
     }
   }
   return 0;
@@ -584,6 +641,75 @@ int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* 
                                             (const double*)scale, n, (double*)grad_x, grad_weights,
                                             reinterpret_cast<int*>(status), s),
                        "fc_linear_bwd");
+}
+
+int fc_linear_dbwd(const fc_linear_desc* desc, const void* grad_out, const void* x, const void* const* weights,
+                   const void* v_grad_x, const void* const* v_grad_weights, const void* scale, int64_t n,
+                   void* d_grad_out, void* d_x, void* const* d_weights, int32_t* status, fc_stream_t stream) {
+  if (int rc = check_linear(desc)) return rc;
+  if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_dbwd: negative size");
+  if (desc->n_active > 0 && (!scale || !weights || (n > 0 && (!grad_out || !x))))
+    return fail(FC_ERR_INVALID, "fc_linear_dbwd: null tensor");
+  for (int l = 0; v_grad_weights && l < desc->n_active; ++l)
+    if (!v_grad_weights[l]) return fail(FC_ERR_INVALID, "fc_linear_dbwd: null weight tangent for rank %d", l);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t esz = desc->dtype == FC_F32 ? 4 : 8;
+  if (n == 0 || desc->n_active == 0) {
+    // no rows (or no active rank): every output is an empty sum
+    int rc = 0;
+    if (d_grad_out) rc |= zero_fill(d_grad_out, n * desc->out_dim * esz, s);
+    if (d_x) rc |= zero_fill(d_x, n * desc->in_dim * esz, s);
+    for (int l = 0; d_weights && l < desc->n_active; ++l)
+      if (d_weights[l])
+        rc |= zero_fill(d_weights[l], (int64_t)desc->f_out_values[l] * desc->f_in_values[l] * esz, s);
+    return rc ? launch_status(FC_ERR_LAUNCH, "fc_linear_dbwd (zero fill)") : FC_OK;
+  }
+  if (desc->dtype == FC_F32)
+    return launch_status(linear_dbwd_t<float>(desc, (const float*)grad_out, (const float*)x, weights,
+                                              (const float*)v_grad_x, v_grad_weights, (const float*)scale, n,
+                                              (float*)d_grad_out, (float*)d_x, d_weights,
+                                              reinterpret_cast<int*>(status), s),
+                         "fc_linear_dbwd");
+  return launch_status(linear_dbwd_t<double>(desc, (const double*)grad_out, (const double*)x, weights,
+                                             (const double*)v_grad_x, v_grad_weights, (const double*)scale, n,
+                                             (double*)d_grad_out, (double*)d_x, d_weights,
+                                             reinterpret_cast<int*>(status), s),
+                       "fc_linear_dbwd");
+}
+
+// ------------------------------------------------------------------ halo exchange
+
+int fc_halo_pack(const void* x, int64_t n_rows, int64_t row_elems, int32_t dtype, const int64_t* idx,
+                 int64_t n_idx, void* buf, int32_t* status, fc_stream_t stream) {
+  if (n_rows < 0 || row_elems < 0 || n_idx < 0) return fail(FC_ERR_INVALID, "fc_halo_pack: negative size");
+  if (dtype != FC_F32 && dtype != FC_F64) return fail(FC_ERR_INVALID, "fc_halo_pack: dtype must be f32 or f64");
+  if (n_idx == 0 || row_elems == 0) return FC_OK;
+  if (!idx || !buf || (n_rows > 0 && !x)) return fail(FC_ERR_INVALID, "fc_halo_pack: null tensor");
+  cudaStream_t s = (cudaStream_t)stream;
+  int* st = reinterpret_cast<int*>(status);
+  if (dtype == FC_F32)
+    return launch_status(halo_pack_dispatch<float>((const float*)x, n_rows, row_elems, idx, n_idx, (float*)buf, st, s),
+                         "fc_halo_pack");
+  return launch_status(halo_pack_dispatch<double>((const double*)x, n_rows, row_elems, idx, n_idx, (double*)buf, st,
+                                                  s),
+                       "fc_halo_pack");
+}
+
+int fc_halo_unpack(const void* buf, int64_t n_idx, int64_t row_elems, int32_t dtype, const int64_t* idx, void* x,
+                   int64_t n_rows, int32_t accumulate, int32_t* status, fc_stream_t stream) {
+  if (n_rows < 0 || row_elems < 0 || n_idx < 0) return fail(FC_ERR_INVALID, "fc_halo_unpack: negative size");
+  if (dtype != FC_F32 && dtype != FC_F64) return fail(FC_ERR_INVALID, "fc_halo_unpack: dtype must be f32 or f64");
+  if (n_idx == 0 || row_elems == 0) return FC_OK;
+  if (!idx || !buf || (n_rows > 0 && !x)) return fail(FC_ERR_INVALID, "fc_halo_unpack: null tensor");
+  cudaStream_t s = (cudaStream_t)stream;
+  int* st = reinterpret_cast<int*>(status);
+  if (dtype == FC_F32)
+    return launch_status(halo_unpack_dispatch<float>((const float*)buf, row_elems, idx, n_idx, (float*)x, n_rows,
+                                                     accumulate, st, s),
+                         "fc_halo_unpack");
+  return launch_status(halo_unpack_dispatch<double>((const double*)buf, row_elems, idx, n_idx, (double*)x, n_rows,
+                                                    accumulate, st, s),
+                       "fc_halo_unpack");
 }
 
 // ------------------------------------------------------------------ linear maps, split weights

@@ -199,6 +199,17 @@ int fc_linear_fwd(const fc_linear_desc* desc, const void* x, const void* const* 
 int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* x,
                   const void* const* weights, const void* scale, int64_t n, void* grad_x,
                   void* const* grad_weights, int32_t* status, fc_stream_t stream);
+/* Double backward. Replaces flashcart::linear_dbwd (o3/_linear.py:571-778): the VJP of
+ * fc_linear_bwd for tangents v_grad_x (like x) and v_grad_weights (like weights), with
+ * gx = g (sW) and gW_l = s_l g^T x per rank:
+ *   d_grad_out = v_grad_x (sW)^T + x (s v_grad_weights)^T,
+ *   d_x = g (s v_grad_weights),  d_weights[l] = s_l g^T v_grad_x.
+ * A NULL tangent counts as zero; each of d_grad_out, d_x and d_weights may be NULL (not
+ * wanted) and is otherwise fully overwritten. With both tangents given, d_grad_out
+ * needs one stream-ordered workspace of n * out_dim elements from the library's pool. */
+int fc_linear_dbwd(const fc_linear_desc* desc, const void* grad_out, const void* x, const void* const* weights,
+                   const void* v_grad_x, const void* const* v_grad_weights, const void* scale, int64_t n,
+                   void* d_grad_out, void* d_x, void* const* d_weights, int32_t* status, fc_stream_t stream);
 
 /* Weights split once. The float32 maps run on the tensor cores as 3xTF32, which needs every
  * weight matrix as tf32 hi and lo parts; fc_linear_fwd/bwd split them on every call.
@@ -217,6 +228,25 @@ int fc_linear_fwd_presplit(const fc_linear_desc* desc, const void* x, const void
 int fc_linear_bwd_presplit(const fc_linear_desc* desc, const void* grad_out, const void* x,
                            const void* const* weights, const void* const* split, const void* scale, int64_t n,
                            void* grad_x, void* const* grad_weights, int32_t* status, fc_stream_t stream);
+
+/* ---------------------------------------------------------------- halo exchange
+ * Row gather / scatter for ghost-atom exchange in a domain decomposition (owned rows
+ * first, ghost rows after them). The transport between ranks is the caller's (NCCL, MPI,
+ * an MD engine's communicator); these move rows between the feature array and the
+ * contiguous send / receive buffers. Replace the device-side halves of
+ * lammps_forward_exchange / lammps_reverse_exchange (utils/lammps.py:67-118): owner rows
+ * copied into ghost rows, ghost-row gradients added into owner rows.
+ * Rows hold row_elems elements of dtype (FC_F32 / FC_F64). An index outside
+ * [0, n_rows) sets FC_DEV_BAD_INDEX in *status (if given) and its row is skipped. */
+/* buf[k, :] = x[idx[k], :] for k < n_idx (rows of a bad index are written as zeros). */
+int fc_halo_pack(const void* x, int64_t n_rows, int64_t row_elems, int32_t dtype, const int64_t* idx,
+                 int64_t n_idx, void* buf, int32_t* status, fc_stream_t stream);
+/* accumulate == 0: x[idx[k], :] = buf[k, :] (ghost rows receive their owners' features;
+ * indices should be distinct). accumulate != 0: x[idx[k], :] += buf[k, :] with atomic
+ * adds (ghost gradients added to their owners; repeated indices allowed, the order of
+ * the additions is not fixed). */
+int fc_halo_unpack(const void* buf, int64_t n_idx, int64_t row_elems, int32_t dtype, const int64_t* idx, void* x,
+                   int64_t n_rows, int32_t accumulate, int32_t* status, fc_stream_t stream);
 
 /* ---------------------------------------------------------------- RMS layer norm
  * Fused forward and first-order backward of RMSLayerNorm (nn/layers.py:413-540, affine,

@@ -145,3 +145,30 @@ def linear_bwd(lib, d, g, x, ws, scale):
     N.check(lib, lib.fc_linear_bwd(ctypes.byref(d), p(g), p(x), ptr_array(ws), p(scale), x.shape[0], p(gx),
                                    ptr_array(gws), None, stream_of(x)), "fc_linear_bwd")
     return gx, gws
+
+
+def linear_dbwd(lib, d, g, x, ws, vx, vws, scale):
+    dg = torch.full_like(g, float("nan"))
+    dx = torch.full_like(x, float("nan"))
+    dws = [torch.full_like(w, float("nan")) for w in ws]
+    N.check(lib, lib.fc_linear_dbwd(ctypes.byref(d), p(g), p(x), ptr_array(ws), p(vx),
+                                    ptr_array(vws) if vws is not None else None, p(scale), x.shape[0], p(dg),
+                                    p(dx), ptr_array(dws), None, stream_of(x)), "fc_linear_dbwd")
+    return dg, dx, dws
+
+
+def _dtype_code(t):
+    return N.FC_F64 if t.dtype == torch.float64 else N.FC_F32
+
+
+def halo_pack(lib, x, idx, status=None):
+    buf = torch.full((idx.numel(), x.shape[1]), float("nan"), dtype=x.dtype, device=x.device)
+    N.check(lib, lib.fc_halo_pack(p(x), x.shape[0], x.shape[1], _dtype_code(x), p(idx), idx.numel(), p(buf),
+                                  p(status), stream_of(x)), "fc_halo_pack")
+    return buf
+
+
+def halo_unpack(lib, buf, idx, x, accumulate, status=None):
+    N.check(lib, lib.fc_halo_unpack(p(buf), idx.numel(), buf.shape[1], _dtype_code(buf), p(idx), p(x), x.shape[0],
+                                    int(accumulate), p(status), stream_of(x)), "fc_halo_unpack")
+    return x

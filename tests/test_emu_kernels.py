@@ -224,3 +224,62 @@ def test_emu_linear_without_rows(golden, emu_lib):
     gx, gws = A.linear_bwd(emu_lib, d, out, x, ws, scale)
     assert gx.shape == x.shape
     assert all((gw == 0).all() for gw in gws)
+
+
+def test_emu_linear_double_backward(golden, emu_lib):
+    """fc_linear_dbwd against the reference's VJP-of-VJP (tangents on grad_x and grad_w),
+    plus the one-tangent forms against the two-tangent result split by linearity."""
+    names = sorted({k.split("/")[1] for k in golden if k.startswith("linear/")})
+    for name in names:
+        k = f"linear/{name}"
+        meta = [int(v) for v in golden[k + "/meta"]]
+        li, lo, fi, fo, has_ws = meta[:5]
+        paths = meta[5:]
+        common = min(li, lo)
+        ws = [golden[f"{k}/w{l}"] for l in range(common + 1)]
+        vws = [golden[f"{k}/tan_w{l}"] for l in range(common + 1)]
+        scale = torch.tensor([1.0 if has_ws == 1 else (fi * paths[l]) ** -0.5 for l in range(common + 1)],
+                             dtype=torch.float64)
+        d = A.linear_desc(li, lo, fi, fo, paths, torch.float64)
+        g, x, vx = golden[k + "/g"], golden[k + "/x"], golden[k + "/tan_x"]
+        dg, dx, dws = A.linear_dbwd(emu_lib, d, g, x, ws, vx, vws, scale)
+        assert (dg - golden[k + "/dd_g"]).abs().max() < TOL, name
+        assert (dx - golden[k + "/dd_x"]).abs().max() < TOL, name
+        for l in range(common + 1):
+            assert (dws[l] - golden[f"{k}/dd_w{l}"]).abs().max() < TOL, (name, l)
+        dg_x, dx_x, dws_x = A.linear_dbwd(emu_lib, d, g, x, ws, vx, None, scale)
+        dg_w, dx_w, dws_w = A.linear_dbwd(emu_lib, d, g, x, ws, None, vws, scale)
+        assert (dx_x == 0).all() and all((w == 0).all() for w in dws_w)
+        assert (dg_x + dg_w - dg).abs().max() < TOL, name
+        assert (dx_w - dx).abs().max() < TOL and all((a - b).abs().max() < TOL for a, b in zip(dws_x, dws))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_emu_halo_pack_and_unpack(emu_lib, dtype):
+    """Pack = row gather, unpack = row copy or (with repeated indices) row sum, as the
+    forward and reverse ghost exchanges need; a bad index is flagged and skipped."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(40, 36, generator=g).to(dtype)
+    send = torch.tensor([5, 0, 39, 5, 17, 22], dtype=torch.int64)
+    buf = A.halo_pack(emu_lib, x, send)
+    assert torch.equal(buf, x.index_select(0, send))
+    ghosts = torch.tensor([30, 31, 32, 33, 34, 35], dtype=torch.int64)
+    y = x.clone()
+    A.halo_unpack(emu_lib, buf, ghosts, y, accumulate=False)
+    ref = x.clone()
+    ref[ghosts] = buf
+    assert torch.equal(y, ref)
+    owners = torch.tensor([1, 2, 1, 1, 7, 2], dtype=torch.int64)
+    acc = torch.zeros(10, 36, dtype=dtype)
+    A.halo_unpack(emu_lib, buf, owners, acc, accumulate=True)
+    ref = torch.zeros(10, 36, dtype=dtype).index_add_(0, owners, buf)
+    assert (acc - ref).abs().max() < (1e-6 if dtype == torch.float32 else 1e-14)
+    status = torch.zeros(1, dtype=torch.int32)
+    bad = torch.tensor([3, 40, -1], dtype=torch.int64)
+    out = A.halo_pack(emu_lib, x, bad, status)
+    assert int(status) & N.FC_DEV_BAD_INDEX
+    assert torch.equal(out[0], x[3]) and (out[1:] == 0).all()
+    status.zero_()
+    tgt = torch.zeros(4, 36, dtype=dtype)
+    A.halo_unpack(emu_lib, out, torch.tensor([0, 4, 1]), tgt, accumulate=True, status=status)
+    assert int(status) & N.FC_DEV_BAD_INDEX and torch.equal(tgt[0], x[3]) and (tgt[1:] == 0).all()

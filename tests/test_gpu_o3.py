@@ -394,3 +394,59 @@ def test_gpu_convolution_ragged_degrees_vs_oracle(cuda_device, sig, dtype):
     for a, b in zip(grads, ref_grads):
         assert (a.double().cpu() - b).abs().max().item() < tol * max(1.0, b.abs().max().item())
     check_device_status(dev)
+
+
+def test_gpu_raw_c_abi_linear_double_backward(golden, cuda_device):
+    """fc_linear_dbwd through the C ABI: float64 against the reference's VJP-of-VJP at its
+    1e-10 tolerance; float32 (3xTF32 GEMMs, a pool workspace for the two-tangent sum)
+    against the float64 result."""
+    lib = N.lib()
+    for name in sorted({k.split("/")[1] for k in golden if k.startswith("linear/")}):
+        k = f"linear/{name}"
+        meta = [int(v) for v in golden[k + "/meta"]]
+        li, lo, fi, fo, has_ws = meta[:5]
+        paths = meta[5:]
+        common = min(li, lo)
+        scale = torch.tensor([1.0 if has_ws == 1 else (fi * paths[l]) ** -0.5 for l in range(common + 1)],
+                             dtype=torch.float64)
+        for dtype in (torch.float64, torch.float32):
+            dev = lambda t: t.to(cuda_device, dtype)  # noqa: E731
+            ws = [dev(golden[f"{k}/w{l}"]) for l in range(common + 1)]
+            vws = [dev(golden[f"{k}/tan_w{l}"]) for l in range(common + 1)]
+            d = A.linear_desc(li, lo, fi, fo, paths, dtype)
+            dg, dx, dws = A.linear_dbwd(lib, d, dev(golden[k + "/g"]), dev(golden[k + "/x"]), ws,
+                                        dev(golden[k + "/tan_x"]), vws, dev(scale))
+            pairs = [(dg, golden[k + "/dd_g"]), (dx, golden[k + "/dd_x"])]
+            pairs += [(dws[l], golden[f"{k}/dd_w{l}"]) for l in range(common + 1)]
+            for got, ref in pairs:
+                err = (got.double().cpu() - ref).abs().max().item()
+                bound = 1e-10 if dtype == torch.float64 else 2e-5 * max(1.0, ref.abs().max().item())
+                assert err < bound, (name, dtype, err)
+    check_device_status(cuda_device)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_gpu_raw_c_abi_halo_pack_and_unpack(cuda_device, dtype):
+    """Row gather / copy / atomic row sum at feature width 2048 (l <= 3, C = 128) over
+    tens of thousands of rows, against index_select / index_copy / index_add; a bad index
+    is flagged in the status word and skipped."""
+    lib = N.lib()
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(30000, 2048, generator=g).to(cuda_device, dtype)
+    send = torch.randint(0, 30000, (12000,), generator=g).to(cuda_device)
+    buf = A.halo_pack(lib, x, send)
+    assert torch.equal(buf, x.index_select(0, send))
+    ghosts = torch.randperm(30000, generator=g)[:12000].to(cuda_device)
+    y = x.clone()
+    A.halo_unpack(lib, buf, ghosts, y, accumulate=False)
+    assert torch.equal(y, x.index_copy(0, ghosts, buf))
+    owners = torch.randint(0, 500, (12000,), generator=g).to(cuda_device)  # ~24 contributions per owner
+    acc = torch.zeros(500, 2048, device=cuda_device, dtype=dtype)
+    A.halo_unpack(lib, buf, owners, acc, accumulate=True)
+    ref = torch.zeros_like(acc).index_add_(0, owners, buf)
+    tol = 1e-5 if dtype == torch.float32 else 1e-12
+    assert (acc - ref).abs().max().item() < tol * ref.abs().max().item()
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    A.halo_pack(lib, x, torch.tensor([1, 30000], device=cuda_device), status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & N.FC_DEV_BAD_INDEX
