@@ -229,7 +229,8 @@ def test_gpu_fp32_linear_tensor_cores_vs_float64(cuda_device, shape):
     check_device_status(cuda_device)
 
 
-@pytest.mark.parametrize("shape", [(64, 2944, 1000), (8, 64, 4099), (2944, 64, 300), (64, 64, 129), (7, 50, 77)])
+@pytest.mark.parametrize("shape", [(64, 2944, 1000), (8, 64, 4099), (2944, 64, 300), (64, 64, 129), (7, 50, 77),
+                                   (96, 200, 3001), (128, 416, 777)])
 def test_gpu_fp32_dense_layer_shapes_vs_float64(cuda_device, shape):
     """Radial-MLP shapes (edge rows x 64 -> paths*F and back) on the TMA-fed tensor-core GEMM."""
     from flashcart_b200.nn.layers import LinearLayer
