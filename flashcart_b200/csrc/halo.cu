@@ -7,7 +7,7 @@
 // transport the caller owns (NCCL, MPI, an MD engine's own communicator), and written into
 // the ghost rows (unpack, copy). In the backward pass the ghost rows' gradients travel the
 // other way and are added to the owners' rows (unpack, accumulate). Reference semantics:
-// `lammps_forward_exchange` / `lammps_reverse_exchange` (flashcart/utils/lammps.py:67-118)
+// `lammps_forward_exchange` / `lammps_reverse_exchange` (utils/lammps.py:67-118)
 // copy owner rows into ghost rows and add ghost-row gradients into owner rows.
 //
 // One CTA walks whole rows (grid-stride over the index list), its threads the row's
