@@ -112,3 +112,32 @@ def test_rotation_helpers_match_oracle_full_tensors():
     rhs = O.irreps(r @ q.T, 3)
     assert (lhs - rhs).abs().max() < 1e-12
     assert rot.shape == x.shape
+
+
+def test_new_entry_points_reject_bad_arguments(emu_lib):
+    """Validation of fc_linear_dbwd and fc_halo_pack / fc_halo_unpack: status codes map to
+    ValueError with the entry point named, before anything is read or launched."""
+    x = torch.zeros(4, 8, dtype=torch.float64)
+    idx = torch.tensor([0, 1])
+    P, I = ctypes.c_void_p, ctypes.c_int64
+    rc = emu_lib.fc_halo_pack(P(x.data_ptr()), 4, 8, 7, P(idx.data_ptr()), 2, P(x.data_ptr()), None, None)
+    with pytest.raises(ValueError, match="fc_halo_pack: dtype"):
+        N.check(emu_lib, rc, "fc_halo_pack")
+    rc = emu_lib.fc_halo_unpack(P(x.data_ptr()), -1, 8, N.FC_F64, P(idx.data_ptr()), P(x.data_ptr()), 4, 0, None,
+                                None)
+    with pytest.raises(ValueError, match="fc_halo_unpack: negative size"):
+        N.check(emu_lib, rc, "fc_halo_unpack")
+    rc = emu_lib.fc_halo_pack(None, 4, 8, N.FC_F64, P(idx.data_ptr()), 2, P(x.data_ptr()), None, None)
+    with pytest.raises(ValueError, match="null tensor"):
+        N.check(emu_lib, rc, "fc_halo_pack")
+    assert emu_lib.fc_halo_pack(None, 0, 8, N.FC_F64, None, 0, None, None, None) == 0  # nothing to move
+    d = A.linear_desc(1, 1, 2, 2, [1, 1], torch.float64)
+    w = [torch.zeros(2, 2, dtype=torch.float64), torch.zeros(2, 2, dtype=torch.float64)]
+    xl = torch.zeros(3, d.in_dim, dtype=torch.float64)
+    g = torch.zeros(3, d.out_dim, dtype=torch.float64)
+    sc = torch.ones(2, dtype=torch.float64)
+    vws = (ctypes.c_void_p * 2)(w[0].data_ptr(), None)
+    rc = emu_lib.fc_linear_dbwd(ctypes.byref(d), P(g.data_ptr()), P(xl.data_ptr()), A.ptr_array(w), None, vws,
+                                P(sc.data_ptr()), I(3), P(g.data_ptr()), None, None, None, None)
+    with pytest.raises(ValueError, match="null weight tangent for rank 1"):
+        N.check(emu_lib, rc, "fc_linear_dbwd")
