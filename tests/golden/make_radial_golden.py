@@ -9,7 +9,10 @@ without r_min), ``BesselBasis`` and ``PolynomialCutoff`` (``nn/radial.py:8-245``
 float64 on distances that cover the interior, r = 0 (Bessel's removable singularity),
 r = r_min, r = r_max and beyond the cutoff, and records the values and the first
 derivative with respect to the distance (autograd of the summed, seeded-weighted output),
-which the forces depend on.
+which the forces depend on. Also the edge geometry of ``utils/geometry.py:25-77``:
+``get_edge_vectors`` on a two-structure batch (one orthorhombic, one triclinic cell,
+integer image shifts) with the gradients of a seeded weighted sum with respect to the
+positions and the cells, and ``to_voigt6`` of random 3 x 3 tensors.
 
 Output: ``tests/golden/radial_golden.pt``.
 """
@@ -55,6 +58,28 @@ def main(src: str) -> None:
         out[f"{name}/value"] = y.detach()
         out[f"{name}/weights"] = w
         out[f"{name}/grad_r"] = dy
+    gspec = importlib.util.spec_from_file_location("ref_geometry",
+                                                   os.path.join(src, "flashcart", "utils", "geometry.py"))
+    geo = importlib.util.module_from_spec(gspec)
+    gspec.loader.exec_module(geo)
+    pos = torch.rand(10, 3, generator=g, dtype=torch.float64) * 6.0
+    cell = torch.stack([torch.diag(torch.tensor([6.0, 7.0, 8.0])),
+                        torch.tensor([[6.0, 0.0, 0.0], [1.5, 6.5, 0.0], [-0.7, 1.1, 7.2]])])
+    batch = torch.tensor([0] * 5 + [1] * 5)
+    recv = torch.tensor([0, 0, 1, 2, 3, 4, 4, 5, 6, 6, 7, 8, 9, 9])
+    send = torch.tensor([1, 3, 2, 2, 4, 0, 1, 6, 7, 9, 5, 9, 8, 5])
+    edge_index = torch.stack([recv, send])
+    shifts = torch.randint(-1, 2, (recv.numel(), 3), generator=g, dtype=torch.int32)
+    p_leaf, c_leaf = pos.clone().requires_grad_(True), cell.clone().requires_grad_(True)
+    vec = geo.get_edge_vectors(p_leaf, c_leaf, shifts, edge_index, batch, use_shifts=True)
+    wv = torch.randn(vec.shape, generator=g, dtype=torch.float64)
+    dpos, dcell = torch.autograd.grad((vec * wv).sum(), [p_leaf, c_leaf])
+    t = torch.randn(4, 3, 3, generator=g, dtype=torch.float64)
+    out.update({"geom/positions": pos, "geom/cell": cell, "geom/batch": batch, "geom/edge_index": edge_index,
+                "geom/shifts": shifts, "geom/vectors": vec.detach(),
+                "geom/vectors_noshift": geo.get_edge_vectors(pos, cell, shifts, edge_index, batch, use_shifts=False),
+                "geom/weights": wv, "geom/grad_positions": dpos, "geom/grad_cell": dcell,
+                "geom/voigt_in": t, "geom/voigt_out": geo.to_voigt6(t)})
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "radial_golden.pt")
     torch.save(out, path)
     print("wrote", path, len(out), "tensors")

@@ -1,4 +1,5 @@
-"""Radial basis and cutoff against the reference's golden vectors (``nn/radial.py:8-245``).
+"""Radial basis, cutoff and edge geometry against the reference's golden vectors
+(``nn/radial.py:8-245``, ``utils/geometry.py:25-77``).
 
 Values and the first derivative with respect to the distance, float64, on distances that
 include r = 0, r = r_min, r = r_max and beyond the cutoff; tolerance 1e-12 as in the
@@ -51,3 +52,22 @@ def test_radial_functions_match_reference_golden(radial_golden, name):
     ref_g = radial_golden[f"{name}/grad_r"]
     assert torch.isfinite(dy).all(), name
     assert (dy - ref_g).abs().max().item() <= 1e-10 * max(1.0, ref_g.abs().max().item()), name
+
+
+def test_edge_geometry_matches_reference_golden(radial_golden):
+    """get_edge_vectors (two structures, orthorhombic and triclinic cells, image shifts; with
+    and without shifts) with its position and cell gradients, and to_voigt6, against the
+    reference's ``utils/geometry.py:25-77``."""
+    from flashcart_b200.model.flashcart import get_edge_vectors, to_voigt6
+
+    G = {k.split("/", 1)[1]: v for k, v in radial_golden.items() if k.startswith("geom/")}
+    pos = G["positions"].clone().requires_grad_(True)
+    cell = G["cell"].clone().requires_grad_(True)
+    vec = get_edge_vectors(pos, cell, G["shifts"], G["edge_index"], G["batch"], use_shifts=True)
+    assert (vec.detach() - G["vectors"]).abs().max().item() < 1e-12
+    dpos, dcell = torch.autograd.grad((vec * G["weights"]).sum(), [pos, cell])
+    assert (dpos - G["grad_positions"]).abs().max().item() < 1e-12
+    assert (dcell - G["grad_cell"]).abs().max().item() < 1e-12
+    plain = get_edge_vectors(G["positions"], G["cell"], G["shifts"], G["edge_index"], G["batch"], use_shifts=False)
+    assert (plain - G["vectors_noshift"]).abs().max().item() < 1e-12
+    assert torch.equal(to_voigt6(G["voigt_in"]), G["voigt_out"])
