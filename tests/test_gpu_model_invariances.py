@@ -103,3 +103,28 @@ def test_gpu_stress_matches_finite_difference(setup):
     fd = (fd + fd.T) / (2.0 * volume)
     torch.testing.assert_close(_voigt_to_full(out["stress"][0]), fd, atol=1.0e-7, rtol=1.0e-6)
     assert fd.abs().max().item() > 1e-5  # the box is not at a stress-free point
+
+
+def test_gpu_batch_equals_structures_one_by_one(setup, cuda_device):
+    """A batch of the periodic box, a water molecule and a lone atom gives each structure's
+    energy, forces and stress as evaluated alone (reference
+    ``tests/model/test_flashcart.py:107-124``)."""
+    from test_model_parity import _isolated_atom_graph
+
+    model, box, out_box = setup
+    mol = _isolated_atom_graph(torch.float64, cuda_device, with_molecule=True)
+    out_mol = model.predict(mol, compute_forces=True, compute_stress=True)
+    nb = box["positions"].shape[0]
+    batch = {
+        "positions": torch.cat([box["positions"], mol["positions"]]),
+        "cell": torch.cat([box["cell"], mol["cell"]]),
+        "atom_types": torch.cat([box["atom_types"], mol["atom_types"]]),
+        "edge_index": torch.cat([box["edge_index"], mol["edge_index"] + nb], dim=1),
+        "shifts": torch.cat([box["shifts"], mol["shifts"].to(box["shifts"].dtype)]),
+        "batch": torch.cat([box["batch"], mol["batch"] + 1]),
+        "n_atoms": torch.cat([box["n_atoms"], mol["n_atoms"]]),
+        "pbc": box["pbc"],
+    }
+    o = model.predict(batch, compute_forces=True, compute_stress=True)
+    for key in ("energy", "forces", "stress"):
+        assert _close(o[key], torch.cat([out_box[key], out_mol[key]]), 1e-10), key
