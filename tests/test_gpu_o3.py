@@ -451,3 +451,42 @@ def test_gpu_raw_c_abi_halo_pack_and_unpack(cuda_device, dtype):
     A.halo_pack(lib, x, torch.tensor([1, 30000], device=cuda_device), status)
     torch.cuda.synchronize()
     assert int(status.item()) & N.FC_DEV_BAD_INDEX
+
+
+@pytest.mark.parametrize("case", [(3, 3, 3, 8, "conv", False, False), (2, 3, 3, 4, "conv", False, False),
+                                  (0, 3, 3, 4, "conv", False, False), (3, 3, 3, 4, "dense", False, True),
+                                  (2, 2, 2, 4, "dense", True, False), (3, 3, 2, 8, "dense", False, False)])
+def test_gpu_rotation_equivariance(cuda_device, case):
+    """TP(R in1, R in2) = R TP(in1, in2) on the kernels, float64, for convolutions and dense
+    products (symmetric, path-reduced), as the reference's
+    ``tests/o3/test_tensor_product.py:326-349`` checks it (atol 1e-10)."""
+    from flashcart_b200.o3.utils import rotate_irreps
+
+    l1, l2, lo, C, kind, sym, red = case
+    dev, f64 = cuda_device, torch.float64
+    conv = kind == "conv"
+    tp = o3.TensorProduct(l1, l2, lo, C, 1 if conv else C, symmetric_product=sym, reduce_paths=red)
+    g = torch.Generator().manual_seed(3)
+    n, e = 30, 240
+    in1 = torch.randn(n, tp.in1_dim, generator=g, dtype=f64)
+    if conv:
+        idx_i = torch.sort(torch.randint(0, n, (e,), generator=g)).values.to(dev)
+        idx_j = torch.randint(0, n, (e,), generator=g).to(dev)
+        in2 = O.irreps(torch.nn.functional.normalize(torch.randn(e, 3, generator=g, dtype=f64), dim=-1), l2)
+        w = torch.randn(e, tp.n_total_paths * C, generator=g, dtype=f64)
+    else:
+        idx_i = idx_j = None
+        in2 = in1 if sym else torch.randn(n, tp.in2_dim, generator=g, dtype=f64)
+        w = torch.randn(n, tp.n_total_paths * C, generator=g, dtype=f64)
+    q, r = torch.linalg.qr(torch.randn(3, 3, generator=g, dtype=f64))
+    R = q * torch.sign(torch.diagonal(r))
+    in1_r = rotate_irreps(in1, R, l1)
+    in2_r = in1_r if sym else rotate_irreps(in2, R, l2)
+    with torch.no_grad():
+        out = tp(in1.to(dev), in2.to(dev), w.to(dev), idx_i, idx_j).cpu()
+        out_r = tp(in1_r.to(dev), in2_r.to(dev), w.to(dev), idx_i, idx_j).cpu()
+    n_paths = [min(1, p) for p in tp.out_paths] if red else tp.out_paths
+    expect = rotate_irreps(out, R, lo, n_paths=n_paths)
+    assert (out_r - expect).abs().max().item() < 1e-10 * max(1.0, expect.abs().max().item())
+    assert out.abs().max().item() > 1e-3
+    check_device_status(dev)
