@@ -107,7 +107,8 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_linear_fwd.restype = ctypes.c_int
     lib.fc_linear_fwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _I64, _P, _P, _P]
     lib.fc_tp_conv_fwd_noalloc.restype = ctypes.c_int
-    lib.fc_tp_conv_fwd_noalloc.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P]
+    lib.fc_tp_conv_fwd_noalloc.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P,
+                                            _P]
     lib.fc_linear_bwd.restype = ctypes.c_int
     lib.fc_linear_bwd.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P, _P]
     lib.fc_linear_dbwd.restype = ctypes.c_int

@@ -351,12 +351,18 @@ constexpr int64_t kNoAllocMaxNodes = int64_t(1) << 18;  // 262,144 receivers -> 
 #ifndef FC_HOST_EMU
 static __device__ __align__(256) int64_t g_noalloc_rowptr[kNoAllocMaxNodes + 1];
 static std::mutex g_noalloc_mutex;
-static int64_t* g_noalloc_ptr[64] = {};
+constexpr int kNoAllocMaxDevices = 64;
+static int64_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
 
+// The address is looked up once per device and kept for the life of the process; it does
+// not survive cudaDeviceReset (a reset device gets a new module load and a new address).
 static int noalloc_rowptr(int64_t** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+  if (cudaGetDevice(&dev) != cudaSuccess)
     return fail(FC_ERR_LAUNCH, "fc_tp_conv_fwd_noalloc: no current CUDA device");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(FC_ERR_UNSUPPORTED, "fc_tp_conv_fwd_noalloc: device ordinal %d beyond the %d devices it serves", dev,
+                kNoAllocMaxDevices);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   if (g_noalloc_ptr[dev] == nullptr) {
     void* ptr = nullptr;
@@ -765,10 +771,11 @@ int fc_linear_bwd_presplit(const fc_linear_desc* desc, const void* grad_out, con
 
 // Convolution forward for callers that cannot allocate device memory (see the header).
 int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* in2, const void* weights,
-                           const int64_t* idx_i, const int64_t* idx_j, int64_t n_nodes, int64_t n_edges, void* out,
-                           int32_t* status, fc_stream_t stream) {
+                           const int64_t* idx_i, const int64_t* idx_j, int64_t n_nodes, int64_t n_in1_rows,
+                           int64_t n_edges, void* out, int32_t* status, fc_stream_t stream) {
   if (int rc = check_desc(desc)) return rc;
-  if (n_nodes < 0 || n_edges < 0) return fail(FC_ERR_INVALID, "fc_tp_conv_fwd_noalloc: negative size");
+  if (n_nodes < 0 || n_in1_rows < 0 || n_edges < 0)
+    return fail(FC_ERR_INVALID, "fc_tp_conv_fwd_noalloc: negative size");
   if (n_nodes > kNoAllocMaxNodes)
     return fail(FC_ERR_CAPACITY,
                 "fc_tp_conv_fwd_noalloc: %lld receiver nodes exceed the fixed workspace of %lld nodes; use "
@@ -781,7 +788,7 @@ int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* 
   if (int rc = noalloc_rowptr(&rowptr)) return rc;
   // the workspace is fully rewritten by this call, so nothing needs clearing
   if (int rc = fc_build_rowptr(idx_i, n_edges, n_nodes, rowptr, status, stream)) return rc;
-  return fc_tp_fwd(desc, in1, in2, weights, rowptr, idx_j, n_nodes, n_nodes, n_edges, out, status, stream);
+  return fc_tp_fwd(desc, in1, in2, weights, rowptr, idx_j, n_nodes, n_in1_rows, n_edges, out, status, stream);
 }
 
 // ------------------------------------------------------------------ RMS layer norm

@@ -112,18 +112,24 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
  * simulation engine plug-in (an MD code whose own memory manager owns every device
  * byte and hands out only pointers into its buffers), or a time-step loop that may not
  * call cudaMalloc because it can synchronise the device and stall the step.
- * Same result as fc_build_rowptr + fc_tp_fwd (convolution), but the receiver CSR is
- * built into a fixed workspace inside the library's own device memory (2 MiB per
- * device, held until process exit), so at most 262,144 receiver nodes are accepted;
- * larger n_nodes returns FC_ERR_CAPACITY without launching anything. The call itself
- * never allocates or frees. The first call on a device looks the workspace up
- * (cudaGetSymbolAddress) with that device current: make it before any stream capture.
- * All calls share the one workspace: calls that can overlap on the GPU (different
- * streams without ordering) race and must be serialised by the caller. */
+ * Same result as fc_build_rowptr + fc_tp_fwd (convolution) with n_out_rows = n_nodes
+ * and n_in1_rows = n_in1_rows: receivers (idx_i, rows of out) are the first n_nodes
+ * atoms, senders (idx_j, rows of in1) may reach further, e.g. an MD plug-in whose
+ * receivers are its nlocal owned atoms and whose senders include the ghosts
+ * (n_in1_rows = nlocal + nghost). The receiver CSR is built into a fixed workspace
+ * inside the library's own device memory (2 MiB per device, held until process exit),
+ * so at most 262,144 receiver nodes are accepted; larger n_nodes returns
+ * FC_ERR_CAPACITY without launching anything (the sender count is not limited). The
+ * call itself never allocates or frees. The first call on a device looks the workspace
+ * up (cudaGetSymbolAddress) with that device current: make it before any stream
+ * capture. The looked-up address is kept for the life of the process and does not
+ * survive cudaDeviceReset (do not reset a device between calls). All calls share the
+ * one workspace: calls that can overlap on the GPU (different streams without
+ * ordering) race and must be serialised by the caller. */
 int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* in2,
                            const void* weights, const int64_t* idx_i, const int64_t* idx_j,
-                           int64_t n_nodes, int64_t n_edges, void* out, int32_t* status,
-                           fc_stream_t stream);
+                           int64_t n_nodes, int64_t n_in1_rows, int64_t n_edges, void* out,
+                           int32_t* status, fc_stream_t stream);
 
 /* Newton-Schulz orthogonalisation of a batch of Muon updates on the tensor cores (bf16).
  * Replaces _batched_newtonschulz (training/muon.py:27-61). update: (batch, rows, cols),
