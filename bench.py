@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Headline benchmark: FlashCart potential energy + forces + stress at 27,648 atoms.
 
-Workload: a seeded 27,648-atom water-like periodic box (9,216 H2O,
+Workload (the MD-scale inference step): a seeded 27,648-atom water-like periodic box (9,216 H2O,
 24 x 24 x 16 jittered lattice, 74.52 x 74.52 x 49.68 A), r_max 5 A (~1.49 M edges), the
 reference architecture with 128 channels, hidden and edge ranks <= 3, 2 interaction
 layers, correlation 3, random-init weights (torch.manual_seed(0)), float32. One step =
@@ -39,7 +39,7 @@ import torch  # noqa: E402
 
 METRIC = "atom-steps/s (E+F+stress) at 27,648 atoms"
 UNIT = "atom-steps/s"
-WORKLOAD = ("config3: 27,648-atom water box (24x24x16 H2O lattice, r_max 5 A), FlashCart C=128, l<=3, "
+WORKLOAD = ("MD-scale inference: 27,648-atom water box (24x24x16 H2O lattice, r_max 5 A), FlashCart C=128, l<=3, "
             "2 interactions, correlation 3, E+F+stress per step")
 FALLBACK_HBM_GBS = 6650.0
 
@@ -52,7 +52,7 @@ def _args():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-atoms", type=int, choices=sorted(CPU_BOXES), default=192,
-                    help="atoms of the CPU sample (same density as config 3; the per-atom rate is the reported "
+                    help="atoms of the CPU sample (same density as the 27,648-atom box; the per-atom rate is the reported "
                          "figure, the 27,648-atom box itself does not fit host RAM in the reference py path)")
     ap.add_argument("--op-case", choices=["conv", "gemm"], default=None,
                     help="run one small operator case (for ncu captures) instead of the benchmark")
@@ -177,6 +177,16 @@ def _count_own_launches(step, graph) -> int:
         if ev.device_type == torch.autograd.DeviceType.CUDA and own.search(ev.name):
             n += 1
     return n
+
+
+def _replay_difference(eager, replayed) -> float:
+    """Largest relative difference (to each output's largest magnitude, at least 1) between
+    the energy, forces and stress of an eager step and of a graph replay."""
+    worst = 0.0
+    for k in ("energy", "forces", "stress"):
+        a, b = replayed[k].double(), eager[k].double()
+        worst = max(worst, (a - b).abs().max().item() / max(1.0, b.abs().max().item()))
+    return worst
 
 
 def _profile_traffic(kernel: str):
@@ -305,8 +315,17 @@ def run_b200(args):
         dist.barrier()
     graphed = GraphedStep(step, graph, warmup=2)
     for _ in range(3):
-        graphed()
+        replayed = graphed()
     torch.cuda.synchronize()
+    # the timed path must give the eager step's result (same inputs; atomics make float32
+    # agree to rounding, not bit for bit)
+    replay_rel = _replay_difference(out, replayed)
+    if world > 1:  # every rank takes the same decision
+        r = torch.tensor([replay_rel], device=dev, dtype=torch.float64)
+        dist.all_reduce(r, op=dist.ReduceOp.MAX)
+        replay_rel = float(r[0])
+    if replay_rel > 1e-5:
+        raise RuntimeError(f"graph replay differs from the eager step: max relative difference {replay_rel:.3e}")
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -387,6 +406,7 @@ def run_b200(args):
                        "execution": "whole step captured as one CUDA graph and replayed; roofline and "
                                     "kernel breakdown from an eager pass of the same steps",
                        "eager_ms_per_step": eager_max,
+                       "replay_vs_eager_max_rel": replay_rel,
                        "parallelism": (f"atom-domain decomposition {'x'.join(map(str, plan.grid))} of the one cell, "
                                        f"halo exchange over NCCL (all-to-all), x{world}") if plan is not None
                        else "one cell on one GPU"},
@@ -468,7 +488,7 @@ def _roof(nbytes: int, ms: float, peak: float, peak_src: str, traffic=None):
 
 
 def run_config1(args):
-    """TensorProduct(2, 2, 2, 64, 1) convolution, E = 2^20 edges over
+    """Isolated tensor-product microbenchmark: TensorProduct(2, 2, 2, 64, 1) convolution, E = 2^20 edges over
     N = 2^16 nodes (receiver-sorted uniform indices), unit-vector moments scaled by
     N(0,1) radial weights as in2, N(0,1) node features and path weights, forward and
     backward with respect to in1, in2 and the weights; fp32."""
@@ -500,17 +520,17 @@ def run_config1(args):
     peak, src = _peaks()
     ms = fwd_ms + bwd_ms
     print(json.dumps({
-        "metric": "TP convolution (2,2)->2 forward + backward, E=2^20, N=2^16, C=64 (BASELINE config 1)",
+        "metric": "TP convolution (2,2)->2 forward + backward, E=2^20, N=2^16, C=64",
         "value": e / (ms * 1e-3), "unit": "edges/s", "n_gpus": 1, "steps": reps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config1", "edges": e, "nodes": n, "channels": c, "paths": tp.n_total_paths,
+        "config": {"workload": "isolated TP convolution microbenchmark", "edges": e, "nodes": n, "channels": c, "paths": tp.n_total_paths,
                    "l2": "inputs larger than L2 (weights 2.9 GB)"},
         "roofline": {"fwd": _roof(fwd_b, fwd_ms, peak, src), "bwd": _roof(bwd_b, bwd_ms, peak, src)},
     }), flush=True)
 
 
 def run_config2(args):
-    """2,000,000 edge vectors uniform in a 5 A ball; moments T^l(r^),
+    """Edge expansion + equivariant linear map: 2,000,000 edge vectors uniform in a 5 A ball; moments T^l(r^),
     l <= 3, times h = Linear(8 -> 128)(Bessel(8, 5 A)(r) * cutoff_6(r)) laid out as
     (E, 2048), then o3.LinearLayer(3, 3, 128, 128) with Xavier-normal weights and
     weight_scale 1 (3xTF32 tensor-core path); forward, fp32."""
@@ -571,10 +591,10 @@ def run_config2(args):
     ms = exp_ms + lin_ms
     xb = e * 16 * C * 4
     print(json.dumps({
-        "metric": "edge expansion + equivariant linear map 128->128, l<=3, 2,000,000 edges (BASELINE config 2)",
+        "metric": "edge expansion + equivariant linear map 128->128, l<=3, 2,000,000 edges",
         "value": e / (ms * 1e-3), "unit": "edges/s", "n_gpus": 1, "steps": reps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "dtype": "f32 (linear map: 3xTF32 tensor cores)",
-        "data": "synthetic", "config": {"workload": "config2", "edges": e, "channels": C,
+        "data": "synthetic", "config": {"workload": "edge expansion + equivariant linear map", "edges": e, "channels": C,
                                          "expansion": "unfused reference composition (torch) writing (E, 2048)"},
         "roofline": {"expansion": _roof(e * 12 + xb, exp_ms, peak, src), "linear": _roof(2 * xb, lin_ms, peak, src)},
         "fused": {"ms_per_step": fused_ms, "value": e / (fused_ms * 1e-3), "unit": "edges/s",
@@ -585,7 +605,7 @@ def run_config2(args):
 
 
 def run_config4(args):
-    """data-parallel training. Per GPU and step 32 seeded random-walk
+    """Data-parallel training. Per GPU and step 32 seeded random-walk
     molecules (20-60 atoms, H/C/N/O 50/30/10/10, seed 1000 rank + step); labels from a
     random-init teacher (config-0 architecture, elements H/C/N/O, seed 1); the student
     (seed 0) takes the energy-per-atom + force MSE with forces from create_graph=True (the
@@ -642,11 +662,11 @@ def run_config4(args):
     if rank == 0:
         mols_per_s = 32 * world / (ms_max * 1e-3)
         print(json.dumps({
-            "metric": "DP training structures/s (32 molecules of 20-60 atoms per GPU, E+F loss, Muon; BASELINE config 4)",
+            "metric": "DP training structures/s (32 molecules of 20-60 atoms per GPU, E+F loss, Muon)",
             "value": mols_per_s, "unit": "structures/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "dtype": "f32", "data": "synthetic",
             "atom_steps_per_s": atoms / max(args.steps, 1) / (ms_max * 1e-3), "final_loss": float(loss),
-            "config": {"workload": "config4", "molecules_per_gpu": 32, "parallelism": f"dp{world}",
+            "config": {"workload": "data-parallel training", "molecules_per_gpu": 32, "parallelism": f"dp{world}",
                        "model": "config-0 architecture, elements H/C/N/O"},
         }), flush=True)
     if world > 1:

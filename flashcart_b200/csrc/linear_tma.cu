@@ -3,9 +3,11 @@
 // C[(m, node), n] = scale * sum_k A[(m, node), k] * B(k, n) for one rank l. The rows of
 // A and C are the (node, m) rows of the rank block; for a fixed m they form a plain
 // strided matrix, so A and C are described to the TMA unit as 3-D tensors
-// (k | n, node, m) and one tile covers 128 nodes of one m. The weights B are split once
-// per call into tf32 hi / lo parts, stored n-major (k contiguous) in a stream-ordered
-// workspace, and fetched by TMA as well.
+// (k | n, node, m) and one tile covers 128 nodes of one m. The weights B come as tf32
+// hi / lo parts stored n-major (k contiguous): the caller's pre-split copy
+// (fc_linear_fwd/bwd_presplit: the operator layer splits a frozen weight set once and
+// keeps it), or else a split made per call into a stream-ordered workspace. TMA fetches
+// them as well.
 //
 // One persistent CTA per SM (320 threads) walks its share of the output tiles:
 //   warp 0     TMA producer: fp32 A slab (128 x 32) + B hi / lo slabs (BN x 32); optional L2
@@ -17,7 +19,8 @@
 //              MMAs read A from there, otherwise they go back to shared memory
 //   warps 6-9  epilogue: TMEM -> registers -> scale -> swizzled staging -> TMA store
 // Operand stages cycle through full (TMA landed) -> split (hi / lo ready) -> empty (MMAs
-// done, tcgen05.commit) mbarriers. The k range of a tile is cut into units of 64; each
+// done, tcgen05.commit) mbarriers. The k range of a tile is cut into units of 128 (KG
+// slabs of 32); each
 // unit accumulates into the next of a ring of TMEM accumulators (acc_full / acc_empty)
 // and the epilogue adds the units in fp32 registers, so the epilogue of one unit
 // overlaps the MMAs of the next. Every wait is bounded: on expiry

@@ -1,4 +1,5 @@
-"""Architectures of the benchmark configurations (BASELINE configs 0 and 3).
+"""Architectures of the benchmark workloads: the 192-atom CPU reference run ("cfg0": 64 channels,
+ranks <= 2) and the MD-scale inference step ("cfg3arch": 128 channels, ranks <= 3).
 
 Flags of the reference's ``configs/default.yaml`` (layer norm, sigmoid gates, cosine
 Chebyshev mapping, path-resolved products), fixed shifts, ``avg_neighbors`` set to

@@ -5,7 +5,8 @@ Run where the reference source is available (never needed at test time)::
     python tests/golden/make_model_golden.py <reference>/src
 
 Cases (architecture flags of the reference's default.yaml, avg_neighbors = measured
-mean degree; the BASELINE configs 0 and 3 architectures):
+mean degree; the architectures of the 192-atom CPU reference run and of the MD-scale
+inference step):
 
 * ``cfg0``: elements [H, O], r_max 5, 64 channels, hidden l<=2, edge l<=2, 8 radial
   functions, 2 interactions, correlation 3, layer norm, sigmoid gates, cosine
