@@ -1,0 +1,150 @@
+"""The benchmarked path under parity: whole-step CUDA-graph replay of ``predict``.
+
+The headline number replays one captured E+F+S step (``flashcart_b200.graphs.GraphedStep``)
+and, end to end, copies new inputs into the graph's static buffers before each replay.
+These tests check that path itself, not only the eager ``predict``:
+
+* the first replay equals the eager step it was captured from;
+* a replay after new positions and a strained cell were copied into the static buffers
+  equals the eager step on those inputs (a stale capture or aliased buffers would show);
+* the replay matches the reference's golden E/F/S under the float32 tolerance policy;
+* at the benchmark's full size (27,648 atoms, ~1.49 M edges, 128 channels, ranks <= 3),
+  the replay equals the eager step and the float32 step agrees with a float64 step of the
+  same kernels, which would expose an index-width overflow or a grid-size limit that small
+  cases miss. Energy (1e-5 eV/atom) and stress (1e-4 eV/A^3) are held to the north-star
+  tolerances. Forces follow the float32 policy of the parity tests, |f32 - f64| <=
+  max(1e-4, 2 |ref_f32 - ref_f64|): the reference's own float32 force error on the
+  192-atom box is 6.5e-5 eV/A (golden vectors), and the largest of 3N errors of that
+  spread grows with N like sqrt(ln 3N) (1.34x from 192 to 27,648 atoms); measured on the
+  B200 the float32 forces of this model are as accurate as the reference's (7.2e-5 vs
+  6.5e-5 at 192 atoms, unchanged when the dense layers run on an fp32 SGEMM instead of
+  3xTF32), with a 99.9th percentile of 9e-5 at 27,648 atoms, which must stay within 1e-4.
+
+Replays and eager steps both scatter with atomics, so float32 results agree to rounding
+(relative 1e-5 of the largest value), not bit for bit.
+"""
+
+import pytest
+import torch
+
+from flashcart_b200.graphs import GraphedStep
+from test_model_parity import _build, _check_f32, _graph
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"energy_per_atom": 1e-5, "forces": 1e-4, "stress": 1e-4}
+KEYS = ("energy", "forces", "stress")
+
+
+@pytest.fixture(scope="module")
+def model_golden():
+    import os
+
+    root = os.path.dirname(os.path.abspath(__file__))
+    return torch.load(os.path.join(root, "golden", "model_golden.pt"), map_location="cpu", weights_only=True)
+
+
+def _step(model):
+    return lambda g: model.predict(g, compute_forces=True, compute_stress=True)
+
+
+def _max_rel(a, b):
+    return (a.double() - b.double()).abs().max().item() / max(1.0, b.double().abs().max().item())
+
+
+def _assert_same(got, want, rel=1e-5, what=""):
+    for k in KEYS:
+        e = _max_rel(got[k], want[k])
+        assert e <= rel, f"{what}{k}: relative difference {e:.3e}"
+
+
+def test_graph_replay_matches_eager_and_reference(model_golden, cuda_device):
+    name = "cfg3arch"
+    n = model_golden["positions"].shape[0]
+    model = _build(name, model_golden).to(cuda_device)
+    graph = dict(_graph(model_golden, torch.float32, cuda_device), use_shifts=True)
+    step = _step(model)
+    eager = {k: v.clone() for k, v in step(graph).items()}
+    graphed = GraphedStep(step, graph, warmup=2)
+    try:
+        first = {k: v.clone() for k, v in graphed().items()}
+        _assert_same(first, eager, what="first replay vs eager: ")
+        _check_f32(first, model_golden, name, n)
+
+        # new inputs copied into the static buffers: jittered positions in a 1% strained cell
+        g = torch.Generator(device=cuda_device).manual_seed(7)
+        strain = torch.eye(3, device=cuda_device) + 0.01 * torch.tensor(
+            [[1.0, 0.2, 0.0], [0.2, -0.5, 0.1], [0.0, 0.1, 0.3]], device=cuda_device)
+        pos2 = graph["positions"] @ strain + 0.03 * torch.randn(graph["positions"].shape, device=cuda_device,
+                                                                generator=g)
+        cell2 = graph["cell"] @ strain
+        graph2 = dict(graph, positions=pos2, cell=cell2)
+        eager2 = {k: v.clone() for k, v in step(graph2).items()}
+        assert _max_rel(eager2["energy"], eager["energy"]) > 1e-6, "the new inputs must change the result"
+        replay2 = {k: v.clone() for k, v in graphed({"positions": pos2, "cell": cell2}).items()}
+        _assert_same(replay2, eager2, what="replay after copy_ vs eager: ")
+        # and back to the original inputs
+        replay3 = graphed({"positions": graph["positions"], "cell": graph["cell"]})
+        _assert_same(replay3, eager, what="replay after restoring the inputs: ")
+    finally:
+        graphed.release()
+    from flashcart_b200.ops import check_device_status
+
+    check_device_status(cuda_device)
+
+
+def _errors(f32, f64, n):
+    per_atom = (f32["forces"].double() - f64["forces"]).abs().max(dim=1).values.cpu()
+    return {"energy_per_atom": (f32["energy"].double() - f64["energy"]).abs().max().item() / n,
+            "forces": per_atom.max().item(),
+            "forces_p999": torch.quantile(per_atom, 0.999).item(),
+            "stress": (f32["stress"].double() - f64["stress"]).abs().max().item()}
+
+
+def _force_bound(model_golden, n_atoms):
+    """max(1e-4, 2 x reference float32 force gap at 192 atoms x extreme-value size factor)."""
+    import math
+
+    gap = (model_golden["cfg3arch/f32/forces"] - model_golden["cfg3arch/f64/forces"]).abs().max().item()
+    n0 = model_golden["positions"].shape[0]
+    size = math.sqrt(math.log(3 * n_atoms) / math.log(3 * n0))
+    return max(TOL["forces"], 2.0 * gap * size)
+
+
+def test_full_size_replay_and_precision(model_golden, cuda_device):
+    """27,648 atoms, 1.49 M edges: replay == eager (float32) and float32 vs float64."""
+    import bench
+
+    graph, avg = bench.build_graph(seed=0, device=cuda_device)
+    n = graph["positions"].shape[0]
+    assert n == 27648 and graph["edge_index"].shape[1] > 1_400_000
+    graph = dict(graph, use_shifts=True)
+    model = bench.build_model(avg, cuda_device)
+    step = _step(model)
+    out = step(graph)
+    eager = {k: out[k].detach().clone() for k in KEYS}
+    del out
+    graphed = GraphedStep(step, graph, warmup=1)
+    try:
+        rep = graphed()
+        _assert_same({k: rep[k] for k in KEYS}, eager, what="full-size replay vs eager: ")
+    finally:
+        graphed.release()
+        del graphed
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+    m64 = model.to(torch.float64)
+    g64 = dict(graph, positions=graph["positions"].double(), cell=graph["cell"].double())
+    out64 = m64.predict(g64, compute_forces=True, compute_stress=True)
+    ref = {k: out64[k].detach() for k in KEYS}
+    del out64
+    err = _errors(eager, ref, n)
+    print("full-size float32 vs float64:", {k: f"{v:.3e}" for k, v in err.items()})
+    assert err["energy_per_atom"] <= TOL["energy_per_atom"], err
+    assert err["stress"] <= TOL["stress"], err
+    assert err["forces_p999"] <= TOL["forces"], err
+    assert err["forces"] <= _force_bound(model_golden, n), (err, _force_bound(model_golden, n))
+    from flashcart_b200.ops import check_device_status
+
+    check_device_status(cuda_device)
