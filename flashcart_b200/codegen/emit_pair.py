@@ -1,0 +1,496 @@
+"""Channel-pair convolution kernels (float32) for edge attributes shared by all channels.
+
+Emitted into each signature file next to :mod:`flashcart_b200.codegen.emit_conv` and
+used for the same case (the interaction layer's receiver-CSR convolution:
+``in2_features == 1``, ``in1_features == F``, per-edge weights, paths not reduced) when
+the data are float32 and F is 64 or 128 (F/2 consumer threads: one or two warps).
+
+Why pairs. The per-edge arithmetic of one channel is a few hundred FP32 multiply-adds;
+the kernels are bound by instruction issue, not by HBM, and a large share of the issued
+instructions is per-edge overhead that does not depend on the channel (edge-matrix
+loads, barrier waits, index and address work, the reduction of the in2 gradient over
+the channels). Each consumer thread therefore owns two adjacent channels ``2t, 2t+1``:
+
+* the arithmetic of both channels runs as packed ``f32x2`` multiply-adds (one issue slot
+  for two FP32 FMAs, ``__ffma2_rn``), so the FMA pipes, not the issue slot, set the pace;
+* loads and stores of both channels are 8-byte vectors (``float2``), the in1-gradient
+  scatter is one ``red.global.add.v2.f32`` per component;
+* the channel-independent per-edge work (edge-matrix reads, the wait on the prefetch
+  slot, the sender index, the warp reduction of the in2 gradient) is shared by the two.
+
+CTA = one receiver row. ``F/2`` consumer threads plus one producer warp:
+
+* the producer warp reads the receiver's sender indices 32 at a time (one coalesced
+  load), and for each edge waits until its ring slot is free, writes the sender index
+  into the slot header and issues 1-D bulk async copies (``cp.async.bulk``, global ->
+  this CTA's shared memory, no multicast) of the sender's in1 components of the path
+  group and of the edge's path weights; the copies complete on the slot's mbarrier. It
+  never waits for the consumers' arithmetic, only for slot releases, so the gathers run
+  up to RING edges ahead;
+* the consumers walk the edges in chunks of EC: the edge matrices
+  ``M_p[a, i] = sum_j K_p[a, i, j] x2_j`` of the chunk are computed cooperatively into
+  shared memory (stored as duplicated pairs so that one 16-byte load gives two packed
+  operands), then per edge every consumer thread waits for the slot, reads the sender
+  index from the slot header and does the path-group arithmetic for its two channels.
+  Consumers synchronise among themselves with a named barrier; the producer is never
+  part of a CTA-wide barrier after the roles split.
+
+Every wait is bounded (FC_DEV_TIMEOUT and a CTA abort flag on expiry); an aborted CTA's
+producer waits for its in-flight copies before it exits. Data errors (sender index out
+of range) are flagged in the status word and the edge is skipped.
+"""
+
+from __future__ import annotations
+
+from fractions import Fraction
+from typing import List, Sequence, Tuple
+
+from flashcart_b200.codegen import stf
+from flashcart_b200.codegen.emit_conv import GroupSlots, make_groups, _q
+
+NPART = 8     # edge-matrix work split per edge (EC x NPART work items per chunk)
+BUDGET = 32   # accumulator pairs per path group when a signature is split
+# Per path group: large groups (more than SMALL_NACC accumulator pairs) are limited by how
+# many CTAs fit an SM, so they take a small footprint -- chunks of 8 edges, 4 ring slots,
+# the backward's output-gradient pairs in shared memory (each thread reads back only its
+# own values) and a register cap (P3MinBlocks); small groups keep 16-edge chunks, 6 slots
+# and their gradients in registers. Measured on the (3,3)->3 and (0,3)->3 convolutions at
+# C = 128, 1.49 M edges: (3,3)->3 backward 21.8 -> 14.0 ms with the small footprint, while
+# (0,3)->3 is fastest with the large one (1.38 vs 1.93 ms).
+SMALL_NACC = 16
+G_SMEM = None  # None: per group as above; True / False force it (experiments)
+EC = None
+RING = None
+
+
+def group_cfg(gs) -> dict:
+    big = gs.nacc > SMALL_NACC
+    return {"big": big,
+            "ec": EC if EC is not None else (8 if big else 16),
+            "ring": RING if RING is not None else (4 if big else 6),
+            "gsmem": G_SMEM if G_SMEM is not None else big}
+
+
+def _cf(fr: Fraction) -> str:
+    return f"p2({float(fr)!r}f)"
+
+
+def _lin_pairs(terms: Sequence[Tuple[Fraction, str]]) -> str:
+    """Packed linear combination sum c_k * v_k of float2 operands (constant coefficients)."""
+    terms = [(c, v) for c, v in terms if c != 0]
+    if not terms:
+        return "p2(0.0f)"
+    c0, v0 = terms[0]
+    if c0 == 1:
+        e = v0
+    else:
+        e = f"pmul({_cf(c0)}, {v0})"
+    for c, v in terms[1:]:
+        if c == 1:
+            e = f"padd({e}, {v})"
+        else:
+            e = f"pfma({_cf(c)}, {v}, {e})"
+    return e
+
+
+def _chain(pairs: Sequence[Tuple[str, str]], init: str = "") -> str:
+    """sum a_k * b_k (+ init) of float2 operands as one fma chain."""
+    e = init
+    for a, b in pairs:
+        e = f"pmul({a}, {b})" if not e else f"pfma({a}, {b}, {e})"
+    return e or "p2(0.0f)"
+
+
+def _phase1(gs: GroupSlots, ind: str) -> List[str]:
+    L = [f"{ind}switch (part) {{"]
+    per = (gs.nm + NPART - 1) // NPART
+    for part in range(NPART):
+        L.append(f"{ind}  case {part}:")
+        for s in range(part * per, min(gs.nm, (part + 1) * per)):
+            if gs.slots[s] is not None:
+                L.append(f"{ind}    {{ const T v = {gs.m_expr(s)}; m[{s}] = make_float2(v, v); }}")
+        L.append(f"{ind}    break;")
+    L.append(f"{ind}}}")
+    return L
+
+
+def _path_mload(gs: GroupSlots, p: int, ind: str) -> List[str]:
+    """Edge-matrix entries of one path: 16-byte shared loads of two duplicated pairs each."""
+    s0, s1 = gs.range[p]
+    n = s1 - s0
+    n2 = max(1, (n + 1) // 2)
+    L = [f"{ind}float2 mv[{2 * n2}];"]
+    for k in range(n2):
+        L.append(f"{ind}ld2x2(m + {s0 + 2 * k}, mv + {2 * k});")
+    return L
+
+
+def _fwd_body(gs: GroupSlots, ind: str) -> List[str]:
+    sig = gs.sig
+    L = []
+    acc_base = 0
+    for p in gs.paths:
+        r1, r2, o = sig.paths[p]
+        s0 = gs.range[p][0]
+        L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
+        L.extend(_path_mload(gs, p, ind + "  "))
+        L.append(f"{ind}  const float2 wp = ld2(sw + {gs.w_pos[p]} * F);")
+        for a in range(2 * o + 1):
+            pairs = [(f"mv[{gs.index[(p, a, i)] - s0}]", f"x1[{_q(r1, i) - gs.x_lo}]") for i in range(2 * r1 + 1)
+                     if (p, a, i) in gs.index]
+            t = _chain(pairs)
+            L.append(f"{ind}  acc[{acc_base + a}] = pfma(wp, {t}, acc[{acc_base + a}]);")
+        L.append(f"{ind}}}")
+        acc_base += 2 * o + 1
+    return L
+
+
+def _bwd_body(gs: GroupSlots, ind: str, d2p: int) -> List[str]:
+    """Backward of one edge for the thread's channel pair; the first contribution to a
+    gradient register assigns it."""
+    sig = gs.sig
+    L = []
+    base = 0
+    set1, set2 = set(), set()
+
+    def acc(name: str, k: int, a: str, b: str, seen: set) -> str:
+        if k in seen:
+            return f"{name}[{k}] = pfma({a}, {b}, {name}[{k}]);"
+        seen.add(k)
+        return f"{name}[{k}] = pmul({a}, {b});"
+
+    for p in gs.paths:
+        r1, r2, o = sig.paths[p]
+        K = stf.oriented_path_tensor(r1, r2, o)
+        s0 = gs.range[p][0]
+        L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
+        L.extend(_path_mload(gs, p, ind + "  "))
+        L.append(f"{ind}  const float2 wp = ld2(sw + {gs.w_pos[p]} * F);")
+        if gs.gsmem:
+            for a in range(2 * o + 1):
+                L.append(f"{ind}  const float2 ga{base + a} = gb[{base + a} * NC + t];")
+        gname = (lambda k: f"ga{k}") if gs.gsmem else (lambda k: f"g[{k}]")
+        hs = []
+        for i in range(2 * r1 + 1):
+            pairs = [(gname(base + a), f"mv[{gs.index[(p, a, i)] - s0}]") for a in range(2 * o + 1)
+                     if (p, a, i) in gs.index]
+            if pairs:
+                L.append(f"{ind}  const float2 h{i} = {_chain(pairs)};")
+                hs.append(i)
+        gw = _chain([(f"x1[{_q(r1, i) - gs.x_lo}]", f"h{i}") for i in hs])
+        L.append(f"{ind}  if (NEED_W) st2(gwr + {p} * F, {gw});")
+        if hs:
+            L.append(f"{ind}  if (NEED_1) {{")
+            for i in hs:
+                L.append(f"{ind}    " + acc("gx1", _q(r1, i) - gs.x_lo, "wp", f"h{i}", set1))
+            L.append(f"{ind}  }}")
+        body2 = []
+        for j in range(2 * r2 + 1):
+            pairs = []
+            for a in range(2 * o + 1):
+                n = _lin_pairs([(K[a][i][j], f"x1[{_q(r1, i) - gs.x_lo}]") for i in range(2 * r1 + 1)])
+                if n != "p2(0.0f)":
+                    pairs.append((gname(base + a), n))
+            if pairs:
+                body2.append(f"{ind}    " + acc("gx2", _q(r2, j), "wp", _chain(pairs), set2))
+        if body2:
+            L.append(f"{ind}  if (NEED_2) {{")
+            L.extend(body2)
+            L.append(f"{ind}  }}")
+        L.append(f"{ind}}}")
+        base += 2 * o + 1
+    for q in range(gs.x_n):
+        if q not in set1:
+            L.append(f"{ind}gx1[{q}] = p2(0.0f);")
+    for q in range(d2p):
+        if q not in set2:
+            L.append(f"{ind}gx2[{q}] = p2(0.0f);")
+    return L
+
+
+def _setup(gs: GroupSlots, extra_floats: str, ind: str) -> List[str]:
+    """Shared-memory carve-up: M pairs | ring slots | [extra] | slot headers | mbarriers."""
+    return [
+        f"{ind}using T = float;",
+        f"{ind}constexpr int XLO = {gs.x_lo}, XN = {gs.x_n}, NW = {len(gs.paths)}, NMP = {gs.nmp};",
+        f"{ind}const int F = P.F, NC = F >> 1, t = threadIdx.x, lane = t & 31;",
+        f"{ind}const int64_t row = blockIdx.x;",
+        f"{ind}float2* m2 = reinterpret_cast<float2*>(smem);",
+        f"{ind}float* ring = reinterpret_cast<float*>(m2 + NMP * {gs.ec});",
+        f"{ind}const int SLOT = (XN + NW) * F;",
+        f"{ind}float* extra = ring + {gs.ring} * SLOT;",
+        f"{ind}int64_t* sj = reinterpret_cast<int64_t*>(extra + {extra_floats});",
+        f"{ind}uint64_t* full = reinterpret_cast<uint64_t*>(sj + {gs.ring});",
+        f"{ind}uint64_t* empty = full + {gs.ring};",
+        f"{ind}volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + {gs.ring});",
+        f"{ind}const int64_t e0 = P.rowptr[row], ne_all = P.rowptr[row + 1] - e0;",
+        f"{ind}if (t == 0) {{",
+        f"{ind}  for (int s = 0; s < {gs.ring}; ++s) {{ fc_mbar_init(&full[s], 1); fc_mbar_init(&empty[s], NC >> 5); }}",
+        f"{ind}  *abort_flag = 0;",
+        f"{ind}  fc_mbar_init_fence();",
+        f"{ind}}}",
+        f"{ind}__syncthreads();",
+    ]
+
+
+def _producer(gs: GroupSlots, ind: str) -> List[str]:
+    """The producer warp: sender indices 32 at a time, then per edge wait for the slot,
+    header + bulk copies; at the end, an aborted CTA waits for its copies in flight."""
+    L = [f"{ind}if (t >= NC) {{",
+         f"{ind}  const int pl = t - NC;",
+         f"{ind}  int64_t issued = 0;",
+         f"{ind}  for (int64_t base = 0; base < ne_all; base += 32) {{",
+         f"{ind}    const int64_t jv = base + pl < ne_all ? P.idx_j[e0 + base + pl] : 0;",
+         f"{ind}    const int nb = (int)min((int64_t)32, ne_all - base);",
+         f"{ind}    for (int k = 0; k < nb; ++k) {{",
+         f"{ind}      const int64_t j = __shfl_sync(0xffffffffu, jv, k);",
+         f"{ind}      if (pl == 0 && !*abort_flag) {{",
+         f"{ind}        const int64_t kk = base + k;",
+         f"{ind}        const int s = (int)(kk % {gs.ring});",
+         f"{ind}        if (kk < {gs.ring} || fc_mbar_wait(&empty[s], (uint32_t)((kk / {gs.ring} - 1) & 1), abort_flag, P.status)) {{",
+         f"{ind}          const bool ok = (uint64_t)j < (uint64_t)P.n_in1;",
+         f"{ind}          if (!ok) fc_flag(P.status, FC_DEV_BAD_INDEX);",
+         f"{ind}          sj[s] = ok ? j : -1;",
+         f"{ind}          float* dst = ring + s * SLOT;",
+         f"{ind}          fc_mbar_arrive_tx(&full[s], (uint32_t)(((ok ? XN : 0) + NW) * F * 4));",
+         f"{ind}          if (ok) fc_bulk_g2s(dst, P.in1 + j * (int64_t)(D1 * F) + XLO * F, (uint32_t)(XN * F * 4), &full[s]);",
+         f"{ind}          const float* wrow = P.w + (e0 + kk) * (int64_t)(NP * F);"]
+    for (p0, n, r) in gs.w_runs:
+        L.append(f"{ind}          fc_bulk_g2s(dst + (XN + {r}) * F, wrow + {p0} * F, (uint32_t)({n} * F * 4), &full[s]);")
+    L += [f"{ind}          issued = kk + 1;",
+          f"{ind}        }}",
+          f"{ind}      }}",
+          f"{ind}      __syncwarp();",
+          f"{ind}    }}",
+          f"{ind}  }}",
+          f"{ind}  if (pl == 0 && *abort_flag) {{",
+          f"{ind}    for (int64_t kk = issued > {gs.ring} ? issued - {gs.ring} : 0; kk < issued; ++kk)",
+          f"{ind}      for (long long it = 0; it < FC_RING_WAIT_LIMIT; ++it)",
+          f"{ind}        if (fc_mbar_test(&full[kk % {gs.ring}], (uint32_t)((kk / {gs.ring}) & 1))) break;",
+          f"{ind}  }}",
+          f"{ind}  return;",
+          f"{ind}}}"]
+    return L
+
+
+def _phase1_loop(gs: GroupSlots, ind: str) -> List[str]:
+    return [f"{ind}for (int u = t; u < {gs.ec * NPART}; u += NC) {{",
+            f"{ind}  const int le = u % {gs.ec}, part = u / {gs.ec};",
+            f"{ind}  if (le < ne) {{",
+            f"{ind}    T x2[D2];",
+            f"{ind}    const T* __restrict__ a2 = P.in2 + (e0 + eb + le) * (int64_t)D2;",
+            f"{ind}    for (int q = 0; q < D2; ++q) x2[q] = fc_ldg(a2 + q);",
+            f"{ind}    float2* m = m2 + le * NMP;",
+            *_phase1(gs, ind + "    "),
+            f"{ind}  }}",
+            f"{ind}}}",
+            f"{ind}fc_named_sync(1, NC);"]
+
+
+def _edge_begin(gs: GroupSlots, ind: str) -> List[str]:
+    return [f"{ind}const int64_t kk = eb + k;",
+            f"{ind}const int s = (int)(kk % {gs.ring});",
+            f"{ind}const bool landed = fc_mbar_wait(&full[s], (uint32_t)((kk / {gs.ring}) & 1), abort_flag, P.status);",
+            f"{ind}const int64_t j = landed ? sj[s] : -1;"]
+
+
+def _edge_end(ind: str) -> List[str]:
+    return [f"{ind}__syncwarp();",
+            f"{ind}if (lane == 0) fc_mbar_arrive(&empty[s]);"]
+
+
+def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
+    groups = [GroupSlots(sig, g) for g in make_groups(sig, BUDGET)]
+    for gs in groups:
+        for k, v in group_cfg(gs).items():
+            setattr(gs, k, v)
+    d2p = 1
+    while d2p < sig.d2:
+        d2p *= 2
+    acc_out = {}
+    k = 0
+    for p, (r1, r2, o) in enumerate(sig.paths):
+        for a in range(2 * o + 1):
+            acc_out[(p, a)] = store_offsets[k][0]
+            k += 1
+    L = []
+    w = L.append
+    w(f"// ---- channel-pair convolution (float32): {len(groups)} path groups, producer warp")
+    w(f"constexpr int P3_GROUPS = {len(groups)};")
+    for kind in ("fwd", "bwd"):
+        w(f"inline size_t {kind}3_smem(int g, int F) {{")
+        w("  switch (g) {")
+        for gi, gs in enumerate(groups):
+            extra = gs.ec * d2p if kind == "bwd" else 0
+            gextra = f" + {gs.nacc} * F" if (kind == "bwd" and gs.gsmem) else ""
+            w(f"    case {gi}: return (size_t){gs.nmp * gs.ec} * 8 + (size_t)({gs.ring} * ({gs.x_n} + {len(gs.paths)}) * F"
+              f" + {extra}{gextra}) * 4 + {gs.ring * 8 + 2 * gs.ring * 8 + 16};")
+        w("  }")
+        w("  return 0;")
+        w("}")
+    # ---------------- forward
+    for gi, gs in enumerate(groups):
+        w(f"__device__ __forceinline__ void fwd3_g{gi}(const TpParams<float>& P, unsigned char* smem) {{")
+        L.extend(_setup(gs, "0", "  "))
+        L.extend(_producer(gs, "  "))
+        w(f"  float2 acc[{gs.nacc}];")
+        w(f"  for (int q = 0; q < {gs.nacc}; ++q) acc[q] = p2(0.0f);")
+        w(f"  for (int64_t eb = 0; eb < ne_all; eb += {gs.ec}) {{")
+        w(f"    const int ne = (int)min((int64_t){gs.ec}, ne_all - eb);")
+        L.extend(_phase1_loop(gs, "    "))
+        w("    for (int k = 0; k < ne; ++k) {")
+        L.extend(_edge_begin(gs, "      "))
+        w("      if (j >= 0) {")
+        w("        const float* sx = ring + s * SLOT + 2 * t;")
+        w("        float2 x1[XN];")
+        w("        for (int q = 0; q < XN; ++q) x1[q] = ld2(sx + q * F);")
+        w("        const float* sw = sx + XN * F;")
+        w("        const float2* m = m2 + k * NMP;")
+        L.extend(_fwd_body(gs, "        "))
+        w("      }")
+        L.extend(_edge_end("      "))
+        w("    }")
+        w("    fc_named_sync(1, NC);")
+        w("  }")
+        w("  float* __restrict__ o = P.out + row * (int64_t)(OUT_COMPS * F) + 2 * t;")
+        k = 0
+        for p in gs.paths:
+            o_ = sig.paths[p][2]
+            for a in range(2 * o_ + 1):
+                w(f"  st2(o + {acc_out[(p, a)]} * F, acc[{k}]);")
+                k += 1
+        w("}")
+    w("template <int G> struct P3Big;")
+    for gi, gs in enumerate(groups):
+        w(f"template <> struct P3Big<{gi}> {{ static constexpr bool value = {'true' if gs.big else 'false'}; }};")
+    w("template <int G, int NT>")
+    w("__global__ void __launch_bounds__(NT, P3MinBlocks<NT, P3Big<G>::value>::fwd) fwd3_kernel(TpParams<float> P) {")
+    w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
+    for gi in range(len(groups)):
+        w(f"  if constexpr (G == {gi}) fwd3_g{gi}(P, fc_smem_raw);")
+    w("}")
+    # ---------------- backward
+    for gi, gs in enumerate(groups):
+        w("template <int NM>")
+        w(f"__device__ __forceinline__ void bwd3_g{gi}(const TpBwdParams<float>& P, unsigned char* smem, bool multi) {{")
+        w("  // NM: requested gradients as a compile-time mask (1 in1, 2 in2, 4 weights), 0 = read the pointers")
+        w("  const bool NEED_1 = NM ? (NM & 1) != 0 : P.g_in1 != nullptr;")
+        w("  const bool NEED_2 = NM ? (NM & 2) != 0 : P.g_in2 != nullptr;")
+        w("  const bool NEED_W = NM ? (NM & 4) != 0 : P.g_w != nullptr;")
+        L.extend(_setup(gs, f"{gs.ec * d2p}" + (f" + {gs.nacc} * F" if gs.gsmem else ""), "  "))
+        L.extend(_producer(gs, "  "))
+        w("  float* gsm = extra;  // [EC][D2P] grad_in2 partial sums")
+        if gs.gsmem:
+            w(f"  float2* gb = reinterpret_cast<float2*>(gsm + {gs.ec * d2p});  // [NACC][NC] this thread's g pairs")
+        else:
+            w(f"  float2 g[{gs.nacc}];")
+        w("  {")
+        w("    const float* __restrict__ go = P.g_out + row * (int64_t)(OUT_COMPS * F) + 2 * t;")
+        k = 0
+        for p in gs.paths:
+            o_ = sig.paths[p][2]
+            for a in range(2 * o_ + 1):
+                if gs.gsmem:
+                    w(f"    gb[{k} * NC + t] = ldg2(go + {acc_out[(p, a)]} * F);")
+                else:
+                    w(f"    g[{k}] = ldg2(go + {acc_out[(p, a)]} * F);")
+                k += 1
+        w("  }")
+        w(f"  for (int64_t eb = 0; eb < ne_all; eb += {gs.ec}) {{")
+        w(f"    const int ne = (int)min((int64_t){gs.ec}, ne_all - eb);")
+        w(f"    for (int u = t; u < {gs.ec * d2p}; u += NC) gsm[u] = 0.0f;")
+        L.extend(_phase1_loop(gs, "    "))
+        w("    for (int k = 0; k < ne; ++k) {")
+        L.extend(_edge_begin(gs, "      "))
+        w("      if (j >= 0) {")
+        w("        const int64_t e = e0 + kk;")
+        w("        const float* sx = ring + s * SLOT + 2 * t;")
+        w("        float2 x1[XN], gx1[XN];")
+        w(f"        float2 gx2[{d2p}];")
+        w("        for (int q = 0; q < XN; ++q) x1[q] = ld2(sx + q * F);")
+        w("        const float* sw = sx + XN * F;")
+        w("        float* __restrict__ gwr = NEED_W ? P.g_w + e * (int64_t)(NP * F) + 2 * t : nullptr;")
+        w("        const float2* m = m2 + k * NMP;")
+        L.extend(_bwd_body(gs, "        ", d2p))
+        w("        if (NEED_1) {")
+        w("          float* __restrict__ t1 = P.g_in1 + j * (int64_t)(D1 * F) + XLO * F + 2 * t;")
+        w("          for (int q = 0; q < XN; ++q) red2(t1 + q * F, gx1[q]);")
+        w("        }")
+        w("        if (NEED_2) {")
+        w(f"          float v[{d2p}];")
+        w(f"          for (int q = 0; q < {d2p}; ++q) v[q] = gx2[q].x + gx2[q].y;")
+        w(f"          const int comp = fc_warp_transpose_reduce<float, {d2p}>(v);")
+        w(f"          if ((lane & {32 // d2p - 1}) == 0 && comp < D2) atomicAdd(gsm + k * {d2p} + comp, v[0]);")
+        w("        }")
+        w("      }")
+        L.extend(_edge_end("      "))
+        w("    }")
+        w("    fc_named_sync(1, NC);")
+        w("    if (NEED_2) {")
+        w("      for (int u = t; u < ne * D2; u += NC) {")
+        w("        const int k = u / D2, q = u % D2;")
+        w("        float* dst = P.g_in2 + (e0 + eb + k) * (int64_t)D2 + q;")
+        w(f"        const float v = gsm[k * {d2p} + q];")
+        w("        if (multi) atomicAdd(dst, v); else *dst = v;")
+        w("      }")
+        w("    }")
+        w("    fc_named_sync(1, NC);")
+        w("  }")
+        w("}")
+    w("template <int G, int NM, int NT>")
+    w("__global__ void __launch_bounds__(NT, P3MinBlocks<NT, P3Big<G>::value>::bwd) bwd3_kernel(TpBwdParams<float> P) {")
+    w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
+    for gi in range(len(groups)):
+        w(f"  if constexpr (G == {gi}) bwd3_g{gi}<NM>(P, fc_smem_raw, P3_GROUPS > 1);")
+    w("}")
+    # ---------------- launchers
+    w("template <int G, int NT>")
+    w("int launch_fwd3_nt(const TpParams<float>& P, size_t smem, cudaStream_t s) {")
+    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(fwd3_kernel<G, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, "
+      "(int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
+    w("  fwd3_kernel<G, NT><<<(unsigned)P.n_rows, NT, smem, s>>>(P);")
+    w("  return fc_check_launch();")
+    w("}")
+    w("template <int G>")
+    w("int launch_fwd3_group(const TpParams<float>& P, cudaStream_t s) {")
+    w("  const size_t smem = fwd3_smem(G, P.F);")
+    w("  if (smem > 227 * 1024) return FC_ERR_UNSUPPORTED;")
+    w("  switch (P.F) {")
+    w("    case 64: return launch_fwd3_nt<G, 64>(P, smem, s);")
+    w("    case 128: return launch_fwd3_nt<G, 96>(P, smem, s);")
+    w("  }")
+    w("  return FC_ERR_UNSUPPORTED;")
+    w("}")
+    w("template <int G, int NM, int NT>")
+    w("int launch_bwd3_nt(const TpBwdParams<float>& P, size_t smem, cudaStream_t s) {")
+    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(bwd3_kernel<G, NM, NT>, "
+      "cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
+    w("  bwd3_kernel<G, NM, NT><<<(unsigned)P.n_rows, NT, smem, s>>>(P);")
+    w("  return fc_check_launch();")
+    w("}")
+    w("template <int G, int NM>")
+    w("int launch_bwd3_variant(const TpBwdParams<float>& P, size_t smem, cudaStream_t s) {")
+    w("  switch (P.F) {")
+    w("    case 64: return launch_bwd3_nt<G, NM, 64>(P, smem, s);")
+    w("    case 128: return launch_bwd3_nt<G, NM, 96>(P, smem, s);")
+    w("  }")
+    w("  return FC_ERR_UNSUPPORTED;")
+    w("}")
+    w("template <int G>")
+    w("int launch_bwd3_group(const TpBwdParams<float>& P, cudaStream_t s) {")
+    w("  const size_t smem = bwd3_smem(G, P.F);")
+    w("  if (smem > 227 * 1024) return FC_ERR_UNSUPPORTED;")
+    w("  const int nm = (P.g_in1 ? 1 : 0) | (P.g_in2 ? 2 : 0) | (P.g_w ? 4 : 0);")
+    w("  if (nm == 7) return launch_bwd3_variant<G, 7>(P, smem, s);")
+    w("  if (nm == 6) return launch_bwd3_variant<G, 6>(P, smem, s);")
+    w("  return launch_bwd3_variant<G, 0>(P, smem, s);")
+    w("}")
+    for kind, params in (("fwd", "TpParams"), ("bwd", "TpBwdParams")):
+        w(f"inline int launch_{kind}3(const {params}<float>& P, cudaStream_t s) {{")
+        w("  if (P.n_rows == 0) return 0;")
+        w("  if (P.n_rows > 0x7fffffffLL || (P.F != 64 && P.F != 128)) return FC_ERR_UNSUPPORTED;")
+        for gi in range(len(groups)):
+            w(f"  if (int rc = launch_{kind}3_group<{gi}>(P, s)) return rc;")
+        w("  return 0;")
+        w("}")
+    return "\n".join(L) + "\n"

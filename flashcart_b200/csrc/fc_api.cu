@@ -149,6 +149,13 @@ static bool conv2_eligible(const fc_tp_desc* d, bool conv, const void* in1, cons
          !d->shared_weights && !d->reduce_paths;
 }
 
+// The channel-pair kernels (two adjacent channels per thread, packed f32x2 arithmetic)
+// take float32 convolutions with 64 or 128 channels (F/2 threads, whole warps, plus a
+// producer warp); conv2_eligible has checked the rest of the layout.
+static bool pair_eligible(const fc_tp_desc* d) {
+  return d->dtype == FC_F32 && (d->in1_features == 64 || d->in1_features == 128);
+}
+
 template <typename P>
 static void fill_common(P& p, const fc_tp_desc* d, const int64_t* rowptr, const int64_t* idx_j, int64_t n_rows,
                         int64_t n_in1, int32_t* status) {
@@ -457,6 +464,7 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
     TpParams<float> p;
     fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
     p.in1 = (const float*)in1; p.in2 = (const float*)in2; p.w = (const float*)weights; p.out = (float*)out;
+    if (v2 && pair_eligible(desc) && sig->table->fwd3_f32) return launch_status(sig->table->fwd3_f32(p, s), "fc_tp_fwd");
     return launch_status(v2 ? sig->table->fwd2_f32(p, s) : sig->table->fwd_f32(p, s), "fc_tp_fwd");
   }
   TpParams<double> p;
@@ -501,6 +509,7 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
     p.g_out = (const float*)grad_out; p.in1 = (const float*)in1; p.in2 = (const float*)in2;
     p.w = (const float*)weights;
     p.g_in1 = (float*)grad_in1; p.g_in2 = (float*)grad_in2; p.g_w = (float*)grad_weights;
+    if (v2 && pair_eligible(desc) && sig->table->bwd3_f32) return launch_status(sig->table->bwd3_f32(p, s), "fc_tp_bwd");
     return launch_status(v2 ? sig->table->bwd2_f32(p, s) : sig->table->bwd_f32(p, s), "fc_tp_bwd");
   }
   TpBwdParams<double> p;

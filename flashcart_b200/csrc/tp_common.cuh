@@ -10,6 +10,12 @@
 #pragma once
 #include "fc_base.cuh"
 
+#ifndef FC_P3_FWD_MINB
+#define FC_P3_FWD_MINB 5
+#endif
+#ifndef FC_P3_BWD_MINB
+#define FC_P3_BWD_MINB 4
+#endif
 #ifndef FC_TP_BLOCK
 #define FC_TP_BLOCK 256
 #endif
@@ -65,6 +71,9 @@ struct TpTable {
   int (*fwd2_f64)(const TpParams<double>&, cudaStream_t);
   int (*bwd2_f32)(const TpBwdParams<float>&, cudaStream_t);
   int (*bwd2_f64)(const TpBwdParams<double>&, cudaStream_t);
+  // channel-pair convolution kernels (float32, F = 64 or 128; may be null)
+  int (*fwd3_f32)(const TpParams<float>&, cudaStream_t);
+  int (*bwd3_f32)(const TpBwdParams<float>&, cudaStream_t);
 };
 
 struct TpSigEntry {
@@ -88,6 +97,36 @@ __device__ __forceinline__ void ld4(const float* p, float* v) {
 __device__ __forceinline__ void ld4(const double* p, double* v) {
   const double2 a = reinterpret_cast<const double2*>(p)[0], b = reinterpret_cast<const double2*>(p)[1];
   v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+// ---- packed float pairs (two adjacent channels per thread) for the channel-pair kernels:
+// f32x2 arithmetic (one issue slot for two FP32 operations, sm_100), 8-byte loads/stores.
+__device__ __forceinline__ float2 p2(float c) { return make_float2(c, c); }
+__device__ __forceinline__ float2 pmul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 pfma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 padd(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
+__device__ __forceinline__ void st2(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
+// Two consecutive float2 values of shared memory (16-byte aligned) with one 16-byte load.
+__device__ __forceinline__ void ld2x2(const float2* p, float2* v) {
+  const float4 q = *reinterpret_cast<const float4*>(p);
+  v[0] = make_float2(q.x, q.y);
+  v[1] = make_float2(q.z, q.w);
+}
+// Vector atomic add of a channel pair into global memory (one reduction instruction).
+__device__ __forceinline__ void red2(float* p, float2 v) { atomicAdd(reinterpret_cast<float2*>(p), v); }
+// Minimum resident CTAs per SM of the channel-pair kernels by thread count (F/2 consumers
+// + one producer warp): caps the registers a thread may use so that enough consumer
+// warps stay resident (65,536 registers per SM / (CTAs x threads)).
+// Small path groups (BIG false) run uncapped: their registers already allow many CTAs.
+template <int NT, bool BIG> struct P3MinBlocks { static constexpr int fwd = 1, bwd = 1; };
+template <> struct P3MinBlocks<64, true> { static constexpr int fwd = 6, bwd = 6; };
+template <> struct P3MinBlocks<96, true> { static constexpr int fwd = FC_P3_FWD_MINB, bwd = FC_P3_BWD_MINB; };
+
+// Barrier among the first `count` threads of the CTA (a multiple of 32) on barrier `id`.
+__device__ __forceinline__ void fc_named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---- prefetch ring of the convolution kernels: 1-D bulk async copies (global -> this
@@ -278,9 +317,10 @@ int tp_dbwd_launch(const TpDbwdParams<T>& P, cudaStream_t) {
 // Instantiate the launch table of a generated signature; NS::Ops supplies the bodies.
 #ifndef FC_HOST_EMU
 #define FC_CONV2_ENTRIES(NS)                                                              \
-  , &NS::Ops::fwd2<float>, &NS::Ops::fwd2<double>, &NS::Ops::bwd2<float>, &NS::Ops::bwd2<double>
+  , &NS::Ops::fwd2<float>, &NS::Ops::fwd2<double>, &NS::Ops::bwd2<float>, &NS::Ops::bwd2<double>, \
+      &NS::Ops::fwd3, &NS::Ops::bwd3
 #else
-#define FC_CONV2_ENTRIES(NS) , nullptr, nullptr, nullptr, nullptr
+#define FC_CONV2_ENTRIES(NS) , nullptr, nullptr, nullptr, nullptr, nullptr, nullptr
 #endif
 #define FC_DEFINE_TP_SIGNATURE(NAME, NS)                                                  \
   extern const TpTable tp_table_##NAME;                                                   \

@@ -141,7 +141,8 @@ def _conv_inputs(n_nodes, n_edges, C, l1, l2, seed, dtype, dev):
     return [t.to(dev) for t in (idx_i, idx_j)] + [t.to(dev, dtype) for t in (in1, in2)]
 
 
-@pytest.mark.parametrize("sig", [(2, 2, 2, 64), (3, 3, 3, 128), (0, 3, 3, 128), (2, 3, 3, 32)])
+@pytest.mark.parametrize("sig", [(2, 2, 2, 64), (3, 3, 3, 128), (0, 3, 3, 128), (2, 3, 3, 32), (2, 2, 2, 256),
+                                 (1, 2, 2, 64), (3, 3, 3, 64), (3, 3, 2, 128), (1, 3, 3, 192)])
 def test_gpu_fp32_convolution_vs_oracle(cuda_device, sig):
     l1, l2, lo, C = sig
     dev = cuda_device
@@ -183,6 +184,35 @@ def test_gpu_convolution_linearity_and_edge_order_at_size(cuda_device):
         order = torch.argsort(key)
         c = tp(in1, in2[order], w1[order], idx_i[order], idx_j[order])
         assert (c - a).abs().max().item() < 1e-4 * a.abs().max().item()
+    check_device_status(dev)
+
+
+@pytest.mark.parametrize("C", [64, 128])
+def test_gpu_out_of_range_sender_is_reported_and_skipped(cuda_device, C):
+    """A sender index past in1's rows: flagged in the status word, the edge contributes
+    nothing (forward and backward), every other edge as usual."""
+    dev = cuda_device
+    n_nodes, n_edges = 40, 600
+    idx_i, idx_j, in1, in2 = _conv_inputs(n_nodes, n_edges, C, 2, 2, 5, torch.float32, dev)
+    tp = o3.TensorProduct(2, 2, 2, C, 1)
+    w = torch.randn(n_edges, tp.n_total_paths * C, device=dev)
+    bad = idx_j.clone()
+    bad[123] = n_nodes + 7
+    check_device_status(dev)
+    leaves = [in1.requires_grad_(True), in2.requires_grad_(True), w.requires_grad_(True)]
+    out = tp(*leaves, idx_i, bad)
+    g = torch.randn_like(out)
+    grads = torch.autograd.grad(out, leaves, g)
+    with pytest.raises(RuntimeError):
+        check_device_status(dev)
+    keep = torch.ones(n_edges, dtype=torch.bool, device=dev)
+    keep[123] = False
+    ref_leaves = [t.detach().double().cpu().requires_grad_(True) for t in leaves]
+    w_ref = ref_leaves[2] * keep.cpu().double().unsqueeze(1)
+    ref = O.tensor_product(ref_leaves[0], ref_leaves[1], w_ref, idx_i.cpu(), idx_j.cpu(), 2, 2, 2, C, 1)
+    assert (out.detach().double().cpu() - ref).abs().max().item() < 2e-5 * ref.abs().max().item()
+    ref_g1 = torch.autograd.grad(ref, ref_leaves[0], g.double().cpu())[0]
+    assert (grads[0].double().cpu() - ref_g1).abs().max().item() < 2e-5 * ref_g1.abs().max().item()
     check_device_status(dev)
 
 
