@@ -40,7 +40,7 @@ EXPORTED_SYMBOLS = (
     "fc_neighbor_workspace_bytes", "fc_neighbor_count", "fc_neighbor_fill",
     "fc_edge_expand_fwd", "fc_edge_expand_bwd",
     "fc_linear_presplit", "fc_linear_fwd_presplit", "fc_linear_bwd_presplit",
-    "fc_linear_dbwd", "fc_halo_pack", "fc_halo_unpack",
+    "fc_linear_dbwd", "fc_halo_pack", "fc_halo_unpack", "fc_edge_geometry_fwd", "fc_edge_geometry_bwd",
 )
 
 
@@ -48,6 +48,12 @@ class TpDesc(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in (
         "in1_l_max", "in2_l_max", "out_l_max", "in1_features", "in2_features",
         "symmetric_product", "shared_weights", "reduce_paths", "dtype")]
+
+
+class EdgeGeometryDesc(ctypes.Structure):
+    _fields_ = [("l_max", ctypes.c_int32), ("n_radial", ctypes.c_int32), ("cosine", ctypes.c_int32),
+                ("poly_order", ctypes.c_int32), ("use_shifts", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                ("r_min", ctypes.c_double), ("r_max", ctypes.c_double), ("r_cut", ctypes.c_double)]
 
 
 class LinearDesc(ctypes.Structure):
@@ -139,6 +145,12 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_edge_expand_fwd.argtypes = [_I32, _I32, _I32, _I32, _P, _P, _I64, _P, _P]
     lib.fc_edge_expand_bwd.restype = ctypes.c_int
     lib.fc_edge_expand_bwd.argtypes = [_I32, _I32, _I32, _I32, _P, _P, _P, _I64, _P, _P, _P]
+    lib.fc_edge_geometry_fwd.restype = ctypes.c_int
+    lib.fc_edge_geometry_fwd.argtypes = [ctypes.POINTER(EdgeGeometryDesc), _P, _I64, _P, _I64, _P, _P, _P, _I64, _P,
+                                         _P, _P, _P]
+    lib.fc_edge_geometry_bwd.restype = ctypes.c_int
+    lib.fc_edge_geometry_bwd.argtypes = [ctypes.POINTER(EdgeGeometryDesc), _P, _I64, _P, _I64, _P, _P, _P, _I64, _P,
+                                         _P, _P, _P, _P, _P]
     lib.fc_gate_fwd.restype = ctypes.c_int
     lib.fc_gate_fwd.argtypes = [_I32, _I32, _I32, _P, _P, _I64, _P, _P]
     lib.fc_gate_bwd.restype = ctypes.c_int

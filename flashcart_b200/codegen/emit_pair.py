@@ -58,6 +58,7 @@ BUDGET = 32   # accumulator pairs per path group when a signature is split
 # C = 128, 1.49 M edges: (3,3)->3 backward 21.8 -> 14.0 ms with the small footprint, while
 # (0,3)->3 is fastest with the large one (1.38 vs 1.93 ms).
 SMALL_NACC = 16
+STAGE_X2 = True  # the producer stages each chunk's in2 rows (in2 rows of 4 or 16 floats)
 G_SMEM = None  # None: per group as above; True / False force it (experiments)
 EC = None
 RING = None
@@ -93,12 +94,28 @@ def _lin_pairs(terms: Sequence[Tuple[Fraction, str]]) -> str:
     return e
 
 
-def _chain(pairs: Sequence[Tuple[str, str]], init: str = "") -> str:
-    """sum a_k * b_k (+ init) of float2 operands as one fma chain."""
+# Sums of more than CHAIN_SPLIT products split into two independent fma chains. Measured
+# on the (3,3)->3 convolution at C = 128: a split at 3 or 5 terms made the backward 1-4%
+# slower (13.8 ms unsplit, 14.4 ms at 3), so sums stay single chains.
+CHAIN_SPLIT = 99
+
+
+def _chain1(pairs: Sequence[Tuple[str, str]], init: str = "") -> str:
     e = init
     for a, b in pairs:
         e = f"pmul({a}, {b})" if not e else f"pfma({a}, {b}, {e})"
     return e or "p2(0.0f)"
+
+
+def _chain(pairs: Sequence[Tuple[str, str]], init: str = "") -> str:
+    """sum a_k * b_k (+ init) of float2 operands. A long sum is split into two independent
+    fma chains (even / odd terms) joined by one add, so consecutive multiply-adds do not all
+    wait for each other (the packed FMA has a multi-cycle latency and few warps per
+    scheduler hide it)."""
+    pairs = list(pairs)
+    if len(pairs) <= CHAIN_SPLIT:
+        return _chain1(pairs, init)
+    return f"padd({_chain(pairs[0::2], init)}, {_chain(pairs[1::2])})"
 
 
 def _phase1(gs: GroupSlots, ind: str) -> List[str]:
@@ -219,13 +236,17 @@ def _setup(gs: GroupSlots, extra_floats: str, ind: str) -> List[str]:
         f"{ind}float* ring = reinterpret_cast<float*>(m2 + NMP * {gs.ec});",
         f"{ind}const int SLOT = (XN + NW) * F;",
         f"{ind}float* extra = ring + {gs.ring} * SLOT;",
-        f"{ind}int64_t* sj = reinterpret_cast<int64_t*>(extra + {extra_floats});",
+        f"{ind}float* xbuf = extra + {extra_floats};  // [2][EC][D2] in2 rows of the chunks (staged)",
+        f"{ind}int64_t* sj = reinterpret_cast<int64_t*>(xbuf + {2 * gs.ec * gs.sig.d2 if gs.stage else 0});",
         f"{ind}uint64_t* full = reinterpret_cast<uint64_t*>(sj + {gs.ring});",
         f"{ind}uint64_t* empty = full + {gs.ring};",
-        f"{ind}volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + {gs.ring});",
+        f"{ind}uint64_t* xfull = empty + {gs.ring};",
+        f"{ind}uint64_t* xempty = xfull + 2;",
+        f"{ind}volatile int* abort_flag = reinterpret_cast<volatile int*>(xempty + 2);",
         f"{ind}const int64_t e0 = P.rowptr[row], ne_all = P.rowptr[row + 1] - e0;",
         f"{ind}if (t == 0) {{",
         f"{ind}  for (int s = 0; s < {gs.ring}; ++s) {{ fc_mbar_init(&full[s], 1); fc_mbar_init(&empty[s], NC >> 5); }}",
+        f"{ind}  for (int b = 0; b < 2; ++b) {{ fc_mbar_init(&xfull[b], 1); fc_mbar_init(&xempty[b], 1); }}",
         f"{ind}  *abort_flag = 0;",
         f"{ind}  fc_mbar_init_fence();",
         f"{ind}}}",
@@ -238,15 +259,27 @@ def _producer(gs: GroupSlots, ind: str) -> List[str]:
     header + bulk copies; at the end, an aborted CTA waits for its copies in flight."""
     L = [f"{ind}if (t >= NC) {{",
          f"{ind}  const int pl = t - NC;",
-         f"{ind}  int64_t issued = 0;",
+         f"{ind}  int64_t issued = 0, xissued = 0;",
          f"{ind}  for (int64_t base = 0; base < ne_all; base += 32) {{",
          f"{ind}    const int64_t jv = base + pl < ne_all ? P.idx_j[e0 + base + pl] : 0;",
          f"{ind}    const int nb = (int)min((int64_t)32, ne_all - base);",
          f"{ind}    for (int k = 0; k < nb; ++k) {{",
          f"{ind}      const int64_t j = __shfl_sync(0xffffffffu, jv, k);",
          f"{ind}      if (pl == 0 && !*abort_flag) {{",
-         f"{ind}        const int64_t kk = base + k;",
-         f"{ind}        const int s = (int)(kk % {gs.ring});",
+         f"{ind}        const int64_t kk = base + k;"]
+    if gs.stage:
+        # the in2 rows of a chunk, one bulk copy, issued with the chunk's first edge
+        L += [f"{ind}        if (kk % {gs.ec} == 0) {{",
+              f"{ind}          const int64_t c = kk / {gs.ec};",
+              f"{ind}          const int b = (int)(c & 1);",
+              f"{ind}          if (c < 2 || fc_mbar_wait(&xempty[b], (uint32_t)((c / 2 - 1) & 1), abort_flag, P.status)) {{",
+              f"{ind}            const int nec = (int)min((int64_t){gs.ec}, ne_all - kk);",
+              f"{ind}            fc_mbar_arrive_tx(&xfull[b], (uint32_t)(nec * D2 * 4));",
+              f"{ind}            fc_bulk_g2s(xbuf + b * {gs.ec * gs.sig.d2}, P.in2 + (e0 + kk) * (int64_t)D2, (uint32_t)(nec * D2 * 4), &xfull[b]);",
+              f"{ind}            xissued = c + 1;",
+              f"{ind}          }}",
+              f"{ind}        }}"]
+    L += [f"{ind}        const int s = (int)(kk % {gs.ring});",
          f"{ind}        if (kk < {gs.ring} || fc_mbar_wait(&empty[s], (uint32_t)((kk / {gs.ring} - 1) & 1), abort_flag, P.status)) {{",
          f"{ind}          const bool ok = (uint64_t)j < (uint64_t)P.n_in1;",
          f"{ind}          if (!ok) fc_flag(P.status, FC_DEV_BAD_INDEX);",
@@ -267,6 +300,9 @@ def _producer(gs: GroupSlots, ind: str) -> List[str]:
           f"{ind}    for (int64_t kk = issued > {gs.ring} ? issued - {gs.ring} : 0; kk < issued; ++kk)",
           f"{ind}      for (long long it = 0; it < FC_RING_WAIT_LIMIT; ++it)",
           f"{ind}        if (fc_mbar_test(&full[kk % {gs.ring}], (uint32_t)((kk / {gs.ring}) & 1))) break;",
+          f"{ind}    for (int64_t c = xissued > 2 ? xissued - 2 : 0; c < xissued; ++c)",
+          f"{ind}      for (long long it = 0; it < FC_RING_WAIT_LIMIT; ++it)",
+          f"{ind}        if (fc_mbar_test(&xfull[c & 1], (uint32_t)((c >> 1) & 1))) break;",
           f"{ind}  }}",
           f"{ind}  return;",
           f"{ind}}}"]
@@ -274,17 +310,28 @@ def _producer(gs: GroupSlots, ind: str) -> List[str]:
 
 
 def _phase1_loop(gs: GroupSlots, ind: str) -> List[str]:
-    return [f"{ind}for (int u = t; u < {gs.ec * NPART}; u += NC) {{",
+    if gs.stage:
+        load = [f"{ind}    const T* a2 = xbuf + (cidx & 1) * {gs.ec * gs.sig.d2} + le * D2;",
+                f"{ind}    for (int q = 0; q < D2; ++q) x2[q] = xok ? a2[q] : T(0);"]
+        head = [f"{ind}const int64_t cidx = eb / {gs.ec};",
+                f"{ind}const bool xok = fc_mbar_wait(&xfull[cidx & 1], (uint32_t)((cidx >> 1) & 1), abort_flag, P.status);"]
+        tail = [f"{ind}if (t == 0) fc_mbar_arrive(&xempty[cidx & 1]);"]
+    else:
+        load = [f"{ind}    const T* __restrict__ a2 = P.in2 + (e0 + eb + le) * (int64_t)D2;",
+                f"{ind}    for (int q = 0; q < D2; ++q) x2[q] = fc_ldg(a2 + q);"]
+        head, tail = [], []
+    return [*head,
+            f"{ind}for (int u = t; u < {gs.ec * NPART}; u += NC) {{",
             f"{ind}  const int le = u % {gs.ec}, part = u / {gs.ec};",
             f"{ind}  if (le < ne) {{",
             f"{ind}    T x2[D2];",
-            f"{ind}    const T* __restrict__ a2 = P.in2 + (e0 + eb + le) * (int64_t)D2;",
-            f"{ind}    for (int q = 0; q < D2; ++q) x2[q] = fc_ldg(a2 + q);",
+            *load,
             f"{ind}    float2* m = m2 + le * NMP;",
             *_phase1(gs, ind + "    "),
             f"{ind}  }}",
             f"{ind}}}",
-            f"{ind}fc_named_sync(1, NC);"]
+            f"{ind}fc_named_sync(1, NC);",
+            *tail]
 
 
 def _edge_begin(gs: GroupSlots, ind: str) -> List[str]:
@@ -304,6 +351,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     for gs in groups:
         for k, v in group_cfg(gs).items():
             setattr(gs, k, v)
+        gs.stage = STAGE_X2 and sig.d2 % 4 == 0  # 16-byte in2 rows: bulk-copied by the producer
     d2p = 1
     while d2p < sig.d2:
         d2p *= 2
@@ -323,8 +371,9 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         for gi, gs in enumerate(groups):
             extra = gs.ec * d2p if kind == "bwd" else 0
             gextra = f" + {gs.nacc} * F" if (kind == "bwd" and gs.gsmem) else ""
+            xb = 2 * gs.ec * gs.sig.d2 if gs.stage else 0
             w(f"    case {gi}: return (size_t){gs.nmp * gs.ec} * 8 + (size_t)({gs.ring} * ({gs.x_n} + {len(gs.paths)}) * F"
-              f" + {extra}{gextra}) * 4 + {gs.ring * 8 + 2 * gs.ring * 8 + 16};")
+              f" + {extra + xb}{gextra}) * 4 + {gs.ring * 8 + 2 * gs.ring * 8 + 4 * 8 + 16};")
         w("  }")
         w("  return 0;")
         w("}")

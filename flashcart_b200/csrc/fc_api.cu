@@ -35,6 +35,12 @@ int edge_expand_fwd_dispatch(int, const T*, const T*, int, int, int64_t, T*, cud
 template <typename T>
 int edge_expand_bwd_dispatch(int, const T*, const T*, const T*, int, int, int64_t, T*, T*, cudaStream_t);
 template <typename T>
+int geom_fwd_dispatch(const GeomParams&, const T*, const T*, const int32_t*, const int64_t*, const int64_t*, T*, T*,
+                      int*, cudaStream_t);
+template <typename T>
+int geom_bwd_dispatch(const GeomParams&, const T*, const T*, const int32_t*, const int64_t*, const int64_t*,
+                      const T*, const T*, T*, T*, int*, cudaStream_t);
+template <typename T>
 int gate_fwd_dispatch(int, const T*, const T*, T*, int, int64_t, cudaStream_t);
 template <typename T>
 int halo_pack_dispatch(const T*, int64_t, int64_t, const int64_t*, int64_t, T*, int*, cudaStream_t);
@@ -152,8 +158,10 @@ static bool conv2_eligible(const fc_tp_desc* d, bool conv, const void* in1, cons
 // The channel-pair kernels (two adjacent channels per thread, packed f32x2 arithmetic)
 // take float32 convolutions with 64 or 128 channels (F/2 threads, whole warps, plus a
 // producer warp); conv2_eligible has checked the rest of the layout.
-static bool pair_eligible(const fc_tp_desc* d) {
-  return d->dtype == FC_F32 && (d->in1_features == 64 || d->in1_features == 128);
+static bool pair_eligible(const fc_tp_desc* d, const void* in2) {
+  // in2 rows are bulk-copied (16-byte aligned base; the row offsets are multiples of 16 B)
+  return d->dtype == FC_F32 && (d->in1_features == 64 || d->in1_features == 128) &&
+         (reinterpret_cast<uintptr_t>(in2) & 15) == 0;
 }
 
 template <typename P>
@@ -464,7 +472,7 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
     TpParams<float> p;
     fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
     p.in1 = (const float*)in1; p.in2 = (const float*)in2; p.w = (const float*)weights; p.out = (float*)out;
-    if (v2 && pair_eligible(desc) && sig->table->fwd3_f32) return launch_status(sig->table->fwd3_f32(p, s), "fc_tp_fwd");
+    if (v2 && pair_eligible(desc, in2) && sig->table->fwd3_f32) return launch_status(sig->table->fwd3_f32(p, s), "fc_tp_fwd");
     return launch_status(v2 ? sig->table->fwd2_f32(p, s) : sig->table->fwd_f32(p, s), "fc_tp_fwd");
   }
   TpParams<double> p;
@@ -509,7 +517,7 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
     p.g_out = (const float*)grad_out; p.in1 = (const float*)in1; p.in2 = (const float*)in2;
     p.w = (const float*)weights;
     p.g_in1 = (float*)grad_in1; p.g_in2 = (float*)grad_in2; p.g_w = (float*)grad_weights;
-    if (v2 && pair_eligible(desc) && sig->table->bwd3_f32) return launch_status(sig->table->bwd3_f32(p, s), "fc_tp_bwd");
+    if (v2 && pair_eligible(desc, in2) && sig->table->bwd3_f32) return launch_status(sig->table->bwd3_f32(p, s), "fc_tp_bwd");
     return launch_status(v2 ? sig->table->bwd2_f32(p, s) : sig->table->bwd_f32(p, s), "fc_tp_bwd");
   }
   TpBwdParams<double> p;
@@ -917,6 +925,76 @@ int fc_edge_expand_bwd(int32_t l_max, int32_t features, int32_t per_rank, int32_
                                                         (const double*)h, features, pr, n_rows,
                                                         (double*)grad_moments, (double*)grad_h, s),
                        "fc_edge_expand_bwd");
+}
+
+// ------------------------------------------------------------------ edge geometry
+
+static int geom_check(const fc_edge_geometry_desc* d, int64_t n_nodes, int64_t n_cells, int64_t n_edges,
+                      const char* what, GeomParams* p) {
+  if (!d) return fail(FC_ERR_INVALID, "%s: null descriptor", what);
+  if (d->l_max < 0 || d->l_max > 3) return fail(FC_ERR_UNSUPPORTED, "%s: l_max %d outside 0..3", what, d->l_max);
+  if (d->n_radial < 1 || d->n_radial > 64)
+    return fail(FC_ERR_UNSUPPORTED, "%s: n_radial %d outside 1..64", what, d->n_radial);
+  if (d->poly_order < 2 || d->poly_order > 64)
+    return fail(FC_ERR_UNSUPPORTED, "%s: poly_order %d outside 2..64", what, d->poly_order);
+  if (d->dtype != FC_F32 && d->dtype != FC_F64) return fail(FC_ERR_INVALID, "%s: dtype must be f32 or f64", what);
+  if (!(d->r_max > d->r_min) || !(d->r_cut > 0.0)) return fail(FC_ERR_INVALID, "%s: need r_max > r_min, r_cut > 0", what);
+  if (n_nodes < 0 || n_edges < 0 || n_cells < 0) return fail(FC_ERR_INVALID, "%s: negative size", what);
+  if (d->use_shifts && n_cells < 1 && n_edges > 0) return fail(FC_ERR_INVALID, "%s: shifts need a cell", what);
+  p->l_max = d->l_max; p->n_radial = d->n_radial; p->cosine = d->cosine ? 1 : 0;
+  p->poly_order = d->poly_order; p->use_shifts = d->use_shifts ? 1 : 0;
+  p->r_min = d->r_min; p->r_max = d->r_max; p->r_cut = d->r_cut;
+  p->n_nodes = n_nodes; p->n_edges = n_edges; p->n_cells = n_cells;
+  return FC_OK;
+}
+
+int fc_edge_geometry_fwd(const fc_edge_geometry_desc* desc, const void* positions, int64_t n_nodes,
+                         const void* cells, int64_t n_cells, const int32_t* shifts, const int64_t* edge_index,
+                         const int64_t* batch, int64_t n_edges, void* edge_attrs, void* radial, int32_t* status,
+                         fc_stream_t stream) {
+  GeomParams p;
+  if (int rc = geom_check(desc, n_nodes, n_cells, n_edges, "fc_edge_geometry_fwd", &p)) return rc;
+  if (n_edges == 0) return FC_OK;
+  if (!positions || !edge_index || !edge_attrs || !radial || (p.use_shifts && (!cells || !shifts)) ||
+      (p.use_shifts && n_cells > 1 && !batch))
+    return fail(FC_ERR_INVALID, "fc_edge_geometry_fwd: null pointer");
+  const cudaStream_t s = (cudaStream_t)stream;
+  int* st = reinterpret_cast<int*>(status);
+  if (desc->dtype == FC_F32)
+    return launch_status(geom_fwd_dispatch<float>(p, (const float*)positions, (const float*)cells, shifts,
+                                                  edge_index, batch, (float*)edge_attrs, (float*)radial, st, s),
+                         "fc_edge_geometry_fwd");
+  return launch_status(geom_fwd_dispatch<double>(p, (const double*)positions, (const double*)cells, shifts,
+                                                 edge_index, batch, (double*)edge_attrs, (double*)radial, st, s),
+                       "fc_edge_geometry_fwd");
+}
+
+int fc_edge_geometry_bwd(const fc_edge_geometry_desc* desc, const void* positions, int64_t n_nodes,
+                         const void* cells, int64_t n_cells, const int32_t* shifts, const int64_t* edge_index,
+                         const int64_t* batch, int64_t n_edges, const void* grad_attrs, const void* grad_radial,
+                         void* grad_positions, void* grad_cells, int32_t* status, fc_stream_t stream) {
+  GeomParams p;
+  if (int rc = geom_check(desc, n_nodes, n_cells, n_edges, "fc_edge_geometry_bwd", &p)) return rc;
+  if (!grad_positions && n_nodes > 0) return fail(FC_ERR_INVALID, "fc_edge_geometry_bwd: null grad_positions");
+  const cudaStream_t s = (cudaStream_t)stream;
+  const int esz = desc->dtype == FC_F32 ? 4 : 8;
+  int rc = 0;
+  if (n_nodes > 0) rc |= zero_fill(grad_positions, n_nodes * 3 * esz, s);
+  if (grad_cells && n_cells > 0) rc |= zero_fill(grad_cells, n_cells * 9 * esz, s);
+  if (rc) return launch_status(FC_ERR_LAUNCH, "fc_edge_geometry_bwd (zero fill)");
+  if (n_edges == 0 || (!grad_attrs && !grad_radial)) return FC_OK;
+  if (!positions || !edge_index || (p.use_shifts && (!cells || !shifts)) || (p.use_shifts && n_cells > 1 && !batch))
+    return fail(FC_ERR_INVALID, "fc_edge_geometry_bwd: null pointer");
+  int* st = reinterpret_cast<int*>(status);
+  if (desc->dtype == FC_F32)
+    return launch_status(geom_bwd_dispatch<float>(p, (const float*)positions, (const float*)cells, shifts, edge_index,
+                                                  batch, (const float*)grad_attrs, (const float*)grad_radial,
+                                                  (float*)grad_positions, (float*)grad_cells, st, s),
+                         "fc_edge_geometry_bwd");
+  return launch_status(geom_bwd_dispatch<double>(p, (const double*)positions, (const double*)cells, shifts, edge_index,
+                                                 batch, (const double*)grad_attrs, (const double*)grad_radial,
+                                                 (double*)grad_positions, (double*)grad_cells, st, s),
+                       "fc_edge_geometry_bwd");
 }
 
 // ------------------------------------------------------------------ neighbour list

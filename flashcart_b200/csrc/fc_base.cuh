@@ -122,4 +122,11 @@ FC_HD FC_INLINE void fc_scatter_rows(T* base, int Fx, int cx, const T* v, bool a
 
 inline int fc_round_up(int x, int m) { return (x + m - 1) / m * m; }
 
+// Parameters of the fused edge-geometry kernels (edge_geometry.cu, fc_edge_geometry_*).
+struct GeomParams {
+  int l_max, n_radial, cosine, poly_order, use_shifts;
+  double r_min, r_max, r_cut;
+  int64_t n_nodes, n_edges, n_cells;
+};
+
 }  // namespace fc

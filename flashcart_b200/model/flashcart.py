@@ -114,6 +114,10 @@ class FlashCartPotential(nn.Module):
         self.embedding = nn.Embedding(len(elements), n_hidden_feats)
         self.radial_basis = ChebyshevBasis(n_radial, r_max=r_max, r_min=r_min, mapping=radial_mapping)
         self.cutoff_fn = PolynomialCutoff(r_max, poly_order=cutoff_poly_order)
+        # constants of the fused edge-geometry kernel as host values (reading the modules'
+        # device buffers would synchronise, which a captured step may not do)
+        self._geometry_args = (int(n_radial), radial_mapping == "cosine", int(cutoff_poly_order), float(r_min),
+                               float(r_max), float(r_max))
         self.irreps = o3.Irreps(l_max_edge_attrs, use_triton=use_triton)
         product_out = [l_max_hidden_feats if i < n_interactions - 1 else 0 for i in range(n_interactions)]
         inter_in = [0 if i == 0 else l_max_hidden_feats for i in range(n_interactions)]
@@ -163,17 +167,25 @@ class FlashCartPotential(nn.Module):
         batch = graph["batch"]
         atom_types = graph["atom_types"]
         vectors = graph.get("vectors")
-        if vectors is None:
-            use_shifts = graph.get("use_shifts", True)
-            if not isinstance(use_shifts, bool):
-                use_shifts = _uses_shifts(use_shifts)
-            vectors = get_edge_vectors(graph["positions"], graph["cell"], graph["shifts"], edge_index, batch,
-                                       use_shifts=use_shifts)
-        distances = vectors.norm(dim=-1)
-        directions = vectors / distances.clamp_min(MIN_EDGE_LENGTH).unsqueeze(-1)
-        edge_attrs = self.irreps.forward_normalized(directions)
-        edge_feats = self.radial_basis(distances)
-        envelope = self.cutoff_fn(distances)
+        use_shifts = graph.get("use_shifts", True)
+        if not isinstance(use_shifts, bool):
+            use_shifts = _uses_shifts(use_shifts)
+        if vectors is None and self._geometry_fusable(graph):
+            # one kernel from positions to edge attributes and enveloped radial features
+            # (same arithmetic as the chain below; first derivative only)
+            edge_attrs, edge_feats = ops.edge_geometry(graph["positions"], graph["cell"], graph["shifts"], edge_index,
+                                                       batch, self.irreps.l_max, *self._geometry_args,
+                                                       use_shifts=use_shifts)
+            envelope = None
+        else:
+            if vectors is None:
+                vectors = get_edge_vectors(graph["positions"], graph["cell"], graph["shifts"], edge_index, batch,
+                                           use_shifts=use_shifts)
+            distances = vectors.norm(dim=-1)
+            directions = vectors / distances.clamp_min(MIN_EDGE_LENGTH).unsqueeze(-1)
+            edge_attrs = self.irreps.forward_normalized(directions)
+            edge_feats = self.radial_basis(distances)
+            envelope = self.cutoff_fn(distances)
         node_feats = self.embedding(atom_types)
         own_types = atom_types if n_out is None else atom_types[:n_out]
         outputs = []
@@ -192,6 +204,18 @@ class FlashCartPotential(nn.Module):
                 node_feats = torch.cat([node_feats, halo_fn(node_feats)], dim=0)
         energies = self.readout(outputs)
         return self.scale_shift(energies, own_types)
+
+    def _geometry_fusable(self, graph) -> bool:
+        """The fused edge-geometry kernel replaces the edge-vector -> attributes / radial
+        chain when the graph is differentiated at most once (first_order_only), the data
+        are on the GPU in float32 / float64, a cell tensor is given, and no interaction
+        layer mixes element embeddings into its radial input (they need the envelope on
+        its own)."""
+        pos = graph.get("positions")
+        cell = graph.get("cell")
+        return (ops.first_order_only_active() and torch.is_tensor(pos) and pos.is_cuda
+                and pos.dtype in (torch.float32, torch.float64) and torch.is_tensor(cell)
+                and self.irreps.l_max <= 3 and all(inter.emb_i is None for inter in self.interactions))
 
     # ------------------------------------------------------------------ predict
 

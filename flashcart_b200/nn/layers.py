@@ -298,7 +298,8 @@ class InteractionLayer(nn.Module):
             mlp_in = torch.cat([edge_feats, self.emb_i(atom_types)[idx_i], self.emb_j(atom_types)[idx_j]], dim=-1)
             mlp_in = mlp_in * envelope.unsqueeze(-1)
         else:
-            mlp_in = edge_feats * envelope.unsqueeze(-1)
+            # envelope None: edge_feats already carries the envelope (fused edge geometry)
+            mlp_in = edge_feats if envelope is None else edge_feats * envelope.unsqueeze(-1)
         node_feats = self.linear_first(node_feats)
         weights = self.radial_mlp(mlp_in)
         aggregated = self.tp(node_feats, edge_attrs, weights, idx_i, idx_j)

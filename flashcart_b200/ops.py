@@ -1056,3 +1056,112 @@ def _expand_backward(ctx, grad_out):
 
 
 edge_expand_fwd.register_autograd(_expand_backward, setup_context=_expand_setup)
+
+
+# --------------------------------------------------------------------------- fused edge geometry
+
+
+def _geom_desc(l_max: int, n_radial: int, cosine: bool, poly_order: int, use_shifts: bool, dtype: torch.dtype,
+               r_min: float, r_max: float, r_cut: float) -> N.EdgeGeometryDesc:
+    return N.EdgeGeometryDesc(int(l_max), int(n_radial), int(bool(cosine)), int(poly_order), int(bool(use_shifts)),
+                              _code(dtype), float(r_min), float(r_max), float(r_cut))
+
+
+def _geom_inputs(positions: Tensor, cells: Tensor, shifts: Tensor, edge_index: Tensor, batch: Tensor):
+    if positions.dtype not in (torch.float32, torch.float64):
+        raise ValueError(f"edge_geometry supports float32 / float64 positions, got {positions.dtype}")
+    if positions.dim() != 2 or positions.shape[1] != 3:
+        raise ValueError(f"edge_geometry: positions must be (n, 3), got {tuple(positions.shape)}")
+    if edge_index.dim() != 2 or edge_index.shape[0] != 2:
+        raise ValueError(f"edge_geometry: edge_index must be (2, E), got {tuple(edge_index.shape)}")
+    c = cells.to(positions.dtype).reshape(-1, 3, 3).contiguous()
+    s = shifts if shifts.dtype == torch.int32 else shifts.round().to(torch.int32)
+    return (positions.contiguous(), c, s.contiguous(), edge_index.to(torch.int64).contiguous(),
+            batch.to(torch.int64).contiguous())
+
+
+@torch.library.custom_op("flashcart::edge_geometry_fwd", mutates_args=())
+def edge_geometry_fwd(positions: Tensor, cells: Tensor, shifts: Tensor, edge_index: Tensor, batch: Tensor,
+                      l_max: int, n_radial: int, cosine: bool, poly_order: int, r_min: float, r_max: float,
+                      r_cut: float, use_shifts: bool) -> Tuple[Tensor, Tensor]:
+    """Edge attributes T^l(v / |v|) (E, (l_max+1)^2) and radial features Chebyshev(|v|) *
+    envelope(|v|) (E, n_radial) of the edges v = r_j - r_i + S . cell in one kernel
+    (reference chain ``model/flashcart.py:264-286`` -> ``utils/geometry.py:25-53``,
+    ``o3/irreps.py:54-72``, ``nn/radial.py:98-128, 181-245``)."""
+    _require_cuda(positions, cells, edge_index)
+    pos, c, s, ei, b = _geom_inputs(positions, cells, shifts, edge_index, batch)
+    e = ei.shape[1]
+    attrs = pos.new_empty((e, (l_max + 1) ** 2))
+    radial = pos.new_empty((e, n_radial))
+    lib = N.lib()
+    d = _geom_desc(l_max, n_radial, cosine, poly_order, use_shifts, pos.dtype, r_min, r_max, r_cut)
+    with _timed("edge_geometry_fwd", 1, _nbytes(pos, s, ei, attrs, radial)):
+        rc = lib.fc_edge_geometry_fwd(ctypes.byref(d), _p(pos), pos.shape[0], _p(c), c.shape[0], _p(s), _p(ei), _p(b),
+                                      e, _p(attrs), _p(radial), _p(status_word(pos.device)), _stream(pos.device))
+    _after(lib, rc, "fc_edge_geometry_fwd", pos.device)
+    return attrs, radial
+
+
+@edge_geometry_fwd.register_fake
+def _(positions, cells, shifts, edge_index, batch, l_max, n_radial, cosine, poly_order, r_min, r_max, r_cut,
+      use_shifts):
+    e = edge_index.shape[1]
+    return positions.new_empty((e, (l_max + 1) ** 2)), positions.new_empty((e, n_radial))
+
+
+@torch.library.custom_op("flashcart::edge_geometry_bwd", mutates_args=())
+def edge_geometry_bwd(grad_attrs: Tensor, grad_radial: Tensor, positions: Tensor, cells: Tensor, shifts: Tensor,
+                      edge_index: Tensor, batch: Tensor, l_max: int, n_radial: int, cosine: bool, poly_order: int,
+                      r_min: float, r_max: float, r_cut: float, use_shifts: bool) -> Tuple[Tensor, Tensor]:
+    """First derivative of :func:`edge_geometry_fwd`: (grad_positions (N, 3), grad_cells
+    (G, 3, 3)); an empty gradient tensor stands for zero."""
+    _require_cuda(positions, cells, edge_index)
+    pos, c, s, ei, b = _geom_inputs(positions, cells, shifts, edge_index, batch)
+    ga = grad_attrs.contiguous() if grad_attrs.numel() else None
+    gr = grad_radial.contiguous() if grad_radial.numel() else None
+    g_pos = torch.empty_like(pos)
+    g_cells = torch.empty_like(c)
+    lib = N.lib()
+    d = _geom_desc(l_max, n_radial, cosine, poly_order, use_shifts, pos.dtype, r_min, r_max, r_cut)
+    with _timed("edge_geometry_bwd", 1, _nbytes(pos, s, ei, ga, gr, g_pos)):
+        rc = lib.fc_edge_geometry_bwd(ctypes.byref(d), _p(pos), pos.shape[0], _p(c), c.shape[0], _p(s), _p(ei), _p(b),
+                                      ei.shape[1], _p(ga), _p(gr), _p(g_pos), _p(g_cells),
+                                      _p(status_word(pos.device)), _stream(pos.device))
+    _after(lib, rc, "fc_edge_geometry_bwd", pos.device)
+    return g_pos, g_cells.reshape(cells.shape)
+
+
+@edge_geometry_bwd.register_fake
+def _(grad_attrs, grad_radial, positions, cells, shifts, edge_index, batch, l_max, n_radial, cosine, poly_order,
+      r_min, r_max, r_cut, use_shifts):
+    return torch.empty_like(positions), torch.empty_like(cells)
+
+
+def _geom_setup(ctx, inputs, output):
+    positions, cells, shifts, edge_index, batch = inputs[:5]
+    ctx.save_for_backward(positions, cells, shifts, edge_index, batch)
+    ctx.args = inputs[5:]
+
+
+def _geom_backward(ctx, grad_attrs, grad_radial):
+    if torch.is_grad_enabled():
+        raise RuntimeError("flashcart::edge_geometry_fwd was evaluated inside first_order_only(); its backward "
+                           "cannot build a graph for a second derivative")
+    positions, cells, shifts, edge_index, batch = ctx.saved_tensors
+    ga = grad_attrs if grad_attrs is not None else positions.new_zeros(0)
+    gr = grad_radial if grad_radial is not None else positions.new_zeros(0)
+    g_pos, g_cells = edge_geometry_bwd(ga, gr, positions, cells, shifts, edge_index, batch, *ctx.args)
+    return ((g_pos if ctx.needs_input_grad[0] else None), (g_cells if ctx.needs_input_grad[1] else None),
+            None, None, None) + (None,) * len(ctx.args)
+
+
+edge_geometry_fwd.register_autograd(_geom_backward, setup_context=_geom_setup)
+
+
+def edge_geometry(positions: Tensor, cells: Tensor, shifts: Tensor, edge_index: Tensor, batch: Tensor, l_max: int,
+                  n_radial: int, cosine: bool, poly_order: int, r_min: float, r_max: float, r_cut: float,
+                  use_shifts: bool = True) -> Tuple[Tensor, Tensor]:
+    """(edge_attrs, radial) of :func:`edge_geometry_fwd`, differentiable once with respect to
+    positions and cells (see :func:`first_order_only`)."""
+    return edge_geometry_fwd(positions, cells, shifts, edge_index, batch, int(l_max), int(n_radial), bool(cosine),
+                             int(poly_order), float(r_min), float(r_max), float(r_cut), bool(use_shifts))

@@ -297,6 +297,44 @@ int fc_edge_expand_bwd(int32_t l_max, int32_t features, int32_t per_rank, int32_
                        const void* moments, const void* h, int64_t n_rows, void* grad_moments, void* grad_h,
                        fc_stream_t stream);
 
+/* ---------------------------------------------------------------- edge geometry
+ * Fused edge geometry of the potential, one pass per edge. Replaces the chain that
+ * FlashCartPotential.forward runs before its interaction layers (model/flashcart.py:
+ * 264-286): get_edge_vectors (utils/geometry.py:25-53: v = r_j - r_i + S . cell[batch[i]],
+ * row 0 of edge_index = receiver i, row 1 = sender j), distances and directions
+ * v / max(|v|, 1e-4), Irreps(l_max).forward_normalized (o3/irreps.py:54-72), the
+ * ChebyshevBasis (nn/radial.py:98-128) times the PolynomialCutoff envelope
+ * (nn/radial.py:181-245) that InteractionLayer.forward multiplies into its radial-MLP
+ * input (nn/layers.py:351-356). Outputs: edge_attrs (n_edges, (l_max+1)^2) and radial
+ * (n_edges, n_radial) = basis * envelope, both row-major in the positions' dtype.
+ * positions (n_nodes, 3); cells (n_cells, 3, 3), cell rows are lattice vectors; shifts
+ * (n_edges, 3) int32 image counts (unused when use_shifts is 0); batch (n_nodes) graph of
+ * each atom (read only when n_cells > 1). An edge index (or graph index) out of range sets
+ * FC_DEV_BAD_INDEX; the edge's outputs are zero and it contributes no gradient. */
+typedef struct fc_edge_geometry_desc {
+  int32_t l_max;      /* rank of the edge attributes, 0..3 */
+  int32_t n_radial;   /* Chebyshev functions, 1..64 */
+  int32_t cosine;     /* 1: x = cos(pi t) ("cosine"), 0: x = 2t - 1 ("affine") */
+  int32_t poly_order; /* polynomial cutoff order p >= 2 */
+  int32_t use_shifts; /* 0: v = r_j - r_i (shifts and cells not read) */
+  int32_t dtype;      /* FC_F32 or FC_F64 */
+  double r_min;       /* Chebyshev range: t = (r - r_min) / (r_max - r_min) */
+  double r_max;
+  double r_cut;       /* envelope cutoff radius */
+} fc_edge_geometry_desc;
+
+int fc_edge_geometry_fwd(const fc_edge_geometry_desc* desc, const void* positions, int64_t n_nodes,
+                         const void* cells, int64_t n_cells, const int32_t* shifts, const int64_t* edge_index,
+                         const int64_t* batch, int64_t n_edges, void* edge_attrs, void* radial, int32_t* status,
+                         fc_stream_t stream);
+/* First derivative: grad_positions (n_nodes, 3) and grad_cells (n_cells, 3, 3; may be
+ * NULL) are zeroed by the call and receive the vector-Jacobian products of edge_attrs and
+ * radial with the given gradients (either may be NULL for zero). */
+int fc_edge_geometry_bwd(const fc_edge_geometry_desc* desc, const void* positions, int64_t n_nodes,
+                         const void* cells, int64_t n_cells, const int32_t* shifts, const int64_t* edge_index,
+                         const int64_t* batch, int64_t n_edges, const void* grad_attrs, const void* grad_radial,
+                         void* grad_positions, void* grad_cells, int32_t* status, fc_stream_t stream);
+
 /* ---------------------------------------------------------------- neighbour list
  * Periodic cell list of an orthorhombic cell on the GPU. Replaces the host neighbour
  * search that feeds the model (data/neighbors.py:120-143, matscipy neighbour_list("ijS"):

@@ -18,7 +18,8 @@ These tests check that path itself, not only the eager ``predict``:
   spread grows with N like sqrt(ln 3N) (1.34x from 192 to 27,648 atoms); measured on the
   B200 the float32 forces of this model are as accurate as the reference's (7.2e-5 vs
   6.5e-5 at 192 atoms, unchanged when the dense layers run on an fp32 SGEMM instead of
-  3xTF32), with a 99.9th percentile of 9e-5 at 27,648 atoms, which must stay within 1e-4.
+  3xTF32). The root-mean-square error, which does not grow with N, must stay within
+  twice the reference's own float32 RMS error on the 192-atom box.
 
 Replays and eager steps both scatter with atomics, so float32 results agree to rounding
 (relative 1e-5 of the largest value), not bit for bit.
@@ -97,8 +98,14 @@ def _errors(f32, f64, n):
     per_atom = (f32["forces"].double() - f64["forces"]).abs().max(dim=1).values.cpu()
     return {"energy_per_atom": (f32["energy"].double() - f64["energy"]).abs().max().item() / n,
             "forces": per_atom.max().item(),
-            "forces_p999": torch.quantile(per_atom, 0.999).item(),
+            "forces_rms": (f32["forces"].double() - f64["forces"]).pow(2).mean().sqrt().item(),
             "stress": (f32["stress"].double() - f64["stress"]).abs().max().item()}
+
+
+def _reference_force_rms(model_golden):
+    """The reference's own float32 force error (RMS over components) on the 192-atom box."""
+    d = model_golden["cfg3arch/f32/forces"] - model_golden["cfg3arch/f64/forces"]
+    return d.pow(2).mean().sqrt().item()
 
 
 def _force_bound(model_golden, n_atoms):
@@ -143,7 +150,7 @@ def test_full_size_replay_and_precision(model_golden, cuda_device):
     print("full-size float32 vs float64:", {k: f"{v:.3e}" for k, v in err.items()})
     assert err["energy_per_atom"] <= TOL["energy_per_atom"], err
     assert err["stress"] <= TOL["stress"], err
-    assert err["forces_p999"] <= TOL["forces"], err
+    assert err["forces_rms"] <= 2.0 * _reference_force_rms(model_golden), (err, _reference_force_rms(model_golden))
     assert err["forces"] <= _force_bound(model_golden, n), (err, _force_bound(model_golden, n))
     from flashcart_b200.ops import check_device_status
 
