@@ -203,15 +203,15 @@ def _profile_traffic(kernel: str):
     return None
 
 
-# water boxes of the CPU sample: molecules per lattice axis at the config-3 spacing and seed.
-# The float32 oracle port peaks near 24 MB of host memory per atom (37 GB at 1,536 atoms),
+# water boxes of the CPU sample: molecules per lattice axis at the benchmark box's spacing and seed.
+# The float32 oracle port peaks near 20 MB of host memory per atom (31 GB at 1,536 atoms),
 # so 3,072 atoms does not fit a 62 GB host and is not offered.
 CPU_BOXES = {192: (4, 4, 4), 1536: (8, 8, 8)}
 
 
 def cpu_reference_sample(steps: int, warmup: int, min_seconds: float = 0.0, atoms: int = 192):
     """The oracle port of the potential on the host cores: a water box of ``atoms`` atoms
-    (192 by default), config-3 architecture."""
+    (192 by default), the 128-channel rank <= 3 architecture of the benchmark."""
     from flashcart_b200.data import neighbors, synthetic
     from flashcart_b200.model.flashcart import FlashCartPotential
     from flashcart_b200.model.presets import water_model_kwargs
@@ -234,9 +234,16 @@ def cpu_reference_sample(steps: int, warmup: int, min_seconds: float = 0.0, atom
         n_done += 1
     dt = time.perf_counter() - t0
     n_atoms = len(s["positions"])
-    return {"value": n_atoms * n_done / dt, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n_done} E+F+S steps of a {n_atoms}-atom water box ({ei.shape[1]} edges) with the config-3 "
-                      f"architecture, float32, oracle port (torch CPU) on {cores} threads; per-atom rate"}, dt / n_done
+    rec = {"value": n_atoms * n_done / dt, "unit": UNIT, "cores": cores, "kind": "port",
+           "sample": f"{n_done} E+F+S steps of a {n_atoms}-atom water box ({ei.shape[1]} edges) with the 128-channel, "
+                     f"rank <= 3 architecture, float32, oracle port (torch CPU) on {cores} threads; per-atom rate"}
+    # how the port's speed compares with the reference's own PyTorch path (measured where the
+    # reference source is available, oracle/time_port_vs_reference.py)
+    cmp_path = os.path.join(ROOT, "oracle", "port_vs_reference_cpu.json")
+    if os.path.exists(cmp_path):
+        with open(cmp_path) as f:
+            rec["port_vs_reference_py"] = json.load(f)
+    return rec, dt / n_done
 
 
 # --------------------------------------------------------------------------------- arms
@@ -389,6 +396,22 @@ def run_b200(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max, e2e_max, eager_max = float(t[0]), float(t[1]), float(t[2])
+    ranks = None
+    if world > 1:
+        # what limits the scaling: per-rank step time (graphed), halo time (eager pass: pack,
+        # NCCL all-to-all, unpack, forward and backward) and each rank's share of the edges
+        halo_ms = sum(sum(v) for k, v in durs.items() if k.startswith("halo")) / args.steps
+        mine = torch.tensor([ms, eager_ms, halo_ms, float(plan.edge_index.shape[1]), float(plan.n_own),
+                             float(plan.n_ghost)], device=dev, dtype=torch.float64)
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        every = torch.stack(every).cpu()
+        ranks = {"step_ms": [round(float(v), 3) for v in every[:, 0]],
+                 "eager_ms": [round(float(v), 3) for v in every[:, 1]],
+                 "halo_ms_per_step": [round(float(v), 3) for v in every[:, 2]],
+                 "edges": [int(v) for v in every[:, 3]], "owned_atoms": [int(v) for v in every[:, 4]],
+                 "ghost_atoms": [int(v) for v in every[:, 5]],
+                 "edge_imbalance_max_over_min": float(every[:, 3].max() / every[:, 3].min())}
     graphed.release()
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -422,6 +445,8 @@ def run_b200(args):
             "kernels_ms_per_step": {k: sum(v) / args.steps for k, v in sorted(durs.items(),
                                                                                key=lambda kv: -sum(kv[1]))},
         }
+        if ranks is not None:
+            line["ranks"] = ranks
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -635,13 +660,14 @@ def run_config4(args):
     torch.manual_seed(0)
     student = FlashCartPotential(**kw, avg_neighbors=avg).to(dev)
     opts = training.make_optimizer(student)
+    buckets = training.GradientBuckets(student) if world > 1 else None
     batches = []
     for g in graphs:
         lab = teacher.predict(g, compute_forces=True)
         batches.append((g, lab["energy"].detach(), lab["forces"].detach()))
     n_atoms = [int(b[0]["positions"].shape[0]) for b in batches]
     for st in range(args.warmup):
-        training.train_step(student, *batches[st], opts)
+        training.train_step(student, *batches[st], opts, buckets=buckets)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -649,7 +675,7 @@ def run_config4(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for st in range(args.warmup, n_steps):
-        loss = training.train_step(student, *batches[st], opts)
+        loss = training.train_step(student, *batches[st], opts, buckets=buckets)
     e1.record()
     torch.cuda.synchronize()
     ops.check_device_status(dev)

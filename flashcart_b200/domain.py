@@ -67,6 +67,28 @@ class DomainPlan:
     recv_pos: List[torch.Tensor] = field(default_factory=list)   # per source: ghost rows
 
     @property
+    def send_all(self) -> torch.Tensor:
+        """Owned-local rows of every destination, concatenated in rank order (the send buffer)."""
+        if getattr(self, "_send_all", None) is None or self._send_all.device != self.owned.device:
+            self._send_all = torch.cat(self.send_idx) if self.send_idx else self.owned.new_zeros(0)
+        return self._send_all
+
+    @property
+    def recv_all(self) -> torch.Tensor:
+        """Ghost rows of every source, concatenated in rank order (the receive buffer)."""
+        if getattr(self, "_recv_all", None) is None or self._recv_all.device != self.owned.device:
+            self._recv_all = torch.cat(self.recv_pos) if self.recv_pos else self.owned.new_zeros(0)
+        return self._recv_all
+
+    @property
+    def send_splits(self) -> List[int]:
+        return [int(i.numel()) for i in self.send_idx]
+
+    @property
+    def recv_splits(self) -> List[int]:
+        return [int(p.numel()) for p in self.recv_pos]
+
+    @property
     def n_own(self) -> int:
         return int(self.owned.numel())
 
@@ -80,9 +102,11 @@ class DomainPlan:
 
     def to(self, device) -> "DomainPlan":
         mv = lambda t: t.to(device)
-        return DomainPlan(self.rank, self.world, self.grid, mv(self.owned), mv(self.ghosts), mv(self.edge_index),
-                          mv(self.shifts), mv(self.global_edges), [mv(t) for t in self.send_idx],
-                          [mv(t) for t in self.recv_pos])
+        p = DomainPlan(self.rank, self.world, self.grid, mv(self.owned), mv(self.ghosts), mv(self.edge_index),
+                       mv(self.shifts), mv(self.global_edges), [mv(t) for t in self.send_idx],
+                       [mv(t) for t in self.recv_pos])
+        p.send_all, p.recv_all  # concatenated index lists, built once on the device
+        return p
 
 
 def build_plans(positions, cell, edge_index, shifts, world: int) -> List[DomainPlan]:
@@ -146,40 +170,71 @@ def _all_to_all(recv: torch.Tensor, send: torch.Tensor, out_splits, in_splits, g
         dist.all_to_all_single(recv, send, out_splits, in_splits, group=group)
 
 
+def _pack(x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """Rows ``x[idx]`` as one contiguous send buffer: the device kernel (``fc_halo_pack``) for
+    CUDA tensors, torch indexing for the CPU ranks of the host tests."""
+    if x.is_cuda:
+        from flashcart_b200 import ops
+
+        return ops.halo_pack(x, idx)
+    return x.index_select(0, idx).contiguous()
+
+
+def _unpack(x: torch.Tensor, buf: torch.Tensor, idx: torch.Tensor, accumulate: bool) -> torch.Tensor:
+    """``x[idx] = buf`` or ``x[idx] += buf`` in place (``fc_halo_unpack`` on the GPU)."""
+    if x.is_cuda:
+        from flashcart_b200 import ops
+
+        return ops.halo_unpack_(x, buf, idx, accumulate)
+    if accumulate:
+        return x.index_add_(0, idx, buf)
+    x[idx] = buf
+    return x
+
+
+def _exchange(send: torch.Tensor, recv_rows: int, out_splits, in_splits, group) -> torch.Tensor:
+    recv = send.new_empty((recv_rows,) + tuple(send.shape[1:]))
+    if send.is_cuda:
+        from flashcart_b200 import ops
+
+        with ops.timed_region("halo_all_to_all", 2 * send.numel() * send.element_size()):
+            _all_to_all(recv, send, out_splits, in_splits, group)
+    else:
+        _all_to_all(recv, send, out_splits, in_splits, group)
+    return recv
+
+
 class HaloExchange(torch.autograd.Function):
     """Owned rows -> this rank's ghost rows over a process group (all-to-all with uneven
-    splits); backward sends the ghost gradients to their owners and adds them there."""
+    splits); backward sends the ghost gradients to their owners and adds them there. On
+    the GPU the rows are packed and unpacked by this library's kernels
+    (``fc_halo_pack`` / ``fc_halo_unpack``) and move over NCCL."""
 
     @staticmethod
     def forward(ctx, x_owned: torch.Tensor, plan: DomainPlan, group=None):
         ctx.plan, ctx.group, ctx.n_own = plan, group, x_owned.shape[0]
         rest = tuple(x_owned.shape[1:])
-        send = torch.cat([x_owned.index_select(0, i) for i in plan.send_idx]).contiguous()
-        out = x_owned.new_empty((plan.n_ghost,) + rest)
+        x_owned = x_owned.contiguous()
+        send = _pack(x_owned, plan.send_all)
         if plan.world == 1:
             recv = send
         else:
-            recv = x_owned.new_empty((sum(int(p.numel()) for p in plan.recv_pos),) + rest)
-            _all_to_all(recv, send, [int(p.numel()) for p in plan.recv_pos],
-                        [int(i.numel()) for i in plan.send_idx], group)
-        out[torch.cat(plan.recv_pos)] = recv
-        return out
+            recv = _exchange(send, sum(plan.recv_splits), plan.recv_splits, plan.send_splits, group)
+        out = x_owned.new_empty((plan.n_ghost,) + rest)
+        return _unpack(out, recv, plan.recv_all, accumulate=False)
 
     @staticmethod
     def backward(ctx, g_ghost: torch.Tensor):
         plan = ctx.plan
         g_ghost = g_ghost.contiguous()
         rest = tuple(g_ghost.shape[1:])
-        send = g_ghost.index_select(0, torch.cat(plan.recv_pos)).contiguous()
+        send = _pack(g_ghost, plan.recv_all)
         if plan.world == 1:
             recv = send
         else:
-            recv = g_ghost.new_empty((sum(int(i.numel()) for i in plan.send_idx),) + rest)
-            _all_to_all(recv, send, [int(i.numel()) for i in plan.send_idx],
-                        [int(p.numel()) for p in plan.recv_pos], ctx.group)
+            recv = _exchange(send, sum(plan.send_splits), plan.send_splits, plan.recv_splits, ctx.group)
         g_owned = g_ghost.new_zeros((ctx.n_own,) + rest)
-        g_owned.index_add_(0, torch.cat(plan.send_idx), recv)
-        return g_owned, None, None
+        return _unpack(g_owned, recv, plan.send_all, accumulate=True), None, None
 
 
 def halo(plan: DomainPlan, group=None) -> Callable[[torch.Tensor], torch.Tensor]:

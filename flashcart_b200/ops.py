@@ -1165,3 +1165,61 @@ def edge_geometry(positions: Tensor, cells: Tensor, shifts: Tensor, edge_index: 
     positions and cells (see :func:`first_order_only`)."""
     return edge_geometry_fwd(positions, cells, shifts, edge_index, batch, int(l_max), int(n_radial), bool(cosine),
                              int(poly_order), float(r_min), float(r_max), float(r_cut), bool(use_shifts))
+
+
+# --------------------------------------------------------------------------- halo exchange rows
+
+
+def halo_pack(x: Tensor, idx: Tensor) -> Tensor:
+    """``buf[k] = x[idx[k]]`` for rows of any width (``fc_halo_pack``): the send buffer of a
+    halo exchange, one coalesced row copy per index (reference semantics: the owner rows
+    that ``lammps_forward_exchange`` sends, ``utils/lammps.py:67-94``)."""
+    _require_cuda(x, idx)
+    xc = x.contiguous()
+    re = 1
+    for d in xc.shape[1:]:
+        re *= int(d)
+    buf = xc.new_empty((idx.numel(),) + tuple(xc.shape[1:]))
+    if idx.numel() == 0:
+        return buf
+    lib = N.lib()
+    with _timed("halo_pack", 1, _nbytes(buf) * 2):
+        rc = lib.fc_halo_pack(_p(xc), xc.shape[0], re, _code(xc.dtype), _p(idx), idx.numel(), _p(buf),
+                              _p(status_word(x.device)), _stream(x.device))
+    _after(lib, rc, "fc_halo_pack", x.device)
+    return buf
+
+
+def halo_unpack_(x: Tensor, buf: Tensor, idx: Tensor, accumulate: bool) -> Tensor:
+    """``x[idx[k]] = buf[k]`` (ghost rows receive their owners' features) or, with
+    ``accumulate``, ``x[idx[k]] += buf[k]`` (ghost gradients added to their owners;
+    ``lammps_reverse_exchange``, ``utils/lammps.py:96-118``), in place (``fc_halo_unpack``)."""
+    _require_cuda(x, buf, idx)
+    if idx.numel() == 0:
+        return x
+    if not x.is_contiguous():
+        raise ValueError("halo_unpack_: x must be contiguous")
+    b = buf.contiguous()
+    lib = N.lib()
+    re = 1
+    for d in b.shape[1:]:
+        re *= int(d)
+    with _timed("halo_unpack", 1, _nbytes(b) * 2):
+        rc = lib.fc_halo_unpack(_p(b), idx.numel(), re, _code(b.dtype), _p(idx), _p(x), x.shape[0],
+                                int(bool(accumulate)), _p(status_word(x.device)), _stream(x.device))
+    _after(lib, rc, "fc_halo_unpack", x.device)
+    return x
+
+
+class timed_region:
+    """CUDA-event timing of a host region under the kernel timer (e.g. a collective); it
+    counts no launch of this library."""
+
+    def __init__(self, name: str, nbytes: int = 0):
+        self._t = _timed(name, 0, nbytes)
+
+    def __enter__(self):
+        return self._t.__enter__()
+
+    def __exit__(self, *exc):
+        return self._t.__exit__(*exc)

@@ -165,8 +165,96 @@ def make_optimizer(model: nn.Module, lr: float = 1e-2, weight_decay: float = 1e-
     return main, aux
 
 
+class GradientBuckets:
+    """Bucketed gradient averaging overlapped with the backward pass (the DDP scheme that
+    Lightning Fabric applies in ``fabric.backward``, reference ``training/tasks.py:444``).
+
+    Parameters are grouped, in reverse registration order (the order in which their
+    gradients tend to become ready), into buckets of about ``bucket_bytes``. A hook after
+    each parameter's gradient accumulation copies the gradient into its bucket's flat
+    buffer; a full bucket starts its all-reduce asynchronously while the backward goes on.
+    Buckets start strictly in index order, so every rank issues the same collectives in the
+    same order whatever the order in which its gradients complete. :meth:`finish` (after
+    ``backward``) starts the buckets that are still pending (a parameter without gradient
+    counts as zeros), waits for all of them, averages and writes the gradients back.
+    CUDA tensors on a gloo group are staged through host memory (synchronously).
+    """
+
+    def __init__(self, model: nn.Module, group=None, bucket_bytes: int = 4 << 20):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        params = [p for p in model.parameters() if p.requires_grad]
+        self.buckets: List[List[nn.Parameter]] = []
+        cur, size = [], 0
+        for p in reversed(params):
+            cur.append(p)
+            size += p.numel() * p.element_size()
+            if size >= bucket_bytes:
+                self.buckets.append(cur)
+                cur, size = [], 0
+        if cur:
+            self.buckets.append(cur)
+        self.where = {id(p): b for b, ps in enumerate(self.buckets) for p in ps}
+        self._hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in params]
+        self._reset()
+
+    def _reset(self) -> None:
+        self.pending = [len(ps) for ps in self.buckets]
+        self.flat: List[Optional[torch.Tensor]] = [None] * len(self.buckets)
+        self.handles: List[Optional[object]] = [None] * len(self.buckets)
+        self.next = 0
+
+    def _fill(self, b: int) -> torch.Tensor:
+        ps = self.buckets[b]
+        ref = ps[0]
+        flat = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1) for p in ps])
+        return flat.to(ref.dtype)
+
+    def _launch_ready(self, force: bool = False) -> None:
+        while self.next < len(self.buckets) and (force or self.pending[self.next] == 0):
+            b = self.next
+            flat = self._fill(b)
+            if flat.is_cuda and dist.get_backend(self.group) == "gloo":
+                host = flat.cpu()
+                dist.all_reduce(host, group=self.group)
+                flat.copy_(host)
+                self.handles[b] = None
+            else:
+                self.handles[b] = dist.all_reduce(flat, group=self.group, async_op=True)
+            self.flat[b] = flat
+            self.next += 1
+
+    def _ready(self, p: torch.Tensor) -> None:
+        b = self.where[id(p)]
+        self.pending[b] -= 1
+        if self.world > 1:
+            self._launch_ready()
+
+    def finish(self) -> None:
+        if self.world > 1:
+            self._launch_ready(force=True)
+            for b, ps in enumerate(self.buckets):
+                if self.handles[b] is not None:
+                    self.handles[b].wait()
+                flat = self.flat[b] / self.world
+                off = 0
+                for p in ps:
+                    n = p.numel()
+                    if p.grad is not None:
+                        p.grad.copy_(flat[off:off + n].view_as(p))
+                    else:
+                        p.grad = flat[off:off + n].view_as(p).clone()
+                    off += n
+        self._reset()
+
+    def remove(self) -> None:
+        for h in self._hooks:
+            h.remove()
+
+
 def allreduce_gradients(model: nn.Module, group=None) -> None:
-    """Average the gradients over the ranks with one flat all-reduce."""
+    """Average the gradients over the ranks with one flat all-reduce (after the backward;
+    :class:`GradientBuckets` overlaps the same averaging with the backward)."""
     world = dist.get_world_size(group)
     if world == 1:
         return
@@ -188,14 +276,18 @@ def allreduce_gradients(model: nn.Module, group=None) -> None:
         off += n
 
 
-def train_step(model, graph, energy_label, forces_label, optimizers, group=None) -> torch.Tensor:
-    """Loss, backward (double backward through the forces), gradient all-reduce, updates."""
+def train_step(model, graph, energy_label, forces_label, optimizers, group=None,
+               buckets: Optional[GradientBuckets] = None) -> torch.Tensor:
+    """Loss, backward (double backward through the forces), gradient all-reduce (bucketed
+    and overlapped with the backward when ``buckets`` is given), updates."""
     main, aux = optimizers
     for opt in [main, *aux]:
         opt.zero_grad(set_to_none=True)
     loss, _ = energy_force_loss(model, graph, energy_label, forces_label)
     loss.backward()
-    if dist.is_available() and dist.is_initialized():
+    if buckets is not None:
+        buckets.finish()
+    elif dist.is_available() and dist.is_initialized():
         allreduce_gradients(model, group)
     for opt in [main, *aux]:
         opt.step()

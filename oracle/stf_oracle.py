@@ -224,6 +224,15 @@ def _rank_block(x: torch.Tensor, l: int, features: int) -> torch.Tensor:
     return x[:, start: start + (2 * l + 1) * features].reshape(x.shape[0], 2 * l + 1, features)
 
 
+def _rank_blocks(x: torch.Tensor, l_max: int, features: int) -> List[torch.Tensor]:
+    """All rank blocks of x as (rows, 2l+1, features) views from one split (columns past
+    the last full block, if any, are left out)."""
+    sizes = [(2 * l + 1) * features for l in range(l_max + 1)]
+    rest = x.shape[1] - sum(sizes)
+    parts = torch.split(x, sizes + ([rest] if rest > 0 else []), dim=1)
+    return [parts[l].reshape(x.shape[0], 2 * l + 1, features) for l in range(l_max + 1)]
+
+
 def tensor_product(in1, in2, weights, idx_i, idx_j, in1_l_max, in2_l_max, out_l_max, in1_features,
                    in2_features, symmetric_product=False, shared_weights=False, reduce_paths=False):
     """Weighted Cartesian tensor product, optionally as an edge convolution.
@@ -238,19 +247,30 @@ def tensor_product(in1, in2, weights, idx_i, idx_j, in1_l_max, in2_l_max, out_l_
     if conv:
         in1 = in1.index_select(0, idx_j)
     n = in1.shape[0]
+    n_out = n_nodes if conv else n
     F = max(in1_features, in2_features)
     paths = enumerate_paths(in1_l_max, in2_l_max, out_l_max, symmetric_product)
     per_l: List[List[torch.Tensor]] = [[] for _ in range(out_l_max + 1)]
+    # rank blocks split once (one backward concatenation instead of a zero-filled full-width
+    # gradient per sliced path)
+    split1 = _rank_blocks(in1, in1_l_max, in1_features)
+    split2 = _rank_blocks(in2, in2_l_max, in2_features)
+    wparts = torch.split(weights, F, dim=0 if shared_weights else 1)
     for p, (l1, l2, lo, swapped) in enumerate(paths):
         if swapped:
-            a = _rank_block(in2, l1, in2_features)
-            b = _rank_block(in1, l2, in1_features)
+            a = split2[l1]
+            b = split1[l2]
         else:
-            a = _rank_block(in1, l1, in1_features)
-            b = _rank_block(in2, l2, in2_features)
+            a = split1[l1]
+            b = split2[l2]
         y = _apply_path(path_coefficients(l1, l2, lo), a, b, n, F)
-        w = weights[p * F:(p + 1) * F] if shared_weights else weights[:, p * F:(p + 1) * F].unsqueeze(1)
-        per_l[lo].append(y * w)
+        w = wparts[p] if shared_weights else wparts[p].unsqueeze(1)
+        y = y * w
+        if conv:
+            # the sum over a receiver's edges, path by path (the same sum as scattering the
+            # stacked edge rows, without the edges x output-width intermediate)
+            y = y.new_zeros((n_nodes,) + tuple(y.shape[1:])).index_add(0, idx_i, y)
+        per_l[lo].append(y)
     blocks = []
     for lo, bucket in enumerate(per_l):
         if not bucket:
@@ -260,13 +280,8 @@ def tensor_product(in1, in2, weights, idx_i, idx_j, in1_l_max, in2_l_max, out_l_
         # as an empty sum (CSR grid over receivers, o3/_tensor_product.py:396-412); the
         # oracle gives that empty sum
         t = sum(bucket) if reduce_paths else torch.stack(bucket, dim=2)
-        blocks.append(t.reshape(n, math.prod(t.shape[1:])))
-    out = torch.cat(blocks, dim=-1) if blocks else in1.new_zeros(n, 0)
-    if conv:
-        res = out.new_zeros(n_nodes, out.shape[1])
-        res.index_add_(0, idx_i, out)
-        out = res
-    return out
+        blocks.append(t.reshape(n_out, math.prod(t.shape[1:])))
+    return torch.cat(blocks, dim=-1) if blocks else in1.new_zeros(n_out, 0)
 
 
 def irreps(x: torch.Tensor, l_max: int) -> torch.Tensor:

@@ -14,7 +14,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from flashcart_b200.training import allreduce_gradients, batch_graph, synthetic_molecules
+from flashcart_b200.training import GradientBuckets, allreduce_gradients, batch_graph, synthetic_molecules
 
 HERE = os.path.dirname(__file__)
 
@@ -86,35 +86,62 @@ def test_student_init_and_optimizer_routing_match_reference(train_golden):
     assert sorted(no_decay) == sorted(train_golden["routing/no_decay"])
 
 
-def _dp_worker(rank, world, port, outdir):
+def _net():
+    torch.manual_seed(0)
+    net = torch.nn.Sequential(torch.nn.Linear(3, 5), torch.nn.Tanh(), torch.nn.Linear(5, 4), torch.nn.Tanh(),
+                              torch.nn.Linear(4, 2))
+    net.register_parameter("unused", torch.nn.Parameter(torch.ones(3)))  # receives no gradient
+    return net
+
+
+def _loss(net, rank, step):
+    x = torch.arange(6.0).reshape(2, 3) + rank + 0.5 * step
+    return net(x).square().sum()
+
+
+def _dp_worker(rank, world, port, outdir, mode):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        torch.manual_seed(0)
-        lin = torch.nn.Linear(3, 2)
-        x = torch.arange(6.0).reshape(2, 3) + rank
-        lin(x).square().sum().backward()
-        allreduce_gradients(lin)
-        torch.save({k: p.grad for k, p in lin.named_parameters()}, os.path.join(outdir, f"g{rank}.pt"))
+        net = _net()
+        # tiny buckets: one parameter or two per bucket, started during the backward
+        buckets = GradientBuckets(net, bucket_bytes=64) if mode == "buckets" else None
+        out = []
+        for step in range(2):
+            net.zero_grad(set_to_none=True)
+            _loss(net, rank, step).backward()
+            if buckets is not None:
+                buckets.finish()
+            else:
+                allreduce_gradients(net)
+            out.append({k: (p.grad.clone() if p.grad is not None else None) for k, p in net.named_parameters()})
+        torch.save(out, os.path.join(outdir, f"g{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
-def test_gradient_allreduce_averages_over_ranks():
+@pytest.mark.parametrize("mode", ["flat", "buckets"])
+def test_gradient_allreduce_averages_over_ranks(mode):
+    """Gradient averaging over two gloo ranks, flat after the backward and bucketed during
+    it (two steps in a row, a parameter without gradient)."""
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_dp_worker, args=(2, 29800 + os.getpid() % 100, d), nprocs=2, start_method="spawn")
+        port = 29800 + os.getpid() % 100 + (7 if mode == "buckets" else 0)
+        mp.start_processes(_dp_worker, args=(2, port, d, mode), nprocs=2, start_method="spawn")
         got = [torch.load(os.path.join(d, f"g{r}.pt")) for r in range(2)]
-    ref = {}
-    for r in range(2):
-        torch.manual_seed(0)
-        lin = torch.nn.Linear(3, 2)
-        (lin(torch.arange(6.0).reshape(2, 3) + r)).square().sum().backward()
-        for k, p in lin.named_parameters():
-            ref[k] = ref.get(k, 0) + p.grad / 2
-    for g in got:
-        for k in ref:
-            assert torch.allclose(g[k], ref[k], atol=1e-6)
+    for step in range(2):
+        ref = {}
+        for r in range(2):
+            net = _net()
+            _loss(net, r, step).backward()
+            for k, p in net.named_parameters():
+                if p.grad is not None:
+                    ref[k] = ref.get(k, 0) + p.grad / 2
+        for g in got:
+            for k in ref:
+                assert torch.allclose(g[step][k], ref[k], atol=1e-6), (mode, step, k)
+            if mode == "buckets":
+                assert torch.equal(g[step]["unused"], torch.zeros(3))
 
 
 @pytest.mark.gpu
