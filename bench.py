@@ -56,6 +56,9 @@ def _args():
                          "figure, the 27,648-atom box itself does not fit host RAM in the reference py path)")
     ap.add_argument("--op-case", choices=["conv", "gemm"], default=None,
                     help="run one small operator case (for ncu captures) instead of the benchmark")
+    ap.add_argument("--allreduce", choices=["buckets", "flat"], default="buckets",
+                    help="data-parallel training: gradient all-reduce in buckets during the backward, or one "
+                         "flat all-reduce after it")
     ap.add_argument("--config", type=int, choices=[1, 2, 3, 4], default=3,
                     help="3: the headline E+F+S step; 1: the isolated TP convolution microbenchmark; "
                          "2: edge expansion + equivariant linear map (one GPU, one JSON line); "
@@ -660,7 +663,7 @@ def run_config4(args):
     torch.manual_seed(0)
     student = FlashCartPotential(**kw, avg_neighbors=avg).to(dev)
     opts = training.make_optimizer(student)
-    buckets = training.GradientBuckets(student) if world > 1 else None
+    buckets = training.GradientBuckets(student) if (world > 1 and args.allreduce == "buckets") else None
     batches = []
     for g in graphs:
         lab = teacher.predict(g, compute_forces=True)
@@ -693,7 +696,8 @@ def run_config4(args):
             "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "dtype": "f32", "data": "synthetic",
             "atom_steps_per_s": atoms / max(args.steps, 1) / (ms_max * 1e-3), "final_loss": float(loss),
             "config": {"workload": "data-parallel training", "molecules_per_gpu": 32, "parallelism": f"dp{world}",
-                       "model": "config-0 architecture, elements H/C/N/O"},
+                       "allreduce": args.allreduce if world > 1 else "none",
+                       "model": "64 channels, ranks <= 2 (the 192-atom CPU run's architecture), elements H/C/N/O"},
         }), flush=True)
     if world > 1:
         dist.barrier()
