@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "fc_edge_expand_fwd", "fc_edge_expand_bwd",
     "fc_linear_presplit", "fc_linear_fwd_presplit", "fc_linear_bwd_presplit",
     "fc_linear_dbwd", "fc_halo_pack", "fc_halo_unpack", "fc_edge_geometry_fwd", "fc_edge_geometry_bwd",
+    "fc_edge_geometry_vec_fwd", "fc_edge_geometry_vec_bwd",
 )
 
 
@@ -151,6 +152,10 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_edge_geometry_bwd.restype = ctypes.c_int
     lib.fc_edge_geometry_bwd.argtypes = [ctypes.POINTER(EdgeGeometryDesc), _P, _I64, _P, _I64, _P, _P, _P, _I64, _P,
                                          _P, _P, _P, _P, _P]
+    lib.fc_edge_geometry_vec_fwd.restype = ctypes.c_int
+    lib.fc_edge_geometry_vec_fwd.argtypes = [ctypes.POINTER(EdgeGeometryDesc), _P, _I64, _P, _P, _P, _P]
+    lib.fc_edge_geometry_vec_bwd.restype = ctypes.c_int
+    lib.fc_edge_geometry_vec_bwd.argtypes = [ctypes.POINTER(EdgeGeometryDesc), _P, _I64, _P, _P, _P, _P, _P]
     lib.fc_gate_fwd.restype = ctypes.c_int
     lib.fc_gate_fwd.argtypes = [_I32, _I32, _I32, _P, _P, _I64, _P, _P]
     lib.fc_gate_bwd.restype = ctypes.c_int

@@ -18,6 +18,11 @@
 //
 // One thread per edge, grid-stride; an index outside [0, n_nodes) flags FC_DEV_BAD_INDEX
 // and the edge gives zeros (forward) / no gradient (backward).
+//
+// Vectors-given mode (fc_edge_geometry_vec_fwd/bwd): the caller supplies v per edge (the
+// LAMMPS ML-IAP rij, calculators/lammps_mliap.py:122-170) and the backward writes dE/dv
+// per edge, the pair forces that ML-IAP takes (lammps_mliap.py:711-738), with plain
+// stores instead of the receiver / sender scatter.
 #include "fc_base.cuh"
 #include "gen/irreps_poly.cuh"
 
@@ -49,6 +54,11 @@ FC_HD FC_INLINE double fc_sqrt(double x) { return sqrt(x); }
 template <typename T>
 FC_HD FC_INLINE bool geom_vector(const GeomParams& p, const T* pos, const T* cells, const int32_t* shifts,
                                  const int64_t* ei, const int64_t* batch, int64_t e, T* v, int64_t* ij_b) {
+  if (p.vectors_given) {  // v supplied per edge (LAMMPS rij): no atoms, shifts or cells
+    for (int c = 0; c < 3; ++c) v[c] = pos[3 * e + c];
+    ij_b[0] = ij_b[1] = e; ij_b[2] = 0;
+    return true;
+  }
   const int64_t i = ei[e], j = ei[p.n_edges + e];
   if (i < 0 || i >= p.n_nodes || j < 0 || j >= p.n_nodes) {
     v[0] = v[1] = v[2] = T(0);
@@ -196,6 +206,16 @@ __global__ void __launch_bounds__(256) geom_bwd_kernel(GeomParams p, const T* po
                                                        const int32_t* shifts, const int64_t* ei, const int64_t* batch,
                                                        const T* g_attrs, const T* g_radial, T* g_pos, T* g_cells,
                                                        int* status) {
+  if (p.vectors_given) {  // gradient per edge vector: one plain store per edge, no scatter
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < p.n_edges;
+         e += (int64_t)gridDim.x * blockDim.x) {
+      T gv[3] = {T(0), T(0), T(0)};
+      int64_t ijb[3];
+      geom_bwd_one<T, L>(p, pos, cells, shifts, ei, batch, g_attrs, g_radial, status, e, gv, ijb);
+      for (int k = 0; k < 3; ++k) g_pos[3 * e + k] = gv[k];
+    }
+    return;
+  }
   const int lane = threadIdx.x & 31;
   // one cell: every edge adds into the same nine cell-gradient values, so each thread
   // keeps its sum in registers and the CTA reduces once at the end (per-warp atomics on
@@ -316,6 +336,10 @@ int geom_bwd_l(const GeomParams& p, const T* pos, const T* cells, const int32_t*
     T gv[3];
     int64_t ijb[3];
     if (!geom_bwd_one<T, L>(p, pos, cells, shifts, ei, batch, g_attrs, g_radial, status, e, gv, ijb)) continue;
+    if (p.vectors_given) {
+      for (int k = 0; k < 3; ++k) g_pos[3 * e + k] = gv[k];
+      continue;
+    }
     for (int k = 0; k < 3; ++k) {
       g_pos[3 * ijb[1] + k] += gv[k];
       g_pos[3 * ijb[0] + k] -= gv[k];

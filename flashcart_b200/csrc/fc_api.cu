@@ -945,6 +945,7 @@ static int geom_check(const fc_edge_geometry_desc* d, int64_t n_nodes, int64_t n
   p->poly_order = d->poly_order; p->use_shifts = d->use_shifts ? 1 : 0;
   p->r_min = d->r_min; p->r_max = d->r_max; p->r_cut = d->r_cut;
   p->n_nodes = n_nodes; p->n_edges = n_edges; p->n_cells = n_cells;
+  p->vectors_given = 0;
   return FC_OK;
 }
 
@@ -995,6 +996,52 @@ int fc_edge_geometry_bwd(const fc_edge_geometry_desc* desc, const void* position
                                                  batch, (const double*)grad_attrs, (const double*)grad_radial,
                                                  (double*)grad_positions, (double*)grad_cells, st, s),
                        "fc_edge_geometry_bwd");
+}
+
+int fc_edge_geometry_vec_fwd(const fc_edge_geometry_desc* desc, const void* vectors, int64_t n_edges,
+                             void* edge_attrs, void* radial, int32_t* status, fc_stream_t stream) {
+  GeomParams p;
+  if (int rc = geom_check(desc, 0, 0, n_edges, "fc_edge_geometry_vec_fwd", &p)) return rc;
+  if (n_edges == 0) return FC_OK;
+  if (!vectors || !edge_attrs || !radial) return fail(FC_ERR_INVALID, "fc_edge_geometry_vec_fwd: null pointer");
+  p.use_shifts = 0;
+  p.vectors_given = 1;
+  const cudaStream_t s = (cudaStream_t)stream;
+  int* st = reinterpret_cast<int*>(status);
+  if (desc->dtype == FC_F32)
+    return launch_status(geom_fwd_dispatch<float>(p, (const float*)vectors, nullptr, nullptr, nullptr, nullptr,
+                                                  (float*)edge_attrs, (float*)radial, st, s),
+                         "fc_edge_geometry_vec_fwd");
+  return launch_status(geom_fwd_dispatch<double>(p, (const double*)vectors, nullptr, nullptr, nullptr, nullptr,
+                                                 (double*)edge_attrs, (double*)radial, st, s),
+                       "fc_edge_geometry_vec_fwd");
+}
+
+int fc_edge_geometry_vec_bwd(const fc_edge_geometry_desc* desc, const void* vectors, int64_t n_edges,
+                             const void* grad_attrs, const void* grad_radial, void* grad_vectors, int32_t* status,
+                             fc_stream_t stream) {
+  GeomParams p;
+  if (int rc = geom_check(desc, 0, 0, n_edges, "fc_edge_geometry_vec_bwd", &p)) return rc;
+  if (n_edges == 0) return FC_OK;
+  if (!vectors || !grad_vectors) return fail(FC_ERR_INVALID, "fc_edge_geometry_vec_bwd: null pointer");
+  p.use_shifts = 0;
+  p.vectors_given = 1;
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (!grad_attrs && !grad_radial) {
+    const int esz = desc->dtype == FC_F32 ? 4 : 8;
+    if (zero_fill(grad_vectors, n_edges * 3 * esz, s)) return launch_status(FC_ERR_LAUNCH, "fc_edge_geometry_vec_bwd");
+    return FC_OK;
+  }
+  int* st = reinterpret_cast<int*>(status);
+  if (desc->dtype == FC_F32)
+    return launch_status(geom_bwd_dispatch<float>(p, (const float*)vectors, nullptr, nullptr, nullptr, nullptr,
+                                                  (const float*)grad_attrs, (const float*)grad_radial,
+                                                  (float*)grad_vectors, nullptr, st, s),
+                         "fc_edge_geometry_vec_bwd");
+  return launch_status(geom_bwd_dispatch<double>(p, (const double*)vectors, nullptr, nullptr, nullptr, nullptr,
+                                                 (const double*)grad_attrs, (const double*)grad_radial,
+                                                 (double*)grad_vectors, nullptr, st, s),
+                       "fc_edge_geometry_vec_bwd");
 }
 
 // ------------------------------------------------------------------ neighbour list

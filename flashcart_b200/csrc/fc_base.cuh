@@ -125,6 +125,7 @@ inline int fc_round_up(int x, int m) { return (x + m - 1) / m * m; }
 // Parameters of the fused edge-geometry kernels (edge_geometry.cu, fc_edge_geometry_*).
 struct GeomParams {
   int l_max, n_radial, cosine, poly_order, use_shifts;
+  int vectors_given;  // positions holds the (n_edges, 3) edge vectors themselves
   double r_min, r_max, r_cut;
   int64_t n_nodes, n_edges, n_cells;
 };

@@ -64,6 +64,9 @@ constexpr long long WAIT_LIMIT = 1ll << 22;
 #ifndef FC_TMA_KG
 #define FC_TMA_KG 4
 #endif
+#ifndef FC_TMA_ATM64
+#define FC_TMA_ATM64 1
+#endif
 constexpr int KG = FC_TMA_KG;
 constexpr int PF_SLABS = 4;   // k slabs per L2 prefetch box (512 bytes of each row)
 #ifndef FC_TMA_PF_AHEAD
@@ -78,10 +81,10 @@ struct Cfg {
   // ATM: the splitters write the tf32 hi / lo parts of A into tensor memory and the MMAs
   // read A from there, so shared memory carries A once (TMA in, splitters out) instead of
   // five times (TMA in, splitters in / hi out / lo out, three MMA reads). Taken for
-  // BN = 128 (the node-level maps: measured 10-38% faster). BN = 64 (long k, the radial
-  // input gradient) measured 6% slower with it, with 4 or 6 stages; BN = 256 tiles
-  // (k <= 64) keep A in shared memory and all of tensor memory for accumulators.
-  static constexpr bool ATM = BN == 128;
+  // BN = 128 (the node-level maps: measured 10-38% faster) and BN = 64 (the radial input
+  // gradient 2944 -> 64 on 1.49 M rows: 6.08 -> 5.79 ms); BN = 256 tiles (k <= 64) keep A
+  // in shared memory and all of tensor memory for accumulators.
+  static constexpr bool ATM = BN == 128 || (BN == 64 && FC_TMA_ATM64);
   static constexpr int STAGE = ATM ? TILE_A + 2 * TILE_B : 2 * TILE_A + 2 * TILE_B;
   static constexpr int STAGES = ATM ? 4 : RING_BYTES / STAGE;
   static constexpr int A_COLS = ATM ? STAGES * 2 * BK : 0;  // tensor-memory A stages: hi | lo columns

@@ -204,6 +204,36 @@ def _exchange(send: torch.Tensor, recv_rows: int, out_splits, in_splits, group) 
     return recv
 
 
+def ghost_rows_from_owners(x_owned: torch.Tensor, plan: DomainPlan, group=None,
+                           out: torch.Tensor = None) -> torch.Tensor:
+    """Forward exchange: this rank's ghost rows (``plan.ghosts`` order) from the owned rows
+    of every rank; ``out`` (n_ghost, ...) contiguous is written in place when given."""
+    x_owned = x_owned.contiguous()
+    send = _pack(x_owned, plan.send_all)
+    if plan.world == 1:
+        recv = send
+    else:
+        recv = _exchange(send, sum(plan.recv_splits), plan.recv_splits, plan.send_splits, group)
+    if out is None:
+        out = x_owned.new_empty((plan.n_ghost,) + tuple(x_owned.shape[1:]))
+    return _unpack(out, recv, plan.recv_all, accumulate=False)
+
+
+def owners_from_ghost_rows(g_ghost: torch.Tensor, plan: DomainPlan, group=None,
+                           out_owned: torch.Tensor = None) -> torch.Tensor:
+    """Reverse exchange: ghost rows travel to their owners and are added into the owned
+    rows (``out_owned`` (n_own, ...) contiguous, accumulated in place; zeros when None)."""
+    g_ghost = g_ghost.contiguous()
+    send = _pack(g_ghost, plan.recv_all)
+    if plan.world == 1:
+        recv = send
+    else:
+        recv = _exchange(send, sum(plan.send_splits), plan.send_splits, plan.recv_splits, group)
+    if out_owned is None:
+        out_owned = g_ghost.new_zeros((plan.n_own,) + tuple(g_ghost.shape[1:]))
+    return _unpack(out_owned, recv, plan.send_all, accumulate=True)
+
+
 class HaloExchange(torch.autograd.Function):
     """Owned rows -> this rank's ghost rows over a process group (all-to-all with uneven
     splits); backward sends the ghost gradients to their owners and adds them there. On
@@ -212,29 +242,12 @@ class HaloExchange(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x_owned: torch.Tensor, plan: DomainPlan, group=None):
-        ctx.plan, ctx.group, ctx.n_own = plan, group, x_owned.shape[0]
-        rest = tuple(x_owned.shape[1:])
-        x_owned = x_owned.contiguous()
-        send = _pack(x_owned, plan.send_all)
-        if plan.world == 1:
-            recv = send
-        else:
-            recv = _exchange(send, sum(plan.recv_splits), plan.recv_splits, plan.send_splits, group)
-        out = x_owned.new_empty((plan.n_ghost,) + rest)
-        return _unpack(out, recv, plan.recv_all, accumulate=False)
+        ctx.plan, ctx.group = plan, group
+        return ghost_rows_from_owners(x_owned, plan, group)
 
     @staticmethod
     def backward(ctx, g_ghost: torch.Tensor):
-        plan = ctx.plan
-        g_ghost = g_ghost.contiguous()
-        rest = tuple(g_ghost.shape[1:])
-        send = _pack(g_ghost, plan.recv_all)
-        if plan.world == 1:
-            recv = send
-        else:
-            recv = _exchange(send, sum(plan.send_splits), plan.send_splits, plan.recv_splits, ctx.group)
-        g_owned = g_ghost.new_zeros((ctx.n_own,) + rest)
-        return _unpack(g_owned, recv, plan.send_all, accumulate=True), None, None
+        return owners_from_ghost_rows(g_ghost, ctx.plan, ctx.group), None, None
 
 
 def halo(plan: DomainPlan, group=None) -> Callable[[torch.Tensor], torch.Tensor]:

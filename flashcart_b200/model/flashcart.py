@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import contextlib
 from collections.abc import Mapping
+from pathlib import Path
 from typing import Callable, Any, Dict, List, Optional
 
 import torch
@@ -170,7 +171,23 @@ class FlashCartPotential(nn.Module):
         use_shifts = graph.get("use_shifts", True)
         if not isinstance(use_shifts, bool):
             use_shifts = _uses_shifts(use_shifts)
-        if vectors is None and self._geometry_fusable(graph):
+        # the next layer's senders: owned rows -> owned + ghost rows
+        exchange: Optional[Callable[[torch.Tensor], torch.Tensor]] = None
+        if bool(graph.get("lammps_exchange", False)):
+            # LAMMPS ML-IAP layout (reference model/flashcart.py:255-301): owned atoms first,
+            # then ghosts; batch covers the owned atoms, atom_types all of them, and the
+            # ghost rows come from the ML-IAP forward exchange between layers
+            from flashcart_b200.lammps import lammps_exchange_features
+
+            n_out = int(batch.shape[0])
+            n_total = int(atom_types.shape[0])
+            exchange = lambda x: lammps_exchange_features(x, n_out, n_total)
+        elif halo_fn is not None:
+            exchange = lambda x: torch.cat([x, halo_fn(x)], dim=0)
+        if vectors is not None and self._vectors_fusable(vectors):
+            edge_attrs, edge_feats = ops.edge_geometry_vec(vectors, self.irreps.l_max, *self._geometry_args)
+            envelope = None
+        elif vectors is None and self._geometry_fusable(graph):
             # one kernel from positions to edge attributes and enveloped radial features
             # (same arithmetic as the chain below; first derivative only)
             edge_attrs, edge_feats = ops.edge_geometry(graph["positions"], graph["cell"], graph["shifts"], edge_index,
@@ -200,8 +217,8 @@ class FlashCartPotential(nn.Module):
             else:
                 node_feats = feats
             outputs.append(node_feats[:, :self.n_hidden_feats])
-            if halo_fn is not None and i + 1 < len(self.interactions):
-                node_feats = torch.cat([node_feats, halo_fn(node_feats)], dim=0)
+            if exchange is not None and i + 1 < len(self.interactions):
+                node_feats = exchange(node_feats)
         energies = self.readout(outputs)
         return self.scale_shift(energies, own_types)
 
@@ -217,70 +234,103 @@ class FlashCartPotential(nn.Module):
                 and pos.dtype in (torch.float32, torch.float64) and torch.is_tensor(cell)
                 and self.irreps.l_max <= 3 and all(inter.emb_i is None for inter in self.interactions))
 
+    def _vectors_fusable(self, vectors) -> bool:
+        """The vectors-given form of the fused geometry kernel (LAMMPS ``rij``) under the
+        same conditions as :meth:`_geometry_fusable`."""
+        return (ops.first_order_only_active() and torch.is_tensor(vectors) and vectors.is_cuda
+                and vectors.dtype in (torch.float32, torch.float64) and self.irreps.l_max <= 3
+                and all(inter.emb_i is None for inter in self.interactions))
+
     # ------------------------------------------------------------------ predict
 
     def predict(self, graph, compute_forces: bool = False, compute_stress: bool = False,
-                create_graph: Optional[bool] = False) -> Dict[str, torch.Tensor]:
+                create_graph: Optional[bool] = False, compute_edge_forces: bool = False) -> Dict[str, torch.Tensor]:
         """Energies and requested derivatives (reference ``model/atomistic.py:75-340``).
 
         Returns ``node_energies`` (N,), ``energy`` (G,), and when requested ``forces``
-        (N, 3) = -dE/dR, ``stress`` (G, 6) = (dE/dD)/det(cell) in Voigt order and
+        (N, 3) = -dE/dR, ``stress`` (G, 6) = (dE/dD)/det(cell) in Voigt order,
         ``virials`` = -stress * volume, D being a symmetric virtual strain applied to
-        positions and cell.
+        positions and cell, and ``edge_forces`` (E, 3) = dE/dv of the graph's ``vectors``.
         """
-        if create_graph is False and (compute_forces or compute_stress):
+        if create_graph is False and (compute_forces or compute_stress or compute_edge_forces):
             # Forces and stress need derivatives with respect to the geometry only; with the
             # parameters frozen the operators skip their weight gradients (identical results).
             frozen = [p for p in self.parameters() if p.requires_grad]
             for p in frozen:
                 p.requires_grad_(False)
             try:
-                return self.predict(graph, compute_forces, compute_stress, create_graph=None)
+                return self.predict(graph, compute_forces, compute_stress, create_graph=None,
+                                    compute_edge_forces=compute_edge_forces)
             finally:
                 for p in frozen:
                     p.requires_grad_(True)
         create_graph = bool(create_graph)
+        g = self._prepare_predict_graph(graph, compute_forces, compute_stress, compute_edge_forces)
+        return self._predict_impl(g, compute_forces, compute_stress, compute_edge_forces, create_graph)
+
+    def _prepare_predict_graph(self, graph, compute_forces: bool, compute_stress: bool,
+                               compute_edge_forces: bool) -> Dict[str, Any]:
+        """Graph fields for the requested derivatives (reference ``model/atomistic.py:158-240``):
+        detached positions (strained for the stress, requiring grad for forces), the strain
+        ``displacement``, and detached ``vectors`` requiring grad for edge forces."""
         g = dict(graph.to_dict() if hasattr(graph, "to_dict") else graph)
         g["use_shifts"] = _uses_shifts(g.get("use_shifts", g.get("pbc")))
-        positions = g["positions"].detach()
-        cell = g["cell"].detach() if torch.is_tensor(g.get("cell")) else None
-        displacement = None
-        if compute_stress:
-            if cell is None:
-                raise ValueError("Cannot compute stress without cell information.")
-            displacement = torch.zeros_like(cell).requires_grad_(True)
-            sym = 0.5 * (displacement + displacement.transpose(-1, -2))
-            scaling = torch.eye(3, device=cell.device, dtype=cell.dtype).unsqueeze(0) + sym
-            if scaling.shape[0] == 1:
-                positions = rows_times_3x3(positions, scaling[0])
-            else:
-                per_atom = scaling.index_select(0, g["batch"])
-                positions = torch.bmm(positions.unsqueeze(-2), per_atom).squeeze(-2)
-            cell = cell @ scaling
-        if compute_forces:
-            positions.requires_grad_(True)
-        g["positions"] = positions
-        g["cell"] = cell
+        if compute_forces or compute_stress or torch.is_tensor(g.get("positions")):
+            positions = g["positions"].detach()
+            cell = g["cell"].detach() if torch.is_tensor(g.get("cell")) else None
+            if compute_stress:
+                if cell is None:
+                    raise ValueError("Cannot compute stress without cell information.")
+                displacement = torch.zeros_like(cell).requires_grad_(True)
+                sym = 0.5 * (displacement + displacement.transpose(-1, -2))
+                scaling = torch.eye(3, device=cell.device, dtype=cell.dtype).unsqueeze(0) + sym
+                if scaling.shape[0] == 1:
+                    positions = rows_times_3x3(positions, scaling[0])
+                else:
+                    per_atom = scaling.index_select(0, g["batch"])
+                    positions = torch.bmm(positions.unsqueeze(-2), per_atom).squeeze(-2)
+                cell = cell @ scaling
+                g["displacement"] = displacement
+            if compute_forces:
+                positions.requires_grad_(True)
+            g["positions"] = positions
+            g["cell"] = cell
+        if compute_edge_forces:
+            vectors = g.get("vectors")
+            if vectors is None:
+                raise ValueError("Cannot compute edge forces without graph.vectors.")
+            g["vectors"] = vectors.detach().requires_grad_(True)
+        return g
+
+    def _predict_impl(self, g: Dict[str, Any], compute_forces: bool, compute_stress: bool,
+                      compute_edge_forces: bool, create_graph: bool) -> Dict[str, torch.Tensor]:
+        """Energies and derivatives of a prepared graph (reference ``model/atomistic.py:276-340``);
+        the LAMMPS interface calls it directly with differentiable ``vectors``."""
         # without create_graph the graph is differentiated once: fused first-order kernels
-        # (RMS layer norm) may replace their composed, twice-differentiable forms
+        # (RMS layer norm, edge geometry) may replace their composed, twice-differentiable forms
         with ops.first_order_only() if not create_graph else contextlib.nullcontext():
             node_energies = self(g)
             n_graphs = int(g["n_atoms"].shape[0]) if "n_atoms" in g else int(g["batch"].max().item()) + 1
             energy = torch.zeros(n_graphs, dtype=node_energies.dtype, device=node_energies.device)
             energy = energy.index_add(0, g["batch"], node_energies)
             out = {"node_energies": node_energies, "energy": energy}
-            inputs = ([positions] if compute_forces else []) + ([displacement] if compute_stress else [])
-            grads = torch.autograd.grad(energy.sum(), inputs, create_graph=create_graph) if inputs else None
+            inputs = (([g["positions"]] if compute_forces else []) + ([g["displacement"]] if compute_stress else [])
+                      + ([g["vectors"]] if compute_edge_forces else []))
+            grads = (torch.autograd.grad(energy.sum(), inputs, create_graph=create_graph,
+                                         allow_unused=compute_edge_forces) if inputs else None)
         if inputs:
             k = 0
             if compute_forces:
                 out["forces"] = -grads[0]
                 k = 1
             if compute_stress:
-                volume = torch.det(cell)
+                volume = torch.det(g["cell"])
                 stress = to_voigt6(grads[k] / volume.view(-1, 1, 1))
                 out["stress"] = stress
                 out["virials"] = -stress * volume.unsqueeze(-1)
+                k += 1
+            if compute_edge_forces:
+                out["edge_forces"] = grads[k] if grads[k] is not None else torch.zeros_like(g["vectors"])
             if not create_graph:
                 out["node_energies"] = out["node_energies"].detach()
                 out["energy"] = out["energy"].detach()
@@ -353,3 +403,44 @@ class FlashCartPotential(nn.Module):
                         avg_neighbors=None, use_triton=False, recompute_radial=False)
         kw = {k: cfg.get(k, v) for k, v in defaults.items()}
         return cls(elements=cfg["elements"], r_max=cfg["r_max"], **kw)
+
+    # ------------------------------------------------------------------ checkpoints
+    # Inference checkpoint directory of the reference (model/atomistic.py:15-47, 441-527):
+    # ``model.pt`` (state dict), ``model_config.yaml`` (to_model_config), optional ``meta.yaml``.
+
+    def save_weights(self, path, filename: str = "model.pt") -> None:
+        path = Path(path)
+        path.mkdir(parents=True, exist_ok=True)
+        torch.save(self.state_dict(), path / filename)
+
+    def load_weights(self, path, filename: str = "model.pt", map_location="cpu") -> None:
+        self.load_state_dict(torch.load(Path(path) / filename, weights_only=True, map_location=map_location))
+
+    def save_inference_checkpoint(self, path, meta: Optional[Dict[str, Any]] = None) -> None:
+        import yaml
+
+        path = Path(path)
+        self.save_weights(path)
+        with open(path / "model_config.yaml", "w") as f:
+            yaml.safe_dump(self.to_model_config(), f, sort_keys=False)
+        if meta is not None:
+            with open(path / "meta.yaml", "w") as f:
+                yaml.safe_dump(meta, f, sort_keys=False)
+
+    @classmethod
+    def load_model_config(cls, ckpt_dir) -> Dict[str, Any]:
+        import yaml
+
+        cfg = Path(ckpt_dir) / "model_config.yaml"
+        if not cfg.exists():
+            raise FileNotFoundError(f"No model_config.yaml in {ckpt_dir}.")
+        with open(cfg) as f:
+            return yaml.safe_load(f)
+
+    @classmethod
+    def from_checkpoint(cls, ckpt_dir, device=None, map_location="cpu") -> "FlashCartPotential":
+        model = cls.from_config(cls.load_model_config(ckpt_dir))
+        model.load_weights(ckpt_dir, map_location=map_location)
+        if device is not None:
+            model = model.to(device)
+        return model.eval()

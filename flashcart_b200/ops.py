@@ -1167,19 +1167,111 @@ def edge_geometry(positions: Tensor, cells: Tensor, shifts: Tensor, edge_index: 
                              int(poly_order), float(r_min), float(r_max), float(r_cut), bool(use_shifts))
 
 
+def _vec_input(vectors: Tensor) -> Tensor:
+    if vectors.dtype not in (torch.float32, torch.float64):
+        raise ValueError(f"edge_geometry_vec supports float32 / float64 vectors, got {vectors.dtype}")
+    if vectors.dim() != 2 or vectors.shape[1] != 3:
+        raise ValueError(f"edge_geometry_vec: vectors must be (E, 3), got {tuple(vectors.shape)}")
+    return vectors.contiguous()
+
+
+@torch.library.custom_op("flashcart::edge_geometry_vec_fwd", mutates_args=())
+def edge_geometry_vec_fwd(vectors: Tensor, l_max: int, n_radial: int, cosine: bool, poly_order: int, r_min: float,
+                          r_max: float, r_cut: float) -> Tuple[Tensor, Tensor]:
+    """:func:`edge_geometry_fwd` of edge vectors given per edge (the LAMMPS ML-IAP ``rij``,
+    reference ``calculators/lammps_mliap.py:122-170``; the ``vectors`` branch of
+    ``model/flashcart.py:264-286``)."""
+    _require_cuda(vectors)
+    v = _vec_input(vectors)
+    e = v.shape[0]
+    attrs = v.new_empty((e, (l_max + 1) ** 2))
+    radial = v.new_empty((e, n_radial))
+    lib = N.lib()
+    d = _geom_desc(l_max, n_radial, cosine, poly_order, False, v.dtype, r_min, r_max, r_cut)
+    with _timed("edge_geometry_fwd", 1, _nbytes(v, attrs, radial)):
+        rc = lib.fc_edge_geometry_vec_fwd(ctypes.byref(d), _p(v), e, _p(attrs), _p(radial),
+                                          _p(status_word(v.device)), _stream(v.device))
+    _after(lib, rc, "fc_edge_geometry_vec_fwd", v.device)
+    return attrs, radial
+
+
+@edge_geometry_vec_fwd.register_fake
+def _(vectors, l_max, n_radial, cosine, poly_order, r_min, r_max, r_cut):
+    e = vectors.shape[0]
+    return vectors.new_empty((e, (l_max + 1) ** 2)), vectors.new_empty((e, n_radial))
+
+
+@torch.library.custom_op("flashcart::edge_geometry_vec_bwd", mutates_args=())
+def edge_geometry_vec_bwd(grad_attrs: Tensor, grad_radial: Tensor, vectors: Tensor, l_max: int, n_radial: int,
+                          cosine: bool, poly_order: int, r_min: float, r_max: float, r_cut: float) -> Tensor:
+    """dE/dv per edge (E, 3) from the gradients of :func:`edge_geometry_vec_fwd`'s outputs
+    (an empty gradient tensor stands for zero): the LAMMPS pair forces."""
+    _require_cuda(vectors)
+    v = _vec_input(vectors)
+    ga = grad_attrs.contiguous() if grad_attrs.numel() else None
+    gr = grad_radial.contiguous() if grad_radial.numel() else None
+    g_v = torch.empty_like(v)
+    lib = N.lib()
+    d = _geom_desc(l_max, n_radial, cosine, poly_order, False, v.dtype, r_min, r_max, r_cut)
+    with _timed("edge_geometry_bwd", 1, _nbytes(v, ga, gr, g_v)):
+        rc = lib.fc_edge_geometry_vec_bwd(ctypes.byref(d), _p(v), v.shape[0], _p(ga), _p(gr), _p(g_v),
+                                          _p(status_word(v.device)), _stream(v.device))
+    _after(lib, rc, "fc_edge_geometry_vec_bwd", v.device)
+    return g_v
+
+
+@edge_geometry_vec_bwd.register_fake
+def _(grad_attrs, grad_radial, vectors, l_max, n_radial, cosine, poly_order, r_min, r_max, r_cut):
+    return torch.empty_like(vectors)
+
+
+def _geom_vec_setup(ctx, inputs, output):
+    ctx.save_for_backward(inputs[0])
+    ctx.args = inputs[1:]
+
+
+def _geom_vec_backward(ctx, grad_attrs, grad_radial):
+    if torch.is_grad_enabled():
+        raise RuntimeError("flashcart::edge_geometry_vec_fwd was evaluated inside first_order_only(); its backward "
+                           "cannot build a graph for a second derivative")
+    (vectors,) = ctx.saved_tensors
+    ga = grad_attrs if grad_attrs is not None else vectors.new_zeros(0)
+    gr = grad_radial if grad_radial is not None else vectors.new_zeros(0)
+    return (edge_geometry_vec_bwd(ga, gr, vectors, *ctx.args),) + (None,) * len(ctx.args)
+
+
+edge_geometry_vec_fwd.register_autograd(_geom_vec_backward, setup_context=_geom_vec_setup)
+
+
+def edge_geometry_vec(vectors: Tensor, l_max: int, n_radial: int, cosine: bool, poly_order: int, r_min: float,
+                      r_max: float, r_cut: float) -> Tuple[Tensor, Tensor]:
+    """(edge_attrs, radial) of edge vectors given per edge, differentiable once with respect
+    to the vectors (see :func:`first_order_only`)."""
+    return edge_geometry_vec_fwd(vectors, int(l_max), int(n_radial), bool(cosine), int(poly_order), float(r_min),
+                                 float(r_max), float(r_cut))
+
+
 # --------------------------------------------------------------------------- halo exchange rows
 
 
-def halo_pack(x: Tensor, idx: Tensor) -> Tensor:
+def halo_pack(x: Tensor, idx: Tensor, out: Optional[Tensor] = None) -> Tensor:
     """``buf[k] = x[idx[k]]`` for rows of any width (``fc_halo_pack``): the send buffer of a
     halo exchange, one coalesced row copy per index (reference semantics: the owner rows
-    that ``lammps_forward_exchange`` sends, ``utils/lammps.py:67-94``)."""
+    that ``lammps_forward_exchange`` sends, ``utils/lammps.py:67-94``). ``out``, when
+    given, is the contiguous (len(idx), ...) buffer written in place (e.g. the ghost rows
+    of a feature matrix)."""
     _require_cuda(x, idx)
     xc = x.contiguous()
     re = 1
     for d in xc.shape[1:]:
         re *= int(d)
-    buf = xc.new_empty((idx.numel(),) + tuple(xc.shape[1:]))
+    if out is None:
+        buf = xc.new_empty((idx.numel(),) + tuple(xc.shape[1:]))
+    else:
+        if (not out.is_contiguous() or out.dtype != xc.dtype or out.device != xc.device
+                or tuple(out.shape) != (idx.numel(),) + tuple(xc.shape[1:])):
+            raise ValueError("halo_pack: out must be a contiguous (len(idx), ...) tensor of x's dtype and device")
+        buf = out
     if idx.numel() == 0:
         return buf
     lib = N.lib()

@@ -335,6 +335,18 @@ int fc_edge_geometry_bwd(const fc_edge_geometry_desc* desc, const void* position
                          const int64_t* batch, int64_t n_edges, const void* grad_attrs, const void* grad_radial,
                          void* grad_positions, void* grad_cells, int32_t* status, fc_stream_t stream);
 
+/* The same geometry from edge vectors given per edge (n_edges, 3) instead of positions:
+ * the LAMMPS ML-IAP layout, where LAMMPS supplies rij with the periodic translation
+ * applied (replaces the vectors branch of model/flashcart.py:264-286 for the graphs of
+ * calculators/lammps_mliap.py:122-170). desc->use_shifts is ignored. The backward writes
+ * grad_vectors (n_edges, 3) = the vector-Jacobian product per edge (dE/dv: the pair
+ * forces of lammps_mliap.py:711-738), zeros when both gradients are NULL. */
+int fc_edge_geometry_vec_fwd(const fc_edge_geometry_desc* desc, const void* vectors, int64_t n_edges,
+                             void* edge_attrs, void* radial, int32_t* status, fc_stream_t stream);
+int fc_edge_geometry_vec_bwd(const fc_edge_geometry_desc* desc, const void* vectors, int64_t n_edges,
+                             const void* grad_attrs, const void* grad_radial, void* grad_vectors, int32_t* status,
+                             fc_stream_t stream);
+
 /* ---------------------------------------------------------------- neighbour list
  * Periodic cell list of an orthorhombic cell on the GPU. Replaces the host neighbour
  * search that feeds the model (data/neighbors.py:120-143, matscipy neighbour_list("ijS"):
