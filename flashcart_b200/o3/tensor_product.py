@@ -63,8 +63,11 @@ class TensorProduct(nn.Module):
             raise NotImplementedError(
                 f"flashcart_b200 tensor product supports l_max <= {FC_MAX_L}; got in1_l_max={self.in1_l_max}, "
                 f"in2_l_max={self.in2_l_max}, out_l_max={self.out_l_max}.")
-        if self.symmetric_product and in1 is not in2:
-            torch._assert_async((in1 == in2).all(), "Symmetric product requires in1 == in2.")
+        if self.symmetric_product and in1 is not in2 and in1.is_cuda:
+            # the reference's device assert (o3/tensor_product.py:131) as a status-word bit
+            from flashcart_b200 import ops
+
+            ops.flag_if((in1 != in2).any(), ops.DEV_NOT_SYMMETRIC, in1.device)
         conv = idx_i is not None and idx_j is not None
         rows = in2.shape[0] if conv else in1.shape[0]
         expected = self.n_total_paths * self.out_features

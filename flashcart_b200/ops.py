@@ -72,11 +72,25 @@ def status_word(device: torch.device) -> Tensor:
     return w
 
 
+# status bits raised by host-composed checks (above the kernels' FC_DEV_* bits)
+DEV_NOT_UNIT = 1 << 8
+DEV_NOT_SYMMETRIC = 1 << 9
+
+
+def flag_if(cond: Tensor, bit: int, device: torch.device) -> None:
+    """OR ``bit`` into the device status word where the 0-d bool ``cond`` holds, without a
+    host synchronisation (the check surfaces at the next :func:`check_device_status`)."""
+    w = status_word(device)
+    w.bitwise_or_(cond.to(torch.int32) * bit)
+
+
 def check_device_status(device: Optional[torch.device] = None, clear: bool = True) -> None:
     """Synchronise and raise if a kernel flagged bad data since the last check.
 
-    Mirrors the reference's ``torch._assert_async`` guards: unsorted receivers
-    (``o3/_tensor_product.py:397-401``) and out-of-range edge indices.
+    Mirrors the reference's ``torch._assert_async`` guards (unsorted receivers,
+    ``o3/_tensor_product.py:397-401``; unit-length directions, ``o3/irreps.py:66-69``;
+    symmetric-product operands, ``o3/tensor_product.py:131``) and out-of-range edge
+    indices, as error bits instead of device asserts: the CUDA context stays usable.
     """
     device = device or torch.device("cuda", torch.cuda.current_device())
     w = status_word(device)
@@ -91,6 +105,10 @@ def check_device_status(device: Optional[torch.device] = None, clear: bool = Tru
         msgs.append("An edge index points outside its node array.")
     if v & N.FC_DEV_TIMEOUT:
         msgs.append("A bounded device-side wait expired; the results of that call are invalid.")
+    if v & DEV_NOT_UNIT:
+        msgs.append("Irreps.forward_normalized requires unit-length input vectors.")
+    if v & DEV_NOT_SYMMETRIC:
+        msgs.append("Symmetric product requires in1 == in2.")
     if msgs:
         raise RuntimeError(" ".join(msgs))
 
