@@ -211,6 +211,19 @@ int gemm_dispatch<float>(const LinGemmArgs<float>& a, int precision, int* status
   return lin_gemm_tc(a, precision != FC_PREC_TF32, status, s);
 }
 
+// All ranks of a map in one launch where the layout allows (float32 on the TMA path);
+// 1 = not taken, the caller launches per rank.
+template <typename T>
+static int gemm_dispatch_grouped(const LinGemmArgs<T>*, int, int, int*, cudaStream_t) {
+  return 1;
+}
+#ifndef FC_HOST_EMU
+template <>
+int gemm_dispatch_grouped<float>(const LinGemmArgs<float>* a, int n, int precision, int* status, cudaStream_t s) {
+  return lin_gemm_tma_grouped(a, n, precision != FC_PREC_TF32, status, s);
+}
+#endif
+
 // zero columns [from, width) of every row
 template <typename T>
 static int zero_tail(T* p, int64_t rows, int64_t width, int64_t from, cudaStream_t s) {
@@ -235,8 +248,9 @@ static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* 
     end = d->out_offsets[l] + (int64_t)d->m_values[l] * d->f_out_values[l];
   }
   if (int rc = zero_tail(out, n, d->out_dim, end, s)) return rc;
+  LinGemmArgs<T> args[FC_MAX_L + 1];
   for (int l = 0; l < d->n_active; ++l) {
-    LinGemmArgs<T> a;
+    LinGemmArgs<T>& a = args[l];
     a.a = LinRows<T>{x, d->in_dim, d->in_offsets[l], d->f_in_values[l], d->m_values[l]};
     a.w = (const T*)weights[l];
     a.ldw = d->f_in_values[l];
@@ -247,8 +261,11 @@ static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* 
     a.R = n * d->m_values[l];
     a.K = d->f_in_values[l];
     a.N = d->f_out_values[l];
-    if (int rc = gemm_dispatch<T>(a, d->precision, status, s)) return rc;
   }
+  const int g = d->n_active > 1 ? gemm_dispatch_grouped<T>(args, d->n_active, d->precision, status, s) : 1;
+  if (g != 1) return g;
+  for (int l = 0; l < d->n_active; ++l)
+    if (int rc = gemm_dispatch<T>(args[l], d->precision, status, s)) return rc;
   return 0;
 }
 
@@ -272,8 +289,9 @@ static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const v
       prev = d->in_offsets[l] + (int64_t)d->m_values[l] * d->f_in_values[l];
     }
     if (int rc = zero_tail(gx, n, d->in_dim, prev, s)) return rc;
+    LinGemmArgs<T> args[FC_MAX_L + 1];
     for (int l = 0; l < d->n_active; ++l) {
-      LinGemmArgs<T> a;
+      LinGemmArgs<T>& a = args[l];
       a.a = LinRows<T>{g, d->out_dim, d->out_offsets[l], d->f_out_values[l], d->m_values[l]};
       a.w = (const T*)weights[l];
       a.ldw = d->f_in_values[l];
@@ -284,8 +302,11 @@ static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const v
       a.R = n * d->m_values[l];
       a.K = d->f_out_values[l];
       a.N = d->f_in_values[l];
-      if (int rc = gemm_dispatch<T>(a, d->precision, status, s)) return rc;
     }
+    const int grp = d->n_active > 1 ? gemm_dispatch_grouped<T>(args, d->n_active, d->precision, status, s) : 1;
+    if (grp != 1 && grp != 0) return grp;
+    for (int l = 0; grp == 1 && l < d->n_active; ++l)
+      if (int rc = gemm_dispatch<T>(args[l], d->precision, status, s)) return rc;
   }
   if (gw) {
     for (int l = 0; l < d->n_active; ++l) {

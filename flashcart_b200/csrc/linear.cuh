@@ -49,6 +49,8 @@ int lin_gemm(const LinGemmArgs<T>& a, cudaStream_t s);
 int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s);
 // TMA-fed persistent variant; returns 1 (nothing launched) when the layout is not eligible.
 int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s);
+// all ranks of one map in one launch (uniform rank blocks, back to back); 1 = not eligible
+int lin_gemm_tma_grouped(const LinGemmArgs<float>* a, int n, bool split, int* status, cudaStream_t s);
 template <typename T>
 int lin_wgrad(LinWgradArgs<T> a, cudaStream_t s);
 // B(k, n) of a GEMM (W[n*ldw + k] if trans_b, else W[k*ldw + n]) as tf32 hi rows then lo

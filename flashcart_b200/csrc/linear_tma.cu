@@ -104,8 +104,16 @@ struct Args {
   int n_col_tiles;
   int64_t row_tiles;      // 128-node tiles per m
   int64_t n_tiles;
-  const float* scale;
+  const float* scale;     // per rank (indexed by rank_of_m)
+  int n_ranks;            // weight sets in this launch (grouped launch: all ranks of a map)
+  int rank_of_m[16];      // rank whose weights and scale row m of the tile uses
   int* status;
+};
+
+// The weights of every rank of a grouped launch (unused entries are never read).
+struct BMaps {
+  CUtensorMap hi[4];
+  CUtensorMap lo[4];
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -267,9 +275,9 @@ __device__ __forceinline__ TileCoord tile_coord(const Args& a, int64_t t) {
 
 template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
-    lin_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
-                   const __grid_constant__ CUtensorMap map_blo, const __grid_constant__ CUtensorMap map_c,
-                   const __grid_constant__ CUtensorMap map_pf, const Args a) {
+    lin_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm,
+                   const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_pf,
+                   const Args a) {
   using C = Cfg<BN>;
   constexpr int S = C::STAGES;
   constexpr int B_OFF = C::ATM ? C::TILE_A : 2 * C::TILE_A;  // B hi | lo after the A slab (and its lo half)
@@ -316,8 +324,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_pf)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_bhi)) : "memory");
-      if (SPLIT) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_blo)) : "memory");
+      for (int r = 0; r < a.n_ranks; ++r) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bm.hi[r])) : "memory");
+        if (SPLIT) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bm.lo[r])) : "memory");
+      }
       constexpr uint32_t bytes = C::TILE_A + (SPLIT ? 2 : 1) * C::TILE_B;
       // prefetch cursor: PF_AHEAD slabs ahead of the loads, one L2 prefetch per PF_SLABS slabs
       int64_t pi = 0;
@@ -345,9 +355,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint8_t* st = smem + s * C::STAGE;
           const uint32_t fb = smem_u32(&full[s]);
           arrive_tx(fb, bytes);
+          const int r = a.rank_of_m[tc.m];
           tma_load_3d(smem_u32(st), &map_a, kt * BK, tc.node0, tc.m, fb);
-          tma_load_2d(smem_u32(st + B_OFF), &map_bhi, kt * BK, tc.col0 * BN, fb);
-          if (SPLIT) tma_load_2d(smem_u32(st + B_OFF + C::TILE_B), &map_blo, kt * BK, tc.col0 * BN, fb);
+          tma_load_2d(smem_u32(st + B_OFF), &bm.hi[r], kt * BK, tc.col0 * BN, fb);
+          if (SPLIT) tma_load_2d(smem_u32(st + B_OFF + C::TILE_B), &bm.lo[r], kt * BK, tc.col0 * BN, fb);
         }
       }
       // drain: the last load issued into every stage must have landed before the CTA exits
@@ -480,7 +491,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const float sc = *a.scale;
+    float sc = a.scale[0];   // the scale of the current tile's rank
     uint8_t* stage0 = epi + (warp - EPI_WARP0) * 2 * 4096;
     int nbuf = 0;
     int64_t u = 0;
@@ -519,6 +530,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     for (int64_t i = 0; i < my_tiles && !*abort_flag; ++i) {
       const TileCoord tc = tile_coord(a, blockIdx.x + i * gridDim.x);
+      sc = a.scale[a.rank_of_m[tc.m]];
       const int col0 = tc.col0 * BN;
       const int nchunks = min(BN, a.N - col0 + 31) / 32;
       bool ok = true;
@@ -651,8 +663,8 @@ static bool encode_b(CUtensorMap* map, const float* base, int kp, int N, int box
 }
 
 template <int BN, bool SPLIT>
-static int launch(const CUtensorMap& ma, const CUtensorMap& mbh, const CUtensorMap& mbl, const CUtensorMap& mc,
-                  const CUtensorMap& mpf, const Args& args, DeviceState* ds, int grid, cudaStream_t s) {
+static int launch(const CUtensorMap& ma, const BMaps& bm, const CUtensorMap& mc, const CUtensorMap& mpf,
+                  const Args& args, DeviceState* ds, int grid, cudaStream_t s) {
   constexpr int bi = BN == 64 ? 0 : BN == 128 ? 1 : 2;
   if (!ds->attr_set[bi][SPLIT]) {
     if (cudaFuncSetAttribute(lin_tma_kernel<BN, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -660,82 +672,118 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mbh, const CUtensorM
       return FC_ERR_LAUNCH;
     ds->attr_set[bi][SPLIT] = true;
   }
-  lin_tma_kernel<BN, SPLIT><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ma, mbh, mbl, mc, mpf, args);
+  lin_tma_kernel<BN, SPLIT><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ma, bm, mc, mpf, args);
   return fc_check_launch();
 }
 
 }  // namespace tma
 
-// Returns 1 when the shape / layout is not eligible (the caller uses the non-TMA kernel).
-int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s) {
+// One launch over the rank blocks a[0..n) of one map (n = 1: a single rank). The caller has
+// checked that the blocks share K, N, row strides and node count and lie back to back in
+// the row (a[l].off == a[l-1].off + a[l-1].M * ms), so one 3-D map over (k, node, m) with
+// m_total rows covers all of them; each tile's m selects its rank's weights and scale.
+// Returns 1 when the layout is not eligible (the caller uses another path).
+static int run_tma(const LinGemmArgs<float>* a, int n, bool split, int* status, cudaStream_t s) {
   using namespace tma;
-  if (a.K <= 0 || a.R <= 0 || a.N <= 0 || a.a.M != a.c.M || a.R % a.a.M) return 1;
+  int m_total = 0;
+  for (int l = 0; l < n; ++l) m_total += a[l].a.M;
+  if (n < 1 || n > 4 || m_total > 16) return 1;
+  const LinGemmArgs<float>& a0 = a[0];
+  if (a0.K <= 0 || a0.R <= 0 || a0.N <= 0 || a0.a.M != a0.c.M || a0.R % a0.a.M) return 1;
   std::lock_guard<std::mutex> lock(g_mu);
   if (!encode_fn()) return 1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FC_ERR_LAUNCH;
   DeviceState* ds = device_state(dev);
   if (!ds) return FC_ERR_LAUNCH;
-  const int M = a.a.M;
-  const int64_t nodes = a.R / M;
-  const int nk = (a.K + BK - 1) / BK;
+  const int64_t nodes = a0.R / a0.a.M;
+  const int nk = (a0.K + BK - 1) / BK;
   const int nu = (nk + KG - 1) / KG;
   // 256-column tiles only when one unit covers k (their sum would need 256 registers)
-  const int BN = (a.N > 128 && nu == 1) ? 256 : a.N > 64 ? 128 : 64;
-  const int kp = (a.K + 3) & ~3;
+  const int BN = (a0.N > 128 && nu == 1) ? 256 : a0.N > 64 ? 128 : 64;
+  const int kp = (a0.K + 3) & ~3;
   if (nodes > 0x7fffffffLL) return 1;
 
-  CUtensorMap ma, mbh, mbl, mc, mpf;
-  if (!encode_rows(&ma, a.a.p + a.a.off, a.K, nodes, M, a.a.ld, a.a.ms, BM)) return 1;
-  if (!encode_rows(&mpf, a.a.p + a.a.off, a.K, nodes, M, a.a.ld, a.a.ms, BM, PF_SLABS * BK)) return 1;
-  if (!encode_rows(&mc, a.c.p + a.c.off, a.N, nodes, M, a.c.ld, a.c.ms, 32)) return 1;
+  CUtensorMap ma, mc, mpf;
+  BMaps bm;
+  if (!encode_rows(&ma, a0.a.p + a0.a.off, a0.K, nodes, m_total, a0.a.ld, a0.a.ms, BM)) return 1;
+  if (!encode_rows(&mpf, a0.a.p + a0.a.off, a0.K, nodes, m_total, a0.a.ld, a0.a.ms, BM, PF_SLABS * BK)) return 1;
+  if (!encode_rows(&mc, a0.c.p + a0.c.off, a0.N, nodes, m_total, a0.c.ld, a0.c.ms, 32)) return 1;
 
+  const size_t per_rank = (size_t)a0.N * kp * (split ? 2 : 1);
   float* ws = nullptr;
-  float* bhi = nullptr;
-  if (a.bsplit) {
-    bhi = const_cast<float*>(a.bsplit);  // split once by the caller (lin_presplit layout)
-  } else {
-    const size_t wbytes = (size_t)a.N * kp * 4 * (split ? 2 : 1);
-    if (fc_pool_alloc(reinterpret_cast<void**>(&ws), wbytes, s)) return FC_ERR_LAUNCH;
-    bhi = ws;
-  }
-  float* blo = split ? bhi + (size_t)a.N * kp : nullptr;
+  if (!a0.bsplit && fc_pool_alloc(reinterpret_cast<void**>(&ws), per_rank * n * 4, s)) return FC_ERR_LAUNCH;
   int rc = 0;
-  if (!encode_b(&mbh, bhi, kp, a.N, BN) || (split && !encode_b(&mbl, blo, kp, a.N, BN))) rc = 1;
-  if (!split) mbl = mbh;
-  if (rc == 0 && !a.bsplit) {
-    const int64_t total = (int64_t)a.N * kp;
-    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * ds->sms);
-    presplit_kernel<<<blocks, 256, 0, s>>>(a.w, a.ldw, a.trans_b, a.K, a.N, kp, bhi, blo);
-    if (cudaGetLastError() != cudaSuccess) rc = FC_ERR_LAUNCH;
+  for (int l = 0; l < n && rc == 0; ++l) {
+    // split once by the caller (lin_presplit layout), else into this call's workspace
+    float* bhi = a0.bsplit ? const_cast<float*>(a[l].bsplit) : ws + per_rank * l;
+    float* blo = split ? bhi + (size_t)a0.N * kp : nullptr;
+    if (!encode_b(&bm.hi[l], bhi, kp, a0.N, BN) || (split && !encode_b(&bm.lo[l], blo, kp, a0.N, BN))) {
+      rc = 1;
+      break;
+    }
+    if (!split) bm.lo[l] = bm.hi[l];
+    if (!a0.bsplit) {
+      const int64_t total = (int64_t)a0.N * kp;
+      const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * ds->sms);
+      presplit_kernel<<<blocks, 256, 0, s>>>(a[l].w, a[l].ldw, a[l].trans_b, a0.K, a0.N, kp, bhi, blo);
+      if (cudaGetLastError() != cudaSuccess) rc = FC_ERR_LAUNCH;
+    }
   }
   if (rc == 0) {
     Args args;
     args.nodes = nodes;
-    args.M = M;
-    args.K = a.K;
-    args.N = a.N;
+    args.M = m_total;
+    args.K = a0.K;
+    args.N = a0.N;
     args.nk = nk;
     args.nu = nu;
-    args.n_col_tiles = (a.N + BN - 1) / BN;
+    args.n_col_tiles = (a0.N + BN - 1) / BN;
     args.row_tiles = (nodes + BM - 1) / BM;
-    args.n_tiles = args.row_tiles * M * args.n_col_tiles;
-    args.scale = a.scale;
+    args.n_tiles = args.row_tiles * m_total * args.n_col_tiles;
+    args.scale = a0.scale;  // scales of consecutive ranks are consecutive (scale + l)
+    args.n_ranks = n;
+    for (int l = 0, m = 0; l < n; ++l)
+      for (int j = 0; j < a[l].a.M; ++j) args.rank_of_m[m++] = l;
+    for (int m = m_total; m < 16; ++m) args.rank_of_m[m] = 0;
     args.status = status;
     const int grid = (int)std::min<int64_t>(args.n_tiles, ds->sms);
     if (BN == 64)
-      rc = split ? launch<64, true>(ma, mbh, mbl, mc, mpf, args, ds, grid, s)
-                 : launch<64, false>(ma, mbh, mbl, mc, mpf, args, ds, grid, s);
+      rc = split ? launch<64, true>(ma, bm, mc, mpf, args, ds, grid, s)
+                 : launch<64, false>(ma, bm, mc, mpf, args, ds, grid, s);
     else if (BN == 128)
-      rc = split ? launch<128, true>(ma, mbh, mbl, mc, mpf, args, ds, grid, s)
-                 : launch<128, false>(ma, mbh, mbl, mc, mpf, args, ds, grid, s);
+      rc = split ? launch<128, true>(ma, bm, mc, mpf, args, ds, grid, s)
+                 : launch<128, false>(ma, bm, mc, mpf, args, ds, grid, s);
     else
-      rc = split ? launch<256, true>(ma, mbh, mbl, mc, mpf, args, ds, grid, s)
-                 : launch<256, false>(ma, mbh, mbl, mc, mpf, args, ds, grid, s);
+      rc = split ? launch<256, true>(ma, bm, mc, mpf, args, ds, grid, s)
+                 : launch<256, false>(ma, bm, mc, mpf, args, ds, grid, s);
   }
   // stream-ordered: the workspace returns to the pool after the kernels that read it
   if (ws && fc_pool_free(ws, s) && rc == 0) rc = FC_ERR_LAUNCH;
   return rc;
+}
+
+// Returns 1 when the shape / layout is not eligible (the caller uses the non-TMA kernel).
+int lin_gemm_tma(const LinGemmArgs<float>& a, bool split, int* status, cudaStream_t s) {
+  return run_tma(&a, 1, split, status, s);
+}
+
+// All ranks of one linear map in one launch when their blocks are uniform (same K, N,
+// strides and node count, back to back in the row); 1 = not eligible.
+int lin_gemm_tma_grouped(const LinGemmArgs<float>* a, int n, bool split, int* status, cudaStream_t s) {
+  if (n < 2 || n > 4) return 1;
+  const LinGemmArgs<float>& a0 = a[0];
+  for (int l = 1; l < n; ++l) {
+    const LinGemmArgs<float>& b = a[l];
+    const LinGemmArgs<float>& p = a[l - 1];
+    if (b.K != a0.K || b.N != a0.N || b.a.p != a0.a.p || b.c.p != a0.c.p || b.a.ld != a0.a.ld ||
+        b.c.ld != a0.c.ld || b.a.ms != a0.a.ms || b.c.ms != a0.c.ms || b.a.M != b.c.M ||
+        (b.bsplit == nullptr) != (a0.bsplit == nullptr) || b.scale != p.scale + 1)
+      return 1;
+    if (b.a.M < 1 || b.R % b.a.M || b.R / b.a.M != a0.R / a0.a.M) return 1;
+    if (b.a.off != p.a.off + (int64_t)p.a.M * p.a.ms || b.c.off != p.c.off + (int64_t)p.c.M * p.c.ms) return 1;
+  }
+  return run_tma(a, n, split, status, s);
 }
 
 int lin_presplit(const float* w, int ldw, int trans_b, int K, int N, float* out, cudaStream_t s) {
