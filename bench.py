@@ -608,7 +608,12 @@ def run_config2(args):
         exp_ms = _event_ms(expand, reps, args.warmup)
         lin_ms = _event_ms(lambda: lin(x), reps, args.warmup)
         y_ref = lin(x)
+        # bf16 storage path of the same map: bf16 in / out, fp32 accumulation on tcgen05
+        x_bf = x.to(torch.bfloat16)
         del x
+        bf16_ms = _event_ms(lambda: lin(x_bf), reps, args.warmup)
+        bf16_rel = ((lin(x_bf).float() - y_ref).abs().max() / y_ref.abs().max()).item()
+        del x_bf
         y = fused()
         rel = ((y - y_ref).abs().max() / y_ref.abs().max()).item()
         del y, y_ref
@@ -625,6 +630,8 @@ def run_config2(args):
         "data": "synthetic", "config": {"workload": "edge expansion + equivariant linear map", "edges": e, "channels": C,
                                          "expansion": "unfused reference composition (torch) writing (E, 2048)"},
         "roofline": {"expansion": _roof(e * 12 + xb, exp_ms, peak, src), "linear": _roof(2 * xb, lin_ms, peak, src)},
+        "linear_bf16": {"ms": bf16_ms, "how": "x, W, y in bf16, tcgen05 kind::f16 with fp32 accumulation",
+                        "max_rel_diff_vs_fp32": bf16_rel, "roofline": _roof(xb, bf16_ms, peak, src)},
         "fused": {"ms_per_step": fused_ms, "value": e / (fused_ms * 1e-3), "unit": "edges/s",
                   "how": "Y_l = T_l (x) (h W_l^T): GEMM 128 -> 4 x 128 (3xTF32) on h, fc_edge_expand_fwd writes Y",
                   "max_rel_diff_vs_unfused": rel,

@@ -34,6 +34,11 @@ template <typename T>
 int edge_expand_fwd_dispatch(int, const T*, const T*, int, int, int64_t, T*, cudaStream_t);
 template <typename T>
 int edge_expand_bwd_dispatch(int, const T*, const T*, const T*, int, int, int64_t, T*, T*, cudaStream_t);
+#ifndef FC_HOST_EMU
+int lin_bf16_rank(const void* x, int64_t ld, int64_t off, int64_t ms, int M, int64_t nodes, const void* w, int K,
+                  int N, const float* scale, void* y, int64_t out_ld, int64_t out_off, int64_t out_ms, int* status,
+                  cudaStream_t s);
+#endif
 template <typename T>
 int geom_fwd_dispatch(const GeomParams&, const T*, const T*, const int32_t*, const int64_t*, const int64_t*, T*, T*,
                       int*, cudaStream_t);
@@ -194,7 +199,7 @@ static int check_linear(const fc_linear_desc* d) {
     if (d->out_offsets[l] < 0 || d->out_offsets[l] + (int64_t)d->m_values[l] * d->f_out_values[l] > d->out_dim)
       return fail(FC_ERR_INVALID, "linear: rank %d exceeds the output row", l);
   }
-  if (d->dtype != FC_F32 && d->dtype != FC_F64) return fail(FC_ERR_INVALID, "linear: bad dtype");
+  if (d->dtype != FC_F32 && d->dtype != FC_F64 && d->dtype != FC_BF16) return fail(FC_ERR_INVALID, "linear: bad dtype");
   if (d->precision != FC_PREC_IEEE && d->precision != FC_PREC_TF32)
     return fail(FC_ERR_INVALID, "linear: bad precision");
   return FC_OK;
@@ -649,6 +654,33 @@ int fc_irreps_dbwd(const void* grad_out, const void* x, const void* v, int64_t n
   return fail(FC_ERR_INVALID, "fc_irreps_dbwd: bad dtype");
 }
 
+// bf16 storage: one tensor-core launch per rank block (csrc/linear_bf16.cu); columns of y
+// outside the active ranks are zeroed.
+static int linear_fwd_bf16(const fc_linear_desc* d, const void* x, const void* const* weights, const float* scale,
+                           int64_t n, void* out, int* status, cudaStream_t s) {
+#ifdef FC_HOST_EMU
+  (void)d; (void)x; (void)weights; (void)scale; (void)n; (void)out; (void)status; (void)s;
+  return fail(FC_ERR_UNSUPPORTED, "fc_linear_fwd: bf16 maps run on the GPU only");
+#else
+  int64_t end = 0;
+  if (d->n_active > 0) {
+    const int l = d->n_active - 1;
+    end = d->out_offsets[l] + (int64_t)d->m_values[l] * d->f_out_values[l];
+  }
+  if (int rc = zero_tail(reinterpret_cast<uint16_t*>(out), n, d->out_dim, end, s)) return rc;
+  for (int l = 0; l < d->n_active; ++l) {
+    const int rc = lin_bf16_rank(x, d->in_dim, d->in_offsets[l], d->f_in_values[l], d->m_values[l], n, weights[l],
+                                 d->f_in_values[l], d->f_out_values[l], scale + l, out, d->out_dim,
+                                 d->out_offsets[l], d->f_out_values[l], status, s);
+    if (rc == FC_ERR_UNSUPPORTED)
+      return fail(FC_ERR_UNSUPPORTED, "fc_linear_fwd (bf16): rank %d is not 16-byte aligned (offsets and widths "
+                                      "must be multiples of 8)", l);
+    if (rc) return rc;
+  }
+  return 0;
+#endif
+}
+
 int fc_linear_fwd(const fc_linear_desc* desc, const void* x, const void* const* weights, const void* scale,
                   int64_t n, void* out, int32_t* status, fc_stream_t stream) {
   if (int rc = check_linear(desc)) return rc;
@@ -659,6 +691,9 @@ int fc_linear_fwd(const fc_linear_desc* desc, const void* x, const void* const* 
   for (int l = 0; l < desc->n_active; ++l)
     if (!weights[l]) return fail(FC_ERR_INVALID, "fc_linear_fwd: null weight for rank %d", l);
   cudaStream_t s = (cudaStream_t)stream;
+  if (desc->dtype == FC_BF16) return launch_status(linear_fwd_bf16(desc, x, weights, (const float*)scale, n, out,
+                                                                   reinterpret_cast<int*>(status), s),
+                                                   "fc_linear_fwd (bf16)");
   if (desc->dtype == FC_F32)
     return launch_status(linear_fwd_t<float>(desc, (const float*)x, weights, (const float*)scale, n, (float*)out,
                                              reinterpret_cast<int*>(status), s),
@@ -672,6 +707,7 @@ int fc_linear_bwd(const fc_linear_desc* desc, const void* grad_out, const void* 
                   const void* scale, int64_t n, void* grad_x, void* const* grad_weights, int32_t* status,
                   fc_stream_t stream) {
   if (int rc = check_linear(desc)) return rc;
+  if (desc->dtype == FC_BF16) return fail(FC_ERR_UNSUPPORTED, "fc_linear_bwd: bf16 maps are forward only");
   if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_bwd: negative size");
   if (desc->n_active > 0 && (!scale || !weights || (n > 0 && (!grad_out || !x))))
     return fail(FC_ERR_INVALID, "fc_linear_bwd: null tensor");
@@ -691,6 +727,7 @@ int fc_linear_dbwd(const fc_linear_desc* desc, const void* grad_out, const void*
                    const void* v_grad_x, const void* const* v_grad_weights, const void* scale, int64_t n,
                    void* d_grad_out, void* d_x, void* const* d_weights, int32_t* status, fc_stream_t stream) {
   if (int rc = check_linear(desc)) return rc;
+  if (desc->dtype == FC_BF16) return fail(FC_ERR_UNSUPPORTED, "fc_linear_dbwd: bf16 maps are forward only");
   if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_dbwd: negative size");
   if (desc->n_active > 0 && (!scale || !weights || (n > 0 && (!grad_out || !x))))
     return fail(FC_ERR_INVALID, "fc_linear_dbwd: null tensor");

@@ -534,7 +534,8 @@ def _linear_desc(x: Tensor, out_dim: int, in_offsets, out_offsets, m_values, f_i
     if n > N.FC_MAX_L + 1:
         raise NotImplementedError(f"flashcart_b200 linear supports at most {N.FC_MAX_L + 1} ranks, got {n}")
     d.n_active = n
-    d.dtype = _code(x.dtype)
+    # bfloat16: the forward's bf16 storage path (tensor cores, fp32 accumulation)
+    d.dtype = N.FC_BF16 if x.dtype == torch.bfloat16 else _code(x.dtype)
     d.precision = N.FC_PREC_TF32 if (precision == "tf32" and x.dtype == torch.float32) else N.FC_PREC_IEEE
     d.in_dim = x.shape[1]
     d.out_dim = int(out_dim)
@@ -602,7 +603,7 @@ def _linear_fwd_impl(x: Tensor, weights: Sequence[Tensor], out_dim: int, lists, 
     x = x.contiguous()
     n_active = len(lists[0])
     ws = [w.to(x.dtype).contiguous() for w in weights[:n_active]]
-    sc = scale.to(device=x.device, dtype=x.dtype).contiguous()
+    sc = scale.to(device=x.device, dtype=torch.float32 if x.dtype == torch.bfloat16 else x.dtype).contiguous()
     out = x.new_empty((x.shape[0], int(out_dim)))
     d = _linear_desc(x, out_dim, lists[0], lists[1], lists[3], lists[4], lists[5], precision)
     split = _split_weights(lib, d, ws, False)

@@ -53,7 +53,7 @@ typedef void* fc_stream_t;
 /* dtypes */
 #define FC_F32 0
 #define FC_F64 1
-#define FC_BF16 2  /* fc_newton_schulz input only */
+#define FC_BF16 2  /* fc_newton_schulz input; fc_linear_fwd storage (x, weights, y in bf16) */
 
 /* linear-map arithmetic */
 #define FC_PREC_IEEE 0 /* fp32-accurate: fp64 FMA, or fp32 on tensor cores as 3xTF32 (hi*hi+hi*lo+lo*hi) */
@@ -181,11 +181,15 @@ int fc_irreps_dbwd(const void* grad_out, const void* x, const void* v, int64_t n
  * op flashcart::linear_fwd (in_offsets, out_offsets, m_values, f_in_values,
  * f_out_values; o3/_linear.py:113-166, 328-385) plus the row widths.
  * `weights` is a HOST array of per-rank DEVICE pointers, `scale` a DEVICE array with
- * one entry per active rank (dtype of x).
+ * one entry per active rank (dtype of x; float32 for FC_BF16).
+ * dtype FC_BF16 (forward only): x, weights (f_out, f_in) and y in bf16, products on the
+ * tensor cores (tcgen05 kind::f16) accumulated in fp32 and rounded once to bf16: the
+ * bf16 storage path of the linear maps, half the bytes of the float32 maps. Rank blocks,
+ * offsets and row widths must be multiples of 8 elements (16-byte TMA rows).
  * ------------------------------------------------------------------------------ */
 typedef struct fc_linear_desc {
   int32_t n_active;                     /* active ranks, 0..FC_MAX_L+1 */
-  int32_t dtype;                        /* FC_F32 / FC_F64 */
+  int32_t dtype;                        /* FC_F32 / FC_F64, or FC_BF16 (fc_linear_fwd only) */
   int32_t precision;                    /* FC_PREC_IEEE or FC_PREC_TF32 (fp32 only) */
   int32_t reserved;
   int64_t in_dim, out_dim;              /* row widths of x and y */

@@ -520,3 +520,43 @@ def test_gpu_rotation_equivariance(cuda_device, case):
     assert (out_r - expect).abs().max().item() < 1e-10 * max(1.0, expect.abs().max().item())
     assert out.abs().max().item() > 1e-3
     check_device_status(dev)
+
+
+@pytest.mark.parametrize("nodes", [3000, 129, 1])
+def test_gpu_bf16_linear_map_storage_path(cuda_device, nodes):
+    """bf16 storage path of the equivariant linear map (fc_linear_fwd with FC_BF16: tcgen05
+    kind::f16, fp32 accumulation, one bf16 rounding of the result): against the float64 map
+    of the same bf16-rounded inputs (only the output rounding and the fp32 accumulation
+    differ) and against the float32 map (bf16 input rounding included). Tolerances: 2^-8
+    relative to the output scale (one bf16 rounding), 2e-2 for the float32 comparison."""
+    torch.manual_seed(nodes)
+    lin = o3.LinearLayer(3, 3, 128, 128, weight_scale=1.0).to(cuda_device)
+    with torch.no_grad():
+        for w in lin.weight:
+            w.normal_(0.0, (2.0 / 256) ** 0.5)
+    x = torch.randn(nodes, 16 * 128, device=cuda_device)
+    with torch.no_grad():
+        y32 = lin(x)
+        xb = x.to(torch.bfloat16)
+        yb = lin(xb)
+        assert yb.dtype == torch.bfloat16 and yb.shape == y32.shape
+        lin64 = o3.LinearLayer(3, 3, 128, 128, weight_scale=1.0).to(cuda_device, torch.float64)
+        for w64, w in zip(lin64.weight, lin.weight):
+            w64.copy_(w.to(torch.bfloat16).double())
+        y64 = lin64(xb.double())
+    scale = float(y64.abs().max())
+    assert float((yb.double() - y64).abs().max()) <= 2.0 ** -8 * scale
+    assert float((yb.float() - y32).abs().max()) <= 2e-2 * float(y32.abs().max())
+    check_device_status(cuda_device)
+
+
+def test_gpu_bf16_linear_rejects_unaligned_and_backward(cuda_device):
+    lin = o3.LinearLayer(1, 1, 12, 12).to(cuda_device)  # 12 channels: rows not 16-byte multiples
+    x = torch.randn(10, 4 * 12, device=cuda_device, dtype=torch.bfloat16)
+    with torch.no_grad(), pytest.raises(NotImplementedError):
+        lin(x)
+    lin2 = o3.LinearLayer(1, 1, 16, 16).to(cuda_device)
+    x2 = torch.randn(10, 4 * 16, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+    y = lin2(x2)
+    with pytest.raises(NotImplementedError):
+        y.sum().backward()
