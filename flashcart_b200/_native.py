@@ -28,6 +28,8 @@ FC_DEV_TIMEOUT = 4
 FC_F32 = 0
 FC_F64 = 1
 FC_BF16 = 2
+FC_ACT_NONE = 0
+FC_ACT_SILU = 1
 FC_PREC_IEEE = 0
 FC_PREC_TF32 = 1
 FC_MAX_L = 3
@@ -60,7 +62,7 @@ class EdgeGeometryDesc(ctypes.Structure):
 class LinearDesc(ctypes.Structure):
     _fields_ = [
         ("n_active", ctypes.c_int32), ("dtype", ctypes.c_int32),
-        ("precision", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("precision", ctypes.c_int32), ("act", ctypes.c_int32),
         ("in_dim", ctypes.c_int64), ("out_dim", ctypes.c_int64),
         ("in_offsets", ctypes.c_int64 * (FC_MAX_L + 1)),
         ("out_offsets", ctypes.c_int64 * (FC_MAX_L + 1)),

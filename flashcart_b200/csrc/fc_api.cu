@@ -202,6 +202,9 @@ static int check_linear(const fc_linear_desc* d) {
   if (d->dtype != FC_F32 && d->dtype != FC_F64 && d->dtype != FC_BF16) return fail(FC_ERR_INVALID, "linear: bad dtype");
   if (d->precision != FC_PREC_IEEE && d->precision != FC_PREC_TF32)
     return fail(FC_ERR_INVALID, "linear: bad precision");
+  if (d->act != FC_ACT_NONE && d->act != FC_ACT_SILU) return fail(FC_ERR_INVALID, "linear: bad activation");
+  if (d->act != FC_ACT_NONE && d->dtype != FC_F32)
+    return fail(FC_ERR_UNSUPPORTED, "linear: input activations are float32 (tensor-core path) only");
   return FC_OK;
 }
 
@@ -266,6 +269,7 @@ static int linear_fwd_t(const fc_linear_desc* d, const T* x, const void* const* 
     a.R = n * d->m_values[l];
     a.K = d->f_in_values[l];
     a.N = d->f_out_values[l];
+    a.act = d->act == FC_ACT_SILU ? 1 : 0;
   }
   const int g = d->n_active > 1 ? gemm_dispatch_grouped<T>(args, d->n_active, d->precision, status, s) : 1;
   if (g != 1) return g;
@@ -307,11 +311,19 @@ static int linear_bwd_t(const fc_linear_desc* d, const T* g, const T* x, const v
       a.R = n * d->m_values[l];
       a.K = d->f_out_values[l];
       a.N = d->f_in_values[l];
+      if (d->act == FC_ACT_SILU) {
+        a.act = 2;
+        a.aux = LinRows<T>{x, d->in_dim, d->in_offsets[l], d->f_in_values[l], d->m_values[l]};
+      }
     }
     const int grp = d->n_active > 1 ? gemm_dispatch_grouped<T>(args, d->n_active, d->precision, status, s) : 1;
     if (grp != 1 && grp != 0) return grp;
     for (int l = 0; grp == 1 && l < d->n_active; ++l)
       if (int rc = gemm_dispatch<T>(args[l], d->precision, status, s)) return rc;
+  }
+  if (gw && d->act != FC_ACT_NONE) {
+    for (int l = 0; l < d->n_active; ++l)
+      if (gw[l]) return fail(FC_ERR_UNSUPPORTED, "linear: no weight gradients with an input activation");
   }
   if (gw) {
     for (int l = 0; l < d->n_active; ++l) {
@@ -728,6 +740,7 @@ int fc_linear_dbwd(const fc_linear_desc* desc, const void* grad_out, const void*
                    void* d_grad_out, void* d_x, void* const* d_weights, int32_t* status, fc_stream_t stream) {
   if (int rc = check_linear(desc)) return rc;
   if (desc->dtype == FC_BF16) return fail(FC_ERR_UNSUPPORTED, "fc_linear_dbwd: bf16 maps are forward only");
+  if (desc->act != FC_ACT_NONE) return fail(FC_ERR_UNSUPPORTED, "fc_linear_dbwd: no input activation");
   if (n < 0) return fail(FC_ERR_INVALID, "fc_linear_dbwd: negative size");
   if (desc->n_active > 0 && (!scale || !weights || (n > 0 && (!grad_out || !x))))
     return fail(FC_ERR_INVALID, "fc_linear_dbwd: null tensor");

@@ -30,6 +30,10 @@ struct LinGemmArgs {
   // optional: the weights already split into tf32 hi | lo rows (n-major, k padded to a
   // multiple of 4), as lin_presplit writes them; null = split inside the call
   const T* bsplit = nullptr;
+  // activation: 0 none; 1 C = (sW) silu(A) (forward); 2 C = silu'(aux) * (sW) A with aux
+  // laid out like C (the backward's input gradient, aux = the forward's input)
+  int act = 0;
+  LinRows<T> aux{};
 };
 
 template <typename T>

@@ -284,6 +284,7 @@ int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream
   // TMA-fed persistent kernel where the layout allows it, else this one
   const int rc = lin_gemm_tma(a, split, status, s);
   if (rc != 1) return rc;
+  if (a.act != 0) return FC_ERR_UNSUPPORTED;  // activations exist on the TMA path only
   const int64_t tiles = ((a.R + tc::BM - 1) / tc::BM) * ((a.N + tc::BN - 1) / tc::BN);
   if (tiles > 0x7fffffff) return FC_ERR_UNSUPPORTED;
   dim3 grid((unsigned)tiles);
@@ -308,7 +309,10 @@ int lin_gemm_tc(const LinGemmArgs<float>& a, bool split, int* status, cudaStream
 
 #else
 
-int lin_gemm_tc(const LinGemmArgs<float>& a, bool, int*, cudaStream_t s) { return lin_gemm<float>(a, s); }
+int lin_gemm_tc(const LinGemmArgs<float>& a, bool, int*, cudaStream_t s) {
+  if (a.act != 0) return FC_ERR_UNSUPPORTED;  // input activations exist on the GPU's TMA path only
+  return lin_gemm<float>(a, s);
+}
 
 // host emulation of the split (same integer rounding to tf32 as the kernel)
 int lin_presplit(const float* w, int ldw, int trans_b, int K, int N, float* out, cudaStream_t) {

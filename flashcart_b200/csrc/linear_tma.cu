@@ -104,6 +104,8 @@ struct Args {
   int n_col_tiles;
   int64_t row_tiles;      // 128-node tiles per m
   int64_t n_tiles;
+  const float* aux;       // ACT == 2: silu' of these values multiplies C (laid out like C)
+  int64_t aux_ld, aux_ms;
   const float* scale;     // per rank (indexed by rank_of_m)
   int n_ranks;            // weight sets in this launch (grouped launch: all ranks of a map)
   int rank_of_m[16];      // rank whose weights and scale row m of the tile uses
@@ -149,6 +151,18 @@ __device__ __forceinline__ float round_tf32(float x) {
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
 #endif
+}
+
+// SiLU and its derivative for the activation modes (fast exp / divide intrinsics; the
+// argument is clamped to +-80, where the sigmoid is 0 or 1 to float32 precision).
+__device__ __forceinline__ float act_sigmoid(float z) {
+  z = fminf(fmaxf(z, -80.f), 80.f);
+  return __fdividef(1.f, 1.f + __expf(-z));
+}
+__device__ __forceinline__ float act_silu(float z) { return z * act_sigmoid(z); }
+__device__ __forceinline__ float act_dsilu(float z) {
+  const float sg = act_sigmoid(z);
+  return sg * (1.f + z * (1.f - sg));
 }
 
 __device__ __forceinline__ uint64_t make_desc(uint32_t saddr) {
@@ -273,7 +287,8 @@ __device__ __forceinline__ TileCoord tile_coord(const Args& a, int64_t t) {
   return c;
 }
 
-template <int BN, bool SPLIT>
+// ACT: 0 plain; 1 the splitters apply SiLU to A; 2 the epilogue multiplies by SiLU'(aux).
+template <int BN, bool SPLIT, int ACT>
 __global__ void __launch_bounds__(THREADS, 1)
     lin_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm,
                    const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_pf,
@@ -456,9 +471,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float4 x = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
-            const float xs[4] = {x.x, x.y, x.z, x.w};
+            float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
+              if (ACT == 1) xs[e] = act_silu(xs[e]);
               const float hv = round_tf32(xs[e]);
               h[4 * c + e] = __float_as_uint(hv);
               l[4 * c + e] = __float_as_uint(SPLIT ? round_tf32(xs[e] - hv) : 0.f);
@@ -475,7 +491,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int j = 0; j < C::TILE_A / 16 / (32 * SPLIT_WARPS); ++j) {
             const int q = t + 32 * SPLIT_WARPS * j;
-            const float4 x = hi[q];
+            float4 x = hi[q];
+            if (ACT == 1) x = make_float4(act_silu(x.x), act_silu(x.y), act_silu(x.z), act_silu(x.w));
             const float4 h = make_float4(round_tf32(x.x), round_tf32(x.y), round_tf32(x.z), round_tf32(x.w));
             hi[q] = h;
             if (SPLIT)
@@ -497,6 +514,27 @@ __global__ void __launch_bounds__(THREADS, 1)
     int64_t u = 0;
     // one staged TMA store of 32 columns (this warp's 32 rows) from registers
     auto store_chunk = [&](const float* vals, int col, const TileCoord& tc) {
+      float f[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) f[c] = sc * vals[c];
+      if constexpr (ACT == 2) {
+        // this lane's row of the tile: 32 aux values (128 contiguous bytes)
+        const int64_t node = (int64_t)tc.node0 + q * 32 + lane;
+        if (node < a.nodes) {
+          // 16-byte loads (the aux rows have the TMA layout of the GEMM's input: 16-byte
+          // aligned rows, N a multiple of 4)
+          const float4* ar = reinterpret_cast<const float4*>(a.aux + node * a.aux_ld + (int64_t)tc.m * a.aux_ms + col);
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (col + 4 * c < a.N) {
+              const float4 z = __ldg(ar + c);
+              f[4 * c] *= act_dsilu(z.x);
+              f[4 * c + 1] *= act_dsilu(z.y);
+              f[4 * c + 2] *= act_dsilu(z.z);
+              f[4 * c + 3] *= act_dsilu(z.w);
+            }
+        }
+      }
       if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // buffer used two stores ago
       __syncwarp();
       uint8_t* buf = stage0 + nbuf * 4096;
@@ -504,7 +542,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         *reinterpret_cast<float4*>(row + ((c ^ (lane & 7)) << 4)) =
-            make_float4(sc * vals[4 * c], sc * vals[4 * c + 1], sc * vals[4 * c + 2], sc * vals[4 * c + 3]);
+            make_float4(f[4 * c], f[4 * c + 1], f[4 * c + 2], f[4 * c + 3]);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) {
@@ -610,7 +648,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 struct DeviceState {
   bool ready = false;
   int sms = 0;
-  bool attr_set[3][2] = {};
+  bool attr_set[3][2][3] = {};
 };
 
 static std::mutex g_mu;
@@ -662,18 +700,31 @@ static bool encode_b(CUtensorMap* map, const float* base, int kp, int N, int box
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, bool SPLIT>
+template <int BN, bool SPLIT, int ACT>
 static int launch(const CUtensorMap& ma, const BMaps& bm, const CUtensorMap& mc, const CUtensorMap& mpf,
                   const Args& args, DeviceState* ds, int grid, cudaStream_t s) {
   constexpr int bi = BN == 64 ? 0 : BN == 128 ? 1 : 2;
-  if (!ds->attr_set[bi][SPLIT]) {
-    if (cudaFuncSetAttribute(lin_tma_kernel<BN, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (!ds->attr_set[bi][SPLIT][ACT]) {
+    if (cudaFuncSetAttribute(lin_tma_kernel<BN, SPLIT, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg<BN>::SMEM) != cudaSuccess)
       return FC_ERR_LAUNCH;
-    ds->attr_set[bi][SPLIT] = true;
+    ds->attr_set[bi][SPLIT][ACT] = true;
   }
-  lin_tma_kernel<BN, SPLIT><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ma, bm, mc, mpf, args);
+  lin_tma_kernel<BN, SPLIT, ACT><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ma, bm, mc, mpf, args);
   return fc_check_launch();
+}
+
+// the activation modes instantiated: SiLU on the input for every tile width (the radial
+// MLP's second and last layers), SiLU' epilogue for the 64-column input gradients
+template <int BN, bool SPLIT>
+static int launch_act(int act, const CUtensorMap& ma, const BMaps& bm, const CUtensorMap& mc,
+                      const CUtensorMap& mpf, const Args& args, DeviceState* ds, int grid, cudaStream_t s) {
+  if (act == 1) return launch<BN, SPLIT, 1>(ma, bm, mc, mpf, args, ds, grid, s);
+  if (act == 2) {
+    if constexpr (BN == 64) return launch<BN, SPLIT, 2>(ma, bm, mc, mpf, args, ds, grid, s);
+    return 1;
+  }
+  return launch<BN, SPLIT, 0>(ma, bm, mc, mpf, args, ds, grid, s);
 }
 
 }  // namespace tma
@@ -703,6 +754,10 @@ static int run_tma(const LinGemmArgs<float>* a, int n, bool split, int* status, 
   const int BN = (a0.N > 128 && nu == 1) ? 256 : a0.N > 64 ? 128 : 64;
   const int kp = (a0.K + 3) & ~3;
   if (nodes > 0x7fffffffLL) return 1;
+  if (a0.act == 2 && BN != 64) return 1;  // the SiLU' epilogue is instantiated for 64-column tiles
+  if (a0.act == 2 && ((reinterpret_cast<uintptr_t>(a0.aux.p + a0.aux.off) & 15) || (a0.aux.ld & 3) ||
+                      (m_total > 1 && (a0.aux.ms & 3)) || (a0.N & 3)))
+    return 1;  // the epilogue reads aux rows as 16-byte vectors
 
   CUtensorMap ma, mc, mpf;
   BMaps bm;
@@ -747,16 +802,20 @@ static int run_tma(const LinGemmArgs<float>* a, int n, bool split, int* status, 
       for (int j = 0; j < a[l].a.M; ++j) args.rank_of_m[m++] = l;
     for (int m = m_total; m < 16; ++m) args.rank_of_m[m] = 0;
     args.status = status;
+    args.aux = a0.act == 2 ? a0.aux.p + a0.aux.off : nullptr;
+    args.aux_ld = a0.aux.ld;
+    args.aux_ms = m_total > 1 ? a0.aux.ms : 0;
+    const int act = a0.act;
     const int grid = (int)std::min<int64_t>(args.n_tiles, ds->sms);
     if (BN == 64)
-      rc = split ? launch<64, true>(ma, bm, mc, mpf, args, ds, grid, s)
-                 : launch<64, false>(ma, bm, mc, mpf, args, ds, grid, s);
+      rc = split ? launch_act<64, true>(act, ma, bm, mc, mpf, args, ds, grid, s)
+                 : launch_act<64, false>(act, ma, bm, mc, mpf, args, ds, grid, s);
     else if (BN == 128)
-      rc = split ? launch<128, true>(ma, bm, mc, mpf, args, ds, grid, s)
-                 : launch<128, false>(ma, bm, mc, mpf, args, ds, grid, s);
+      rc = split ? launch_act<128, true>(act, ma, bm, mc, mpf, args, ds, grid, s)
+                 : launch_act<128, false>(act, ma, bm, mc, mpf, args, ds, grid, s);
     else
-      rc = split ? launch<256, true>(ma, bm, mc, mpf, args, ds, grid, s)
-                 : launch<256, false>(ma, bm, mc, mpf, args, ds, grid, s);
+      rc = split ? launch_act<256, true>(act, ma, bm, mc, mpf, args, ds, grid, s)
+                 : launch_act<256, false>(act, ma, bm, mc, mpf, args, ds, grid, s);
   }
   // stream-ordered: the workspace returns to the pool after the kernels that read it
   if (ws && fc_pool_free(ws, s) && rc == 0) rc = FC_ERR_LAUNCH;
@@ -781,6 +840,10 @@ int lin_gemm_tma_grouped(const LinGemmArgs<float>* a, int n, bool split, int* st
         (b.bsplit == nullptr) != (a0.bsplit == nullptr) || b.scale != p.scale + 1)
       return 1;
     if (b.a.M < 1 || b.R % b.a.M || b.R / b.a.M != a0.R / a0.a.M) return 1;
+    if (b.act != a0.act) return 1;
+    if (a0.act == 2 && (b.aux.p != a0.aux.p || b.aux.ld != a0.aux.ld || b.aux.ms != a0.aux.ms ||
+                        b.aux.off != p.aux.off + (int64_t)p.aux.M * p.aux.ms))
+      return 1;
     if (b.a.off != p.a.off + (int64_t)p.a.M * p.a.ms || b.c.off != p.c.off + (int64_t)p.c.M * p.c.ms) return 1;
   }
   return run_tma(a, n, split, status, s);

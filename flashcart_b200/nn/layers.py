@@ -97,14 +97,32 @@ class LinearLayer(nn.Module):
         self._meta = torch.zeros(1, 6, dtype=torch.int64)
         self._lists = ([0], [0], [0], [1], [in_features], [out_features])
 
-    def forward(self, x, input_scale: Optional[torch.Tensor] = None):
+    def silu_input_fusable(self, x) -> bool:
+        """The SiLU of the input can be applied inside this layer's GEMM (first derivative
+        only, frozen weights, float32 on the GPU, at most 64 inputs: the input gradient's
+        SiLU' epilogue exists for 64-column tiles; row widths in 16-byte units for TMA)."""
+        return (ops.first_order_only_active() and x.is_cuda and x.dtype == torch.float32
+                and self.weight.dtype == torch.float32 and not self.weight.requires_grad
+                and self.in_features <= 64 and self.in_features % 4 == 0 and self.out_features % 4 == 0)
+
+    def forward(self, x, input_scale: Optional[torch.Tensor] = None, silu_input: bool = False):
         """``input_scale`` (optional 0-d tensor) multiplies the input; the map is linear, so it
-        is applied to the layer's scale instead of to every element of ``x``."""
+        is applied to the layer's scale instead of to every element of ``x``. ``silu_input``
+        makes the layer act on silu(x) (inside its GEMM when :meth:`silu_input_fusable`)."""
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.in_features)
         use_fp64, precision = o3.utils.get_linear_triton_kernel_options(x.dtype)
         w = self.weight if self.weight.dtype == x.dtype else self.weight.to(x.dtype)
         scale = self.scale.reshape(1) if input_scale is None else self.scale.reshape(1) * input_scale
+        if silu_input and self.silu_input_fusable(x2):
+            y = torch.ops.flashcart.linear_silu_fwd(x2, [w], self.out_features, precision, self._lists[0],
+                                                    self._lists[1], self._lists[3], self._lists[4], self._lists[5],
+                                                    scale)
+            if self.bias is not None:
+                y = y + self.bias
+            return y.reshape(*lead, self.out_features)
+        if silu_input:
+            x2 = F.silu(x2)
         y = torch.ops.flashcart.linear_fwd(x2, [w], self._meta, self.out_features, use_fp64, precision,
                                            *self._lists, scale)
         if self.bias is not None:
@@ -124,17 +142,21 @@ LinearLayer.non_muon_parameters = _linear_non_decayable
 class _MLP(nn.Sequential):
     """Linear / rescaled-SiLU stack (the reference's ``nn.Sequential``, same state_dict keys).
     The constant of each rescaled SiLU is handed to the next linear layer's scale instead of
-    being multiplied into the activations (one pass over the edge rows less per layer)."""
+    being multiplied into the activations (one pass over the edge rows less per layer), and
+    the SiLU itself is applied by that layer: inside its GEMM in first-order evaluation with
+    frozen weights (no activation tensor is written; SiLU' is applied in the input
+    gradient's epilogue), else as a separate elementwise pass."""
 
     def forward(self, x):
         mods = list(self)
         pending = None
         for k, m in enumerate(mods):
             if isinstance(m, RescaledSiLULayer) and k + 1 < len(mods) and isinstance(mods[k + 1], LinearLayer):
-                x = F.silu(x)
+                # the next linear layer applies the SiLU to its input (inside its GEMM where
+                # possible) and takes the rescale into its weight scale
                 pending = m.scale
             elif isinstance(m, LinearLayer):
-                x = m(x, input_scale=pending)
+                x = m(x, input_scale=pending, silu_input=pending is not None)
                 pending = None
             else:
                 x = m(x)

@@ -528,8 +528,9 @@ irreps_bwd.register_autograd(_irreps_bwd_backward, setup_context=_irreps_bwd_set
 
 
 def _linear_desc(x: Tensor, out_dim: int, in_offsets, out_offsets, m_values, f_in_values, f_out_values,
-                 precision: str) -> N.LinearDesc:
+                 precision: str, act: int = 0) -> N.LinearDesc:
     d = N.LinearDesc()
+    d.act = int(act)
     n = len(in_offsets)
     if n > N.FC_MAX_L + 1:
         raise NotImplementedError(f"flashcart_b200 linear supports at most {N.FC_MAX_L + 1} ranks, got {n}")
@@ -598,14 +599,14 @@ def _split_weights(lib, d: N.LinearDesc, ws: Sequence[Tensor], backward: bool):
 
 
 def _linear_fwd_impl(x: Tensor, weights: Sequence[Tensor], out_dim: int, lists, precision: str,
-                     scale: Tensor) -> Tensor:
+                     scale: Tensor, act: int = 0) -> Tensor:
     lib = N.lib()
     x = x.contiguous()
     n_active = len(lists[0])
     ws = [w.to(x.dtype).contiguous() for w in weights[:n_active]]
     sc = scale.to(device=x.device, dtype=torch.float32 if x.dtype == torch.bfloat16 else x.dtype).contiguous()
     out = x.new_empty((x.shape[0], int(out_dim)))
-    d = _linear_desc(x, out_dim, lists[0], lists[1], lists[3], lists[4], lists[5], precision)
+    d = _linear_desc(x, out_dim, lists[0], lists[1], lists[3], lists[4], lists[5], precision, act)
     split = _split_weights(lib, d, ws, False)
     with _timed("linear_fwd", n_active, _nbytes(x, out, *ws)):
         if split is not None:
@@ -620,7 +621,7 @@ def _linear_fwd_impl(x: Tensor, weights: Sequence[Tensor], out_dim: int, lists, 
 
 
 def _linear_bwd_impl(grad_out: Tensor, x: Tensor, weights: Sequence[Tensor], need_x: bool, need_w: bool,
-                     lists, precision: str, scale: Tensor) -> Tuple[Tensor, List[Tensor]]:
+                     lists, precision: str, scale: Tensor, act: int = 0) -> Tuple[Tensor, List[Tensor]]:
     lib = N.lib()
     g, x = grad_out.contiguous(), x.contiguous()
     n_active = len(lists[0])
@@ -632,7 +633,7 @@ def _linear_bwd_impl(grad_out: Tensor, x: Tensor, weights: Sequence[Tensor], nee
         if need_x:
             gx.zero_()
         return gx, gws
-    d = _linear_desc(x, g.shape[1], lists[0], lists[1], lists[3], lists[4], lists[5], precision)
+    d = _linear_desc(x, g.shape[1], lists[0], lists[1], lists[3], lists[4], lists[5], precision, act)
     split = _split_weights(lib, d, ws, True) if need_x else None
     with _timed("linear_bwd", n_active * (int(need_x) + int(need_w)), _nbytes(g, x, gx, *ws, *gws)):
         if split is not None:
@@ -678,6 +679,63 @@ def _(grad_out, x, weights, need_x, need_weight, use_fp64, dot_input_precision, 
     n = len(in_offsets)
     return (torch.empty_like(x) if need_x else x.new_empty((0,)),
             [torch.empty_like(w) if need_weight else w.new_empty((0,)) for w in weights[:n]])
+
+
+@torch.library.custom_op("flashcart::linear_silu_fwd", mutates_args=())
+def linear_silu_fwd(x: Tensor, weights: List[Tensor], out_size: int, dot_input_precision: str,
+                    in_offsets: List[int], out_offsets: List[int], m_values: List[int], f_in_values: List[int],
+                    f_out_values: List[int], scale: Tensor) -> Tensor:
+    """``linear_fwd`` of silu(x): the SiLU between two layers of the radial MLP
+    (reference ``nn/layers.py:12-44``) applied by the GEMM's splitter warps to its input
+    tiles, so the activations are never written (``fc_linear_desc.act = FC_ACT_SILU``)."""
+    _require_cuda(x, *weights)
+    lists = (in_offsets, out_offsets, [0] * len(in_offsets), m_values, f_in_values, f_out_values)
+    return _linear_fwd_impl(x, weights, out_size, lists, dot_input_precision, scale, N.FC_ACT_SILU)
+
+
+@linear_silu_fwd.register_fake
+def _(x, weights, out_size, dot_input_precision, in_offsets, out_offsets, m_values, f_in_values, f_out_values,
+      scale):
+    return x.new_empty((x.shape[0], int(out_size)))
+
+
+@torch.library.custom_op("flashcart::linear_silu_bwd", mutates_args=())
+def linear_silu_bwd(grad_out: Tensor, x: Tensor, weights: List[Tensor], dot_input_precision: str,
+                    in_offsets: List[int], out_offsets: List[int], m_values: List[int], f_in_values: List[int],
+                    f_out_values: List[int], scale: Tensor) -> Tensor:
+    """Input gradient of :func:`linear_silu_fwd`: silu'(x) * (grad_out (sW)) with the factor
+    applied in the GEMM's epilogue (frozen weights: no weight gradient)."""
+    _require_cuda(grad_out, x, *weights)
+    lists = (in_offsets, out_offsets, [0] * len(in_offsets), m_values, f_in_values, f_out_values)
+    gx, _ = _linear_bwd_impl(grad_out, x, weights, True, False, lists, dot_input_precision, scale, N.FC_ACT_SILU)
+    return gx
+
+
+@linear_silu_bwd.register_fake
+def _(grad_out, x, weights, dot_input_precision, in_offsets, out_offsets, m_values, f_in_values, f_out_values,
+      scale):
+    return torch.empty_like(x)
+
+
+def _lsilu_setup(ctx, inputs, output):
+    x, weights = inputs[0], inputs[1]
+    ctx.save_for_backward(x, inputs[-1], *weights)
+    ctx.n_w = len(weights)
+    ctx.meta = inputs[3:-1]
+
+
+def _lsilu_backward(ctx, grad_out):
+    if torch.is_grad_enabled():
+        raise RuntimeError("flashcart::linear_silu_fwd was evaluated inside first_order_only(); its backward "
+                           "cannot build a graph for a second derivative")
+    x, scale, *weights = ctx.saved_tensors
+    if any(w.requires_grad for w in weights):
+        raise RuntimeError("flashcart::linear_silu_fwd has no weight gradient (frozen weights only)")
+    gx = linear_silu_bwd(grad_out.contiguous(), x, weights, *ctx.meta, scale) if ctx.needs_input_grad[0] else None
+    return (gx, [None] * len(weights), None) + (None,) * 7
+
+
+linear_silu_fwd.register_autograd(_lsilu_backward, setup_context=_lsilu_setup)
 
 
 @torch.library.custom_op("flashcart::linear_dbwd", mutates_args=())

@@ -55,6 +55,11 @@ typedef void* fc_stream_t;
 #define FC_F64 1
 #define FC_BF16 2  /* fc_newton_schulz input; fc_linear_fwd storage (x, weights, y in bf16) */
 
+/* activation applied to a linear map's input (fc_linear_desc.act): the radial MLP's SiLU
+ * between its layers (nn/layers.py:12-44) folded into the next layer's GEMM */
+#define FC_ACT_NONE 0
+#define FC_ACT_SILU 1
+
 /* linear-map arithmetic */
 #define FC_PREC_IEEE 0 /* fp32-accurate: fp64 FMA, or fp32 on tensor cores as 3xTF32 (hi*hi+hi*lo+lo*hi) */
 #define FC_PREC_TF32 1 /* fp32 only: one tf32 tensor-core product, fp32 accumulation */
@@ -191,7 +196,9 @@ typedef struct fc_linear_desc {
   int32_t n_active;                     /* active ranks, 0..FC_MAX_L+1 */
   int32_t dtype;                        /* FC_F32 / FC_F64, or FC_BF16 (fc_linear_fwd only) */
   int32_t precision;                    /* FC_PREC_IEEE or FC_PREC_TF32 (fp32 only) */
-  int32_t reserved;
+  int32_t act;                          /* FC_ACT_NONE, or FC_ACT_SILU (fp32 on the TMA path only):
+                                           forward y = (sW) silu(x), backward grad_x = silu'(x) *
+                                           ((sW)^T g); no weight gradients (frozen weights) */
   int64_t in_dim, out_dim;              /* row widths of x and y */
   int64_t in_offsets[FC_MAX_L + 1];
   int64_t out_offsets[FC_MAX_L + 1];

@@ -560,3 +560,39 @@ def test_gpu_bf16_linear_rejects_unaligned_and_backward(cuda_device):
     y = lin2(x2)
     with pytest.raises(NotImplementedError):
         y.sum().backward()
+
+
+@pytest.mark.parametrize("widths", [[8, 64, 64, 2944], [256, 64, 64, 1]])
+def test_gpu_mlp_silu_inside_gemm_equals_composed(cuda_device, widths):
+    """The radial / readout MLP with each SiLU applied inside the next layer's GEMM (its
+    splitter warps) and SiLU' in the input gradient's epilogue (first-order evaluation,
+    frozen weights) equals the composed SiLU passes: output and input gradient within
+    float32 rounding of the 3xTF32 GEMMs."""
+    from flashcart_b200 import ops
+    from flashcart_b200.nn.layers import _mlp
+
+    torch.manual_seed(len(widths) + widths[0])
+    mlp = _mlp(widths).to(cuda_device)
+    for p in mlp.parameters():
+        p.requires_grad_(False)
+    x = torch.randn(20000, widths[0], device=cuda_device)
+    go = torch.randn(20000, widths[-1], device=cuda_device)
+    xa = x.clone().requires_grad_(True)
+    ya = mlp(xa)
+    (ga,) = torch.autograd.grad(ya, xa, go)
+    xb = x.clone().requires_grad_(True)
+    timer = ops.KernelTimer()
+    ops.set_kernel_timer(timer)
+    try:
+        with ops.first_order_only():
+            yb = mlp(xb)
+            (gb,) = torch.autograd.grad(yb, xb, go)
+    finally:
+        ops.set_kernel_timer(None)
+    names = [r[0] for r in timer.records]
+    assert names.count("linear_fwd") == 3 and names.count("linear_bwd") == 3
+    fused = sum(1 for m in mlp if hasattr(m, "silu_input_fusable") and m.out_features % 4 == 0) - 1
+    assert fused >= 1
+    assert float((ya - yb).abs().max() / ya.abs().max()) < 2e-5
+    assert float((ga - gb).abs().max() / ga.abs().max()) < 2e-5
+    check_device_status(cuda_device)
