@@ -13,8 +13,9 @@
 // 64-wide k slabs of x and W (bf16, 128-byte swizzle) into a 2-stage ring (three CTAs per
 // SM overlap one another's loads, MMAs and stores); one thread issues
 // tcgen05.mma.kind::f16 (both operands bf16) into a 128 x 128 fp32 accumulator; after the last
-// slab every warp reads its 32 rows from tensor memory, scales, rounds to bf16 and stores
-// 16-byte vectors. Every wait is bounded (FC_DEV_TIMEOUT); the MMAs are drained before the
+// slab every warp reads its 32 rows from tensor memory, scales, rounds to bf16, stages them
+// in the freed operand buffers as two 128-byte-swizzled 64-column boxes and stores them with
+// TMA (16-byte row stores when the output block is not 16-byte aligned). Every wait is bounded (FC_DEV_TIMEOUT); the MMAs are drained before the
 // tensor memory is freed.
 #include "fc_base.cuh"
 
@@ -24,6 +25,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace fc {
@@ -47,7 +49,7 @@ struct Args {
   const float* scale;   // this rank's scale (float32)
   __nv_bfloat16* out;   // first element of the output rank block
   int64_t out_ld, out_ms;
-  int vec;              // 16-byte stores allowed (alignment checked on the host)
+  int vec;              // aligned output block: staged TMA stores through map_c
   int* status;
 };
 
@@ -89,7 +91,7 @@ __device__ __forceinline__ bool wait_parity(uint32_t mbar, uint32_t parity, int*
 
 __global__ void __launch_bounds__(128, 3)
     lin_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                    const Args a) {
+                    const __grid_constant__ CUtensorMap map_c, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
@@ -192,23 +194,51 @@ __global__ void __launch_bounds__(128, 3)
         : "r"(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cb));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     const int col = n0 + cb;
-    if (!ready || node >= a.nodes || col >= a.N) continue;
-    if (a.vec && col + 32 <= a.N) {
-      uint32_t pk[16];
+    if (a.vec) {
+      if (!ready) continue;
+      // staged for the TMA store: this warp's 32 rows as two 64-column boxes (128-byte rows,
+      // 16-byte chunk c of row r at c ^ (r & 7)) in the operand stages, free after `done`
+      uint8_t* box = smem + warp * 8192 + (cb >> 6) * 4096 + lane * 128;
+      const int c0 = ((cb & 63) * 2) >> 4;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const __nv_bfloat162 b2 =
-            __floats2bfloat162_rn(sc * __uint_as_float(v[2 * j]), sc * __uint_as_float(v[2 * j + 1]));
-        pk[j] = *reinterpret_cast<const uint32_t*>(&b2);
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w4[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int j = 4 * q + t;
+          const __nv_bfloat162 b2 =
+              __floats2bfloat162_rn(sc * __uint_as_float(v[2 * j]), sc * __uint_as_float(v[2 * j + 1]));
+          w4[t] = *reinterpret_cast<const uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(box + (((c0 + q) ^ (lane & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
-      uint4* dst = reinterpret_cast<uint4*>(orow + col);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col + j < a.N) orow[col + j] = __float2bfloat16_rn(sc * __uint_as_float(v[j]));
+      continue;
     }
+    if (!ready || node >= a.nodes || col >= a.N) continue;
+    // unaligned output block: element stores
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col + j < a.N) orow[col + j] = __float2bfloat16_rn(sc * __uint_as_float(v[j]));
+  }
+  if (a.vec) {
+    // TMA stores of the warp's two boxes (rows beyond the nodes and columns beyond N are
+    // clipped by the unit); the smem reads finish before the CTA exits
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0 && ready && node0 + warp * 32 < a.nodes) {
+      for (int h = 0; h < 2; ++h) {
+        const int x = n0 + 64 * h;
+        if (x >= a.N) break;
+        asm volatile(
+            "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                reinterpret_cast<uint64_t>(&map_c)),
+            "r"(smem_u32(smem + warp * 8192 + h * 4096)), "r"(x), "r"((int)(node0 + warp * 32)), "r"(m)
+            : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
@@ -297,10 +327,23 @@ int lin_bf16_rank(const void* x, int64_t ld, int64_t off, int64_t ms, int M, int
   a.out_ld = out_ld;
   a.out_ms = M > 1 ? out_ms : 0;
   a.vec = ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && out_ld % 8 == 0 && (M == 1 || out_ms % 8 == 0)) ? 1 : 0;
+  CUtensorMap mc;
+  std::memset(&mc, 0, sizeof(mc));
+  if (a.vec) {
+    // (n, node, m) rows of the output block, box 64 x 32 x 1, 128-byte swizzle (the staging layout)
+    const cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)nodes, (cuuint64_t)M};
+    const cuuint64_t strides[2] = {(cuuint64_t)out_ld * 2, (cuuint64_t)(M > 1 ? out_ms : out_ld * nodes) * 2};
+    const cuuint32_t box[3] = {64u, 32u, 1u};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (encode_fn()(&mc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.out, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      a.vec = 0;
+  }
   a.status = status;
   const int64_t tiles = a.row_tiles * a.n_col_tiles;
   if (tiles > 0x7fffffffLL || M > 65535) return FC_ERR_UNSUPPORTED;
-  lin_bf16_kernel<<<dim3((unsigned)tiles, (unsigned)M), 128, SMEM, s>>>(ma, mb, a);
+  lin_bf16_kernel<<<dim3((unsigned)tiles, (unsigned)M), 128, SMEM, s>>>(ma, mb, mc, a);
   return fc_check_launch();
 }
 
