@@ -95,11 +95,17 @@ def build_model(avg_neighbors: float, device):
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region.
+
+    NVML (read-only queries) polled every 10 ms from a thread, so a timed region of a few
+    tens of milliseconds (8 ranks) still gets samples; the first sample is taken when the
+    sampler starts, i.e. at the start of the timed region. Where NVML cannot be loaded,
+    ``nvidia-smi -lms 200`` in a subprocess (which misses regions shorter than 200 ms)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, local_rank: int):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -111,8 +117,49 @@ class ClockSampler:
         self.idx = idx
         self.proc = None
         self.file = None
+        self.thread = None
+        self.samples = []  # (sm_mhz, max_mhz, reasons)
+        self.source = None
+
+    def _nvml_handle(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+        except Exception:  # NVML missing or no such device: fall back to nvidia-smi
+            return None, None
+
+    def _nvml_sample(self, nv, h):
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        flags = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        self.samples.append((float(sm), float(mx), {n for n, f in zip(self.NAMES, flags) if bits & f}))
 
     def start(self):
+        import threading
+
+        nv, h = self._nvml_handle()
+        if nv is not None:
+            self.source = "nvml"
+            self._stop = threading.Event()
+            try:
+                self._nvml_sample(nv, h)
+            except Exception:
+                nv = None
+        if nv is not None:
+            def poll():
+                while not self._stop.wait(0.010):
+                    try:
+                        self._nvml_sample(nv, h)
+                    except Exception:
+                        return
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        self.source = "nvidia-smi"
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -121,9 +168,7 @@ class ClockSampler:
         except (OSError, ValueError):
             self.proc = None
 
-    def stop(self):
-        if self.proc is None:
-            return None
+    def _read_smi(self):
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -133,24 +178,28 @@ class ClockSampler:
         self.file.seek(0)
         rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
         os.unlink(self.file.name)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             r = [c.strip() for c in r]
             if len(r) < 9:
                 continue
             try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
+                sm, mx = float(r[1]), float(r[2])
             except ValueError:
                 continue
-            for n, v in zip(names, r[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+            self.samples.append((sm, mx, {n for n, v in zip(self.NAMES, r[5:9]) if v.lower() == "active"}))
+
+    def stop(self):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+        elif self.proc is not None:
+            self._read_smi()
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = set().union(*(r for _, _, r in self.samples))
+        return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
+                "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": self.source}
 
 
 # --------------------------------------------------------------------------------- helpers
@@ -384,10 +433,12 @@ def run_b200(args):
     torch.cuda.synchronize()
     e2e_ms = a0.elapsed_time(a1) / args.steps
 
-    # roofline of the dominant kernel (largest total device time in the timed region)
+    # roofline of the dominant kernel (largest total device time in the timed region). The
+    # halo collective is not a candidate: its eager-pass time includes the wait for the
+    # slowest rank (ranks drift apart in eager mode), so it is timed on its own below.
     durs = timer.durations_ms()
     nbytes = timer.bytes_per_call()
-    top = max(durs, key=lambda k: sum(durs[k]))
+    top = max((k for k in durs if not k.startswith("halo")), key=lambda k: sum(durs[k]))
     avg_ms = sum(durs[top]) / len(durs[top])
     bytes_per_launch = sum(nbytes[top]) / len(nbytes[top])
     peak, peak_src = _peaks()
@@ -404,14 +455,16 @@ def run_b200(args):
         # what limits the scaling: per-rank step time (graphed), halo time (eager pass: pack,
         # NCCL all-to-all, unpack, forward and backward) and each rank's share of the edges
         halo_ms = sum(sum(v) for k, v in durs.items() if k.startswith("halo")) / args.steps
+        alone_ms = _halo_alone_ms(plan, graph_feature_width(model), dev)
         mine = torch.tensor([ms, eager_ms, halo_ms, float(plan.edge_index.shape[1]), float(plan.n_own),
-                             float(plan.n_ghost)], device=dev, dtype=torch.float64)
+                             float(plan.n_ghost), alone_ms], device=dev, dtype=torch.float64)
         every = [torch.zeros_like(mine) for _ in range(world)]
         dist.all_gather(every, mine)
         every = torch.stack(every).cpu()
         ranks = {"step_ms": [round(float(v), 3) for v in every[:, 0]],
                  "eager_ms": [round(float(v), 3) for v in every[:, 1]],
                  "halo_ms_per_step": [round(float(v), 3) for v in every[:, 2]],
+                 "halo_exchange_alone_ms": [round(float(v), 4) for v in every[:, 6]],
                  "edges": [int(v) for v in every[:, 3]], "owned_atoms": [int(v) for v in every[:, 4]],
                  "ghost_atoms": [int(v) for v in every[:, 5]],
                  "edge_imbalance_max_over_min": float(every[:, 3].max() / every[:, 3].min())}
@@ -454,6 +507,34 @@ def run_b200(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def graph_feature_width(model) -> int:
+    """Width of the node features that the halo exchange moves between interaction layers."""
+    return int(model.node_dim)
+
+
+def _halo_alone_ms(plan, width: int, dev, reps: int = 20) -> float:
+    """One forward halo exchange (pack, NCCL all-to-all, unpack) of a layer's node features
+    (owned rows x width floats), timed on its own after a barrier: the per-exchange cost
+    without the rank skew that the eager pass adds. Every rank runs the same exchanges."""
+    import torch.distributed as dist
+
+    from flashcart_b200.domain import ghost_rows_from_owners
+
+    x = torch.randn(plan.n_own, width, device=dev)
+    out = x.new_empty((plan.n_ghost, width))
+    for _ in range(3):
+        ghost_rows_from_owners(x, plan, out=out)
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        ghost_rows_from_owners(x, plan, out=out)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
 
 
 def run_op_case(case: str):
