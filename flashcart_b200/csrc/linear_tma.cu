@@ -67,6 +67,9 @@ constexpr long long WAIT_LIMIT = 1ll << 22;
 #ifndef FC_TMA_ATM64
 #define FC_TMA_ATM64 1
 #endif
+#ifndef FC_TMA_WIDE64
+#define FC_TMA_WIDE64 1
+#endif
 constexpr int KG = FC_TMA_KG;
 constexpr int PF_SLABS = 4;   // k slabs per L2 prefetch box (512 bytes of each row)
 #ifndef FC_TMA_PF_AHEAD
@@ -89,7 +92,13 @@ struct Cfg {
   static constexpr int STAGES = ATM ? 4 : RING_BYTES / STAGE;
   static constexpr int A_COLS = ATM ? STAGES * 2 * BK : 0;  // tensor-memory A stages: hi | lo columns
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + BAR_BYTES + 1024;
-  static constexpr int NACC = (512 - A_COLS) / BN;  // TMEM accumulators in the ring (the other columns)
+  // WIDE (BN = 64, 3xTF32): per k step one N = 128 MMA Ahi x [Bhi | Blo] (the two B parts
+  // are adjacent in the stage) and one N = 64 MMA Alo x Bhi, instead of three N = 64 MMAs;
+  // an N = 64 MMA costs about as much time as an N = 128 one. Each accumulation unit then
+  // holds two 64-column halves that the epilogue adds.
+  static constexpr bool WIDE = BN == 64 && FC_TMA_WIDE64;
+  static constexpr int ACC_W = WIDE ? 2 * BN : BN;  // accumulator columns per unit (3xTF32)
+  static constexpr int NACC = (512 - A_COLS) / ACC_W;  // TMEM accumulators in the ring (the other columns)
   static constexpr int TMEM_COLS = 512;
   static_assert(STAGES >= 2 && STAGES <= 8, "operand ring");
   static_assert(NACC >= 2, "accumulator ring");
@@ -295,6 +304,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                    const Args a) {
   using C = Cfg<BN>;
   constexpr int S = C::STAGES;
+  constexpr bool WIDE = C::WIDE && SPLIT;
+  constexpr int AW = C::ACC_W;  // ring stride of the accumulators (the same without SPLIT: only WIDE fills 2 BN)
   constexpr int B_OFF = C::ATM ? C::TILE_A : 2 * C::TILE_A;  // B hi | lo after the A slab (and its lo half)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -399,7 +410,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;");
-          const uint32_t d = tmem + (uint32_t)(C::A_COLS + b * BN);
+          const uint32_t d = tmem + (uint32_t)(C::A_COLS + b * AW);
           const int k_end = min(a.nk, (j + 1) * KG);
           for (int kt = j * KG; kt < k_end; ++kt, ++g) {
             const int s = (int)(g % S);
@@ -417,7 +428,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               for (int kk = 0; kk < BK / 8; ++kk) {
                 const uint64_t off = (uint64_t)((kk * 32) >> 4);
                 const uint32_t acc = (kt > j * KG || kk > 0) ? 1u : 0u;
-                if (SPLIT) {
+                if (WIDE) {
+                  mma_ta<2 * BN>(d, tah + kk * 8, dbh + off, acc);  // [Ahi Bhi | Ahi Blo]
+                  mma_ta<BN>(d, tal + kk * 8, dbh + off, 1u);       // + Alo Bhi in the first half
+                } else if (SPLIT) {
                   mma_ta<BN>(d, tal + kk * 8, dbh + off, acc);
                   mma_ta<BN>(d, tah + kk * 8, dbl + off, 1u);
                   mma_ta<BN>(d, tah + kk * 8, dbh + off, 1u);
@@ -431,7 +445,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               for (int kk = 0; kk < BK / 8; ++kk) {
                 const uint64_t off = (uint64_t)((kk * 32) >> 4);
                 const uint32_t acc = (kt > j * KG || kk > 0) ? 1u : 0u;
-                if (SPLIT) {
+                if (WIDE) {
+                  mma<2 * BN>(d, dah + off, dbh + off, acc);
+                  mma<BN>(d, dal + off, dbh + off, 1u);
+                } else if (SPLIT) {
                   mma<BN>(d, dal + off, dbh + off, acc);
                   mma<BN>(d, dah + off, dbl + off, 1u);
                   mma<BN>(d, dah + off, dbh + off, 1u);
@@ -579,7 +596,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("tcgen05.fence::after_thread_sync;");
         for (int cb = 0; cb < nchunks; ++cb) {
           float f[32];
-          load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COLS + b * BN + cb * 32), f);
+          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COLS + b * AW + cb * 32);
+          load32(ta, f);
+          if constexpr (WIDE) {
+            float f2[32];
+            load32(ta + BN, f2);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) f[c] += f2[c];
+          }
           store_chunk(f, col0 + cb * 32, tc);
         }
         asm volatile("tcgen05.fence::before_thread_sync;");
@@ -599,11 +623,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           asm volatile("tcgen05.fence::after_thread_sync;");
 #pragma unroll
-          for (int cb = 0; cb < BN / 32; ++cb) {
+          for (int cb = 0; cb < (WIDE ? 2 * BN : BN) / 32; ++cb) {
             float f[32];
-            load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COLS + b * BN + cb * 32), f);
+            load32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(C::A_COLS + b * AW + cb * 32), f);
 #pragma unroll
-            for (int c = 0; c < 32; ++c) acc[cb * 32 + c] += f[c];
+            for (int c = 0; c < 32; ++c) acc[(cb % (BN / 32)) * 32 + c] += f[c];
           }
           asm volatile("tcgen05.fence::before_thread_sync;");
           __syncwarp();
