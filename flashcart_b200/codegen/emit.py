@@ -27,7 +27,7 @@ import sys
 from fractions import Fraction
 from typing import Dict, List, Sequence, Tuple
 
-from flashcart_b200.codegen import emit_conv, emit_pair, stf
+from flashcart_b200.codegen import emit_conv, emit_dense, emit_pair, stf
 
 L_MAX = 3
 GEN_DIR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "csrc", "gen")
@@ -437,6 +437,7 @@ def emit_signature(sig: Sig) -> str:
     w("#ifndef FC_HOST_EMU")
     L.append(emit_conv.emit(sig, stores))
     L.append(emit_pair.emit(sig, stores))
+    L.append(emit_dense.emit(sig, stores))
     w("#endif")
     w("struct Ops {")
     w("  static constexpr int NP = sig_np, NACC = sig_nacc;".replace("sig_np", str(sig.npaths)).replace("sig_nacc", str(sig.nacc)))
@@ -452,6 +453,8 @@ def emit_signature(sig: Sig) -> str:
       "{ return launch_bwd2<T>(P, s); }")
     w("  static int fwd3(const TpParams<float>& P, cudaStream_t s) { return launch_fwd3(P, s); }")
     w("  static int bwd3(const TpBwdParams<float>& P, cudaStream_t s) { return launch_bwd3(P, s); }")
+    w("  static int dpfwd(const TpParams<float>& P, cudaStream_t s) { return launch_dpfwd(P, s); }")
+    w("  static int dpbwd(const TpBwdParams<float>& P, cudaStream_t s) { return launch_dpbwd(P, s); }")
     w("#endif")
     w("};")
     w(f"}}  // namespace sig_{n}")

@@ -74,6 +74,10 @@ struct TpTable {
   // channel-pair convolution kernels (float32, F = 64 or 128; may be null)
   int (*fwd3_f32)(const TpParams<float>&, cudaStream_t);
   int (*bwd3_f32)(const TpBwdParams<float>&, cudaStream_t);
+  // channel-pair dense products (no edges, both inputs with F = 64 or 128 channels,
+  // weights per row; float32; may be null)
+  int (*dpfwd_f32)(const TpParams<float>&, cudaStream_t);
+  int (*dpbwd_f32)(const TpBwdParams<float>&, cudaStream_t);
 };
 
 struct TpSigEntry {
@@ -318,9 +322,9 @@ int tp_dbwd_launch(const TpDbwdParams<T>& P, cudaStream_t) {
 #ifndef FC_HOST_EMU
 #define FC_CONV2_ENTRIES(NS)                                                              \
   , &NS::Ops::fwd2<float>, &NS::Ops::fwd2<double>, &NS::Ops::bwd2<float>, &NS::Ops::bwd2<double>, \
-      &NS::Ops::fwd3, &NS::Ops::bwd3
+      &NS::Ops::fwd3, &NS::Ops::bwd3, &NS::Ops::dpfwd, &NS::Ops::dpbwd
 #else
-#define FC_CONV2_ENTRIES(NS) , nullptr, nullptr, nullptr, nullptr, nullptr, nullptr
+#define FC_CONV2_ENTRIES(NS) , nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr
 #endif
 #define FC_DEFINE_TP_SIGNATURE(NAME, NS)                                                  \
   extern const TpTable tp_table_##NAME;                                                   \
