@@ -54,7 +54,7 @@ def _args():
     ap.add_argument("--cpu-atoms", type=int, choices=sorted(CPU_BOXES), default=192,
                     help="atoms of the CPU sample (same density as the 27,648-atom box; the per-atom rate is the reported "
                          "figure, the 27,648-atom box itself does not fit host RAM in the reference py path)")
-    ap.add_argument("--op-case", choices=["conv", "gemm", "linear_bf16"], default=None,
+    ap.add_argument("--op-case", choices=["conv", "gemm", "linear_bf16", "dense"], default=None,
                     help="run one small operator case (for ncu captures) instead of the benchmark")
     ap.add_argument("--allreduce", choices=["buckets", "flat"], default="buckets",
                     help="data-parallel training: gradient all-reduce in buckets during the backward, or one "
@@ -541,7 +541,9 @@ def run_op_case(case: str):
     """Small single-operator cases with the benchmark's shapes, sized for ncu captures (a few GB):
     ``conv``: conv products (3,3)->3 and (0,3)->3, C=128, forward + backward, on a 3,456-atom water
     box; ``gemm``: the radial-MLP output layer 64 -> 23*128 and its input gradient on 200,000 rows;
-    ``linear_bf16``: the bf16 storage path of o3.LinearLayer(3, 3, 128, 128) on 400,000 rows."""
+    ``linear_bf16``: the bf16 storage path of o3.LinearLayer(3, 3, 128, 128) on 400,000 rows;
+    ``dense``: the product layers' node-level product (3,3)->3, C=128, shared frozen weights,
+    forward + input gradients on the benchmark's 27,648 rows."""
     from flashcart_b200 import o3
     from flashcart_b200.data import neighbors, synthetic
     from flashcart_b200.nn.layers import LinearLayer
@@ -565,6 +567,14 @@ def run_op_case(case: str):
             torch.ops.flashcart.tp_bwd(torch.randn_like(out), in1, x2, w, ei[0], ei[1], l1, l2, lo, c, 1, False,
                                        False, tp._in1_offs, tp._in2_offs, tp._out_sizes, tp._n_paths_per_l,
                                        tp.n_total_paths, False, l1 > 0, True, True)
+    elif case == "dense":
+        tp = o3.TensorProduct(3, 3, 3, 128, 128, shared_weights=True)
+        n = 27_648
+        in1 = torch.randn(n, tp.in1_dim, device=dev, generator=g, requires_grad=True)
+        in2 = torch.randn(n, tp.in2_dim, device=dev, generator=g, requires_grad=True)
+        w = torch.randn(tp.n_total_paths * 128, device=dev, generator=g)
+        out = tp(in1, in2, w)
+        torch.autograd.grad(out, [in1, in2], torch.randn_like(out))
     elif case == "linear_bf16":
         lin = o3.LinearLayer(3, 3, 128, 128, weight_scale=1.0).to(dev)
         x = torch.randn(400_000, 16 * 128, device=dev, generator=g).to(torch.bfloat16)

@@ -3,9 +3,10 @@
 Emitted into each signature file next to the generic bodies of
 :mod:`flashcart_b200.codegen.emit`, for the case of the product layers
 (``nn/layers.py:768-1018`` of the reference: ``TensorProduct`` of two node-feature
-tensors with per-node path weights): no edges (``rowptr == NULL``, output row = in1 row =
-in2 row), both inputs with the same ``F`` channels (64 or 128), weights per row, paths
-not reduced.
+tensors): no edges (``rowptr == NULL``, output row = in1 row = in2 row), both inputs with
+the same ``F`` channels (64 or 128), paths not reduced, weights per row or shared by all
+rows (the element-agnostic products; their backward takes this kernel only when no
+weight gradient is requested, since a shared weight gradient is a reduction over rows).
 
 Each thread owns two adjacent channels ``2t, 2t+1`` of one row (``F/2`` threads per
 row, several rows per 128-thread CTA). Loads and stores are 8-byte ``float2`` vectors and
@@ -68,7 +69,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("  const int c = 2 * (int)(threadIdx.x % tpr);")
     w("  const float* __restrict__ a1 = P.in1 + row * (int64_t)(D1 * F) + c;")
     w("  const float* __restrict__ a2 = P.in2 + row * (int64_t)(D2 * F) + c;")
-    w("  const float* __restrict__ wr = P.w + row * (int64_t)(NP * F) + c;")
+    w("  const float* __restrict__ wr = P.w + (P.shared_w ? 0 : row * (int64_t)(NP * F)) + c;")
     w("  float* __restrict__ o = P.out + row * (int64_t)(OUT_COMPS * F) + c;")
     w("  float2 x1[D1], x2[D2];")
     w("#pragma unroll")
@@ -99,7 +100,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("  const int c = 2 * (int)(threadIdx.x % tpr);")
     w("  const float* __restrict__ a1 = P.in1 + row * (int64_t)(D1 * F) + c;")
     w("  const float* __restrict__ a2 = P.in2 + row * (int64_t)(D2 * F) + c;")
-    w("  const float* __restrict__ wr = P.w + row * (int64_t)(NP * F) + c;")
+    w("  const float* __restrict__ wr = P.w + (P.shared_w ? 0 : row * (int64_t)(NP * F)) + c;")
     w("  const float* __restrict__ go = P.g_out + row * (int64_t)(OUT_COMPS * F) + c;")
     w("  float* __restrict__ gwr = NEED_W ? P.g_w + row * (int64_t)(NP * F) + c : nullptr;")
     w("  float2 x1[D1], x2[D2], gx1[D1], gx2[D2];")

@@ -171,13 +171,16 @@ static bool pair_eligible(const fc_tp_desc* d, const void* in2) {
 }
 
 // The dense channel-pair kernels: no edges, both inputs with the same 64 or 128 channels,
-// one weight row per output row, paths kept, float32, 8-byte aligned tensors (float2
-// loads and stores; every row offset is a multiple of F floats).
+// paths kept, float32, 8-byte aligned tensors (float2 loads and stores; every row offset
+// is a multiple of F floats); weights per row, or shared when no shared weight gradient
+// (a reduction over rows) is asked for.
 #ifndef FC_DENSE_PAIR
 #define FC_DENSE_PAIR 1
 #endif
-static bool dense_pair_eligible(const fc_tp_desc* d, bool conv, std::initializer_list<const void*> ptrs) {
-  if (!FC_DENSE_PAIR || conv || d->dtype != FC_F32 || d->shared_weights || d->reduce_paths) return false;
+static bool dense_pair_eligible(const fc_tp_desc* d, bool conv, const void* grad_weights,
+                                std::initializer_list<const void*> ptrs) {
+  if (!FC_DENSE_PAIR || conv || d->dtype != FC_F32 || d->reduce_paths) return false;
+  if (d->shared_weights && grad_weights != nullptr) return false;
   if (d->in1_features != d->in2_features || (d->in1_features != 64 && d->in1_features != 128)) return false;
   uintptr_t bits = 0;
   for (const void* q : ptrs) bits |= reinterpret_cast<uintptr_t>(q);
@@ -526,7 +529,7 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
     fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
     p.in1 = (const float*)in1; p.in2 = (const float*)in2; p.w = (const float*)weights; p.out = (float*)out;
     if (v2 && pair_eligible(desc, in2) && sig->table->fwd3_f32) return launch_status(sig->table->fwd3_f32(p, s), "fc_tp_fwd");
-    if (sig->table->dpfwd_f32 && dense_pair_eligible(desc, rowptr != nullptr, {in1, in2, weights, out}))
+    if (sig->table->dpfwd_f32 && dense_pair_eligible(desc, rowptr != nullptr, nullptr, {in1, in2, weights, out}))
       return launch_status(sig->table->dpfwd_f32(p, s), "fc_tp_fwd");
     return launch_status(v2 ? sig->table->fwd2_f32(p, s) : sig->table->fwd_f32(p, s), "fc_tp_fwd");
   }
@@ -574,7 +577,7 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
     p.g_in1 = (float*)grad_in1; p.g_in2 = (float*)grad_in2; p.g_w = (float*)grad_weights;
     if (v2 && pair_eligible(desc, in2) && sig->table->bwd3_f32) return launch_status(sig->table->bwd3_f32(p, s), "fc_tp_bwd");
     if (sig->table->dpbwd_f32 &&
-        dense_pair_eligible(desc, conv, {grad_out, in1, in2, weights, grad_in1, grad_in2, grad_weights}))
+        dense_pair_eligible(desc, conv, grad_weights, {grad_out, in1, in2, weights, grad_in1, grad_in2, grad_weights}))
       return launch_status(sig->table->dpbwd_f32(p, s), "fc_tp_bwd");
     return launch_status(v2 ? sig->table->bwd2_f32(p, s) : sig->table->bwd_f32(p, s), "fc_tp_bwd");
   }

@@ -332,7 +332,11 @@ class InteractionLayer(nn.Module):
         if self.skip_projection is not None:
             skip = self.skip_projection(residual)
             if self.in1_l_max == 0:
-                out = torch.cat([out[:, :self.out_features] + skip, out[:, self.out_features:]], dim=-1)
+                # the skip reaches the l = 0 block only: added in place into the fresh output
+                # of linear_second (whose backward does not read it) instead of
+                # concatenating a new row (a copy of every rank block, and in the backward a
+                # zero-filled row per slice plus their sum)
+                out[:, :self.out_features].add_(skip)
             else:
                 out = out + skip
         if self.layer_norm is not None:

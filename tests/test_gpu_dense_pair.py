@@ -50,9 +50,36 @@ def test_gpu_dense_pair_matches_float64(cuda_device, sig, C, n):
     check_device_status(dev)
 
 
+@pytest.mark.parametrize("C", [128, 64])
+def test_gpu_dense_pair_shared_weights_without_weight_gradient(cuda_device, C):
+    """Shared frozen weights (the element-agnostic product layers): forward and both input
+    gradients on the pair kernels."""
+    dev = cuda_device
+    tp = o3.TensorProduct(3, 3, 3, C, C, shared_weights=True)
+    g = torch.Generator(device=dev).manual_seed(5)
+    n = 515
+    in1 = torch.randn(n, tp.in1_dim, device=dev, generator=g)
+    in2 = torch.randn(n, tp.in2_dim, device=dev, generator=g)
+    w = torch.randn(tp.n_total_paths * C, device=dev, generator=g)
+    go = torch.randn(n, tp(in1, in2, w).shape[1], device=dev, generator=g)
+
+    def run(a, b, ww, gg):
+        leaves = [a.clone().requires_grad_(True), b.clone().requires_grad_(True)]
+        out = tp(leaves[0], leaves[1], ww)
+        return out.detach(), torch.autograd.grad(out, leaves, gg)
+
+    o32, g32 = run(in1, in2, w, go)
+    o64, g64 = run(in1.double(), in2.double(), w.double(), go.double())
+    assert _rel(o32, o64) < 2e-6
+    for a, b in zip(g32, g64):
+        assert _rel(a, b) < 2e-6
+    check_device_status(dev)
+
+
 @pytest.mark.parametrize("C,shared", [(96, False), (128, True)])
 def test_gpu_dense_products_outside_the_pair_layout(cuda_device, C, shared):
-    """96 channels and shared weights take the generic kernels; same check."""
+    """96 channels, and shared weights with their gradient requested, take the generic
+    kernels; same check."""
     dev = cuda_device
     tp = o3.TensorProduct(3, 3, 3, C, C, shared_weights=shared)
     g = torch.Generator(device=dev).manual_seed(3)
