@@ -34,7 +34,9 @@ BLOCK = 128
 # and their gradients (4 x D float2 values per thread); uncapped it takes 254 registers (2
 # CTAs per SM). Measured on the (3,3)->3 product at 27,648 rows, C = 128: 0.87 ms at 2
 # CTAs, 0.69 ms at 3 (168 registers), 0.74 ms at 4 (128 registers, more local spills);
-# the one-channel-per-thread body took 0.70 ms.
+# the one-channel-per-thread body took 0.70 ms. Issuing each path's weight and gradient
+# loads one path ahead of their use made the backward slower (0.53 -> 0.59 ms with shared
+# weights): the extra live registers cost more than the hidden latency.
 BWD_MIN_CTAS = 3
 
 
