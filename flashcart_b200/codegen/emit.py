@@ -437,6 +437,7 @@ def emit_signature(sig: Sig) -> str:
     w("#ifndef FC_HOST_EMU")
     L.append(emit_conv.emit(sig, stores))
     L.append(emit_pair.emit(sig, stores))
+    L.append(emit_pair.emit_fwd4(sig, stores))
     L.append(emit_dense.emit(sig, stores))
     w("#endif")
     w("struct Ops {")
@@ -455,6 +456,8 @@ def emit_signature(sig: Sig) -> str:
     w("  static int bwd3(const TpBwdParams<float>& P, cudaStream_t s) { return launch_bwd3(P, s); }")
     w("  static int dpfwd(const TpParams<float>& P, cudaStream_t s) { return launch_dpfwd(P, s); }")
     w("  static int dpbwd(const TpBwdParams<float>& P, cudaStream_t s) { return launch_dpbwd(P, s); }")
+    w("  static constexpr int (*fwd4_fn)(const TpParams<float>&, cudaStream_t) = "
+      + ("&launch_fwd4;" if emit_pair.has_fwd4(sig) else "nullptr;"))
     w("#endif")
     w("};")
     w(f"}}  // namespace sig_{n}")

@@ -225,12 +225,13 @@ def _bwd_body(gs: GroupSlots, ind: str, d2p: int) -> List[str]:
     return L
 
 
-def _setup(gs: GroupSlots, extra_floats: str, ind: str) -> List[str]:
+def _setup(gs: GroupSlots, extra_floats: str, ind: str, channels_per_thread: int = 2) -> List[str]:
     """Shared-memory carve-up: M pairs | ring slots | [extra] | slot headers | mbarriers."""
+    nc_shift = {2: 1, 4: 2}[channels_per_thread]
     return [
         f"{ind}using T = float;",
         f"{ind}constexpr int XLO = {gs.x_lo}, XN = {gs.x_n}, NW = {len(gs.paths)}, NMP = {gs.nmp};",
-        f"{ind}const int F = P.F, NC = F >> 1, t = threadIdx.x, lane = t & 31;",
+        f"{ind}const int F = P.F, NC = F >> {nc_shift}, t = threadIdx.x, lane = t & 31;",
         f"{ind}const int64_t row = blockIdx.x;",
         f"{ind}float2* m2 = reinterpret_cast<float2*>(smem);",
         f"{ind}float* ring = reinterpret_cast<float*>(m2 + NMP * {gs.ec});",
@@ -542,4 +543,149 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
             w(f"  if (int rc = launch_{kind}3_group<{gi}>(P, s)) return rc;")
         w("  return 0;")
         w("}")
+    return "\n".join(L) + "\n"
+
+
+# ---------------------------------------------------------------------------------------
+# Four-channel forward (F = 128): one consumer warp per receiver, each thread owning the
+# channels 4t .. 4t+3 as two packed pairs. Every 16-byte broadcast of an edge-matrix pair
+# then feeds four channels instead of two, so the edge matrices are read from shared
+# memory by one warp per receiver instead of two (the forward's shared-memory wavefronts
+# are mostly these broadcasts); sender rows and weights come as 16-byte loads. A thread
+# holds two register copies of its accumulators, so it is emitted only for signatures
+# whose paths fit one group of at most BUDGET4 accumulator pairs. Measured at C = 128 on
+# the 1.49 M-edge benchmark graph: (0,3)->3 (one group of 16) 0.89 -> 0.73 ms; (3,3)->3
+# split into eight such groups instead of the pair kernel's three took 8.6 ms against 5.8
+# (each group walks the edges and gathers its sender rows again, at half the consumer
+# warps per SM), so larger signatures keep the pair kernel.
+BUDGET4 = 16
+FWD4_MIN_CTAS = 5
+
+
+def make_groups4(sig) -> List[List[int]]:
+    order = sorted(range(len(sig.paths)), key=lambda p: (-sig.paths[p][0], p))
+    groups, cur, used = [], [], 0
+    for p in order:
+        n = 2 * sig.paths[p][2] + 1
+        if cur and (used + n > BUDGET4 or sig.paths[cur[-1]][0] != sig.paths[p][0]):
+            groups.append(sorted(cur))
+            cur, used = [], 0
+        cur.append(p)
+        used += n
+    if cur:
+        groups.append(sorted(cur))
+    nacc = lambda g: sum(2 * sig.paths[p][2] + 1 for p in g)
+    while len(groups) > 1 and nacc(groups[-1]) + nacc(groups[-2]) <= BUDGET4:
+        last = groups.pop()
+        groups[-1] = sorted(groups[-1] + last)
+    return groups
+
+
+def _fwd4_body(gs: GroupSlots, ind: str) -> List[str]:
+    sig = gs.sig
+    L = []
+    acc_base = 0
+    for p in gs.paths:
+        r1, r2, o = sig.paths[p]
+        s0 = gs.range[p][0]
+        L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
+        L.extend(_path_mload(gs, p, ind + "  "))
+        L.append(f"{ind}  float2 wpa, wpb;")
+        L.append(f"{ind}  ld4p(sw + {gs.w_pos[p]} * F, wpa, wpb);")
+        for a in range(2 * o + 1):
+            for h in ("a", "b"):
+                pairs = [(f"mv[{gs.index[(p, a, i)] - s0}]", f"x1{h}[{_q(r1, i) - gs.x_lo}]")
+                         for i in range(2 * r1 + 1) if (p, a, i) in gs.index]
+                L.append(f"{ind}  acc{h}[{acc_base + a}] = pfma(wp{h}, {_chain(pairs)}, acc{h}[{acc_base + a}]);")
+        L.append(f"{ind}}}")
+        acc_base += 2 * o + 1
+    return L
+
+
+def has_fwd4(sig) -> bool:
+    return len(make_groups4(sig)) == 1
+
+
+def emit_fwd4(sig, store_offsets: List[Tuple[int, int]]) -> str:
+    if not has_fwd4(sig):
+        return ""
+    groups = [GroupSlots(sig, g) for g in make_groups4(sig)]
+    for gs in groups:
+        gs.big, gs.ec, gs.ring, gs.gsmem = True, 8, 4, False
+        gs.stage = STAGE_X2 and sig.d2 % 4 == 0
+    acc_out = {}
+    k = 0
+    for p, (r1, r2, o) in enumerate(sig.paths):
+        for a in range(2 * o + 1):
+            acc_out[(p, a)] = store_offsets[k][0]
+            k += 1
+    L = []
+    w = L.append
+    w(f"// ---- four-channel convolution forward (float32, F = 128): {len(groups)} path groups")
+    w("#ifndef FC_P4_FWD_MINB")
+    w(f"#define FC_P4_FWD_MINB {FWD4_MIN_CTAS}")
+    w("#endif")
+    w(f"constexpr int P4_GROUPS = {len(groups)};")
+    w("inline size_t fwd4_smem(int g, int F) {")
+    w("  switch (g) {")
+    for gi, gs in enumerate(groups):
+        xb = 2 * gs.ec * gs.sig.d2 if gs.stage else 0
+        w(f"    case {gi}: return (size_t){gs.nmp * gs.ec} * 8 + (size_t)({gs.ring} * ({gs.x_n} + {len(gs.paths)}) * F"
+          f" + {xb}) * 4 + {gs.ring * 8 + 2 * gs.ring * 8 + 4 * 8 + 16};")
+    w("  }")
+    w("  return 0;")
+    w("}")
+    for gi, gs in enumerate(groups):
+        w(f"__device__ __forceinline__ void fwd4_g{gi}(const TpParams<float>& P, unsigned char* smem) {{")
+        L.extend(_setup(gs, "0", "  ", channels_per_thread=4))
+        L.extend(_producer(gs, "  "))
+        w(f"  float2 acca[{gs.nacc}], accb[{gs.nacc}];")
+        w(f"  for (int q = 0; q < {gs.nacc}; ++q) {{ acca[q] = p2(0.0f); accb[q] = p2(0.0f); }}")
+        w(f"  for (int64_t eb = 0; eb < ne_all; eb += {gs.ec}) {{")
+        w(f"    const int ne = (int)min((int64_t){gs.ec}, ne_all - eb);")
+        L.extend(_phase1_loop(gs, "    "))
+        w("    for (int k = 0; k < ne; ++k) {")
+        L.extend(_edge_begin(gs, "      "))
+        w("      if (j >= 0) {")
+        w("        const float* sx = ring + s * SLOT + 4 * t;")
+        w("        float2 x1a[XN], x1b[XN];")
+        w("        for (int q = 0; q < XN; ++q) ld4p(sx + q * F, x1a[q], x1b[q]);")
+        w("        const float* sw = sx + XN * F;")
+        w("        const float2* m = m2 + k * NMP;")
+        L.extend(_fwd4_body(gs, "        "))
+        w("      }")
+        L.extend(_edge_end("      "))
+        w("    }")
+        w("    fc_named_sync(1, NC);")
+        w("  }")
+        w("  float* __restrict__ o = P.out + row * (int64_t)(OUT_COMPS * F) + 4 * t;")
+        k = 0
+        for p in gs.paths:
+            o_ = sig.paths[p][2]
+            for a in range(2 * o_ + 1):
+                w(f"  st4p(o + {acc_out[(p, a)]} * F, acca[{k}], accb[{k}]);")
+                k += 1
+        w("}")
+    w("template <int G>")
+    w("__global__ void __launch_bounds__(64, FC_P4_FWD_MINB) fwd4_kernel(TpParams<float> P) {")
+    w("  extern __shared__ __align__(16) unsigned char fc_smem_raw[];")
+    for gi in range(len(groups)):
+        w(f"  if constexpr (G == {gi}) fwd4_g{gi}(P, fc_smem_raw);")
+    w("}")
+    w("template <int G>")
+    w("int launch_fwd4_group(const TpParams<float>& P, cudaStream_t s) {")
+    w("  const size_t smem = fwd4_smem(G, P.F);")
+    w("  if (smem > 227 * 1024) return FC_ERR_UNSUPPORTED;")
+    w("  if (smem > 48 * 1024 && cudaFuncSetAttribute(fwd4_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, "
+      "(int)smem) != cudaSuccess) return FC_ERR_LAUNCH;")
+    w("  fwd4_kernel<G><<<(unsigned)P.n_rows, 64, smem, s>>>(P);")
+    w("  return fc_check_launch();")
+    w("}")
+    w("inline int launch_fwd4(const TpParams<float>& P, cudaStream_t s) {")
+    w("  if (P.n_rows == 0) return 0;")
+    w("  if (P.n_rows > 0x7fffffffLL || P.F != 128) return FC_ERR_UNSUPPORTED;")
+    for gi in range(len(groups)):
+        w(f"  if (int rc = launch_fwd4_group<{gi}>(P, s)) return rc;")
+    w("  return 0;")
+    w("}")
     return "\n".join(L) + "\n"

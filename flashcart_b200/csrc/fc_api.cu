@@ -174,6 +174,9 @@ static bool pair_eligible(const fc_tp_desc* d, const void* in2) {
 // paths kept, float32, 8-byte aligned tensors (float2 loads and stores; every row offset
 // is a multiple of F floats); weights per row, or shared when no shared weight gradient
 // (a reduction over rows) is asked for.
+#ifndef FC_FWD4
+#define FC_FWD4 1
+#endif
 #ifndef FC_DENSE_PAIR
 #define FC_DENSE_PAIR 1
 #endif
@@ -528,7 +531,14 @@ int fc_tp_fwd(const fc_tp_desc* desc, const void* in1, const void* in2, const vo
     TpParams<float> p;
     fill_common(p, desc, rowptr, idx_j, n_out_rows, n_in1_rows, status);
     p.in1 = (const float*)in1; p.in2 = (const float*)in2; p.w = (const float*)weights; p.out = (float*)out;
-    if (v2 && pair_eligible(desc, in2) && sig->table->fwd3_f32) return launch_status(sig->table->fwd3_f32(p, s), "fc_tp_fwd");
+    if (v2 && pair_eligible(desc, in2) && sig->table->fwd3_f32) {
+      // 128 channels: the four-channel forward (one consumer warp per receiver; 16-byte
+      // output stores need a 16-byte aligned output)
+      if (FC_FWD4 && desc->in1_features == 128 && sig->table->fwd4_f32 &&
+          (reinterpret_cast<uintptr_t>(out) & 15) == 0)
+        return launch_status(sig->table->fwd4_f32(p, s), "fc_tp_fwd");
+      return launch_status(sig->table->fwd3_f32(p, s), "fc_tp_fwd");
+    }
     if (sig->table->dpfwd_f32 && dense_pair_eligible(desc, rowptr != nullptr, nullptr, {in1, in2, weights, out}))
       return launch_status(sig->table->dpfwd_f32(p, s), "fc_tp_fwd");
     return launch_status(v2 ? sig->table->fwd2_f32(p, s) : sig->table->fwd_f32(p, s), "fc_tp_fwd");

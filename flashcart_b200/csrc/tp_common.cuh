@@ -78,6 +78,9 @@ struct TpTable {
   // weights per row; float32; may be null)
   int (*dpfwd_f32)(const TpParams<float>&, cudaStream_t);
   int (*dpbwd_f32)(const TpBwdParams<float>&, cudaStream_t);
+  // four-channel convolution forward (float32, F = 128; null unless the signature's
+  // paths fit one group)
+  int (*fwd4_f32)(const TpParams<float>&, cudaStream_t);
 };
 
 struct TpSigEntry {
@@ -117,6 +120,15 @@ __device__ __forceinline__ void ld2x2(const float2* p, float2* v) {
   const float4 q = *reinterpret_cast<const float4*>(p);
   v[0] = make_float2(q.x, q.y);
   v[1] = make_float2(q.z, q.w);
+}
+// Four consecutive floats (16-byte aligned) as two channel pairs, and back.
+__device__ __forceinline__ void ld4p(const float* p, float2& a, float2& b) {
+  const float4 q = *reinterpret_cast<const float4*>(p);
+  a = make_float2(q.x, q.y);
+  b = make_float2(q.z, q.w);
+}
+__device__ __forceinline__ void st4p(float* p, float2 a, float2 b) {
+  *reinterpret_cast<float4*>(p) = make_float4(a.x, a.y, b.x, b.y);
 }
 // Vector atomic add of a channel pair into global memory (one reduction instruction).
 __device__ __forceinline__ void red2(float* p, float2 v) { atomicAdd(reinterpret_cast<float2*>(p), v); }
@@ -322,9 +334,9 @@ int tp_dbwd_launch(const TpDbwdParams<T>& P, cudaStream_t) {
 #ifndef FC_HOST_EMU
 #define FC_CONV2_ENTRIES(NS)                                                              \
   , &NS::Ops::fwd2<float>, &NS::Ops::fwd2<double>, &NS::Ops::bwd2<float>, &NS::Ops::bwd2<double>, \
-      &NS::Ops::fwd3, &NS::Ops::bwd3, &NS::Ops::dpfwd, &NS::Ops::dpbwd
+      &NS::Ops::fwd3, &NS::Ops::bwd3, &NS::Ops::dpfwd, &NS::Ops::dpbwd, NS::Ops::fwd4_fn
 #else
-#define FC_CONV2_ENTRIES(NS) , nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr
+#define FC_CONV2_ENTRIES(NS) , nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr
 #endif
 #define FC_DEFINE_TP_SIGNATURE(NAME, NS)                                                  \
   extern const TpTable tp_table_##NAME;                                                   \
