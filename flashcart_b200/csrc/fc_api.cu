@@ -890,6 +890,79 @@ int fc_linear_bwd_presplit(const fc_linear_desc* desc, const void* grad_out, con
                        "fc_linear_bwd_presplit");
 }
 
+// Residual forms (fc_linear_fwd_residual / fc_linear_bwd_residual): the map's GEMM adds
+// the residual in its epilogue (LinGemmArgs act 3). TMA path only.
+static int linear_residual_t(const fc_linear_desc* d, bool backward, const float* a_rows, const void* const* weights,
+                             const void* const* split, const float* scale, int64_t n, const float* residual,
+                             float* c, int* status, cudaStream_t s, const char* what) {
+  if (int rc = check_linear(d)) return rc;
+  if (d->dtype != FC_F32 || d->act != FC_ACT_NONE)
+    return fail(FC_ERR_UNSUPPORTED, "%s: float32 maps without an input activation only", what);
+  if (n < 0) return fail(FC_ERR_INVALID, "%s: negative size", what);
+  const int64_t a_dim = backward ? d->out_dim : d->in_dim, c_dim = backward ? d->in_dim : d->out_dim;
+  int64_t prev = 0;
+  for (int l = 0; l < d->n_active; ++l) {
+    const int64_t off = backward ? d->in_offsets[l] : d->out_offsets[l];
+    if (off != prev) return fail(FC_ERR_UNSUPPORTED, "%s: the active ranks must cover the output row", what);
+    prev = off + (int64_t)d->m_values[l] * (backward ? d->f_in_values[l] : d->f_out_values[l]);
+  }
+  if (prev != c_dim) return fail(FC_ERR_UNSUPPORTED, "%s: the active ranks must cover the output row", what);
+  if (n == 0 || d->n_active == 0) return FC_OK;
+  if (!a_rows || !weights || !scale || !residual || !c) return fail(FC_ERR_INVALID, "%s: null tensor", what);
+#ifdef FC_HOST_EMU
+  (void)a_dim; (void)split; (void)status; (void)s;
+  return fail(FC_ERR_UNSUPPORTED, "%s: tensor-core path only", what);
+#else
+  LinGemmArgs<float> args[FC_MAX_L + 1];
+  for (int l = 0; l < d->n_active; ++l) {
+    LinGemmArgs<float>& a = args[l];
+    const int64_t a_off = backward ? d->out_offsets[l] : d->in_offsets[l];
+    const int64_t c_off = backward ? d->in_offsets[l] : d->out_offsets[l];
+    const int ka = backward ? d->f_out_values[l] : d->f_in_values[l];
+    const int nc = backward ? d->f_in_values[l] : d->f_out_values[l];
+    a.a = LinRows<float>{a_rows, a_dim, a_off, ka, d->m_values[l]};
+    a.w = (const float*)weights[l];
+    a.ldw = d->f_in_values[l];
+    a.trans_b = backward ? 0 : 1;
+    a.bsplit = split ? (const float*)split[l] : nullptr;
+    a.scale = scale + l;
+    a.c = LinRows<float>{c, c_dim, c_off, nc, d->m_values[l]};
+    a.R = n * d->m_values[l];
+    a.K = ka;
+    a.N = nc;
+    a.act = 3;
+    a.aux = LinRows<float>{residual, c_dim, c_off, nc, d->m_values[l]};
+  }
+  const bool split3 = d->precision != FC_PREC_TF32;
+  int rc = d->n_active > 1 ? lin_gemm_tma_grouped(args, d->n_active, split3, status, s) : 1;
+  for (int l = 0; rc == 1 && l < d->n_active; ++l) {
+    const int r = lin_gemm_tma(args[l], split3, status, s);
+    if (r == 1) return fail(FC_ERR_UNSUPPORTED, "%s: layout not on the tensor-core path (rank %d)", what, l);
+    if (r) return r;
+    if (l == d->n_active - 1) rc = 0;
+  }
+  return rc;
+#endif
+}
+
+int fc_linear_fwd_residual(const fc_linear_desc* desc, const void* x, const void* const* weights,
+                           const void* const* split, const void* scale, int64_t n, const void* residual, void* out,
+                           int32_t* status, fc_stream_t stream) {
+  const int rc = linear_residual_t(desc, false, (const float*)x, weights, split, (const float*)scale, n,
+                                   (const float*)residual, (float*)out, reinterpret_cast<int*>(status),
+                                   (cudaStream_t)stream, "fc_linear_fwd_residual");
+  return rc == FC_ERR_LAUNCH ? launch_status(rc, "fc_linear_fwd_residual") : rc;
+}
+
+int fc_linear_bwd_residual(const fc_linear_desc* desc, const void* grad_out, const void* const* weights,
+                           const void* const* split, const void* scale, int64_t n, const void* residual,
+                           void* grad_x, int32_t* status, fc_stream_t stream) {
+  const int rc = linear_residual_t(desc, true, (const float*)grad_out, weights, split, (const float*)scale, n,
+                                   (const float*)residual, (float*)grad_x, reinterpret_cast<int*>(status),
+                                   (cudaStream_t)stream, "fc_linear_bwd_residual");
+  return rc == FC_ERR_LAUNCH ? launch_status(rc, "fc_linear_bwd_residual") : rc;
+}
+
 // Convolution forward for callers that cannot allocate device memory (see the header).
 int fc_tp_conv_fwd_noalloc(const fc_tp_desc* desc, const void* in1, const void* in2, const void* weights,
                            const int64_t* idx_i, const int64_t* idx_j, int64_t n_nodes, int64_t n_in1_rows,

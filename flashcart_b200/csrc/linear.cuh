@@ -31,7 +31,8 @@ struct LinGemmArgs {
   // multiple of 4), as lin_presplit writes them; null = split inside the call
   const T* bsplit = nullptr;
   // activation: 0 none; 1 C = (sW) silu(A) (forward); 2 C = silu'(aux) * (sW) A with aux
-  // laid out like C (the backward's input gradient, aux = the forward's input)
+  // laid out like C (the backward's input gradient, aux = the forward's input); 3 C =
+  // (sW) A + aux (a residual laid out like C, possibly C itself; TMA path only)
   int act = 0;
   LinRows<T> aux{};
 };

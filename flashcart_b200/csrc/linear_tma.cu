@@ -113,7 +113,7 @@ struct Args {
   int n_col_tiles;
   int64_t row_tiles;      // 128-node tiles per m
   int64_t n_tiles;
-  const float* aux;       // ACT == 2: silu' of these values multiplies C (laid out like C)
+  const float* aux;       // ACT == 2: silu' of these values multiplies C; ACT == 3: added to C (laid out like C)
   int64_t aux_ld, aux_ms;
   const float* scale;     // per rank (indexed by rank_of_m)
   int n_ranks;            // weight sets in this launch (grouped launch: all ranks of a map)
@@ -296,7 +296,8 @@ __device__ __forceinline__ TileCoord tile_coord(const Args& a, int64_t t) {
   return c;
 }
 
-// ACT: 0 plain; 1 the splitters apply SiLU to A; 2 the epilogue multiplies by SiLU'(aux).
+// ACT: 0 plain; 1 the splitters apply SiLU to A; 2 the epilogue multiplies by SiLU'(aux);
+// 3 the epilogue adds aux (a residual laid out like C; it may be C itself).
 template <int BN, bool SPLIT, int ACT>
 __global__ void __launch_bounds__(THREADS, 1)
     lin_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm,
@@ -552,6 +553,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
       }
+      if constexpr (ACT == 3) {
+        // this lane's row of the residual: plain (coherent) 16-byte loads, since the
+        // residual may be the output itself (each element is read here before this
+        // thread's staged store of it)
+        const int64_t node = (int64_t)tc.node0 + q * 32 + lane;
+        if (node < a.nodes) {
+          const float4* ar = reinterpret_cast<const float4*>(a.aux + node * a.aux_ld + (int64_t)tc.m * a.aux_ms + col);
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (col + 4 * c < a.N) {
+              const float4 z = ar[c];
+              f[4 * c] += z.x;
+              f[4 * c + 1] += z.y;
+              f[4 * c + 2] += z.z;
+              f[4 * c + 3] += z.w;
+            }
+        }
+      }
       if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // buffer used two stores ago
       __syncwarp();
       uint8_t* buf = stage0 + nbuf * 4096;
@@ -672,7 +691,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 struct DeviceState {
   bool ready = false;
   int sms = 0;
-  bool attr_set[3][2][3] = {};
+  bool attr_set[3][2][4] = {};
 };
 
 static std::mutex g_mu;
@@ -739,13 +758,18 @@ static int launch(const CUtensorMap& ma, const BMaps& bm, const CUtensorMap& mc,
 }
 
 // the activation modes instantiated: SiLU on the input for every tile width (the radial
-// MLP's second and last layers), SiLU' epilogue for the 64-column input gradients
+// MLP's second and last layers), SiLU' epilogue for the 64-column input gradients, the
+// residual-add epilogue for 64- and 128-column tiles (node-level maps)
 template <int BN, bool SPLIT>
 static int launch_act(int act, const CUtensorMap& ma, const BMaps& bm, const CUtensorMap& mc,
                       const CUtensorMap& mpf, const Args& args, DeviceState* ds, int grid, cudaStream_t s) {
   if (act == 1) return launch<BN, SPLIT, 1>(ma, bm, mc, mpf, args, ds, grid, s);
   if (act == 2) {
     if constexpr (BN == 64) return launch<BN, SPLIT, 2>(ma, bm, mc, mpf, args, ds, grid, s);
+    return 1;
+  }
+  if (act == 3) {
+    if constexpr (BN <= 128) return launch<BN, SPLIT, 3>(ma, bm, mc, mpf, args, ds, grid, s);
     return 1;
   }
   return launch<BN, SPLIT, 0>(ma, bm, mc, mpf, args, ds, grid, s);
@@ -779,7 +803,8 @@ static int run_tma(const LinGemmArgs<float>* a, int n, bool split, int* status, 
   const int kp = (a0.K + 3) & ~3;
   if (nodes > 0x7fffffffLL) return 1;
   if (a0.act == 2 && BN != 64) return 1;  // the SiLU' epilogue is instantiated for 64-column tiles
-  if (a0.act == 2 && ((reinterpret_cast<uintptr_t>(a0.aux.p + a0.aux.off) & 15) || (a0.aux.ld & 3) ||
+  if (a0.act == 3 && BN > 128) return 1;   // the residual epilogue: 64- and 128-column tiles
+  if (a0.act >= 2 && ((reinterpret_cast<uintptr_t>(a0.aux.p + a0.aux.off) & 15) || (a0.aux.ld & 3) ||
                       (m_total > 1 && (a0.aux.ms & 3)) || (a0.N & 3)))
     return 1;  // the epilogue reads aux rows as 16-byte vectors
 
@@ -826,7 +851,7 @@ static int run_tma(const LinGemmArgs<float>* a, int n, bool split, int* status, 
       for (int j = 0; j < a[l].a.M; ++j) args.rank_of_m[m++] = l;
     for (int m = m_total; m < 16; ++m) args.rank_of_m[m] = 0;
     args.status = status;
-    args.aux = a0.act == 2 ? a0.aux.p + a0.aux.off : nullptr;
+    args.aux = a0.act >= 2 ? a0.aux.p + a0.aux.off : nullptr;
     args.aux_ld = a0.aux.ld;
     args.aux_ms = m_total > 1 ? a0.aux.ms : 0;
     const int act = a0.act;
@@ -865,7 +890,7 @@ int lin_gemm_tma_grouped(const LinGemmArgs<float>* a, int n, bool split, int* st
       return 1;
     if (b.a.M < 1 || b.R % b.a.M || b.R / b.a.M != a0.R / a0.a.M) return 1;
     if (b.act != a0.act) return 1;
-    if (a0.act == 2 && (b.aux.p != a0.aux.p || b.aux.ld != a0.aux.ld || b.aux.ms != a0.aux.ms ||
+    if (a0.act >= 2 && (b.aux.p != a0.aux.p || b.aux.ld != a0.aux.ld || b.aux.ms != a0.aux.ms ||
                         b.aux.off != p.aux.off + (int64_t)p.aux.M * p.aux.ms))
       return 1;
     if (b.a.off != p.a.off + (int64_t)p.a.M * p.a.ms || b.c.off != p.c.off + (int64_t)p.c.M * p.c.ms) return 1;

@@ -328,17 +328,18 @@ class InteractionLayer(nn.Module):
         if out_nodes is not None:
             aggregated = aggregated[:out_nodes]
         # aggregated / sqrt(avg_neighbors), folded into the scales of the linear map
-        out = self.linear_second(aggregated, input_scale=1.0 / self.sqrt_avg_neighbors)
-        if self.skip_projection is not None:
-            skip = self.skip_projection(residual)
-            if self.in1_l_max == 0:
-                # the skip reaches the l = 0 block only: added in place into the fresh output
-                # of linear_second (whose backward does not read it) instead of
-                # concatenating a new row (a copy of every rank block, and in the backward a
-                # zero-filled row per slice plus their sum)
-                out[:, :self.out_features].add_(skip)
-            else:
-                out = out + skip
+        if self.skip_projection is not None and self.in1_l_max != 0:
+            # the skip projection is added in linear_second's epilogue where that is possible
+            out = self.linear_second(aggregated, input_scale=1.0 / self.sqrt_avg_neighbors,
+                                     residual=self.skip_projection(residual))
+        else:
+            out = self.linear_second(aggregated, input_scale=1.0 / self.sqrt_avg_neighbors)
+        if self.skip_projection is not None and self.in1_l_max == 0:
+            # the skip reaches the l = 0 block only: added in place into the fresh output of
+            # linear_second (whose backward does not read it) instead of concatenating a new
+            # row (a copy of every rank block, and in the backward a zero-filled row per slice
+            # plus their sum)
+            out[:, :self.out_features].add_(self.skip_projection(residual))
         if self.layer_norm is not None:
             out = self.layer_norm(out)
         return out
@@ -385,7 +386,8 @@ class EquivariantGatedLayer(_ChildSpecialParameters, nn.Module):
         if ops.first_order_only_active() and values.is_cuda and values.dtype in (torch.float32, torch.float64):
             # one fused pass over the rank blocks (first derivative only)
             gated = ops.gate_fwd(values, gates, self.l_max, self.hidden_features)
-            return node_feats + self.output_linear(gated)
+            # the residual is added in the output map's epilogue where that is possible
+            return self.output_linear(gated, residual=node_feats)
         parts = []
         for l, (a, b) in enumerate(self.hidden_slices):
             parts.append((values[:, a:b].view(n, 2 * l + 1, self.hidden_features) * gates[:, l].unsqueeze(1))
@@ -512,6 +514,9 @@ class ProductLayer(_ChildSpecialParameters, nn.Module):
             self.step0_weight_index = None
 
     def forward(self, node_feats, atom_types=None):
+        if (not self.path_reduced and self.skip_projection is not None
+                and all(isinstance(s, nn.Identity) for s in self.irreps_selectors)):
+            return self._forward_summed_in_maps(node_feats, atom_types)
         out = None  # sum of the selected products (the reference starts from zeros; 0 + x == x)
         prod = node_feats
         for step in range(self.correlation):
@@ -536,6 +541,33 @@ class ProductLayer(_ChildSpecialParameters, nn.Module):
             out = self.final_linear(out)
         if self.skip_projection is not None:
             out = out + self.skip_projection(node_feats)
+        if self.layer_norm is not None:
+            out = self.layer_norm(out)
+        return out
+
+
+    def _forward_summed_in_maps(self, node_feats, atom_types=None):
+        """The same sum (every step's product, all ranks kept, plus the skip projection) with
+        the additions moved into the maps that produce their terms: the skip projection adds
+        the first product and the last product map adds the rest (in their GEMM epilogues
+        where ``ops.linear_residual_fusable`` allows), so only the middle products are
+        summed separately."""
+        prods, prod = [], node_feats
+        for step in range(self.correlation):
+            if step == 0:
+                if self.step0_weight_index is not None:
+                    w = self.path_weights[0](atom_types)
+                    prod = node_feats * w[..., self.step0_weight_index]
+            else:
+                w = self.path_weights[step](atom_types).to(node_feats.dtype)
+                prod = self.tensor_products[step - 1](prod, node_feats, w)
+            if step < self.correlation - 1:
+                prod = self.product_linears[step](prod)
+                prods.append(prod)
+        acc = self.skip_projection(node_feats, residual=prods[0])
+        for p in prods[1:]:
+            acc = acc + p
+        out = self.product_linears[self.correlation - 1](prod, residual=acc)
         if self.layer_norm is not None:
             out = self.layer_norm(out)
         return out

@@ -72,9 +72,13 @@ class LinearLayer(nn.Module):
         for l in range(self.common_l_max + 1):
             self.weight.append(nn.Parameter(torch.randn(out_features, in_features * self.in_paths[l])))
 
-    def forward(self, x: torch.Tensor, input_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, input_scale: Optional[torch.Tensor] = None,
+                residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         """``input_scale`` (optional, 0-d tensor) multiplies the input: the map is linear, so
-        it is applied to the per-rank scales instead of to every element of ``x``."""
+        it is applied to the per-rank scales instead of to every element of ``x``.
+        ``residual`` (optional, laid out like the output) is added to the result: inside the
+        GEMM's epilogue where ``ops.linear_residual_fusable`` allows (first-order
+        evaluation, frozen float32 weights), else as a separate sum."""
         if x.shape[-1] != self.in_dim:
             raise RuntimeError(f"Incorrect last dimension for x. Expected {self.in_dim}, got {x.shape[-1]}.")
         if x.dim() != 2:
@@ -82,6 +86,13 @@ class LinearLayer(nn.Module):
         use_fp64, precision = get_linear_triton_kernel_options(x.dtype)
         weights = [w if w.dtype == x.dtype else w.to(x.dtype) for w in self.weight]
         scale = self.scale if input_scale is None else self.scale * input_scale
+        if residual is not None:
+            in_offs, out_offs, _, m, fi, fo = self.meta_lists
+            if ops.linear_residual_fusable(x, weights, self.out_dim, m, fi, fo, in_offs, out_offs, residual):
+                return torch.ops.flashcart.linear_residual_fwd(x, weights, residual, self.out_dim, precision, in_offs,
+                                                               out_offs, m, fi, fo, scale)
+            return torch.ops.flashcart.linear_fwd(x, weights, self.meta, self.out_dim, use_fp64, precision,
+                                                  *self.meta_lists, scale) + residual
         return torch.ops.flashcart.linear_fwd(x, weights, self.meta, self.out_dim, use_fp64, precision,
                                               *self.meta_lists, scale)
 

@@ -738,6 +738,145 @@ def _lsilu_backward(ctx, grad_out):
 linear_silu_fwd.register_autograd(_lsilu_backward, setup_context=_lsilu_setup)
 
 
+# --------------------------------------------------------------------------- residual sums
+
+
+def linear_residual_fusable(x: Tensor, weights: Sequence[Tensor], out_dim: int, m_values: Sequence[int],
+                            f_in_values: Sequence[int], f_out_values: Sequence[int], in_offsets: Sequence[int],
+                            out_offsets: Sequence[int], residual: Tensor) -> bool:
+    """``map(x) + residual`` (and its input gradient ``map^T(g) + residual``) can be one GEMM
+    with the sum in its epilogue (``fc_linear_fwd_residual`` / ``fc_linear_bwd_residual``):
+    first-order evaluation with frozen float32 weights on the GPU, active ranks covering the
+    whole input and output rows, at most 128 channels per rank on both sides (the
+    node-level maps) in multiples of 4, 16-byte aligned contiguous rows."""
+    if not (first_order_only_active() and x.is_cuda and x.dtype == torch.float32 and x.dim() == 2
+            and residual.dtype == torch.float32 and residual.device == x.device
+            and tuple(residual.shape) == (x.shape[0], int(out_dim)) and residual.is_contiguous() and x.is_contiguous()
+            and all(w.dtype == torch.float32 and not w.requires_grad for w in weights)):
+        return False
+    if x.data_ptr() % 16 or residual.data_ptr() % 16 or not m_values:
+        return False
+    pi = po = 0
+    for l in range(len(m_values)):
+        if in_offsets[l] != pi or out_offsets[l] != po:
+            return False
+        if f_in_values[l] > 128 or f_out_values[l] > 128 or f_in_values[l] % 4 or f_out_values[l] % 4:
+            return False
+        pi += m_values[l] * f_in_values[l]
+        po += m_values[l] * f_out_values[l]
+    return pi == x.shape[1] and po == int(out_dim)
+
+
+def _linear_residual_impl(rows: Tensor, weights: Sequence[Tensor], out_dim: int, lists, precision: str,
+                          scale: Tensor, residual: Tensor, backward: bool, out: Optional[Tensor] = None) -> Tensor:
+    """out = map(rows) + residual (forward) or map^T(rows) + residual (backward: rows is the
+    output gradient and out_dim the input row width); ``out`` may be ``residual`` itself."""
+    lib = N.lib()
+    rows = rows.contiguous()
+    n_active = len(lists[0])
+    ws = [w.to(rows.dtype).contiguous() for w in weights[:n_active]]
+    sc = scale.to(device=rows.device, dtype=rows.dtype).contiguous()
+    if out is None:
+        out = rows.new_empty((rows.shape[0], int(out_dim)))
+    in_dim, o_dim = (int(out_dim), rows.shape[1]) if backward else (rows.shape[1], int(out_dim))
+    d = _linear_desc(rows.new_empty((0, in_dim)), o_dim, lists[0], lists[1], lists[3], lists[4], lists[5], precision, 0)
+    split = _split_weights(lib, d, ws, backward)
+    fn = lib.fc_linear_bwd_residual if backward else lib.fc_linear_fwd_residual
+    name = "linear_bwd" if backward else "linear_fwd"
+    with _timed(name, 1, _nbytes(rows, out, residual, *ws)):
+        rc = fn(ctypes.byref(d), _p(rows), _ptr_array(ws), split, _p(sc), rows.shape[0], _p(residual), _p(out),
+                ctypes.c_void_p(status_word(rows.device).data_ptr()), _stream(rows.device))
+    _after(lib, rc, "fc_linear_bwd_residual" if backward else "fc_linear_fwd_residual", rows.device)
+    return out
+
+
+def _linear_input_grad(g: Tensor, in_size: int, weights: Sequence[Tensor], lists, precision: str,
+                       scale: Tensor) -> Tensor:
+    """grad_x = map^T(g) alone (frozen weights, no input activation): fc_linear_bwd reads its
+    ``x`` argument only for weight gradients and activations, so the output buffer stands
+    in for it."""
+    lib = N.lib()
+    n_active = len(lists[0])
+    ws = [w.to(g.dtype).contiguous() for w in weights[:n_active]]
+    sc = scale.to(device=g.device, dtype=g.dtype).contiguous()
+    gx = g.new_empty((g.shape[0], int(in_size)))
+    d = _linear_desc(gx, g.shape[1], lists[0], lists[1], lists[3], lists[4], lists[5], precision, 0)
+    split = _split_weights(lib, d, ws, True)
+    with _timed("linear_bwd", n_active, _nbytes(g, gx, *ws)):
+        if split is not None:
+            rc = lib.fc_linear_bwd_presplit(ctypes.byref(d), _p(g), _p(gx), _ptr_array(ws), split, _p(sc), g.shape[0],
+                                            _p(gx), None, ctypes.c_void_p(status_word(g.device).data_ptr()),
+                                            _stream(g.device))
+        else:
+            rc = lib.fc_linear_bwd(ctypes.byref(d), _p(g), _p(gx), _ptr_array(ws), _p(sc), g.shape[0], _p(gx), None,
+                                   ctypes.c_void_p(status_word(g.device).data_ptr()), _stream(g.device))
+    _after(lib, rc, "fc_linear_bwd", g.device)
+    return gx
+
+
+@torch.library.custom_op("flashcart::linear_residual_fwd", mutates_args=())
+def linear_residual_fwd(x: Tensor, weights: List[Tensor], residual: Tensor, out_size: int, dot_input_precision: str,
+                        in_offsets: List[int], out_offsets: List[int], m_values: List[int], f_in_values: List[int],
+                        f_out_values: List[int], scale: Tensor) -> Tensor:
+    """``linear_fwd(x) + residual`` with the sum done in the GEMM's epilogue: the residual
+    connections around the node-level maps (the gate layer's ``node_feats +
+    output_linear(...)``, reference ``nn/layers.py:609-635``; the interaction's skip sum,
+    ``nn/layers.py:395-405``), without a separate pass over the rows. Frozen weights."""
+    _require_cuda(x, residual, *weights)
+    lists = (in_offsets, out_offsets, [0] * len(in_offsets), m_values, f_in_values, f_out_values)
+    return _linear_residual_impl(x, weights, out_size, lists, dot_input_precision, scale, residual, False)
+
+
+@linear_residual_fwd.register_fake
+def _(x, weights, residual, out_size, dot_input_precision, in_offsets, out_offsets, m_values, f_in_values,
+      f_out_values, scale):
+    return x.new_empty((x.shape[0], int(out_size)))
+
+
+@torch.library.custom_op("flashcart::linear_residual_bwd", mutates_args=())
+def linear_residual_bwd(grad_out: Tensor, weights: List[Tensor], residual: Tensor, in_size: int,
+                        dot_input_precision: str, in_offsets: List[int], out_offsets: List[int], m_values: List[int],
+                        f_in_values: List[int], f_out_values: List[int], scale: Tensor) -> Tensor:
+    """``map^T(grad_out) + residual``: an input gradient and the gradient that reaches the same
+    tensor by another path, summed in the GEMM's epilogue. Frozen weights."""
+    _require_cuda(grad_out, residual, *weights)
+    lists = (in_offsets, out_offsets, [0] * len(in_offsets), m_values, f_in_values, f_out_values)
+    return _linear_residual_impl(grad_out, weights, in_size, lists, dot_input_precision, scale, residual, True)
+
+
+@linear_residual_bwd.register_fake
+def _(grad_out, weights, residual, in_size, dot_input_precision, in_offsets, out_offsets, m_values, f_in_values,
+      f_out_values, scale):
+    return grad_out.new_empty((grad_out.shape[0], int(in_size)))
+
+
+def _lres_setup(ctx, inputs, output):
+    x, weights = inputs[0], inputs[1]
+    ctx.save_for_backward(inputs[-1], *weights)
+    ctx.n_w = len(weights)
+    ctx.in_size = x.shape[1]
+    ctx.meta = inputs[4:-1]
+
+
+def _lres_backward(ctx, grad_out):
+    if torch.is_grad_enabled():
+        raise RuntimeError("flashcart::linear_residual_fwd was evaluated inside first_order_only(); its backward "
+                           "cannot build a graph for a second derivative")
+    scale, *weights = ctx.saved_tensors
+    if any(w.requires_grad for w in weights):
+        raise RuntimeError("flashcart::linear_residual_fwd has no weight gradient (frozen weights only)")
+    g = grad_out.contiguous()
+    gx = None
+    if ctx.needs_input_grad[0]:
+        prec, in_offs, out_offs, m, fi, fo = ctx.meta
+        lists = (in_offs, out_offs, [0] * len(in_offs), m, fi, fo)
+        gx = _linear_input_grad(g, ctx.in_size, weights, lists, prec, scale)
+    return (gx, [None] * len(weights), g if ctx.needs_input_grad[2] else None) + (None,) * 8
+
+
+linear_residual_fwd.register_autograd(_lres_backward, setup_context=_lres_setup)
+
+
 @torch.library.custom_op("flashcart::linear_dbwd", mutates_args=())
 def linear_dbwd(grad_out: Tensor, x: Tensor, weights: List[Tensor], v_grad_x: Tensor, v_grad_weight: List[Tensor],
                 use_fp64: bool, dot_input_precision: str, need_d_grad_out: bool, need_d_x: bool,

@@ -246,6 +246,24 @@ int fc_linear_bwd_presplit(const fc_linear_desc* desc, const void* grad_out, con
                            const void* const* weights, const void* const* split, const void* scale, int64_t n,
                            void* grad_x, void* const* grad_weights, int32_t* status, fc_stream_t stream);
 
+/* Residual forms of the float32 maps: out = (sW) x + residual and grad_x = (sW)^T grad_out
+ * + residual, the residual laid out like the output row (out_dim, resp. in_dim floats per
+ * row; it may be the output buffer itself, which then accumulates), added in the GEMM's
+ * epilogue instead of by a separate pass over the rows. They carry the residual
+ * connections of the node-level layers around the maps of o3/_linear.py:328-538 (the gate
+ * layer's `node_feats + output_linear(...)`, nn/layers.py:609-635, the interaction's skip
+ * sum, nn/layers.py:395-405, and the sums of their gradients). float32 on the TMA-fed
+ * tensor-core path only: the active ranks must cover the whole row, their blocks must be
+ * uniform with at most 128 output columns (node-level maps), act must be FC_ACT_NONE, and
+ * rows must be 16-byte aligned; otherwise FC_ERR_UNSUPPORTED and nothing is written.
+ * split: the lin_presplit buffers, or NULL (split per call). No weight gradients. */
+int fc_linear_fwd_residual(const fc_linear_desc* desc, const void* x, const void* const* weights,
+                           const void* const* split, const void* scale, int64_t n, const void* residual, void* out,
+                           int32_t* status, fc_stream_t stream);
+int fc_linear_bwd_residual(const fc_linear_desc* desc, const void* grad_out, const void* const* weights,
+                           const void* const* split, const void* scale, int64_t n, const void* residual,
+                           void* grad_x, int32_t* status, fc_stream_t stream);
+
 /* ---------------------------------------------------------------- halo exchange
  * Row gather / scatter for ghost-atom exchange in a domain decomposition (owned rows
  * first, ghost rows after them). The transport between ranks is the caller's (NCCL, MPI,

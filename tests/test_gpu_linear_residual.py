@@ -1,0 +1,114 @@
+"""Residual forms of the float32 linear maps (fc_linear_fwd_residual / fc_linear_bwd_residual,
+flashcart::linear_residual_fwd): map(x) + residual and map^T(g) + residual with the sum in
+the GEMM's epilogue, as the node-level layers use them for their residual connections
+(reference ``nn/layers.py:395-405, 609-635``).
+
+Checked against the separate sum on the same kernels (forward and both input gradients,
+float32, tolerance 2e-6 of the output scale: the epilogue adds the residual to the
+float32 accumulation instead of rounding first), an accumulation into the output buffer
+itself, a layout the epilogue does not take (256 output channels per rank: the separate
+sum), and the C-ABI's refusals.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+from flashcart_b200 import _native as N
+from flashcart_b200 import o3, ops
+from flashcart_b200.ops import check_device_status
+
+pytestmark = pytest.mark.gpu
+
+
+def _frozen(lin):
+    for p in lin.parameters():
+        p.requires_grad_(False)
+    return lin
+
+
+def _rel(a, b):
+    return (a.double() - b.double()).abs().max().item() / max(1.0, b.double().abs().max().item())
+
+
+@pytest.mark.parametrize("shape", [(3, 3, 128, 128, 2000), (2, 2, 64, 64, 777), (3, 3, 128, 128, 1)])
+def test_gpu_linear_residual_matches_separate_sum(cuda_device, shape):
+    li, lo, fi, fo, n = shape
+    dev = cuda_device
+    torch.manual_seed(n)
+    lin = _frozen(o3.LinearLayer(li, lo, fi, fo).to(dev))
+    x = torch.randn(n, lin.in_dim, device=dev)
+    r = torch.randn(n, lin.out_dim, device=dev)
+    g = torch.randn(n, lin.out_dim, device=dev)
+    with ops.first_order_only():
+        x1, r1 = x.clone().requires_grad_(True), r.clone().requires_grad_(True)
+        in_offs, out_offs, _, m, f_in, f_out = lin.meta_lists
+        assert ops.linear_residual_fusable(x1, list(lin.weight), lin.out_dim, m, f_in, f_out, in_offs, out_offs, r1)
+        y1 = lin(x1, residual=r1)
+        gx1, gr1 = torch.autograd.grad(y1, [x1, r1], g)
+    x2, r2 = x.clone().requires_grad_(True), r.clone().requires_grad_(True)
+    y2 = lin(x2) + r2
+    gx2, gr2 = torch.autograd.grad(y2, [x2, r2], g)
+    assert _rel(y1, y2) < 2e-6
+    assert _rel(gx1, gx2) < 2e-6
+    assert torch.equal(gr1, gr2)
+    check_device_status(dev)
+
+
+def test_gpu_linear_residual_accumulates_in_place_through_the_c_abi(cuda_device):
+    """grad_x += map^T(g) with the residual and the output the same buffer, twice."""
+    dev = cuda_device
+    torch.manual_seed(3)
+    lin = _frozen(o3.LinearLayer(3, 3, 128, 128).to(dev))
+    n = 1500
+    g = torch.randn(n, lin.out_dim, device=dev)
+    base = torch.randn(n, lin.in_dim, device=dev)
+    in_offs, out_offs, _, m, f_in, f_out = lin.meta_lists
+    lists = (in_offs, out_offs, [0] * len(in_offs), m, f_in, f_out)
+    gx_alone = ops._linear_input_grad(g, lin.in_dim, list(lin.weight), lists, "ieee", lin.scale)
+    buf = base.clone()
+    for _ in range(2):
+        ops._linear_residual_impl(g, list(lin.weight), lin.in_dim, lists, "ieee", lin.scale, buf, True, out=buf)
+    want = base + 2 * gx_alone
+    assert _rel(buf, want) < 2e-6
+    check_device_status(dev)
+
+
+def test_gpu_linear_residual_outside_the_epilogue_layout(cuda_device):
+    """256 output channels per rank are not taken by the epilogue: the layer sums separately."""
+    dev = cuda_device
+    torch.manual_seed(4)
+    lin = _frozen(o3.LinearLayer(1, 1, 64, 256).to(dev))
+    x = torch.randn(300, lin.in_dim, device=dev)
+    r = torch.randn(300, lin.out_dim, device=dev)
+    in_offs, out_offs, _, m, f_in, f_out = lin.meta_lists
+    with ops.first_order_only():
+        assert not ops.linear_residual_fusable(x, list(lin.weight), lin.out_dim, m, f_in, f_out, in_offs, out_offs, r)
+        y = lin(x, residual=r)
+    assert _rel(y, lin(x) + r) < 1e-6
+    check_device_status(dev)
+
+
+def test_gpu_linear_residual_c_abi_refusals(cuda_device):
+    dev = cuda_device
+    lib = N.lib()
+    lin = _frozen(o3.LinearLayer(1, 1, 8, 8).to(dev))
+    x = torch.randn(10, lin.in_dim, device=dev)
+    r = torch.randn(10, lin.out_dim, device=dev)
+    out = torch.empty_like(r)
+    ws = list(lin.weight)
+    arr = (ctypes.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    in_offs, out_offs, _, m, f_in, f_out = lin.meta_lists
+    d = ops._linear_desc(x, lin.out_dim, in_offs, out_offs, m, f_in, f_out, "ieee", N.FC_ACT_SILU)
+    rc = lib.fc_linear_fwd_residual(ctypes.byref(d), ctypes.c_void_p(x.data_ptr()), arr, None,
+                                    ctypes.c_void_p(lin.scale.data_ptr()), 10, ctypes.c_void_p(r.data_ptr()),
+                                    ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(status.data_ptr()), None)
+    assert rc == N.FC_ERR_UNSUPPORTED and b"activation" in lib.fc_last_error()
+    xd = x.double()
+    d = ops._linear_desc(xd, lin.out_dim, in_offs, out_offs, m, f_in, f_out, "ieee", 0)
+    rc = lib.fc_linear_fwd_residual(ctypes.byref(d), ctypes.c_void_p(xd.data_ptr()), arr, None,
+                                    ctypes.c_void_p(lin.scale.data_ptr()), 10, ctypes.c_void_p(r.data_ptr()),
+                                    ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(status.data_ptr()), None)
+    assert rc == N.FC_ERR_UNSUPPORTED
