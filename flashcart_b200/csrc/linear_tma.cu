@@ -125,6 +125,7 @@ struct Args {
 struct BMaps {
   CUtensorMap hi[4];
   CUtensorMap lo[4];
+  CUtensorMap r;  // ACT >= 2: the aux rows, laid out like C (loaded per 32 x 32 box by the epilogue)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -317,7 +318,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + C::NACC;
   uint64_t* drain = acc_empty + C::NACC;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* aux_bar = drain + 1;  // per epilogue warp and staging buffer: the aux box has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 8);
+  static_assert((3 * S + 2 * C::NACC + 1 + 8) * 8 + 8 <= BAR_BYTES, "barrier area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -337,6 +340,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(smem_u32(&acc_empty[b])));
     }
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(drain)));
+    for (int b = 0; b < 8; ++b) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&aux_bar[b])));
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -529,52 +533,49 @@ __global__ void __launch_bounds__(THREADS, 1)
     float sc = a.scale[0];   // the scale of the current tile's rank
     uint8_t* stage0 = epi + (warp - EPI_WARP0) * 2 * 4096;
     int nbuf = 0;
+    uint32_t aux_ph = 0;  // bit b: phase of this warp's aux barrier of staging buffer b
     int64_t u = 0;
     // one staged TMA store of 32 columns (this warp's 32 rows) from registers
     auto store_chunk = [&](const float* vals, int col, const TileCoord& tc) {
       float f[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) f[c] = sc * vals[c];
-      if constexpr (ACT == 2) {
-        // this lane's row of the tile: 32 aux values (128 contiguous bytes)
-        const int64_t node = (int64_t)tc.node0 + q * 32 + lane;
-        if (node < a.nodes) {
-          // 16-byte loads (the aux rows have the TMA layout of the GEMM's input: 16-byte
-          // aligned rows, N a multiple of 4)
-          const float4* ar = reinterpret_cast<const float4*>(a.aux + node * a.aux_ld + (int64_t)tc.m * a.aux_ms + col);
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (col + 4 * c < a.N) {
-              const float4 z = __ldg(ar + c);
-              f[4 * c] *= act_dsilu(z.x);
-              f[4 * c + 1] *= act_dsilu(z.y);
-              f[4 * c + 2] *= act_dsilu(z.z);
-              f[4 * c + 3] *= act_dsilu(z.w);
-            }
-        }
-      }
-      if constexpr (ACT == 3) {
-        // this lane's row of the residual: plain (coherent) 16-byte loads, since the
-        // residual may be the output itself (each element is read here before this
-        // thread's staged store of it)
-        const int64_t node = (int64_t)tc.node0 + q * 32 + lane;
-        if (node < a.nodes) {
-          const float4* ar = reinterpret_cast<const float4*>(a.aux + node * a.aux_ld + (int64_t)tc.m * a.aux_ms + col);
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (col + 4 * c < a.N) {
-              const float4 z = ar[c];
-              f[4 * c] += z.x;
-              f[4 * c + 1] += z.y;
-              f[4 * c + 2] += z.z;
-              f[4 * c + 3] += z.w;
-            }
-        }
-      }
       if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // buffer used two stores ago
       __syncwarp();
       uint8_t* buf = stage0 + nbuf * 4096;
       uint8_t* row = buf + lane * 128;
+      if constexpr (ACT >= 2) {
+        // the aux box of this chunk (32 rows x 32 columns, laid out like C) comes into the
+        // staging buffer by TMA, in the swizzled layout the store uses; each lane then reads
+        // its row, applies it, and writes the result over it (the same bytes, same thread)
+        const uint32_t rb = smem_u32(&aux_bar[(warp - EPI_WARP0) * 2 + nbuf]);
+        if (lane == 0) {
+          arrive_tx(rb, 4096);
+          tma_load_3d(smem_u32(buf), &bm.r, col, tc.node0 + q * 32, tc.m, rb);
+        }
+        const uint32_t par = (aux_ph >> nbuf) & 1u;
+        aux_ph ^= 1u << nbuf;
+        if (!wait_parity(rb, par, abort_flag, a.status)) {
+          // the load may still land: let it finish (bounded) before the buffer is reused
+          for (long long it = 0; it < WAIT_LIMIT; ++it)
+            if (test_parity(rb, par)) break;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 z = *reinterpret_cast<const float4*>(row + ((c ^ (lane & 7)) << 4));
+          if constexpr (ACT == 2) {
+            f[4 * c] *= act_dsilu(z.x);
+            f[4 * c + 1] *= act_dsilu(z.y);
+            f[4 * c + 2] *= act_dsilu(z.z);
+            f[4 * c + 3] *= act_dsilu(z.w);
+          } else {
+            f[4 * c] += z.x;
+            f[4 * c + 1] += z.y;
+            f[4 * c + 2] += z.z;
+            f[4 * c + 3] += z.w;
+          }
+        }
+      }
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         *reinterpret_cast<float4*>(row + ((c ^ (lane & 7)) << 4)) =
@@ -813,6 +814,11 @@ static int run_tma(const LinGemmArgs<float>* a, int n, bool split, int* status, 
   if (!encode_rows(&ma, a0.a.p + a0.a.off, a0.K, nodes, m_total, a0.a.ld, a0.a.ms, BM)) return 1;
   if (!encode_rows(&mpf, a0.a.p + a0.a.off, a0.K, nodes, m_total, a0.a.ld, a0.a.ms, BM, PF_SLABS * BK)) return 1;
   if (!encode_rows(&mc, a0.c.p + a0.c.off, a0.N, nodes, m_total, a0.c.ld, a0.c.ms, 32)) return 1;
+  if (a0.act >= 2) {
+    if (!encode_rows(&bm.r, a0.aux.p + a0.aux.off, a0.N, nodes, m_total, a0.aux.ld, a0.aux.ms, 32)) return 1;
+  } else {
+    bm.r = mc;  // unused
+  }
 
   const size_t per_rank = (size_t)a0.N * kp * (split ? 2 : 1);
   float* ws = nullptr;

@@ -375,10 +375,25 @@ class EquivariantGatedLayer(_ChildSpecialParameters, nn.Module):
         for w in self.output_linear.weight:
             nn.init.zeros_(w)
 
+    def _fused_ok(self, node_feats) -> bool:
+        """One autograd node for the whole layer (first-order evaluation, frozen float32
+        weights, the residual-epilogue layout for both equivariant maps)."""
+        if not (ops.first_order_only_active() and node_feats.is_cuda and node_feats.dtype == torch.float32
+                and node_feats.is_contiguous() and node_feats.data_ptr() % 16 == 0
+                and not any(p.requires_grad for p in self.parameters())):
+            return False
+        for lin in (self.value_linear, self.output_linear):
+            in_offs, out_offs, _, m, fi, fo = lin.meta_lists
+            if not ops.linear_residual_layout_ok(lin.in_dim, lin.out_dim, m, fi, fo, in_offs, out_offs):
+                return False
+        return self.gate_linear.in_features % 4 == 0 and self.gate_linear.out_features % 4 == 0
+
     def forward(self, node_feats):
         if node_feats.shape[-1] != self.in_dim:
             raise RuntimeError(f"Incorrect last dimension for node_feats. Expected {self.in_dim}, "
                                f"got {node_feats.shape[-1]}.")
+        if self._fused_ok(node_feats):
+            return _GatedResidualFirstOrder.apply(node_feats, self)
         n = node_feats.shape[0]
         values = self.value_linear(node_feats)
         gates = self.gate_activation(self.gate_linear(node_feats[:, :self.in_features]))
@@ -393,6 +408,53 @@ class EquivariantGatedLayer(_ChildSpecialParameters, nn.Module):
             parts.append((values[:, a:b].view(n, 2 * l + 1, self.hidden_features) * gates[:, l].unsqueeze(1))
                          .flatten(1))
         return node_feats + self.output_linear(torch.cat(parts, dim=-1))
+
+
+class _GatedResidualFirstOrder(torch.autograd.Function):
+    """``EquivariantGatedLayer`` as one autograd node for first-order evaluation with frozen
+    weights. The input feeds three consumers (the value map, the gate map through its l = 0
+    block, and the residual); composed, their gradients are summed by separate passes over
+    the rows (and the l = 0 slice's gradient is first written into a zero-filled row). Here
+    the value map's input gradient is computed with the incoming gradient as its residual
+    (one GEMM epilogue) and the gate map's gradient is added into the l = 0 block."""
+
+    @staticmethod
+    def forward(ctx, node_feats, layer):
+        n = node_feats.shape[0]
+        values = layer.value_linear(node_feats)
+        gpre = layer.gate_linear(node_feats[:, :layer.in_features])
+        gates = layer.gate_activation(gpre).view(n, layer.l_max + 1, layer.hidden_features)
+        gated = ops.gate_fwd(values, gates, layer.l_max, layer.hidden_features)
+        out = layer.output_linear(gated, residual=node_feats)
+        ctx.save_for_backward(values, gates, gpre)
+        ctx.layer = layer
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        if torch.is_grad_enabled():
+            raise RuntimeError("EquivariantGatedLayer was evaluated inside first_order_only(); its backward cannot "
+                               "build a graph for a second derivative")
+        values, gates, gpre = ctx.saved_tensors
+        layer = ctx.layer
+        g = g.contiguous()
+        if g.data_ptr() % 16:  # the epilogue reads the residual as 16-byte vectors
+            g = g.clone()
+        _, precision = o3.utils.get_linear_triton_kernel_options(g.dtype)
+        out_map, value_map, gate_map = layer.output_linear, layer.value_linear, layer.gate_linear
+        g_gated = ops._linear_input_grad(g, out_map.in_dim, list(out_map.weight), out_map.meta_lists, precision,
+                                         out_map.scale)
+        g_values, g_gates = ops.gate_bwd(g_gated, values, gates, layer.l_max, layer.hidden_features)
+        with torch.enable_grad():
+            gp = gpre.detach().requires_grad_(True)
+            (g_gpre,) = torch.autograd.grad(layer.gate_activation(gp), gp, g_gates.reshape(gpre.shape))
+        # value map's input gradient + the residual's gradient, in one epilogue
+        g_x = ops._linear_residual_impl(g_values.contiguous(), list(value_map.weight), value_map.in_dim,
+                                        value_map.meta_lists, precision, value_map.scale, g, True)
+        g_x0 = ops._linear_input_grad(g_gpre.contiguous(), gate_map.in_features, [gate_map.weight],
+                                      gate_map._lists, precision, gate_map.scale.reshape(1))
+        g_x[:, :layer.in_features] += g_x0
+        return g_x, None
 
 
 class IrrepsSelector(_NoSpecialParameters, nn.Module):

@@ -741,6 +741,24 @@ linear_silu_fwd.register_autograd(_lsilu_backward, setup_context=_lsilu_setup)
 # --------------------------------------------------------------------------- residual sums
 
 
+def linear_residual_layout_ok(in_dim: int, out_dim: int, m_values: Sequence[int], f_in_values: Sequence[int],
+                              f_out_values: Sequence[int], in_offsets: Sequence[int],
+                              out_offsets: Sequence[int]) -> bool:
+    """The rank layout the residual epilogue takes: active ranks covering both rows, at most
+    128 channels per rank on both sides, in multiples of 4."""
+    if not m_values:
+        return False
+    pi = po = 0
+    for l in range(len(m_values)):
+        if in_offsets[l] != pi or out_offsets[l] != po:
+            return False
+        if f_in_values[l] > 128 or f_out_values[l] > 128 or f_in_values[l] % 4 or f_out_values[l] % 4:
+            return False
+        pi += m_values[l] * f_in_values[l]
+        po += m_values[l] * f_out_values[l]
+    return pi == int(in_dim) and po == int(out_dim)
+
+
 def linear_residual_fusable(x: Tensor, weights: Sequence[Tensor], out_dim: int, m_values: Sequence[int],
                             f_in_values: Sequence[int], f_out_values: Sequence[int], in_offsets: Sequence[int],
                             out_offsets: Sequence[int], residual: Tensor) -> bool:
@@ -754,17 +772,10 @@ def linear_residual_fusable(x: Tensor, weights: Sequence[Tensor], out_dim: int, 
             and tuple(residual.shape) == (x.shape[0], int(out_dim)) and residual.is_contiguous() and x.is_contiguous()
             and all(w.dtype == torch.float32 and not w.requires_grad for w in weights)):
         return False
-    if x.data_ptr() % 16 or residual.data_ptr() % 16 or not m_values:
+    if x.data_ptr() % 16 or residual.data_ptr() % 16:
         return False
-    pi = po = 0
-    for l in range(len(m_values)):
-        if in_offsets[l] != pi or out_offsets[l] != po:
-            return False
-        if f_in_values[l] > 128 or f_out_values[l] > 128 or f_in_values[l] % 4 or f_out_values[l] % 4:
-            return False
-        pi += m_values[l] * f_in_values[l]
-        po += m_values[l] * f_out_values[l]
-    return pi == x.shape[1] and po == int(out_dim)
+    return linear_residual_layout_ok(x.shape[1], out_dim, m_values, f_in_values, f_out_values, in_offsets,
+                                     out_offsets)
 
 
 def _linear_residual_impl(rows: Tensor, weights: Sequence[Tensor], out_dim: int, lists, precision: str,

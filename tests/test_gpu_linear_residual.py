@@ -112,3 +112,31 @@ def test_gpu_linear_residual_c_abi_refusals(cuda_device):
                                     ctypes.c_void_p(lin.scale.data_ptr()), 10, ctypes.c_void_p(r.data_ptr()),
                                     ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(status.data_ptr()), None)
     assert rc == N.FC_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("gate", ["sigmoid", "silu"])
+def test_gpu_gated_layer_single_node_matches_composed(cuda_device, gate):
+    """EquivariantGatedLayer as one autograd node (first-order evaluation, frozen weights:
+    the value map's input gradient takes the residual's gradient in its epilogue) against
+    the composed layer, output and input gradient."""
+    from flashcart_b200.nn.layers import EquivariantGatedLayer
+
+    dev = cuda_device
+    torch.manual_seed(7)
+    layer = _frozen(EquivariantGatedLayer(3, 128, 128, gate_activation=gate).to(dev))
+    with torch.no_grad():
+        for w in layer.output_linear.weight:
+            w.normal_()  # zero at initialisation: make the gated branch contribute
+    x = torch.randn(1200, layer.in_dim, device=dev)
+    g = torch.randn_like(x)
+    with ops.first_order_only():
+        x1 = x.clone().requires_grad_(True)
+        assert layer._fused_ok(x1)
+        y1 = layer(x1)
+        (gx1,) = torch.autograd.grad(y1, [x1], g)
+    x2 = x.clone().requires_grad_(True)
+    y2 = layer(x2)
+    (gx2,) = torch.autograd.grad(y2, [x2], g)
+    assert _rel(y1, y2) < 2e-6
+    assert _rel(gx1, gx2) < 2e-6
+    check_device_status(dev)
