@@ -42,7 +42,7 @@ EXPORTED_SYMBOLS = (
     "fc_neighbor_workspace_bytes", "fc_neighbor_count", "fc_neighbor_fill",
     "fc_edge_expand_fwd", "fc_edge_expand_bwd",
     "fc_linear_presplit", "fc_linear_fwd_presplit", "fc_linear_bwd_presplit",
-    "fc_linear_fwd_residual", "fc_linear_bwd_residual",
+    "fc_linear_fwd_residual", "fc_linear_bwd_residual", "fc_tp_bwd_residual",
     "fc_linear_dbwd", "fc_halo_pack", "fc_halo_unpack", "fc_edge_geometry_fwd", "fc_edge_geometry_bwd",
     "fc_edge_geometry_vec_fwd", "fc_edge_geometry_vec_bwd",
 )
@@ -145,6 +145,9 @@ def bind(path: str) -> ctypes.CDLL:
     lib.fc_linear_fwd_presplit.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P]
     lib.fc_linear_bwd_presplit.restype = ctypes.c_int
     lib.fc_linear_bwd_presplit.argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P]
+    lib.fc_tp_bwd_residual.restype = ctypes.c_int
+    lib.fc_tp_bwd_residual.argtypes = [ctypes.POINTER(TpDesc), _P, _P, _P, _P, _I64, _P, _I64, ctypes.c_int32, _P,
+                                       _P, _P, _P, _P]
     for name in ("fc_linear_fwd_residual", "fc_linear_bwd_residual"):
         getattr(lib, name).restype = ctypes.c_int
         getattr(lib, name).argtypes = [ctypes.POINTER(LinearDesc), _P, _P, _P, _P, _I64, _P, _P, _P, _P]

@@ -153,12 +153,23 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
             w("    }")
         w("  }")
     w("  if (NEED_1) {")
-    w("    float* __restrict__ t1 = P.g_in1 + row * (int64_t)(D1 * F) + c;")
+    w("    float* t1 = P.g_in1 + row * (int64_t)(D1 * F) + c;")
+    w("    if (P.r_in1) {  // residual of the leading components (plain loads: it may alias an output)")
+    w("      const float* r1 = P.r_in1 + row * P.r1_ld + c;")
+    w("#pragma unroll")
+    w("      for (int q = 0; q < D1; ++q)")
+    w("        if (q < P.r1_comps) gx1[q] = padd(gx1[q], ld2(r1 + q * F));")
+    w("    }")
     w("#pragma unroll")
     w("    for (int q = 0; q < D1; ++q) st2(t1 + q * F, gx1[q]);")
     w("  }")
     w("  if (NEED_2) {")
-    w("    float* __restrict__ t2 = P.g_in2 + row * (int64_t)(D2 * F) + c;")
+    w("    float* t2 = P.g_in2 + row * (int64_t)(D2 * F) + c;")
+    w("    if (P.r_in2) {")
+    w("      const float* r2 = P.r_in2 + row * (int64_t)(D2 * F) + c;")
+    w("#pragma unroll")
+    w("      for (int q = 0; q < D2; ++q) gx2[q] = padd(gx2[q], ld2(r2 + q * F));")
+    w("    }")
     w("#pragma unroll")
     w("    for (int q = 0; q < D2; ++q) st2(t2 + q * F, gx2[q]);")
     w("  }")

@@ -599,6 +599,38 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
   return launch_status(v2 ? sig->table->bwd2_f64(p, s) : sig->table->bwd_f64(p, s), "fc_tp_bwd");
 }
 
+int fc_tp_bwd_residual(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2,
+                       const void* weights, int64_t n_rows, const void* residual_in1, int64_t residual_in1_ld,
+                       int32_t residual_in1_comps, const void* residual_in2, void* grad_in1, void* grad_in2,
+                       int32_t* status, fc_stream_t stream) {
+  if (int rc = check_desc(desc)) return rc;
+  if (n_rows < 0) return fail(FC_ERR_INVALID, "fc_tp_bwd_residual: negative size");
+  const TpSigEntry* sig = find_sig(desc);
+  if (!dense_pair_eligible(desc, false, nullptr, {grad_out, in1, in2, weights, residual_in1, residual_in2, grad_in1,
+                                                  grad_in2}))
+    return fail(FC_ERR_UNSUPPORTED, "fc_tp_bwd_residual: float32 dense products of 64 / 128 channels with paths "
+                                    "kept and 8-byte aligned rows only");
+  const int64_t d1 = (int64_t)(desc->in1_l_max + 1) * (desc->in1_l_max + 1);
+  if (residual_in1 && (residual_in1_comps < 0 || residual_in1_comps > d1 ||
+                       residual_in1_ld < (int64_t)residual_in1_comps * desc->in1_features || (residual_in1_ld & 1)))
+    return fail(FC_ERR_INVALID, "fc_tp_bwd_residual: residual_in1 layout");
+  if (n_rows == 0) return FC_OK;
+  if (sig == nullptr || sig->npaths == 0 || sig->table->dpbwd_f32 == nullptr)
+    return fail(FC_ERR_UNSUPPORTED, "fc_tp_bwd_residual: no dense pair kernel for this signature");
+  if (!grad_out || !in1 || !in2 || !weights) return fail(FC_ERR_INVALID, "fc_tp_bwd_residual: null tensor");
+  TpBwdParams<float> p;
+  fill_common(p, desc, nullptr, nullptr, n_rows, n_rows, status);
+  p.g_out = (const float*)grad_out; p.in1 = (const float*)in1; p.in2 = (const float*)in2;
+  p.w = (const float*)weights;
+  p.g_in1 = (float*)grad_in1; p.g_in2 = (float*)grad_in2; p.g_w = nullptr;
+  p.r_in1 = (const float*)residual_in1;
+  p.r_in2 = (const float*)residual_in2;
+  p.r1_ld = residual_in1_ld;
+  p.r1_comps = residual_in1 ? residual_in1_comps : 0;
+  const int rc = sig->table->dpbwd_f32(p, (cudaStream_t)stream);
+  return rc == FC_ERR_LAUNCH || rc == 0 ? launch_status(rc, "fc_tp_bwd_residual") : rc;
+}
+
 int fc_tp_dbwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2, const void* weights,
                const void* v_in1, const void* v_in2, const void* v_weights, const int64_t* rowptr,
                const int64_t* idx_j, int64_t n_out_rows, int64_t n_in1_rows, int64_t n_in2_rows, void* d_grad_out,

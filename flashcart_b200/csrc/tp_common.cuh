@@ -39,6 +39,13 @@ struct TpBwdParams {
   int64_t n_rows, n_in1;
   int F, F1, F2, shared_w, reduce;
   int* status;
+  // dense channel-pair backward only (fc_tp_bwd_residual): added to the input gradients;
+  // r_in1 covers the first r1_comps components of each in1 row (row stride r1_ld), r_in2
+  // whole in2 rows; either may be null, r_in2 may be g_in2 itself
+  const T* r_in1 = nullptr;
+  const T* r_in2 = nullptr;
+  int64_t r1_ld = 0;
+  int r1_comps = 0;
 };
 
 template <typename T>

@@ -575,7 +575,37 @@ class ProductLayer(_ChildSpecialParameters, nn.Module):
         else:
             self.step0_weight_index = None
 
+    def _selected_comps(self) -> Optional[int]:
+        """Leading components of a step's output that enter the sum (all when its selector is
+        the identity), or None when the steps select differently."""
+        comps = set()
+        d = (self.in_l_max + 1) ** 2
+        for sel in self.irreps_selectors:
+            if isinstance(sel, nn.Identity):
+                continue
+            if sel.stop % self.in_features:
+                return None
+            comps.add(sel.stop // self.in_features)
+        return d if not comps else (comps.pop() if len(comps) == 1 else None)
+
+    def _single_node_ok(self, node_feats) -> bool:
+        """One autograd node for the whole layer: first-order evaluation, frozen float32
+        weights shared by all atoms, no step-0 weighting, paths kept, the products on the
+        dense channel-pair kernels (64 or 128 channels)."""
+        if not (ops.first_order_only_active() and node_feats.is_cuda and node_feats.dtype == torch.float32
+                and node_feats.is_contiguous() and node_feats.data_ptr() % 16 == 0 and not self.path_reduced
+                and self.skip_projection is not None and self.step0_weight_index is None
+                and self.in_features in (64, 128) and self._selected_comps() is not None
+                and not any(p.requires_grad for p in self.parameters())):
+            return False
+        return all(tp.in1_features == tp.in2_features and not tp.reduce_paths for tp in self.tensor_products)
+
     def forward(self, node_feats, atom_types=None):
+        if self._single_node_ok(node_feats):
+            ws = [self.path_weights[step](atom_types).to(node_feats.dtype).contiguous()
+                  for step in range(1, self.correlation)]
+            out = _ProductSumFirstOrder.apply(node_feats, self, *ws)
+            return self.layer_norm(out) if self.layer_norm is not None else out
         if (not self.path_reduced and self.skip_projection is not None
                 and all(isinstance(s, nn.Identity) for s in self.irreps_selectors)):
             return self._forward_summed_in_maps(node_feats, atom_types)
@@ -633,6 +663,73 @@ class ProductLayer(_ChildSpecialParameters, nn.Module):
         if self.layer_norm is not None:
             out = self.layer_norm(out)
         return out
+
+
+class _ProductSumFirstOrder(torch.autograd.Function):
+    """``ProductLayer`` (before its layer norm) as one autograd node for first-order
+    evaluation with frozen weights. Composed, every input of the layer's sum has several
+    consumers: the node features feed the first map, every product and the skip projection;
+    each intermediate product feeds the next product and the sum (through a slice when the
+    layer keeps only the low ranks). Their gradients are then summed by separate passes
+    over the rows, after zero-filled rows for the slices. Here the backward walks the
+    products in reverse with those sums inside the kernels: each dense product's backward
+    adds the sum's gradient to its in1 gradient (on the selected leading components) and
+    accumulates its in2 gradient into the running gradient of the node features, which
+    starts as the skip projection's input gradient and ends in the first map's epilogue."""
+
+    @staticmethod
+    def forward(ctx, node_feats, layer, *ws):
+        comps = layer._selected_comps()
+        width = comps * layer.in_features
+        prods, prod = [], node_feats
+        for step in range(layer.correlation):
+            if step > 0:
+                prod = layer.tensor_products[step - 1](prod, node_feats, ws[step - 1])
+            if step < layer.correlation - 1:
+                prod = layer.product_linears[step](prod)
+                prods.append(prod)
+        sel = (lambda p: p) if width == prods[0].shape[1] else (lambda p: p[:, :width].contiguous())
+        acc = layer.skip_projection(node_feats, residual=sel(prods[0]))
+        for p in prods[1:]:
+            acc = acc + sel(p)
+        out = layer.product_linears[layer.correlation - 1](prod, residual=acc)
+        ctx.save_for_backward(node_feats, *prods, *ws)
+        ctx.layer, ctx.comps, ctx.n_prods = layer, comps, len(prods)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        if torch.is_grad_enabled():
+            raise RuntimeError("ProductLayer was evaluated inside first_order_only(); its backward cannot build a "
+                               "graph for a second derivative")
+        saved = ctx.saved_tensors
+        x, prods, ws = saved[0], saved[1:1 + ctx.n_prods], saved[1 + ctx.n_prods:]
+        layer, comps = ctx.layer, ctx.comps
+        g = g.contiguous()
+        if g.data_ptr() % 16:
+            g = g.clone()
+        _, precision = o3.utils.get_linear_triton_kernel_options(g.dtype)
+
+        def input_grad(lin, rows):
+            return ops._linear_input_grad(rows.contiguous(), lin.in_dim, list(lin.weight), lin.meta_lists, precision,
+                                          lin.scale)
+
+        g_t = input_grad(layer.product_linears[layer.correlation - 1], g)
+        gx = input_grad(layer.skip_projection, g)  # the running gradient of the node features
+        for k in range(layer.correlation - 1, 0, -1):
+            g_prod, gx = ops.tp_dense_bwd_residual(layer.tensor_products[k - 1], g_t, prods[k - 1], x, ws[k - 1],
+                                                   g, comps, gx, out_in2=gx)
+            lin = layer.product_linears[k - 1]
+            if k - 1 > 0:
+                g_t = input_grad(lin, g_prod)
+                continue
+            in_offs, out_offs, _, m, fi, fo = lin.meta_lists
+            if ops.linear_residual_layout_ok(lin.in_dim, lin.out_dim, m, fi, fo, in_offs, out_offs):
+                gx = ops._linear_residual_impl(g_prod, list(lin.weight), lin.in_dim, lin.meta_lists, precision,
+                                               lin.scale, gx, True, out=gx)
+            else:
+                gx = gx + input_grad(lin, g_prod)
+        return (gx, None) + (None,) * len(ws)
 
 
 class EnergyReadoutLayer(nn.Module):

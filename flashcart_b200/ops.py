@@ -741,6 +741,36 @@ linear_silu_fwd.register_autograd(_lsilu_backward, setup_context=_lsilu_setup)
 # --------------------------------------------------------------------------- residual sums
 
 
+def tp_dense_bwd_residual(tp, grad_out: Tensor, in1: Tensor, in2: Tensor, weights: Tensor,
+                          residual_in1: Optional[Tensor], residual_in1_comps: int, residual_in2: Optional[Tensor],
+                          out_in2: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
+    """Input gradients of the dense product ``tp(in1, in2, weights)`` (no edges) with other
+    gradients of the same inputs added in the kernel (``fc_tp_bwd_residual``):
+    grad_in1 = VJP + residual_in1 on the first ``residual_in1_comps`` components of each
+    in1 row (``residual_in1`` holds just those, ``residual_in1_comps * F`` values per row),
+    grad_in2 = VJP + residual_in2 (whole rows; ``out_in2`` may be ``residual_in2`` itself,
+    which then accumulates). Frozen weights: no weight gradient."""
+    _require_cuda(grad_out, in1, in2, weights)
+    lib = N.lib()
+    g, in1, in2, weights = grad_out.contiguous(), in1.contiguous(), in2.contiguous(), weights.contiguous()
+    desc = _tp_desc(tp.in1_l_max, tp.in2_l_max, tp.out_l_max, tp.in1_features, tp.in2_features,
+                    tp.symmetric_product, tp.shared_weights, tp.reduce_paths, in1.dtype)
+    g1 = torch.empty_like(in1)
+    g2 = torch.empty_like(in2) if out_in2 is None else out_in2
+    r1 = residual_in1
+    with _timed(f"tp_bwd_dense_{tp.in1_l_max}{tp.in2_l_max}{tp.out_l_max}", 1,
+                _nbytes(g, in1, in2, weights, g1, g2, *([r1] if r1 is not None else []),
+                        *([residual_in2] if residual_in2 is not None and residual_in2 is not g2 else []))):
+        rc = lib.fc_tp_bwd_residual(ctypes.byref(desc), _p(g), _p(in1), _p(in2), _p(weights), in1.shape[0],
+                                    _p(r1) if r1 is not None else None, r1.stride(0) if r1 is not None else 0,
+                                    int(residual_in1_comps) if r1 is not None else 0,
+                                    _p(residual_in2) if residual_in2 is not None else None, _p(g1), _p(g2),
+                                    ctypes.c_void_p(status_word(in1.device).data_ptr()), _stream(in1.device))
+    _after(lib, rc, "fc_tp_bwd_residual", in1.device)
+    return g1, g2
+
+
+
 def linear_residual_layout_ok(in_dim: int, out_dim: int, m_values: Sequence[int], f_in_values: Sequence[int],
                               f_out_values: Sequence[int], in_offsets: Sequence[int],
                               out_offsets: Sequence[int]) -> bool:

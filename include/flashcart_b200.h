@@ -155,6 +155,19 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
               const void* weights, const int64_t* rowptr, const int64_t* idx_j, int64_t n_out_rows,
               int64_t n_in1_rows, int64_t n_in2_rows, void* grad_in1, void* grad_in2,
               void* grad_weights, int32_t* status, fc_stream_t stream);
+/* Backward of a dense product (no edges) with gradients from elsewhere added in the same
+ * pass: grad_in1 = VJP_in1 + residual_in1 over the first residual_in1_comps components of
+ * each in1 row (residual rows of residual_in1_ld elements; the rest of the row has no
+ * residual), grad_in2 = VJP_in2 + residual_in2 (whole rows, may be grad_in2 itself). For
+ * the node-level products of the product layers (o3/_tensor_product.py:588-787 with
+ * rowptr == NULL), whose inputs also feed other terms of the layer's sum
+ * (nn/layers.py:768-1018). float32, both inputs with 64 or 128 channels, paths kept, no
+ * weight gradient, 8-byte aligned rows; otherwise FC_ERR_UNSUPPORTED. Either residual may
+ * be NULL. */
+int fc_tp_bwd_residual(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2,
+                       const void* weights, int64_t n_rows, const void* residual_in1, int64_t residual_in1_ld,
+                       int32_t residual_in1_comps, const void* residual_in2, void* grad_in1, void* grad_in2,
+                       int32_t* status, fc_stream_t stream);
 
 /* Double backward: VJP of fc_tp_bwd with tangents (v_in1, v_in2, v_weights) on its
  * three outputs (NULL = zero tangent). Replaces the autograd of flashcart::tp_bwd

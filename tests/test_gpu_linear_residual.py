@@ -140,3 +140,62 @@ def test_gpu_gated_layer_single_node_matches_composed(cuda_device, gate):
     assert _rel(y1, y2) < 2e-6
     assert _rel(gx1, gx2) < 2e-6
     check_device_status(dev)
+
+
+@pytest.mark.parametrize("out_l_max,C", [(3, 128), (0, 128), (2, 64)])
+def test_gpu_product_layer_single_node_matches_composed(cuda_device, out_l_max, C):
+    """ProductLayer as one autograd node (first-order evaluation, frozen weights: the dense
+    products' backward adds the sum's gradient to their in1 gradient and accumulates their
+    in2 gradient into the node-feature gradient, fc_tp_bwd_residual) against the composed
+    layer, for a layer that keeps every rank and one that keeps the low ranks only."""
+    from flashcart_b200.nn.layers import ProductLayer
+
+    dev = cuda_device
+    torch.manual_seed(11 + out_l_max)
+    in_l_max = 3 if C == 128 else 2
+    layer = ProductLayer(in_l_max, min(out_l_max, in_l_max), C, correlation=3, use_sc=True,
+                         use_layer_norm=True).to(dev)
+    _frozen(layer)
+    with torch.no_grad():
+        for p in layer.parameters():
+            if p.dim() > 0:
+                p.add_(0.1 * torch.randn_like(p))
+    x = torch.randn(900, layer.in_dim, device=dev) * 0.5
+    with ops.first_order_only():
+        x1 = x.clone().requires_grad_(True)
+        assert layer._single_node_ok(x1)
+        y1 = layer(x1)
+        g = torch.randn_like(y1)
+        (gx1,) = torch.autograd.grad(y1, [x1], g)
+    x2 = x.clone().requires_grad_(True)
+    y2 = layer(x2)
+    (gx2,) = torch.autograd.grad(y2, [x2], g)
+    assert _rel(y1, y2) < 5e-6
+    assert _rel(gx1, gx2) < 5e-6
+    check_device_status(dev)
+
+
+def test_gpu_tp_bwd_residual_through_the_c_abi(cuda_device):
+    """fc_tp_bwd_residual against fc_tp_bwd plus the residuals, twice into the same in2 buffer."""
+    dev = cuda_device
+    torch.manual_seed(12)
+    C, n = 128, 700
+    tp = o3.TensorProduct(3, 3, 3, C, C, shared_weights=True)
+    in1 = torch.randn(n, tp.in1_dim, device=dev)
+    in2 = torch.randn(n, tp.in2_dim, device=dev)
+    w = torch.randn(tp.n_total_paths * C, device=dev)
+    with torch.no_grad():
+        out = tp(in1, in2, w)
+    go = torch.randn_like(out)
+    a, b = in1.clone().requires_grad_(True), in2.clone().requires_grad_(True)
+    ref1, ref2 = torch.autograd.grad(tp(a, b, w), [a, b], go)
+    r1 = torch.randn(n, 4 * C, device=dev)  # the first 4 components (l <= 1) of each in1 row
+    r2 = torch.randn(n, tp.in2_dim, device=dev)
+    acc = r2.clone()
+    for _ in range(2):
+        g1, acc = ops.tp_dense_bwd_residual(tp, go, in1, in2, w, r1, 4, acc, out_in2=acc)
+    want1 = ref1.clone()
+    want1[:, :4 * C] += r1
+    assert _rel(g1, want1) < 2e-6
+    assert _rel(acc, r2 + 2 * ref2) < 2e-6
+    check_device_status(dev)
