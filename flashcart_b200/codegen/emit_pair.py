@@ -135,8 +135,12 @@ def _phase1(gs: GroupSlots, ind: str) -> List[str]:
 # 16-byte boundary, so one 16-byte broadcast load carries four entries (the duplicated-pair
 # layout carries two) and the packed operands are formed in registers. The forward is bound
 # by these shared-memory broadcasts; measured on the (3,3)->3 convolution of the 27,648-atom
-# water box (C = 128): 5.81 -> 5.13 ms per call.
+# water box (C = 128): 5.81 -> 5.13 ms per call. The backward and the four-channel forward
+# read the same layout: (3,3)->3 backward 13.72 -> 12.84 ms, (0,3)->3 backward 1.62 -> 1.57
+# ms, (0,3)->3 four-channel forward 0.73 -> 0.71 ms.
 FWD_SCALAR_M = True
+SCALAR_M_BWD = True
+SCALAR_M_FWD4 = True
 
 
 def scalar_offsets(gs: GroupSlots):
@@ -213,7 +217,7 @@ def _fwd_body(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
     return L
 
 
-def _bwd_body(gs: GroupSlots, ind: str, d2p: int) -> List[str]:
+def _bwd_body(gs: GroupSlots, ind: str, d2p: int, scalar: bool = False) -> List[str]:
     """Backward of one edge for the thread's channel pair; the first contribution to a
     gradient register assigns it."""
     sig = gs.sig
@@ -232,7 +236,7 @@ def _bwd_body(gs: GroupSlots, ind: str, d2p: int) -> List[str]:
         K = stf.oriented_path_tensor(r1, r2, o)
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
-        L.extend(_path_mload(gs, p, ind + "  "))
+        L.extend(_path_mload_scalar(gs, p, ind + "  ") if scalar else _path_mload(gs, p, ind + "  "))
         L.append(f"{ind}  const float2 wp = ld2(sw + {gs.w_pos[p]} * F);")
         if gs.gsmem:
             for a in range(2 * o + 1):
@@ -485,7 +489,10 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("  const bool NEED_1 = NM ? (NM & 1) != 0 : P.g_in1 != nullptr;")
         w("  const bool NEED_2 = NM ? (NM & 2) != 0 : P.g_in2 != nullptr;")
         w("  const bool NEED_W = NM ? (NM & 4) != 0 : P.g_w != nullptr;")
+        scal = SCALAR_M_BWD and scalar_offsets(gs)[1] <= 2 * gs.nmp
         L.extend(_setup(gs, f"{gs.ec * d2p}" + (f" + {gs.nacc} * F" if gs.gsmem else ""), "  "))
+        if scal:
+            w(f"  constexpr int NMF = {scalar_offsets(gs)[1]};  // edge-matrix floats per edge (scalar layout)")
         L.extend(_producer(gs, "  "))
         w("  float* gsm = extra;  // [EC][D2P] grad_in2 partial sums")
         if gs.gsmem:
@@ -507,7 +514,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w(f"  for (int64_t eb = 0; eb < ne_all; eb += {gs.ec}) {{")
         w(f"    const int ne = (int)min((int64_t){gs.ec}, ne_all - eb);")
         w(f"    for (int u = t; u < {gs.ec * d2p}; u += NC) gsm[u] = 0.0f;")
-        L.extend(_phase1_loop(gs, "    "))
+        L.extend(_phase1_loop(gs, "    ", scalar=scal))
         w("    for (int k = 0; k < ne; ++k) {")
         L.extend(_edge_begin(gs, "      "))
         w("      if (j >= 0) {")
@@ -518,8 +525,11 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("        for (int q = 0; q < XN; ++q) x1[q] = ld2(sx + q * F);")
         w("        const float* sw = sx + XN * F;")
         w("        float* __restrict__ gwr = NEED_W ? P.g_w + e * (int64_t)(NP * F) + 2 * t : nullptr;")
-        w("        const float2* m = m2 + k * NMP;")
-        L.extend(_bwd_body(gs, "        ", d2p))
+        if scal:
+            w("        const float* mf = reinterpret_cast<const float*>(m2) + k * NMF;")
+        else:
+            w("        const float2* m = m2 + k * NMP;")
+        L.extend(_bwd_body(gs, "        ", d2p, scalar=scal))
         w("        if (NEED_1) {")
         w("          float* __restrict__ t1 = P.g_in1 + j * (int64_t)(D1 * F) + XLO * F + 2 * t;")
         w("          for (int q = 0; q < XN; ++q) red2(t1 + q * F, gx1[q]);")
@@ -639,7 +649,7 @@ def make_groups4(sig) -> List[List[int]]:
     return groups
 
 
-def _fwd4_body(gs: GroupSlots, ind: str) -> List[str]:
+def _fwd4_body(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
     sig = gs.sig
     L = []
     acc_base = 0
@@ -647,7 +657,7 @@ def _fwd4_body(gs: GroupSlots, ind: str) -> List[str]:
         r1, r2, o = sig.paths[p]
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
-        L.extend(_path_mload(gs, p, ind + "  "))
+        L.extend(_path_mload_scalar(gs, p, ind + "  ") if scalar else _path_mload(gs, p, ind + "  "))
         L.append(f"{ind}  float2 wpa, wpb;")
         L.append(f"{ind}  ld4p(sw + {gs.w_pos[p]} * F, wpa, wpb);")
         for a in range(2 * o + 1):
@@ -694,14 +704,17 @@ def emit_fwd4(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("  return 0;")
     w("}")
     for gi, gs in enumerate(groups):
+        scal = SCALAR_M_FWD4 and scalar_offsets(gs)[1] <= 2 * gs.nmp
         w(f"__device__ __forceinline__ void fwd4_g{gi}(const TpParams<float>& P, unsigned char* smem) {{")
         L.extend(_setup(gs, "0", "  ", channels_per_thread=4))
+        if scal:
+            w(f"  constexpr int NMF = {scalar_offsets(gs)[1]};  // edge-matrix floats per edge (scalar layout)")
         L.extend(_producer(gs, "  "))
         w(f"  float2 acca[{gs.nacc}], accb[{gs.nacc}];")
         w(f"  for (int q = 0; q < {gs.nacc}; ++q) {{ acca[q] = p2(0.0f); accb[q] = p2(0.0f); }}")
         w(f"  for (int64_t eb = 0; eb < ne_all; eb += {gs.ec}) {{")
         w(f"    const int ne = (int)min((int64_t){gs.ec}, ne_all - eb);")
-        L.extend(_phase1_loop(gs, "    "))
+        L.extend(_phase1_loop(gs, "    ", scalar=scal))
         w("    for (int k = 0; k < ne; ++k) {")
         L.extend(_edge_begin(gs, "      "))
         w("      if (j >= 0) {")
@@ -709,8 +722,11 @@ def emit_fwd4(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("        float2 x1a[XN], x1b[XN];")
         w("        for (int q = 0; q < XN; ++q) ld4p(sx + q * F, x1a[q], x1b[q]);")
         w("        const float* sw = sx + XN * F;")
-        w("        const float2* m = m2 + k * NMP;")
-        L.extend(_fwd4_body(gs, "        "))
+        if scal:
+            w("        const float* mf = reinterpret_cast<const float*>(m2) + k * NMF;")
+        else:
+            w("        const float2* m = m2 + k * NMP;")
+        L.extend(_fwd4_body(gs, "        ", scalar=scal))
         w("      }")
         L.extend(_edge_end("      "))
         w("    }")
