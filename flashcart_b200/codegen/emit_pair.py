@@ -29,8 +29,8 @@ CTA = one receiver row. ``F/2`` consumer threads plus one producer warp:
   up to RING edges ahead;
 * the consumers walk the edges in chunks of EC: the edge matrices
   ``M_p[a, i] = sum_j K_p[a, i, j] x2_j`` of the chunk are computed cooperatively into
-  shared memory (stored as duplicated pairs so that one 16-byte load gives two packed
-  operands), then per edge every consumer thread waits for the slot, reads the sender
+  shared memory (plain floats, each path's entries 16-byte aligned, so that one 16-byte
+  broadcast load gives four entries), then per edge every consumer thread waits for the slot, reads the sender
   index from the slot header and does the path-group arithmetic for its two channels.
   Consumers synchronise among themselves with a named barrier; the producer is never
   part of a CTA-wide barrier after the roles split.
@@ -118,29 +118,13 @@ def _chain(pairs: Sequence[Tuple[str, str]], init: str = "") -> str:
     return f"padd({_chain(pairs[0::2], init)}, {_chain(pairs[1::2])})"
 
 
-def _phase1(gs: GroupSlots, ind: str) -> List[str]:
-    L = [f"{ind}switch (part) {{"]
-    per = (gs.nm + NPART - 1) // NPART
-    for part in range(NPART):
-        L.append(f"{ind}  case {part}:")
-        for s in range(part * per, min(gs.nm, (part + 1) * per)):
-            if gs.slots[s] is not None:
-                L.append(f"{ind}    {{ const T v = {gs.m_expr(s)}; m[{s}] = make_float2(v, v); }}")
-        L.append(f"{ind}    break;")
-    L.append(f"{ind}}}")
-    return L
-
-
-# Forward edge matrices as plain floats (FWD_SCALAR_M): each path's entries start on a
-# 16-byte boundary, so one 16-byte broadcast load carries four entries (the duplicated-pair
-# layout carries two) and the packed operands are formed in registers. The forward is bound
-# by these shared-memory broadcasts; measured on the (3,3)->3 convolution of the 27,648-atom
-# water box (C = 128): 5.81 -> 5.13 ms per call. The backward and the four-channel forward
-# read the same layout: (3,3)->3 backward 13.72 -> 12.84 ms, (0,3)->3 backward 1.62 -> 1.57
-# ms, (0,3)->3 four-channel forward 0.73 -> 0.71 ms.
-FWD_SCALAR_M = True
-SCALAR_M_BWD = True
-SCALAR_M_FWD4 = True
+# Edge matrices in shared memory as plain floats: each path's entries start on a 16-byte
+# boundary, so one 16-byte broadcast load carries four entries and the packed f32x2
+# operands are formed in registers. The pair kernels are bound by these shared-memory
+# broadcasts; against the earlier layout of duplicated pairs (two entries per 16-byte load),
+# measured on the 27,648-atom water box (C = 128): (3,3)->3 forward 5.81 -> 5.13 ms, backward
+# 13.72 -> 12.84 ms, (0,3)->3 backward 1.62 -> 1.57 ms, four-channel forward 0.73 -> 0.71 ms.
+# The shared-memory carve-up keeps NMP pairs per edge (2 * NMP >= NMF floats).
 
 
 def scalar_offsets(gs: GroupSlots):
@@ -153,7 +137,7 @@ def scalar_offsets(gs: GroupSlots):
     return off, max(pos, 4)
 
 
-def _phase1_scalar(gs: GroupSlots, ind: str) -> List[str]:
+def _phase1(gs: GroupSlots, ind: str) -> List[str]:
     off, _ = scalar_offsets(gs)
     where = {}
     for p in gs.paths:
@@ -172,7 +156,8 @@ def _phase1_scalar(gs: GroupSlots, ind: str) -> List[str]:
     return L
 
 
-def _path_mload_scalar(gs: GroupSlots, p: int, ind: str) -> List[str]:
+def _path_mload(gs: GroupSlots, p: int, ind: str) -> List[str]:
+    """Edge-matrix entries of one path: 16-byte shared loads of four entries each."""
     off, _ = scalar_offsets(gs)
     s0, s1 = gs.range[p]
     n = s1 - s0
@@ -186,18 +171,7 @@ def _path_mload_scalar(gs: GroupSlots, p: int, ind: str) -> List[str]:
     return L
 
 
-def _path_mload(gs: GroupSlots, p: int, ind: str) -> List[str]:
-    """Edge-matrix entries of one path: 16-byte shared loads of two duplicated pairs each."""
-    s0, s1 = gs.range[p]
-    n = s1 - s0
-    n2 = max(1, (n + 1) // 2)
-    L = [f"{ind}float2 mv[{2 * n2}];"]
-    for k in range(n2):
-        L.append(f"{ind}ld2x2(m + {s0 + 2 * k}, mv + {2 * k});")
-    return L
-
-
-def _fwd_body(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
+def _fwd_body(gs: GroupSlots, ind: str) -> List[str]:
     sig = gs.sig
     L = []
     acc_base = 0
@@ -205,7 +179,7 @@ def _fwd_body(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
         r1, r2, o = sig.paths[p]
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
-        L.extend(_path_mload_scalar(gs, p, ind + "  ") if scalar else _path_mload(gs, p, ind + "  "))
+        L.extend(_path_mload(gs, p, ind + "  "))
         L.append(f"{ind}  const float2 wp = ld2(sw + {gs.w_pos[p]} * F);")
         for a in range(2 * o + 1):
             pairs = [(f"mv[{gs.index[(p, a, i)] - s0}]", f"x1[{_q(r1, i) - gs.x_lo}]") for i in range(2 * r1 + 1)
@@ -217,7 +191,7 @@ def _fwd_body(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
     return L
 
 
-def _bwd_body(gs: GroupSlots, ind: str, d2p: int, scalar: bool = False) -> List[str]:
+def _bwd_body(gs: GroupSlots, ind: str, d2p: int) -> List[str]:
     """Backward of one edge for the thread's channel pair; the first contribution to a
     gradient register assigns it."""
     sig = gs.sig
@@ -236,7 +210,7 @@ def _bwd_body(gs: GroupSlots, ind: str, d2p: int, scalar: bool = False) -> List[
         K = stf.oriented_path_tensor(r1, r2, o)
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
-        L.extend(_path_mload_scalar(gs, p, ind + "  ") if scalar else _path_mload(gs, p, ind + "  "))
+        L.extend(_path_mload(gs, p, ind + "  "))
         L.append(f"{ind}  const float2 wp = ld2(sw + {gs.w_pos[p]} * F);")
         if gs.gsmem:
             for a in range(2 * o + 1):
@@ -365,7 +339,7 @@ def _producer(gs: GroupSlots, ind: str) -> List[str]:
     return L
 
 
-def _phase1_loop(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
+def _phase1_loop(gs: GroupSlots, ind: str) -> List[str]:
     if gs.stage:
         load = [f"{ind}    const T* a2 = xbuf + (cidx & 1) * {gs.ec * gs.sig.d2} + le * D2;",
                 f"{ind}    for (int q = 0; q < D2; ++q) x2[q] = xok ? a2[q] : T(0);"]
@@ -382,9 +356,8 @@ def _phase1_loop(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
             f"{ind}  if (le < ne) {{",
             f"{ind}    T x2[D2];",
             *load,
-            *([f"{ind}    float* mf = reinterpret_cast<float*>(m2) + le * NMF;"] if scalar else
-              [f"{ind}    float2* m = m2 + le * NMP;"]),
-            *(_phase1_scalar(gs, ind + "    ") if scalar else _phase1(gs, ind + "    ")),
+            f"{ind}    float* mf = reinterpret_cast<float*>(m2) + le * NMF;",
+            *_phase1(gs, ind + "    "),
             f"{ind}  }}",
             f"{ind}}}",
             f"{ind}fc_named_sync(1, NC);",
@@ -436,17 +409,15 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("}")
     # ---------------- forward
     for gi, gs in enumerate(groups):
-        scal = FWD_SCALAR_M and scalar_offsets(gs)[1] <= 2 * gs.nmp
         w(f"__device__ __forceinline__ void fwd3_g{gi}(const TpParams<float>& P, unsigned char* smem) {{")
         L.extend(_setup(gs, "0", "  "))
-        if scal:
-            w(f"  constexpr int NMF = {scalar_offsets(gs)[1]};  // edge-matrix floats per edge (scalar layout)")
+        w(f"  constexpr int NMF = {scalar_offsets(gs)[1]};  // edge-matrix floats per edge (scalar layout)")
         L.extend(_producer(gs, "  "))
         w(f"  float2 acc[{gs.nacc}];")
         w(f"  for (int q = 0; q < {gs.nacc}; ++q) acc[q] = p2(0.0f);")
         w(f"  for (int64_t eb = 0; eb < ne_all; eb += {gs.ec}) {{")
         w(f"    const int ne = (int)min((int64_t){gs.ec}, ne_all - eb);")
-        L.extend(_phase1_loop(gs, "    ", scalar=scal))
+        L.extend(_phase1_loop(gs, "    "))
         w("    for (int k = 0; k < ne; ++k) {")
         L.extend(_edge_begin(gs, "      "))
         w("      if (j >= 0) {")
@@ -454,11 +425,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("        float2 x1[XN];")
         w("        for (int q = 0; q < XN; ++q) x1[q] = ld2(sx + q * F);")
         w("        const float* sw = sx + XN * F;")
-        if scal:
-            w("        const float* mf = reinterpret_cast<const float*>(m2) + k * NMF;")
-        else:
-            w("        const float2* m = m2 + k * NMP;")
-        L.extend(_fwd_body(gs, "        ", scalar=scal))
+        w("        const float* mf = reinterpret_cast<const float*>(m2) + k * NMF;")
+        L.extend(_fwd_body(gs, "        "))
         w("      }")
         L.extend(_edge_end("      "))
         w("    }")
@@ -489,10 +457,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("  const bool NEED_1 = NM ? (NM & 1) != 0 : P.g_in1 != nullptr;")
         w("  const bool NEED_2 = NM ? (NM & 2) != 0 : P.g_in2 != nullptr;")
         w("  const bool NEED_W = NM ? (NM & 4) != 0 : P.g_w != nullptr;")
-        scal = SCALAR_M_BWD and scalar_offsets(gs)[1] <= 2 * gs.nmp
         L.extend(_setup(gs, f"{gs.ec * d2p}" + (f" + {gs.nacc} * F" if gs.gsmem else ""), "  "))
-        if scal:
-            w(f"  constexpr int NMF = {scalar_offsets(gs)[1]};  // edge-matrix floats per edge (scalar layout)")
+        w(f"  constexpr int NMF = {scalar_offsets(gs)[1]};  // edge-matrix floats per edge (scalar layout)")
         L.extend(_producer(gs, "  "))
         w("  float* gsm = extra;  // [EC][D2P] grad_in2 partial sums")
         if gs.gsmem:
@@ -514,7 +480,7 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w(f"  for (int64_t eb = 0; eb < ne_all; eb += {gs.ec}) {{")
         w(f"    const int ne = (int)min((int64_t){gs.ec}, ne_all - eb);")
         w(f"    for (int u = t; u < {gs.ec * d2p}; u += NC) gsm[u] = 0.0f;")
-        L.extend(_phase1_loop(gs, "    ", scalar=scal))
+        L.extend(_phase1_loop(gs, "    "))
         w("    for (int k = 0; k < ne; ++k) {")
         L.extend(_edge_begin(gs, "      "))
         w("      if (j >= 0) {")
@@ -525,11 +491,8 @@ def emit(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("        for (int q = 0; q < XN; ++q) x1[q] = ld2(sx + q * F);")
         w("        const float* sw = sx + XN * F;")
         w("        float* __restrict__ gwr = NEED_W ? P.g_w + e * (int64_t)(NP * F) + 2 * t : nullptr;")
-        if scal:
-            w("        const float* mf = reinterpret_cast<const float*>(m2) + k * NMF;")
-        else:
-            w("        const float2* m = m2 + k * NMP;")
-        L.extend(_bwd_body(gs, "        ", d2p, scalar=scal))
+        w("        const float* mf = reinterpret_cast<const float*>(m2) + k * NMF;")
+        L.extend(_bwd_body(gs, "        ", d2p))
         w("        if (NEED_1) {")
         w("          float* __restrict__ t1 = P.g_in1 + j * (int64_t)(D1 * F) + XLO * F + 2 * t;")
         w("          for (int q = 0; q < XN; ++q) red2(t1 + q * F, gx1[q]);")
@@ -649,7 +612,7 @@ def make_groups4(sig) -> List[List[int]]:
     return groups
 
 
-def _fwd4_body(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
+def _fwd4_body(gs: GroupSlots, ind: str) -> List[str]:
     sig = gs.sig
     L = []
     acc_base = 0
@@ -657,7 +620,7 @@ def _fwd4_body(gs: GroupSlots, ind: str, scalar: bool = False) -> List[str]:
         r1, r2, o = sig.paths[p]
         s0 = gs.range[p][0]
         L.append(f"{ind}{{ // path {p}: ({r1},{r2})->{o}")
-        L.extend(_path_mload_scalar(gs, p, ind + "  ") if scalar else _path_mload(gs, p, ind + "  "))
+        L.extend(_path_mload(gs, p, ind + "  "))
         L.append(f"{ind}  float2 wpa, wpb;")
         L.append(f"{ind}  ld4p(sw + {gs.w_pos[p]} * F, wpa, wpb);")
         for a in range(2 * o + 1):
@@ -704,17 +667,15 @@ def emit_fwd4(sig, store_offsets: List[Tuple[int, int]]) -> str:
     w("  return 0;")
     w("}")
     for gi, gs in enumerate(groups):
-        scal = SCALAR_M_FWD4 and scalar_offsets(gs)[1] <= 2 * gs.nmp
         w(f"__device__ __forceinline__ void fwd4_g{gi}(const TpParams<float>& P, unsigned char* smem) {{")
         L.extend(_setup(gs, "0", "  ", channels_per_thread=4))
-        if scal:
-            w(f"  constexpr int NMF = {scalar_offsets(gs)[1]};  // edge-matrix floats per edge (scalar layout)")
+        w(f"  constexpr int NMF = {scalar_offsets(gs)[1]};  // edge-matrix floats per edge (scalar layout)")
         L.extend(_producer(gs, "  "))
         w(f"  float2 acca[{gs.nacc}], accb[{gs.nacc}];")
         w(f"  for (int q = 0; q < {gs.nacc}; ++q) {{ acca[q] = p2(0.0f); accb[q] = p2(0.0f); }}")
         w(f"  for (int64_t eb = 0; eb < ne_all; eb += {gs.ec}) {{")
         w(f"    const int ne = (int)min((int64_t){gs.ec}, ne_all - eb);")
-        L.extend(_phase1_loop(gs, "    ", scalar=scal))
+        L.extend(_phase1_loop(gs, "    "))
         w("    for (int k = 0; k < ne; ++k) {")
         L.extend(_edge_begin(gs, "      "))
         w("      if (j >= 0) {")
@@ -722,11 +683,8 @@ def emit_fwd4(sig, store_offsets: List[Tuple[int, int]]) -> str:
         w("        float2 x1a[XN], x1b[XN];")
         w("        for (int q = 0; q < XN; ++q) ld4p(sx + q * F, x1a[q], x1b[q]);")
         w("        const float* sw = sx + XN * F;")
-        if scal:
-            w("        const float* mf = reinterpret_cast<const float*>(m2) + k * NMF;")
-        else:
-            w("        const float2* m = m2 + k * NMP;")
-        L.extend(_fwd4_body(gs, "        ", scalar=scal))
+        w("        const float* mf = reinterpret_cast<const float*>(m2) + k * NMF;")
+        L.extend(_fwd4_body(gs, "        "))
         w("      }")
         L.extend(_edge_end("      "))
         w("    }")

@@ -122,12 +122,6 @@ __device__ __forceinline__ float2 padd(float2 a, float2 b) { return __fadd2_rn(a
 __device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
 __device__ __forceinline__ float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
 __device__ __forceinline__ void st2(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
-// Two consecutive float2 values of shared memory (16-byte aligned) with one 16-byte load.
-__device__ __forceinline__ void ld2x2(const float2* p, float2* v) {
-  const float4 q = *reinterpret_cast<const float4*>(p);
-  v[0] = make_float2(q.x, q.y);
-  v[1] = make_float2(q.z, q.w);
-}
 // Four consecutive floats (16-byte aligned) as two channel pairs, and back.
 __device__ __forceinline__ void ld4p(const float* p, float2& a, float2& b) {
   const float4 q = *reinterpret_cast<const float4*>(p);
