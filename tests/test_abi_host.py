@@ -141,3 +141,53 @@ def test_new_entry_points_reject_bad_arguments(emu_lib):
                                 P(sc.data_ptr()), I(3), P(g.data_ptr()), None, None, None, None)
     with pytest.raises(ValueError, match="null weight tangent for rank 1"):
         N.check(emu_lib, rc, "fc_linear_dbwd")
+
+
+def test_residual_entry_points_reject_bad_arguments(emu_lib):
+    """Validation of fc_tp_bwd_residual, fc_linear_fwd_residual and fc_linear_bwd_residual:
+    every refusal is decided on the host, before anything is read or launched."""
+    P, I = ctypes.c_void_p, ctypes.c_int64
+    C, n = 128, 4
+    d = N.TpDesc(3, 3, 3, C, C, 0, 1, 0, N.FC_F32)
+    rows = torch.zeros(n, 16 * C)
+    go = torch.zeros(n, 99 * C)
+    w = torch.zeros(23 * C)
+
+    def tp_res(desc, r1, ld, comps, base=rows):
+        return emu_lib.fc_tp_bwd_residual(ctypes.byref(desc), P(go.data_ptr()), P(base.data_ptr()),
+                                          P(rows.data_ptr()), P(w.data_ptr()), I(n), r1, I(ld), comps, None,
+                                          P(rows.data_ptr()), P(rows.data_ptr()), None, None)
+
+    r1 = P(rows.data_ptr())
+    for ld, comps in ((4 * C + 1, 4), (2 * C, 4), (16 * C, 17), (16 * C, -1)):  # odd, short, too many, negative
+        with pytest.raises(ValueError, match="residual_in1 layout"):
+            N.check(emu_lib, tp_res(d, r1, ld, comps), "fc_tp_bwd_residual")
+    for bad in (N.TpDesc(3, 3, 3, C, C, 0, 1, 0, N.FC_F64), N.TpDesc(3, 3, 3, 96, 96, 0, 1, 0, N.FC_F32),
+                N.TpDesc(3, 3, 3, C, C, 0, 1, 1, N.FC_F32)):  # float64, 96 channels, reduced paths
+        assert tp_res(bad, r1, 4 * C, 4) == N.FC_ERR_UNSUPPORTED
+        assert b"float32 dense products" in emu_lib.fc_last_error()
+    odd = P(rows.data_ptr() + 4)  # rows that are not 8-byte aligned
+    assert tp_res(d, odd, 4 * C, 4) == N.FC_ERR_UNSUPPORTED
+    with pytest.raises(ValueError, match="negative size"):
+        N.check(emu_lib, emu_lib.fc_tp_bwd_residual(ctypes.byref(d), None, None, None, None, I(-1), None, I(0), 0,
+                                                    None, None, None, None, None), "fc_tp_bwd_residual")
+
+    ld = A.linear_desc(1, 1, 8, 8, [1, 1], torch.float32)
+    x = torch.zeros(n, ld.in_dim)
+    ws = [torch.zeros(8, 8), torch.zeros(8, 8)]
+    sc = torch.ones(2)
+    for name in ("fc_linear_fwd_residual", "fc_linear_bwd_residual"):
+        fn = getattr(emu_lib, name)
+        assert fn(ctypes.byref(ld), P(x.data_ptr()), A.ptr_array(ws), None, P(sc.data_ptr()), I(0), None, None,
+                  None, None) == 0  # no rows: nothing to do
+        with pytest.raises(ValueError, match="null tensor"):
+            N.check(emu_lib, fn(ctypes.byref(ld), P(x.data_ptr()), A.ptr_array(ws), None, P(sc.data_ptr()), I(n),
+                                None, P(x.data_ptr()), None, None), name)
+        part = A.linear_desc(1, 1, 8, 8, [1, 1], torch.float32)
+        part.n_active = 1  # rank 1 of the output row left to nobody
+        assert fn(ctypes.byref(part), P(x.data_ptr()), A.ptr_array(ws), None, P(sc.data_ptr()), I(n),
+                  P(x.data_ptr()), P(x.data_ptr()), None, None) == N.FC_ERR_UNSUPPORTED
+        assert b"cover the output row" in emu_lib.fc_last_error()
+        xd = A.linear_desc(1, 1, 8, 8, [1, 1], torch.float64)
+        assert fn(ctypes.byref(xd), P(x.data_ptr()), A.ptr_array(ws), None, P(sc.data_ptr()), I(n),
+                  P(x.data_ptr()), P(x.data_ptr()), None, None) == N.FC_ERR_UNSUPPORTED
