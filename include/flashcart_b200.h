@@ -163,7 +163,8 @@ int fc_tp_bwd(const fc_tp_desc* desc, const void* grad_out, const void* in1, con
  * rowptr == NULL), whose inputs also feed other terms of the layer's sum
  * (nn/layers.py:768-1018). float32, both inputs with 64 or 128 channels, paths kept, no
  * weight gradient, 8-byte aligned rows; otherwise FC_ERR_UNSUPPORTED. Either residual may
- * be NULL. */
+ * be NULL. residual_in1_comps must lie in [0, (in1_l_max + 1)^2] and residual_in1_ld be
+ * even and at least residual_in1_comps x in1_features; otherwise FC_ERR_INVALID. */
 int fc_tp_bwd_residual(const fc_tp_desc* desc, const void* grad_out, const void* in1, const void* in2,
                        const void* weights, int64_t n_rows, const void* residual_in1, int64_t residual_in1_ld,
                        int32_t residual_in1_comps, const void* residual_in2, void* grad_in1, void* grad_in2,
